@@ -1,0 +1,131 @@
+"""Generate golden vectors by executing the reference MoELayer on CPU.
+
+Run in a container where the VelvetOptimizer sources are mounted (read-only) at
+``/root/reference``::
+
+    python tests/golden/make_golden.py            # writes tests/golden/*.npz
+
+The reference's Python package is imported in place (``sys.path``), never copied.
+Inputs come from ``oracle.inputs.make_inputs`` (seeded numpy), are loaded into the
+reference module through its own state_dict keys, and the forward runs exactly as
+``MoELayer.forward`` (python/vesper/model.py:317-364).  The router logits are captured
+with a forward hook on ``moe.router``; softmax / top-K are recomputed from them with the
+same torch calls as model.py:323-329 to record the reference's routing.
+
+Each ``<name>.npz`` stores only the case description (JSON) and the outputs, not the
+inputs: tests rebuild the inputs from the seed.
+"""
+from __future__ import annotations
+
+import json
+import os
+import sys
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+REPO = os.path.dirname(os.path.dirname(HERE))
+REFERENCE_PY = "/root/reference/python"
+sys.path.insert(0, REPO)
+
+from oracle.inputs import MoECase, make_inputs  # noqa: E402
+
+# name -> case.  Small enough to commit; together they cover the reference's own edge
+# cases (K == E, E == 2, a single token, empty experts, K = 1) and the option set
+# (biases, FlyLoRA on, Zipf router bias, an all-tied router).
+CASES = {
+    "c1_fp32": MoECase(tokens=512, batch=2, hidden=768, inter=3072, experts=8, top_k=2),
+    "t1_single_token": MoECase(tokens=1, batch=1, hidden=64, inter=128, experts=4, top_k=2, seed=1),
+    "t3_k_eq_e": MoECase(tokens=3, batch=1, hidden=32, inter=64, experts=2, top_k=2, seed=2),
+    "t127_bias": MoECase(tokens=127, batch=1, hidden=96, inter=160, experts=8, top_k=3,
+                         bias_std=0.05, seed=3),
+    "t5_empty_experts": MoECase(tokens=5, batch=1, hidden=48, inter=80, experts=16, top_k=1, seed=4),
+    "t256_lora_zipf": MoECase(tokens=256, batch=2, hidden=128, inter=256, experts=16, top_k=4,
+                              lora_on=True, zipf_alpha=1.2, seed=5),
+    "t64_tied_router": MoECase(tokens=64, batch=4, hidden=64, inter=96, experts=8, top_k=2,
+                               router_std=0.0, seed=6),
+    "t200_era_tails": MoECase(tokens=200, batch=2, hidden=64, inter=128, experts=4, top_k=2,
+                              weight_std=0.5, bias_std=2.0, seed=7),
+}
+
+
+def reference_layer(case: MoECase, inp: dict[str, np.ndarray]):
+    import torch
+    sys.path.insert(0, REFERENCE_PY)
+    from vesper.config import VesperConfig  # noqa: E402
+    from vesper.model import MoELayer  # noqa: E402
+
+    cfg = VesperConfig(hidden_size=case.hidden, intermediate_size=case.inter,
+                       num_heads=1, era_gamma=case.era_gamma,
+                       flylora_rank=case.lora_rank, flylora_alpha=case.lora_alpha)
+    cfg.with_moe(num_experts=case.experts, top_k=case.top_k)
+    cfg.validate()
+    torch.manual_seed(case.seed)
+    moe = MoELayer(cfg)
+    sd = moe.state_dict()
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a))  # noqa: E731
+    new = {"router.weight": t(inp["w_r"]), "router.bias": t(inp["b_r"])}
+    for e in range(case.experts):
+        for p, name in (("g", "gate_proj"), ("u", "up_proj")):
+            pre = f"experts.{e}.{name}"
+            new[f"{pre}.base.weight"] = t(inp[f"w_{p}"][e])
+            new[f"{pre}.base.bias"] = t(inp[f"b_{p}"][e])
+            new[f"{pre}.lora_down.weight"] = t(inp[f"a_{p}"][e])
+            new[f"{pre}.lora_down.bias"] = t(inp[f"ba_{p}"][e])
+            new[f"{pre}.lora_up.weight"] = t(inp[f"l_{p}"][e])
+            new[f"{pre}.lora_up.bias"] = t(inp[f"bl_{p}"][e])
+            new[f"{pre}.proj_a"] = sd[f"{pre}.proj_a"]
+        new[f"experts.{e}.down_proj.weight"] = t(inp["w_d"][e])
+        new[f"experts.{e}.down_proj.bias"] = t(inp["b_d"][e])
+    assert set(new) == set(sd), set(sd) ^ set(new)
+    moe.load_state_dict(new)
+    moe.eval()
+    return moe
+
+
+def run_reference(case: MoECase):
+    import torch
+    import torch.nn.functional as F
+
+    inp = make_inputs(case)
+    moe = reference_layer(case, inp)
+    captured = {}
+    moe.router.register_forward_hook(lambda m, i, o: captured.__setitem__("logits", o.detach().clone()))
+    x = torch.from_numpy(inp["x"]).reshape(case.batch, case.seq, case.hidden)
+    with torch.no_grad():
+        out, aux = moe(x)
+    logits = captured["logits"]
+    probs = F.softmax(logits, dim=-1)                       # model.py:323
+    topv, topi = torch.topk(probs, case.top_k, dim=-1)      # model.py:326
+    topw = topv / topv.sum(dim=-1, keepdim=True)            # model.py:329
+    T = case.tokens
+    idx = topi.reshape(T, case.top_k).numpy().astype(np.int64)
+    counts = np.bincount(idx.reshape(-1), minlength=case.experts)
+    perm = [np.nonzero((idx == e).any(-1))[0] for e in range(case.experts)]  # model.py:346-347
+    return {
+        "logits": logits.reshape(T, case.experts).numpy(),
+        "probs": probs.reshape(T, case.experts).numpy(),
+        "topk_idx": idx,
+        "topk_w": topw.reshape(T, case.top_k).numpy(),
+        "counts": counts.astype(np.int64),
+        "perm_tok": np.concatenate(perm).astype(np.int64) if perm else np.zeros(0, np.int64),
+        "out": out.reshape(T, case.hidden).numpy(),
+        "aux": np.asarray(aux.item(), dtype=np.float32),
+    }
+
+
+def main(names=None):
+    import torch
+    torch.set_num_threads(os.cpu_count() or 1)
+    for name, case in CASES.items():
+        if names and name not in names:
+            continue
+        res = run_reference(case)
+        path = os.path.join(HERE, f"{name}.npz")
+        np.savez_compressed(path, case=np.asarray(json.dumps(case.to_dict())),
+                            torch_version=np.asarray(torch.__version__), **res)
+        print(f"{name}: aux={float(res['aux']):.6f} counts={res['counts'].tolist()} -> {path}")
+
+
+if __name__ == "__main__":
+    main(sys.argv[1:] or None)

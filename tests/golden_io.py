@@ -1,0 +1,20 @@
+"""Load the committed golden vectors (produced by tests/golden/make_golden.py)."""
+import glob
+import json
+import os
+
+import numpy as np
+
+from oracle.inputs import MoECase
+
+GOLDEN_DIR = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+
+
+def golden_names():
+    return sorted(os.path.basename(p)[:-4] for p in glob.glob(os.path.join(GOLDEN_DIR, "*.npz")))
+
+
+def load_golden(name):
+    z = np.load(os.path.join(GOLDEN_DIR, f"{name}.npz"))
+    case = MoECase(**json.loads(str(z["case"])))
+    return case, {k: z[k] for k in z.files if k not in ("case", "torch_version")}
