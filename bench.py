@@ -1,0 +1,429 @@
+#!/usr/bin/env python
+"""MoE-layer forward benchmark on B200 (one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload c5_ep|c3_prefill|c4_skewed|c2_decode]
+
+A step is one MoE FFN layer forward (router -> dispatch -> gate/up GEMM with ERA -> down
+GEMM -> combine -> aux loss) over one batch of synthetic tokens per GPU.  The default
+workload is the expert-parallel layer quoted at 1/2/4/8 GPUs: 65,536 tokens per GPU,
+d_model 4096, expert d_ff 2048, 64 experts, top-4, bf16; x ~ N(0,1), weights ~ N(0,0.02),
+zero biases, FlyLoRA off.
+
+* ``value``  tokens/s of the whole job, inputs resident in HBM, CUDA events around
+  exactly K steps bracketed by barrier + synchronize, max over ranks.  Inputs (x: 512 MiB,
+  weights: 3.2 GiB) are larger than the 126 MB L2, so no flush is needed between steps.
+* ``e2e``    the same metric through ``MoELayer.forward`` with the step's x copied from
+  pinned host memory and the output copied back to pinned host memory inside the timed
+  region.
+* ``roofline`` the dominant kernel (the gate/up grouped GEMM) from CUDA events recorded
+  around every launch of the timed region; algorithmic FLOPs = 4 * T * K * H * I.
+* ``cpu_baseline`` the CPU restatement of the reference algorithm (the oracle, numpy fp32)
+  on a bounded token sample of the same workload on this host's cores.
+* ``--impl reference`` times that CPU implementation alone (no GPU work).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, REPO)
+
+# name -> (tokens per GPU, batch, hidden, inter, experts, top_k, lora_on, zipf_alpha)
+WORKLOADS = {
+    "c5_ep": dict(tokens=65536, batch=16, hidden=4096, inter=2048, experts=64, top_k=4),
+    "c3_prefill": dict(tokens=32768, batch=8, hidden=2048, inter=8192, experts=8, top_k=2),
+    "c4_skewed": dict(tokens=32768, batch=8, hidden=2048, inter=1024, experts=64, top_k=8,
+                      lora_on=True, zipf_alpha=1.2),
+    "c2_decode": dict(tokens=64, batch=64, hidden=2048, inter=8192, experts=8, top_k=2),
+}
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
+
+
+def parse_args():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=50)
+    p.add_argument("--warmup", type=int, default=5)
+    p.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    p.add_argument("--workload", choices=list(WORKLOADS), default="c5_ep")
+    p.add_argument("--cpu-seconds", type=float, default=10.0,
+                   help="target CPU time of the cpu_baseline sample")
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    return p.parse_args()
+
+
+def peaks():
+    path = os.path.join(REPO, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            d = json.load(f)
+        return {"hbm_gbs": float(d["hbm_gbs"]), "bf16_tflops": float(d["bf16_tflops"]),
+                "source": "measured"}
+    except (OSError, KeyError, ValueError):
+        return dict(FALLBACK_PEAKS, source="fallback")
+
+
+def algorithmic(w, elt=2):
+    """Algorithmic work per forward: FLOPs of the expert GEMMs, bytes of the data stages."""
+    T, H, I, E, K = w["tokens"], w["hidden"], w["inter"], w["experts"], w["top_k"]
+    return {
+        "gemm1_flop": 4.0 * T * K * H * I,
+        "gemm2_flop": 2.0 * T * K * H * I,
+        "router_bytes": T * H * elt + E * H * elt + T * E * 4 + T * K * 8,
+        "dispatch_bytes": T * H * elt + T * K * H * elt + T * K * 4,
+        "combine_bytes": T * K * H * elt + T * K * 4 + T * H * elt,
+    }
+
+
+# --------------------------------------------------------------------------------------
+# clocks during the timed region
+# --------------------------------------------------------------------------------------
+class ClockSampler:
+    QUERY = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+             "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+             "clocks_event_reasons.sw_power_cap")
+    NAMES = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+
+    def __init__(self, gpu_id: str):
+        self.proc = None
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                 "-i", gpu_id, "-lms", "100"], stdout=subprocess.PIPE,
+                stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        sm, mx, reasons = [], [], set()
+        for line in out.strip().splitlines():
+            parts = [s.strip() for s in line.split(",")]
+            if len(parts) < 7:
+                continue
+            try:
+                sm.append(float(parts[0]))
+                mx.append(float(parts[1]))
+            except ValueError:
+                continue
+            for name, v in zip(self.NAMES, parts[3:7]):
+                if v.lower().startswith("active"):
+                    reasons.add(name)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "samples": len(sm),
+                "reasons": sorted(reasons)}
+
+
+# --------------------------------------------------------------------------------------
+# our implementation
+# --------------------------------------------------------------------------------------
+def build_layer(w, device, seed=0):
+    import torch
+    from velvetoptimizer_b200 import MoEConfig, MoELayer
+
+    cfg = MoEConfig(hidden_size=w["hidden"], intermediate_size=w["inter"],
+                    moe_num_experts=w["experts"], moe_top_k=w["top_k"], flylora_rank=16,
+                    flylora_alpha=32.0, era_gamma=0.1)
+    with torch.device(device):
+        layer = MoELayer(cfg)
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+    with torch.no_grad():
+        # VesperLM._init_weights: N(0, 0.02) weights, zero biases (model.py:456-467)
+        for m in layer.modules():
+            if isinstance(m, torch.nn.Linear):
+                m.weight.normal_(0.0, 0.02, generator=g)
+                m.bias.zero_()
+        for e in layer.experts:
+            for proj in (e.gate_proj, e.up_proj):
+                if not w.get("lora_on"):
+                    proj.lora_up.weight.zero_()  # FlyLoRA off
+        if w.get("zipf_alpha"):
+            ranks = torch.arange(1, w["experts"] + 1, dtype=torch.float64)
+            pmf = ranks ** (-w["zipf_alpha"])
+            layer.router.bias.copy_(torch.log(pmf / pmf.sum()).float())
+    return layer
+
+
+def cpu_baseline(layer, x_dev, w, seconds):
+    """Time the oracle (CPU restatement of the reference, numpy fp32) on a token sample."""
+    import numpy as np
+    import torch
+    from oracle import moe_oracle as O
+    from oracle.inputs import MoECase
+
+    st = layer.stacked_weights(torch.float32)
+    names = {"router_w": "w_r", "router_b": "b_r", "gate_w": "w_g", "gate_b": "b_g",
+             "up_w": "w_u", "up_b": "b_u", "down_w": "w_d", "down_b": "b_d",
+             "gate_lora_down_w": "a_g", "gate_lora_down_b": "ba_g", "gate_lora_up_w": "l_g",
+             "gate_lora_up_b": "bl_g", "up_lora_down_w": "a_u", "up_lora_down_b": "ba_u",
+             "up_lora_up_w": "l_u", "up_lora_up_b": "bl_u"}
+    p = {names[k]: v.cpu().numpy() for k, v in st.items()}
+    del st
+    case = MoECase(tokens=1, hidden=w["hidden"], inter=w["inter"], experts=w["experts"],
+                   top_k=w["top_k"])
+    xs = x_dev.float().cpu().numpy()
+
+    def run(n):
+        case.tokens = n
+        p["x"] = xs[:n]
+        t0 = time.perf_counter()
+        O.moe_forward(p, case)
+        return time.perf_counter() - t0
+
+    n = min(256, xs.shape[0])
+    t = run(n)
+    n2 = int(min(xs.shape[0], max(n, n * seconds / max(t, 1e-3))))
+    if n2 > n:
+        n, t = n2, run(n2)
+    return {"value": n / t, "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port",
+            "sample": f"{n} of {xs.shape[0]} tokens, numpy fp32 oracle (CPU restatement of "
+                      f"python/vesper/model.py:317-385), {t:.1f} s"}
+
+
+def run_ours(args, rank, world, local_rank):
+    import torch
+    import torch.distributed as dist
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    w = dict(WORKLOADS[args.workload])
+    T, H, E, K = w["tokens"], w["hidden"], w["experts"], w["top_k"]
+    layer = build_layer(w, dev, seed=0)
+    g = torch.Generator(device=dev)
+    g.manual_seed(1000 + rank)
+    x = torch.randn(T, H, generator=g, device=dev).to(torch.bfloat16).reshape(
+        w["batch"], T // w["batch"], H)
+    packed = layer.packed_for(dev, torch.bfloat16)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    # warm-up
+    for _ in range(args.warmup):
+        out, aux = layer(x)
+    torch.cuda.synchronize()
+
+    # ---- device-resident timed region ----
+    props = torch.cuda.get_device_properties(dev)
+    gpu_id = str(getattr(props, "uuid", "") or local_rank)
+    if gpu_id and not gpu_id.startswith("GPU-") and len(gpu_id) > 8:
+        gpu_id = "GPU-" + gpu_id
+    packed.handle.set_profiling(args.steps)
+    stream = torch.cuda.current_stream(dev)
+    t_start = torch.cuda.Event(enable_timing=True)
+    t_end = torch.cuda.Event(enable_timing=True)
+    barrier()
+    torch.cuda.synchronize()
+    sampler = ClockSampler(gpu_id)
+    time.sleep(0.3)
+    launches = 0
+    t_start.record(stream)
+    for _ in range(args.steps):
+        out, aux = layer(x)
+        launches += packed.handle.last_launch_count()
+    t_end.record(stream)
+    t_end.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+    clocks = sampler.stop()
+    ms = t_start.elapsed_time(t_end) / args.steps
+    stages, nprof = packed.handle.stage_times()
+    packed.handle.set_profiling(0)
+    ms_t = torch.tensor([ms], device=dev)
+    if world > 1:
+        dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
+    ms_max = float(ms_t.item())
+    value = world * T / (ms_max * 1e-3)
+
+    # ---- end-to-end through the public module, host buffers in/out ----
+    x_host = torch.empty(x.shape, dtype=x.dtype, pin_memory=True)
+    x_host.copy_(x)
+    out_host = torch.empty(x.shape, dtype=x.dtype, pin_memory=True)
+    aux_host = torch.empty((), dtype=torch.float32, pin_memory=True)
+    for _ in range(2):
+        xd = x_host.to(dev, non_blocking=True)
+        o, a = layer(xd)
+        out_host.copy_(o, non_blocking=True)
+        aux_host.copy_(a, non_blocking=True)
+    barrier()
+    torch.cuda.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        xd = x_host.to(dev, non_blocking=True)
+        o, a = layer(xd)
+        out_host.copy_(o, non_blocking=True)
+        aux_host.copy_(a, non_blocking=True)
+    e1.record(stream)
+    e1.synchronize()
+    barrier()
+    e2e_ms = torch.tensor([e0.elapsed_time(e1) / args.steps], device=dev)
+    if world > 1:
+        dist.all_reduce(e2e_ms, op=dist.ReduceOp.MAX)
+    e2e_value = world * T / (float(e2e_ms.item()) * 1e-3)
+
+    if rank != 0:
+        return None
+
+    pk = peaks()
+    alg = algorithmic(w)
+    g1 = stages.get("gemm1_gate_up_era", float("nan"))
+    achieved = alg["gemm1_flop"] / (g1 * 1e-3) / 1e12
+    stage_report = {}
+    for name, t_ms in stages.items():
+        rec = {"ms": round(t_ms, 4), "share": round(t_ms / max(sum(stages.values()), 1e-9), 4)}
+        if name.startswith("gemm1"):
+            rec.update(achieved=round(achieved, 1), unit="TFLOP/s",
+                       frac=round(achieved / pk["bf16_tflops"], 4))
+        elif name.startswith("gemm2"):
+            a2 = alg["gemm2_flop"] / (t_ms * 1e-3) / 1e12
+            rec.update(achieved=round(a2, 1), unit="TFLOP/s", frac=round(a2 / pk["bf16_tflops"], 4))
+        elif name in ("router", "dispatch", "combine"):
+            gbs = alg[f"{name}_bytes"] / (t_ms * 1e-3) / 1e9
+            rec.update(achieved=round(gbs, 1), unit="GB/s", frac=round(gbs / pk["hbm_gbs"], 4))
+        stage_report[name] = rec
+
+    line = {
+        "metric": "MoE-layer fwd tokens/s",
+        "value": round(value, 1),
+        "unit": "tokens/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms_max, 4),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic: x~N(0,1), weights~N(0,0.02), zero bias, FlyLoRA off, seed 0",
+        "config": {"workload": f"{args.workload}: MoE FFN layer fwd, {T} tokens/GPU, d_model {H}, "
+                               f"expert d_ff {w['inter']}, {E} experts, top-{K}",
+                   "tokens_per_gpu": T, "hidden": H, "inter": w["inter"], "experts": E,
+                   "top_k": K, "parallelism": "single GPU" if world == 1 else f"replicas x{world}",
+                   "l2": "inputs larger than L2 (x 512 MiB, weights 3.2 GiB); no flush"},
+        "e2e": {"value": round(e2e_value, 1), "unit": "tokens/s",
+                "h2d_bytes_per_step": int(x.numel() * x.element_size()),
+                "d2h_bytes_per_step": int(x.numel() * x.element_size() + 4),
+                "api": "velvetoptimizer_b200.MoELayer.forward"},
+        "roofline": {"kernel": "gemm1_gate_up_era (tcgen05 grouped GEMM, fused ERA*up)",
+                     "bound": "tensor", "achieved": round(achieved, 1),
+                     "peak": pk["bf16_tflops"], "peak_source": pk["source"] + " bf16 burst",
+                     "unit": "TFLOP/s", "frac": round(achieved / pk["bf16_tflops"], 4),
+                     "traffic": None, "flop_per_launch": alg["gemm1_flop"],
+                     "avg_launch_ms": round(g1, 4), "launches_timed": nprof},
+        "stages": stage_report,
+        "gpu_launches": launches,
+        "clocks": clocks,
+    }
+    if world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline(layer, x.reshape(T, H), w, args.cpu_seconds)
+    return line
+
+
+# --------------------------------------------------------------------------------------
+# reference arm: the CPU implementation of the path (the oracle port) on host cores
+# --------------------------------------------------------------------------------------
+def run_reference(args):
+    import numpy as np
+    import torch
+    from oracle import moe_oracle as O
+    from oracle.inputs import MoECase
+
+    w = dict(WORKLOADS[args.workload])
+    T, H, I, E, K = w["tokens"], w["hidden"], w["inter"], w["experts"], w["top_k"]
+    r = 16
+    torch.manual_seed(0)
+    gen = lambda *s: torch.empty(*s).normal_(0.0, 0.02).numpy()  # noqa: E731
+    z = lambda *s: np.zeros(s, dtype=np.float32)  # noqa: E731
+    p = {"w_r": gen(E, H), "b_r": z(E), "w_d": gen(E, H, I), "b_d": z(E, H)}
+    for q in ("g", "u"):
+        p[f"w_{q}"], p[f"b_{q}"] = gen(E, I, H), z(E, I)
+        p[f"a_{q}"], p[f"ba_{q}"] = gen(E, r, H), z(E, r)
+        p[f"l_{q}"] = gen(E, I, r) if w.get("lora_on") else z(E, I, r)
+        p[f"bl_{q}"] = z(E, I)
+    if w.get("zipf_alpha"):
+        from oracle.inputs import zipf_router_bias
+        p["b_r"] = zipf_router_bias(E, w["zipf_alpha"])
+    xs = torch.randn(min(T, 8192), H).numpy()
+    case = MoECase(tokens=1, hidden=H, inter=I, experts=E, top_k=K)
+
+    def step(n):
+        case.tokens = n
+        p["x"] = xs[:n]
+        t0 = time.perf_counter()
+        O.moe_forward(p, case)
+        return time.perf_counter() - t0
+
+    # size the per-step sample so warm-up + steps take about two minutes
+    n = 128
+    t = step(n)
+    budget = 120.0 / max(1, args.steps + args.warmup)
+    n = int(min(xs.shape[0], max(64, n * budget / max(t, 1e-3))))
+    for _ in range(args.warmup):
+        step(n)
+    times = [step(n) for _ in range(args.steps)]
+    med = statistics.median(times)
+    value = n / med
+    return {
+        "metric": "MoE-layer fwd tokens/s", "impl": "reference", "value": round(value, 2),
+        "unit": "tokens/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(med * 1e3, 2), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic (same shapes and distributions)",
+        "config": {"workload": args.workload, "tokens_per_step": n, "hidden": H, "inter": I,
+                   "experts": E, "top_k": K},
+        "cpu_baseline": {"value": round(value, 2), "unit": "tokens/s", "cores": os.cpu_count(),
+                         "kind": "port",
+                         "sample": f"{n} tokens per step of the {T}-token workload, numpy fp32 "
+                                   "oracle (CPU restatement of python/vesper/model.py:317-385)"},
+        "e2e": {"value": round(value, 2), "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+
+
+def main():
+    args = parse_args()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        if rank == 0:
+            print(json.dumps(run_reference(args)), flush=True)
+        return 0
+    import torch
+    import torch.distributed as dist
+    if world > 1:
+        from datetime import timedelta
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120),
+                                device_id=torch.device("cuda", local_rank))
+    try:
+        line = run_ours(args, rank, world, local_rank)
+        if line is not None:
+            print(json.dumps(line), flush=True)
+    finally:
+        if world > 1:
+            dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

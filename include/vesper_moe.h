@@ -1,0 +1,179 @@
+/*
+ * vesper_moe.h -- C ABI of the B200 (sm_100a) Mixture-of-Experts FFN forward.
+ *
+ * Drop-in boundary for VelvetOptimizer's MoE layer.  The reference seam is the
+ * nn.Module call `ffn_out, aux_loss = self.ffn(normed)` with
+ * `self.ffn = MoELayer(config)` (python/vesper/model.py:402-403, :419-420); the layer
+ * itself is python/vesper/model.py:305-385.  Its one native FFI precedent is
+ * `extern "C" velvet_complete_update_cuda` (crates/vesper-optimizer/src/cuda/kernels.cu:75-104,
+ * declared in crates/vesper-optimizer/src/cuda/velvet.h:8-26 and bound from Rust in
+ * crates/vesper-optimizer/src/cuda/mod.rs:9-29): raw device pointers, no stream, no status.
+ * This ABI keeps the raw-pointer style and adds an explicit stream, a status code on every
+ * call and a per-handle error string.  Plain C types only: no torch or C++ types cross it.
+ *
+ * Conventions
+ *  - every function returns VMOE_OK (0) or a VMOE_ERR_* code; no C++ exception crosses;
+ *  - "device pointer" = memory on the handle's device; `stream` is a cudaStream_t
+ *    (NULL = legacy default stream);
+ *  - matrices are row-major; Linear weights are [out, in] (y = x W^T + b), stacked over
+ *    experts on the leading axis, exactly as the reference's nn.Linear parameters;
+ *  - one handle per device; calls on one handle must not overlap (not re-entrant);
+ *  - vmoe_forward does not synchronise the host on a single GPU.
+ */
+#ifndef VESPER_MOE_H
+#define VESPER_MOE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define VMOE_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define VMOE_API __attribute__((visibility("default")))
+#else
+#define VMOE_API
+#endif
+
+/* status codes */
+enum {
+  VMOE_OK = 0,
+  VMOE_ERR_INVALID_ARG = 1,       /* null pointer, bad size, top_k > experts, ...     */
+  VMOE_ERR_UNSUPPORTED_SHAPE = 2, /* valid for the reference but not for this build   */
+  VMOE_ERR_CUDA = 3,              /* a CUDA runtime/driver call failed                */
+  VMOE_ERR_NCCL = 4,              /* reserved for the expert-parallel exchange        */
+  VMOE_ERR_TIMEOUT = 5,           /* a bounded device-side wait gave up               */
+  VMOE_ERR_DEVICE_STATUS = 6,     /* a kernel reported an error in the status word    */
+  VMOE_ERR_NOT_READY = 7,         /* vmoe_forward before vmoe_set_weights             */
+  VMOE_ERR_WORKSPACE = 8          /* workspace too small or misaligned                */
+};
+
+/* element type of x, out and the weights; every product accumulates in fp32 */
+enum { VMOE_F32 = 0, VMOE_BF16 = 1 };
+
+/* Layer configuration.  Mirrors VesperConfig's MoE knobs (python/vesper/config.py:17-22,
+ * 33-36) and MoELayer.__init__ (python/vesper/model.py:308-315). */
+typedef struct vmoe_config {
+  int64_t hidden;       /* H  = hidden_size                                          */
+  int64_t inter;        /* I  = intermediate_size (expert d_ff)                      */
+  int32_t num_experts;  /* E  = moe_num_experts, >= 2 (config.py:93)                 */
+  int32_t top_k;        /* K  = moe_top_k, 1 <= K <= E (config.py:92)                */
+  int32_t lora_rank;    /* r  = flylora_rank; 0 = the layer carries no FlyLoRA terms */
+  float lora_scaling;   /* flylora_alpha / flylora_rank (model.py:102)               */
+  float era_gamma;      /* ERA gamma (config.py:22)                                  */
+  int32_t dtype;        /* VMOE_F32 or VMOE_BF16                                     */
+  int64_t capacity;     /* max tokens per expert; 0 = no drop (the reference)        */
+} vmoe_config;
+
+/* Expert and router weights, as device pointers in the config's dtype (biases too).
+ * Shapes use E = num_experts.  The library copies (and repacks) them inside
+ * vmoe_set_weights, so the caller may free or modify its buffers afterwards.
+ * FlyLoRA tensors may be NULL when lora_rank == 0; a NULL lora_up pair means the
+ * branch is off (the reference's zero-initialised lora_up, model.py:120). */
+typedef struct vmoe_weights {
+  const void* router_w;         /* [E, H]   router.weight                          */
+  const void* router_b;         /* [E]      router.bias                            */
+  const void* gate_w;           /* [E, I, H] experts.e.gate_proj.base.weight       */
+  const void* gate_b;           /* [E, I]                                          */
+  const void* up_w;             /* [E, I, H] experts.e.up_proj.base.weight         */
+  const void* up_b;             /* [E, I]                                          */
+  const void* down_w;           /* [E, H, I] experts.e.down_proj.weight            */
+  const void* down_b;           /* [E, H]                                          */
+  const void* gate_lora_down_w; /* [E, r, H] experts.e.gate_proj.lora_down.weight  */
+  const void* gate_lora_down_b; /* [E, r]                                          */
+  const void* gate_lora_up_w;   /* [E, I, r] experts.e.gate_proj.lora_up.weight    */
+  const void* gate_lora_up_b;   /* [E, I]                                          */
+  const void* up_lora_down_w;   /* [E, r, H]                                       */
+  const void* up_lora_down_b;   /* [E, r]                                          */
+  const void* up_lora_up_w;     /* [E, I, r]                                       */
+  const void* up_lora_up_b;     /* [E, I]                                          */
+} vmoe_weights;
+
+typedef struct vmoe_handle vmoe_handle;
+
+/* Create a handle on CUDA device `device`.  Validates the config like
+ * VesperConfig.validate (python/vesper/config.py:89-94).  Replaces the constructor
+ * MoELayer.__init__ (python/vesper/model.py:308-315). */
+VMOE_API int vmoe_create(const vmoe_config* cfg, int device, vmoe_handle** out);
+
+/* Release the handle and every device buffer it owns. */
+VMOE_API int vmoe_destroy(vmoe_handle* h);
+
+/* Copy the weights into library-owned device memory in the kernels' layout, folding
+ * any FlyLoRA branch into the base projection (the branch is linear, so
+ * W + s*U*D and b + s*(U*bd + bu) reproduce base(x) + s*lora_up(lora_down(x)) of
+ * python/vesper/model.py:123-126).  Enqueued on `stream`; returns after the copy is
+ * enqueued.  Replaces MoELayer's parameter set (load_state_dict). */
+VMOE_API int vmoe_set_weights(vmoe_handle* h, const vmoe_weights* w, void* stream);
+
+/* Bytes of device workspace vmoe_forward needs for `tokens` tokens (256-byte aligned). */
+VMOE_API int vmoe_workspace_size(const vmoe_handle* h, int64_t tokens, size_t* bytes);
+
+/* Where vmoe_forward keeps its intermediates inside the workspace (byte offsets), so a
+ * caller can inspect the dispatch: for token t and slot k, slot_of[t*K + k] is the row of
+ * the expert-major permuted buffer that holds x[t] (-1 when capacity dropped it); expert
+ * e owns rows [expert_offsets[e], expert_offsets[e+1]) (padded to 128-row tiles), filled
+ * in ascending token order like the reference's nonzero() (python/vesper/model.py:347). */
+typedef struct vmoe_ws_layout {
+  size_t slot_of;        /* int32 [T*K]                                  */
+  size_t expert_offsets; /* int32 [E+1]                                  */
+  size_t num_tiles;      /* int32 [1]: 128-row tiles in use              */
+  size_t x_perm;         /* [max_rows, H] permuted activations           */
+  size_t h;              /* [max_rows, I_pad] ERA(gate) * up             */
+  size_t y;              /* [max_rows, H_pad] expert outputs             */
+  int64_t max_rows;
+  int64_t h_ld;          /* row pitch of h in elements                   */
+  int64_t y_ld;          /* row pitch of y in elements                   */
+  size_t total;          /* == vmoe_workspace_size                       */
+} vmoe_ws_layout;
+VMOE_API int vmoe_workspace_layout(const vmoe_handle* h, int64_t tokens, vmoe_ws_layout* out);
+
+/* One MoE layer forward over `tokens` rows of x.  Replaces MoELayer.forward
+ * (python/vesper/model.py:317-364):
+ *   x             [T, H]  device, config dtype (the reference's [B, S, H], flattened)
+ *   out           [T, H]  device, config dtype
+ *   router_logits [T, E]  fp32, optional (NULL): the router's logits (model.py:322)
+ *   topk_idx      [T, K]  int32, optional: chosen experts, probability-descending,
+ *                         exact ties broken by lowest expert index (model.py:326)
+ *   topk_w        [T, K]  fp32, optional: renormalised gate weights (model.py:329)
+ *   expert_counts [E]     int32, optional: assignments per expert (before capacity)
+ *   aux_loss      [1]     fp32 device scalar, optional: Switch load-balancing loss
+ *                         E * sum_e f_e P_e (model.py:366-385)
+ *   workspace             device, >= vmoe_workspace_size bytes, 256-byte aligned
+ * All work is enqueued on `stream`; nothing is allocated. */
+VMOE_API int vmoe_forward(vmoe_handle* h, const void* x, int64_t tokens, void* out,
+                 float* router_logits, int32_t* topk_idx, float* topk_w,
+                 int32_t* expert_counts, float* aux_loss,
+                 void* workspace, size_t workspace_bytes, void* stream);
+
+/* Read (and clear) the device status word the kernels write when a bounded wait gives
+ * up or an index check fails.  Synchronises `stream`.  *code = 0 when all is well. */
+VMOE_API int vmoe_device_status(vmoe_handle* h, int32_t* code, void* stream);
+
+/* Per-stage timing, not part of the reference (the benchmark uses it to time the
+ * dominant kernel inside its timed region).  vmoe_set_profiling(h, n) makes the next n
+ * forwards record CUDA events around each kernel on their stream (n = 0 turns it off);
+ * vmoe_stage_times waits for the recorded events, writes the AVERAGE milliseconds per
+ * stage over those forwards to ms[0..min(n, stages)-1] (router, scan, plan, dispatch,
+ * gemm1_gate_up_era, gemm2_down, combine), the number of forwards averaged to
+ * *forwards, and restarts recording. */
+VMOE_API int vmoe_set_profiling(vmoe_handle* h, int n);
+VMOE_API int vmoe_stage_times(vmoe_handle* h, float* ms, int n, int* n_out, int* forwards);
+VMOE_API const char* vmoe_stage_name(int stage);
+
+/* Number of kernel launches the last vmoe_forward enqueued. */
+VMOE_API int vmoe_last_launch_count(const vmoe_handle* h);
+
+/* Last error message of this handle ("" if none), and a static text per code. */
+VMOE_API const char* vmoe_last_error(const vmoe_handle* h);
+VMOE_API const char* vmoe_status_string(int status);
+VMOE_API int vmoe_abi_version(void);
+
+#ifdef __cplusplus
+} /* extern "C" */
+#endif
+
+#endif /* VESPER_MOE_H */

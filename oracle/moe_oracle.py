@@ -153,14 +153,16 @@ def load_balancing_loss(probs, topk_idx, experts):
     return probs.dtype.type(experts) * (f * p_mean).sum()
 
 
-def moe_forward(p, case, *, dtype=np.float32, force_idx=None, token_subset=None):
+def moe_forward(p, case, *, dtype=np.float32, force_idx=None, token_subset=None, capacity=0):
     """Full MoE layer forward (model.py:317-364).
 
     ``p`` is the dict of ``oracle.inputs.make_inputs``.  ``force_idx`` ([T,K]) replaces
     the top-K choice (used to compare outputs on identical routing when a near-tie was
     resolved differently).  ``token_subset`` computes outputs only for those tokens
     (the forward is per-token once routing is fixed), while router, routing and aux
-    loss still cover all T tokens.
+    loss still cover all T tokens.  ``capacity`` > 0 keeps only the first ``capacity``
+    tokens (ascending token order) of each expert -- an extension: the reference has no
+    capacity limit, which is ``capacity=0``.
 
     Returns a dict with logits, probs, topk_idx, topk_w, counts, perm_tok, perm_k,
     out ([T,H], or [len(subset),H]) and aux (0-d).
@@ -182,10 +184,17 @@ def moe_forward(p, case, *, dtype=np.float32, force_idx=None, token_subset=None)
         rows = np.arange(t)
     else:
         rows = np.asarray(token_subset, dtype=np.int64)
+    kept = np.ones_like(idx, dtype=bool)
+    if capacity > 0:
+        for e in range(E):
+            tok = np.nonzero((idx == e).any(axis=-1))[0]
+            for t in tok[capacity:]:
+                kept[t] &= idx[t] != e
     sub_idx, sub_w, xs = idx[rows], w[rows], x[rows]
+    sub_kept = kept[rows]
     out = np.zeros((len(rows), h), dtype=dtype)
     for e in range(E):  # ascending expert order, like the reference's index_add_ loop
-        mask = sub_idx == e
+        mask = (sub_idx == e) & sub_kept
         sel = np.nonzero(mask.any(axis=-1))[0]
         if sel.size == 0:
             continue

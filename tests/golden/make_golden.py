@@ -114,9 +114,27 @@ def run_reference(case: MoECase):
     }
 
 
+def dump_state_dict_keys():
+    """Record the reference MoELayer's state_dict keys and shapes for a small config."""
+    sys.path.insert(0, REFERENCE_PY)
+    from vesper.config import VesperConfig  # noqa: E402
+    from vesper.model import MoELayer  # noqa: E402
+    conf = dict(hidden_size=64, intermediate_size=96, moe_num_experts=3, moe_top_k=2,
+                flylora_rank=8, flylora_alpha=16.0, era_gamma=0.1)
+    cfg = VesperConfig(hidden_size=64, intermediate_size=96, num_heads=1, flylora_rank=8,
+                       flylora_alpha=16.0).with_moe(num_experts=3, top_k=2)
+    keys = {k: list(v.shape) for k, v in MoELayer(cfg).state_dict().items()}
+    path = os.path.join(HERE, "state_dict_keys.json")
+    with open(path, "w") as f:
+        json.dump({"config": conf, "keys": keys}, f, indent=1)
+    print(f"state_dict keys: {len(keys)} -> {path}")
+
+
 def main(names=None):
     import torch
     torch.set_num_threads(os.cpu_count() or 1)
+    if not names:
+        dump_state_dict_keys()
     for name, case in CASES.items():
         if names and name not in names:
             continue

@@ -1,0 +1,260 @@
+"""GPU parity: the CUDA path through the C ABI against the reference goldens and the oracle.
+
+Tolerances (from the path's specification):
+  * expert indices, per-expert counts and the dispatch permutation: bit-exact, except on
+    tokens whose K-th and (K+1)-th router probabilities are a near-tie (counted, reported);
+  * fp32: out, router logits and aux loss within 1e-5 norm-relative error
+    (max|got - ref| / max|ref|) of the reference;
+  * bf16: out within 2e-2 norm-relative of the fp32 oracle on the same bf16-rounded inputs.
+"""
+import numpy as np
+import pytest
+import torch
+
+from oracle import moe_oracle as O
+from oracle.inputs import MoECase, bf16_inputs, make_inputs
+from tests.abi_runner import AbiLayer
+from tests.golden_io import golden_names, load_golden
+
+pytestmark = pytest.mark.gpu
+
+FP32_TOL = 1e-5
+BF16_TOL = 2e-2
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _need_cuda():
+    if not torch.cuda.is_available():
+        pytest.skip("needs a CUDA device")
+
+
+def permutation_from_slots(layer, T, res):
+    """Read slot_of / expert offsets from the workspace; rebuild the token order per expert."""
+    lay = layer.handle.workspace_layout(T)
+    K, E = layer.case.top_k, layer.case.experts
+    ws = layer.ws
+    slot = ws[lay.slot_of:lay.slot_of + 4 * T * K].view(torch.int32).cpu().numpy().reshape(T, K)
+    offs = ws[lay.expert_offsets:lay.expert_offsets + 4 * (E + 1)].view(torch.int32).cpu().numpy()
+    return slot, offs
+
+
+def check_dispatch(layer, T, res, oracle_idx):
+    """Slots are expert-major, padded to 128 rows, token-ascending within each expert."""
+    slot, offs = permutation_from_slots(layer, T, res)
+    E = layer.case.experts
+    counts, perm_tok, _ = O.dispatch(oracle_idx, E)
+    assert np.array_equal(res["counts"], counts)
+    assert (offs[1:] - offs[:-1] >= 0).all() and (offs % 128 == 0).all()
+    got = []
+    for e in range(E):
+        rows = []
+        for t in range(T):
+            for k in range(layer.case.top_k):
+                if oracle_idx[t, k] == e:
+                    rows.append((slot[t, k], t))
+        rows.sort()
+        assert [r for r, _ in rows] == list(range(offs[e], offs[e] + counts[e]))
+        got.extend(t for _, t in rows)
+    assert np.array_equal(np.asarray(got), perm_tok)
+
+
+# ----------------------------------------------------------------------------------------
+# fp32 path against the reference's own outputs
+# ----------------------------------------------------------------------------------------
+@pytest.mark.parametrize("name", golden_names())
+def test_fp32_matches_reference_goldens(name):
+    case, g = load_golden(name)
+    inp = make_inputs(case)
+    layer = AbiLayer(case, inp, "f32")
+    res = layer.run(inp["x"])
+    T, K = case.tokens, case.top_k
+
+    assert O.norm_rel_err(res["logits"], g["logits"]) < FP32_TOL
+    tie = O.near_ties(g["probs"], K, rel=1e-5)
+    assert np.array_equal(res["topk_idx"][~tie], g["topk_idx"][~tie])
+    # the GPU's own routing vs the oracle (lowest-index ties) on the same logits
+    ora = O.moe_forward(inp, case)
+    tie_o = O.near_ties(ora["probs"], K, rel=1e-5)
+    assert np.array_equal(res["topk_idx"][~tie_o], ora["topk_idx"][~tie_o])
+    check_dispatch(layer, T, res, res["topk_idx"])
+
+    if not tie.any():
+        assert O.norm_rel_err(res["out"], g["out"]) < FP32_TOL
+        assert np.array_equal(res["counts"], g["counts"])
+        assert abs(float(res["aux"]) - float(g["aux"])) <= FP32_TOL * abs(float(g["aux"]))
+        assert O.norm_rel_err(res["topk_w"], g["topk_w"]) < FP32_TOL
+    # downstream of routing, on the routing the GPU chose
+    forced = O.moe_forward(inp, case, force_idx=res["topk_idx"])
+    assert O.norm_rel_err(res["out"], forced["out"]) < FP32_TOL
+    assert abs(float(res["aux"]) - float(forced["aux"])) <= FP32_TOL * abs(float(forced["aux"]))
+    layer.close()
+
+
+def test_fp32_tied_router_picks_lowest_index():
+    case, g = load_golden("t64_tied_router")
+    inp = make_inputs(case)
+    layer = AbiLayer(case, inp, "f32")
+    res = layer.run(inp["x"])
+    assert (res["topk_idx"] == np.arange(case.top_k)).all()
+    assert float(res["aux"]) == pytest.approx(1.0, abs=1e-6)
+    layer.close()
+
+
+def test_fp32_deterministic():
+    case, _ = load_golden("t256_lora_zipf")
+    inp = make_inputs(case)
+    layer = AbiLayer(case, inp, "f32")
+    a = layer.run(inp["x"])
+    b = layer.run(inp["x"])
+    for k in ("out", "topk_idx", "topk_w", "counts", "aux", "logits"):
+        assert np.array_equal(a[k], b[k]), k
+    layer.close()
+
+
+# ----------------------------------------------------------------------------------------
+# bf16 tensor-core path against the fp32 oracle on bf16-rounded inputs
+# ----------------------------------------------------------------------------------------
+BF16_CASES = {
+    "small_e8k2": MoECase(tokens=256, hidden=256, inter=256, experts=8, top_k=2, seed=11),
+    "ragged_bias": MoECase(tokens=1000, hidden=512, inter=384, experts=16, top_k=4,
+                           bias_std=0.05, seed=12),
+    "lora_zipf_e32k8": MoECase(tokens=512, hidden=256, inter=512, experts=32, top_k=8,
+                               lora_on=True, zipf_alpha=1.2, seed=13),
+    "odd_dims": MoECase(tokens=130, hidden=200, inter=136, experts=4, top_k=2, seed=14),
+    "single_token_k_eq_e": MoECase(tokens=1, hidden=128, inter=256, experts=4, top_k=4, seed=15),
+    "era_tails": MoECase(tokens=300, hidden=256, inter=256, experts=4, top_k=2, weight_std=0.3,
+                         bias_std=2.0, seed=16),
+}
+
+
+@pytest.mark.parametrize("name", list(BF16_CASES))
+def test_bf16_matches_oracle(name):
+    case = BF16_CASES[name]
+    inp = bf16_inputs(make_inputs(case))
+    layer = AbiLayer(case, inp, "bf16")
+    res = layer.run(inp["x"])
+    ora = O.moe_forward(inp, case)
+    tie = O.near_ties(ora["probs"], case.top_k, rel=1e-4)
+    assert O.norm_rel_err(res["logits"], ora["logits"]) < 1e-4
+    assert np.array_equal(res["topk_idx"][~tie], ora["topk_idx"][~tie])
+    check_dispatch(layer, case.tokens, res, res["topk_idx"])
+    forced = O.moe_forward(inp, case, force_idx=res["topk_idx"])
+    err = O.norm_rel_err(res["out"], forced["out"])
+    assert err < BF16_TOL, err
+    assert abs(float(res["aux"]) - float(forced["aux"])) <= 1e-4 * abs(float(forced["aux"]))
+    layer.close()
+
+
+def test_bf16_deterministic():
+    case = BF16_CASES["ragged_bias"]
+    inp = bf16_inputs(make_inputs(case))
+    layer = AbiLayer(case, inp, "bf16")
+    a = layer.run(inp["x"])
+    b = layer.run(inp["x"])
+    for k in ("out", "topk_idx", "topk_w", "counts", "aux"):
+        assert np.array_equal(a[k], b[k]), k
+    layer.close()
+
+
+@pytest.mark.parametrize("dtype", ["f32", "bf16"])
+def test_capacity_drops_late_tokens(dtype):
+    case = MoECase(tokens=384, hidden=256, inter=256, experts=4, top_k=2, zipf_alpha=1.2, seed=21)
+    inp = make_inputs(case)
+    if dtype == "bf16":
+        inp = bf16_inputs(inp)
+    cap = 100
+    layer = AbiLayer(case, inp, dtype, capacity=cap)
+    res = layer.run(inp["x"])
+    forced = O.moe_forward(inp, case, force_idx=res["topk_idx"], capacity=cap)
+    tol = FP32_TOL if dtype == "f32" else BF16_TOL
+    assert O.norm_rel_err(res["out"], forced["out"]) < tol
+    # counts are reported before the capacity cut, as the reference's aux loss uses them
+    assert res["counts"].sum() == case.tokens * case.top_k
+    layer.close()
+
+
+def test_empty_batch():
+    case = BF16_CASES["small_e8k2"]
+    layer = AbiLayer(case, bf16_inputs(make_inputs(case)), "bf16")
+    res = layer.run(np.zeros((0, case.hidden), dtype=np.float32))
+    assert res["out"].shape == (0, case.hidden)
+    assert np.isnan(res["aux"])          # mean over zero tokens, as in the reference
+    assert (res["counts"] == 0).all()
+    layer.close()
+
+
+def test_workspace_too_small_is_reported():
+    from velvetoptimizer_b200 import _lib
+    case = BF16_CASES["small_e8k2"]
+    layer = AbiLayer(case, bf16_inputs(make_inputs(case)), "bf16")
+    dev = torch.device("cuda", 0)
+    x = torch.zeros(case.tokens, case.hidden, dtype=torch.bfloat16, device=dev)
+    out = torch.empty_like(x)
+    ws = torch.empty(1024, dtype=torch.uint8, device=dev)
+    with pytest.raises(_lib.VmoeError) as ei:
+        layer.handle.forward(x.data_ptr(), case.tokens, out.data_ptr(), None, None, None, None,
+                             None, ws.data_ptr(), ws.numel(), 0)
+    assert ei.value.code == _lib.VMOE_ERR_WORKSPACE
+    layer.close()
+
+
+# ----------------------------------------------------------------------------------------
+# the drop-in module
+# ----------------------------------------------------------------------------------------
+def _load_module(case, inp, dtype):
+    from velvetoptimizer_b200 import MoEConfig, MoELayer
+    cfg = MoEConfig(hidden_size=case.hidden, intermediate_size=case.inter,
+                    moe_num_experts=case.experts, moe_top_k=case.top_k,
+                    flylora_rank=case.lora_rank, flylora_alpha=case.lora_alpha,
+                    era_gamma=case.era_gamma)
+    m = MoELayer(cfg)
+    sd = m.state_dict()
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a))  # noqa: E731
+    new = dict(sd)
+    new["router.weight"], new["router.bias"] = t(inp["w_r"]), t(inp["b_r"])
+    for e in range(case.experts):
+        for p, nm in (("g", "gate_proj"), ("u", "up_proj")):
+            pre = f"experts.{e}.{nm}"
+            new[f"{pre}.base.weight"], new[f"{pre}.base.bias"] = t(inp[f"w_{p}"][e]), t(inp[f"b_{p}"][e])
+            new[f"{pre}.lora_down.weight"] = t(inp[f"a_{p}"][e])
+            new[f"{pre}.lora_down.bias"] = t(inp[f"ba_{p}"][e])
+            new[f"{pre}.lora_up.weight"] = t(inp[f"l_{p}"][e])
+            new[f"{pre}.lora_up.bias"] = t(inp[f"bl_{p}"][e])
+        new[f"experts.{e}.down_proj.weight"] = t(inp["w_d"][e])
+        new[f"experts.{e}.down_proj.bias"] = t(inp["b_d"][e])
+    m.load_state_dict(new)
+    return m.cuda()
+
+
+def test_module_fp32_matches_reference_c1():
+    case, g = load_golden("c1_fp32")
+    inp = make_inputs(case)
+    m = _load_module(case, inp, torch.float32)
+    x = torch.from_numpy(inp["x"]).reshape(case.batch, case.seq, case.hidden).cuda()
+    out, aux = m(x)
+    assert out.shape == (case.batch, case.seq, case.hidden) and out.dtype == torch.float32
+    assert O.norm_rel_err(out.reshape(-1, case.hidden).cpu().numpy(), g["out"]) < FP32_TOL
+    assert abs(aux.item() - float(g["aux"])) <= FP32_TOL * abs(float(g["aux"]))
+    out2, aux2, logits = m(x, return_router_logits=True)
+    assert torch.equal(out, out2)
+    assert O.norm_rel_err(logits.reshape(-1, case.experts).cpu().numpy(), g["logits"]) < FP32_TOL
+    # parameters changed after the first call are repacked on the next one
+    with torch.no_grad():
+        m.experts[0].down_proj.bias.add_(1.0)
+    out3, _ = m(x)
+    assert not torch.equal(out, out3)
+    m.close()
+
+
+def test_module_bf16_lora_matches_oracle():
+    case = BF16_CASES["lora_zipf_e32k8"]
+    inp = make_inputs(case)
+    m = _load_module(case, inp, torch.bfloat16)
+    x = torch.from_numpy(inp["x"]).reshape(1, case.tokens, case.hidden).cuda().to(torch.bfloat16)
+    out, aux, logits = m(x, return_router_logits=True)
+    ib = bf16_inputs(inp)
+    probs = O.softmax(logits.reshape(-1, case.experts).cpu().numpy())
+    _, idx = O.topk_lowest_index(probs, case.top_k)
+    forced = O.moe_forward(ib, case, force_idx=idx)
+    assert O.norm_rel_err(out.float().reshape(-1, case.hidden).cpu().numpy(), forced["out"]) < BF16_TOL
+    m.close()

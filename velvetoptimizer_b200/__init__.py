@@ -1,0 +1,11 @@
+"""B200-native (sm_100a) Mixture-of-Experts FFN forward for VelvetOptimizer.
+
+Public surface:
+  * ``MoELayer`` — drop-in for the reference ``vesper.model.MoELayer``;
+  * ``MoEConfig`` — the MoE knobs of ``VesperConfig``;
+  * ``torch.ops.vesper_moe.forward`` — the custom op over the C ABI (include/vesper_moe.h).
+"""
+from .config import MoEConfig
+from .moe import MoELayer, ExpertFFN, FlyLoRALinear
+
+__all__ = ["MoEConfig", "MoELayer", "ExpertFFN", "FlyLoRALinear"]

@@ -1,0 +1,191 @@
+"""ctypes binding of ``libvesper_moe.so`` (the C ABI declared in include/vesper_moe.h).
+
+The library is the only compute path: if it is missing, importing the op raises instead
+of falling back to anything else.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+from ctypes import POINTER, c_char_p, c_float, c_int, c_int32, c_int64, c_size_t, c_void_p
+
+LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "lib", "libvesper_moe.so")
+
+VMOE_OK = 0
+VMOE_ERR_INVALID_ARG = 1
+VMOE_ERR_UNSUPPORTED_SHAPE = 2
+VMOE_ERR_CUDA = 3
+VMOE_ERR_NCCL = 4
+VMOE_ERR_TIMEOUT = 5
+VMOE_ERR_DEVICE_STATUS = 6
+VMOE_ERR_NOT_READY = 7
+VMOE_ERR_WORKSPACE = 8
+
+VMOE_F32 = 0
+VMOE_BF16 = 1
+
+# every symbol include/vesper_moe.h declares
+EXPORTED = (
+    "vmoe_create", "vmoe_destroy", "vmoe_set_weights", "vmoe_workspace_size",
+    "vmoe_workspace_layout", "vmoe_forward",
+    "vmoe_device_status", "vmoe_set_profiling", "vmoe_stage_times", "vmoe_stage_name",
+    "vmoe_last_launch_count", "vmoe_last_error", "vmoe_status_string", "vmoe_abi_version",
+)
+
+
+class VmoeConfig(ctypes.Structure):
+    _fields_ = [
+        ("hidden", c_int64),
+        ("inter", c_int64),
+        ("num_experts", c_int32),
+        ("top_k", c_int32),
+        ("lora_rank", c_int32),
+        ("lora_scaling", c_float),
+        ("era_gamma", c_float),
+        ("dtype", c_int32),
+        ("capacity", c_int64),
+    ]
+
+
+class VmoeWeights(ctypes.Structure):
+    _fields_ = [(n, c_void_p) for n in (
+        "router_w", "router_b", "gate_w", "gate_b", "up_w", "up_b", "down_w", "down_b",
+        "gate_lora_down_w", "gate_lora_down_b", "gate_lora_up_w", "gate_lora_up_b",
+        "up_lora_down_w", "up_lora_down_b", "up_lora_up_w", "up_lora_up_b",
+    )]
+
+
+class VmoeWsLayout(ctypes.Structure):
+    _fields_ = [("slot_of", c_size_t), ("expert_offsets", c_size_t), ("num_tiles", c_size_t),
+                ("x_perm", c_size_t), ("h", c_size_t), ("y", c_size_t), ("max_rows", c_int64),
+                ("h_ld", c_int64), ("y_ld", c_int64), ("total", c_size_t)]
+
+
+class VmoeError(RuntimeError):
+    def __init__(self, code: int, msg: str):
+        super().__init__(msg)
+        self.code = code
+
+
+_lib = None
+
+
+def load() -> ctypes.CDLL:
+    """Load the library once; raise if it has not been built."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(LIB_PATH):
+        raise ImportError(
+            f"{LIB_PATH} is missing: build it with `python -m velvetoptimizer_b200.build` "
+            "(there is no non-CUDA fallback)")
+    lib = ctypes.CDLL(LIB_PATH)
+    H = c_void_p
+    lib.vmoe_create.argtypes = [POINTER(VmoeConfig), c_int, POINTER(H)]
+    lib.vmoe_create.restype = c_int
+    lib.vmoe_destroy.argtypes = [H]
+    lib.vmoe_destroy.restype = c_int
+    lib.vmoe_set_weights.argtypes = [H, POINTER(VmoeWeights), c_void_p]
+    lib.vmoe_set_weights.restype = c_int
+    lib.vmoe_workspace_size.argtypes = [H, c_int64, POINTER(c_size_t)]
+    lib.vmoe_workspace_size.restype = c_int
+    lib.vmoe_workspace_layout.argtypes = [H, c_int64, POINTER(VmoeWsLayout)]
+    lib.vmoe_workspace_layout.restype = c_int
+    lib.vmoe_forward.argtypes = [H, c_void_p, c_int64, c_void_p, c_void_p, c_void_p, c_void_p,
+                                 c_void_p, c_void_p, c_void_p, c_size_t, c_void_p]
+    lib.vmoe_forward.restype = c_int
+    lib.vmoe_device_status.argtypes = [H, POINTER(c_int32), c_void_p]
+    lib.vmoe_device_status.restype = c_int
+    lib.vmoe_set_profiling.argtypes = [H, c_int]
+    lib.vmoe_set_profiling.restype = c_int
+    lib.vmoe_stage_times.argtypes = [H, POINTER(c_float), c_int, POINTER(c_int), POINTER(c_int)]
+    lib.vmoe_stage_times.restype = c_int
+    lib.vmoe_stage_name.argtypes = [c_int]
+    lib.vmoe_stage_name.restype = c_char_p
+    lib.vmoe_last_launch_count.argtypes = [H]
+    lib.vmoe_last_launch_count.restype = c_int
+    lib.vmoe_last_error.argtypes = [H]
+    lib.vmoe_last_error.restype = c_char_p
+    lib.vmoe_status_string.argtypes = [c_int]
+    lib.vmoe_status_string.restype = c_char_p
+    lib.vmoe_abi_version.argtypes = []
+    lib.vmoe_abi_version.restype = c_int
+    _lib = lib
+    return lib
+
+
+def check(rc: int, handle=None, what: str = "vmoe call") -> None:
+    """Raise VmoeError for a non-zero status, with the handle's error text."""
+    if rc == VMOE_OK:
+        return
+    lib = load()
+    detail = ""
+    if handle:
+        detail = (lib.vmoe_last_error(handle) or b"").decode()
+    status = (lib.vmoe_status_string(rc) or b"").decode()
+    raise VmoeError(rc, f"{what} failed: {status}" + (f" ({detail})" if detail else ""))
+
+
+class Handle:
+    """Owns one ``vmoe_handle`` (one layer configuration on one device)."""
+
+    def __init__(self, cfg: VmoeConfig, device: int):
+        self.lib = load()
+        self.cfg = cfg
+        self.device = device
+        self.ptr = c_void_p()
+        check(self.lib.vmoe_create(ctypes.byref(cfg), device, ctypes.byref(self.ptr)),
+              None, "vmoe_create")
+
+    def close(self) -> None:
+        if self.ptr:
+            self.lib.vmoe_destroy(self.ptr)
+            self.ptr = c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def workspace_size(self, tokens: int) -> int:
+        n = c_size_t()
+        check(self.lib.vmoe_workspace_size(self.ptr, tokens, ctypes.byref(n)), self.ptr,
+              "vmoe_workspace_size")
+        return n.value
+
+    def workspace_layout(self, tokens: int) -> VmoeWsLayout:
+        lay = VmoeWsLayout()
+        check(self.lib.vmoe_workspace_layout(self.ptr, tokens, ctypes.byref(lay)), self.ptr,
+              "vmoe_workspace_layout")
+        return lay
+
+    def set_weights(self, w: VmoeWeights, stream: int) -> None:
+        check(self.lib.vmoe_set_weights(self.ptr, ctypes.byref(w), c_void_p(stream)), self.ptr,
+              "vmoe_set_weights")
+
+    def forward(self, x, tokens, out, logits, idx, topw, counts, aux, ws, ws_bytes, stream):
+        rc = self.lib.vmoe_forward(self.ptr, x, tokens, out, logits, idx, topw, counts, aux, ws,
+                                   ws_bytes, c_void_p(stream))
+        check(rc, self.ptr, "vmoe_forward")
+
+    def device_status(self, stream: int) -> int:
+        code = c_int32()
+        check(self.lib.vmoe_device_status(self.ptr, ctypes.byref(code), c_void_p(stream)),
+              self.ptr, "vmoe_device_status")
+        return code.value
+
+    def set_profiling(self, forwards: int) -> None:
+        """Record per-stage events for the next ``forwards`` forwards (0 = off)."""
+        check(self.lib.vmoe_set_profiling(self.ptr, int(forwards)), self.ptr, "vmoe_set_profiling")
+
+    def stage_times(self) -> tuple[dict[str, float], int]:
+        """(average ms per stage, number of forwards averaged); restarts recording."""
+        buf = (c_float * 16)()
+        n, f = c_int(), c_int()
+        check(self.lib.vmoe_stage_times(self.ptr, buf, 16, ctypes.byref(n), ctypes.byref(f)),
+              self.ptr, "vmoe_stage_times")
+        return {self.lib.vmoe_stage_name(i).decode(): float(buf[i]) for i in range(n.value)}, f.value
+
+    def last_launch_count(self) -> int:
+        return int(self.lib.vmoe_last_launch_count(self.ptr))

@@ -1,0 +1,276 @@
+// Token dispatch and combine: the data-movement half of the MoE forward.
+//
+// Reference behaviour (python/vesper/model.py):
+//   :339-349  for each expert in ascending order, the tokens that chose it, in ascending
+//             token order (token_mask.nonzero()), are gathered: x_e = x_flat[token_idx];
+//   :337,354-357 out starts at zero and receives index_add_(token_idx, y_e * w_e) for
+//             e = 0..E-1 in that order;
+//   :366-385  aux = E * sum_e (count_e / (T*K)) * mean_t p[t, e].
+//
+// B200 layout: the permuted activations are one expert-major buffer whose expert
+// segments are padded to multiples of 128 rows (the grouped-GEMM M tile), so that every
+// M tile belongs to one expert and no GEMM tile needs a row mask.  Slots are assigned
+// without atomics: slot(t, k) = offs[e] + (tokens of earlier 128-token blocks that chose e)
+// + (rank of t among this block's tokens that chose e), which is the reference's stable
+// order and makes every run bit-identical.
+#include "common.cuh"
+#include "kernels.h"
+
+namespace vmoe {
+namespace {
+
+// ---- 1. per-expert exclusive scan over routing blocks --------------------------------
+// grid = E, block = 256: column e of hist[nblk][E] -> excl[nblk][E], counts[e]; column
+// sums of psum in a fixed order.
+__global__ void __launch_bounds__(256)
+scan_blocks_kernel(const int* __restrict__ hist, const float* __restrict__ psum, int nblk, int E,
+                   int* __restrict__ excl, int* __restrict__ counts, float* __restrict__ psum_tot) {
+  const int e = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int per = (nblk + 255) / 256;
+  const int b0 = min(nblk, tid * per), b1 = min(nblk, b0 + per);
+  int local = 0;
+  float ps = 0.f;
+  for (int b = b0; b < b1; ++b) {
+    local += hist[static_cast<int64_t>(b) * E + e];
+    ps += psum[static_cast<int64_t>(b) * E + e];
+  }
+  // block exclusive scan of `local` (warp shuffles, then warp totals)
+  __shared__ int wsum[8];
+  __shared__ float wps[8];
+  int inc = local;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int n = __shfl_up_sync(0xffffffffu, inc, o);
+    if (lane >= o) inc += n;
+  }
+  // fixed-shape tree for the float sum
+  float fs = ps;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) fs += __shfl_xor_sync(0xffffffffu, fs, o);
+  if (lane == 31) wsum[warp] = inc;
+  if (lane == 0) wps[warp] = fs;
+  __syncthreads();
+  int wbase = 0;
+  for (int w = 0; w < warp; ++w) wbase += wsum[w];
+  int run = wbase + inc - local;
+  for (int b = b0; b < b1; ++b) {
+    excl[static_cast<int64_t>(b) * E + e] = run;
+    run += hist[static_cast<int64_t>(b) * E + e];
+  }
+  if (tid == 0) {
+    int tot = 0;
+    float pt = 0.f;
+    for (int w = 0; w < 8; ++w) { tot += wsum[w]; pt += wps[w]; }
+    counts[e] = tot;
+    psum_tot[e] = pt;
+  }
+}
+
+// ---- 2. expert offsets, M-tile map, aux loss ------------------------------------------
+// one block of 1024 threads (E <= 1024)
+__global__ void __launch_bounds__(1024)
+plan_kernel(const int* __restrict__ counts, const float* __restrict__ psum_tot, int64_t T, int E,
+            int K, int64_t capacity, int* __restrict__ offs, int* __restrict__ tile_expert,
+            int* __restrict__ num_tiles, float* __restrict__ aux, int32_t* __restrict__ counts_out) {
+  __shared__ int pad_s[1024];
+  __shared__ int off_s[1025];
+  const int tid = threadIdx.x;
+  if (tid < E) {
+    int kept = counts[tid];
+    if (capacity > 0 && kept > capacity) kept = static_cast<int>(capacity);
+    pad_s[tid] = (kept + kTileM - 1) / kTileM * kTileM;
+    if (counts_out) counts_out[tid] = counts[tid];
+  }
+  __syncthreads();
+  if (tid == 0) {
+    int run = 0;
+    for (int e = 0; e < E; ++e) { off_s[e] = run; run += pad_s[e]; }
+    off_s[E] = run;
+    *num_tiles = run / kTileM;
+    // Switch load-balancing loss (model.py:366-385), fixed summation order
+    const float inv_tk = 1.0f / static_cast<float>(T * K);
+    const float inv_t = 1.0f / static_cast<float>(T);
+    float s = 0.f;
+    for (int e = 0; e < E; ++e) {
+      const float f = static_cast<float>(counts[e]) * inv_tk;
+      const float p = psum_tot[e] * inv_t;
+      s += f * p;
+    }
+    if (aux) *aux = static_cast<float>(E) * s;
+  }
+  __syncthreads();
+  for (int e = tid; e <= E; e += blockDim.x) offs[e] = off_s[e];
+  if (tid < E) {
+    const int t0 = off_s[tid] / kTileM, nt = pad_s[tid] / kTileM;
+    for (int j = 0; j < nt; ++j) tile_expert[t0 + j] = tid;
+  }
+}
+
+// ---- 3. slot assignment + gather -----------------------------------------------------
+// grid = nblk, block = 128 (one thread per token of the routing block)
+template <typename T>
+__global__ void __launch_bounds__(128)
+dispatch_kernel(const T* __restrict__ x, const int32_t* __restrict__ topk_idx,
+                const int* __restrict__ excl, const int* __restrict__ offs, int64_t T_tok, int H,
+                int E, int K, int64_t capacity, int* __restrict__ slot_of, T* __restrict__ x_perm,
+                int64_t xp_ld, int* status) {
+  extern __shared__ uint32_t dsm[];
+  uint32_t* masks = dsm;                            // [4 warps][E] token bitmasks
+  int* wbase = reinterpret_cast<int*>(dsm + 4 * E);  // [4][E]
+  int* slots = wbase + 4 * E;                        // [128][K]
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int64_t blk = blockIdx.x;
+  const int64_t t = blk * kTileM + tid;
+  const bool valid = t < T_tok;
+
+  for (int i = tid; i < 4 * E; i += 128) masks[i] = 0u;
+  __syncthreads();
+  if (valid) {
+    for (int k = 0; k < K; ++k) {
+      const int e = topk_idx[t * K + k];
+      atomicOr(&masks[warp * E + e], 1u << lane);
+    }
+  }
+  __syncthreads();
+  for (int e = tid; e < E; e += 128) {
+    int run = 0;
+    for (int w = 0; w < 4; ++w) { wbase[w * E + e] = run; run += __popc(masks[w * E + e]); }
+  }
+  __syncthreads();
+  const uint32_t lt = (1u << lane) - 1u;
+  for (int k = 0; k < K; ++k) {
+    int slot = -1;
+    if (valid) {
+      const int e = topk_idx[t * K + k];
+      const int rank = excl[blk * E + e] + wbase[warp * E + e] + __popc(masks[warp * E + e] & lt);
+      if (capacity <= 0 || rank < capacity) slot = offs[e] + rank;
+      if (slot >= offs[e + 1]) { report(status, kStatusBadSlot); slot = -1; }
+      slot_of[t * K + k] = slot;
+    }
+    slots[tid * K + k] = slot;
+  }
+  __syncthreads();
+  // gather: each warp copies whole rows with 16-byte vectors, reading x[t] once
+  constexpr int V = Vec16<T>::N;
+  const int nvec = H / V;
+  const int ntok = static_cast<int>(T_tok - blk * kTileM < kTileM ? T_tok - blk * kTileM : kTileM);
+  for (int i = warp; i < ntok; i += 4) {
+    const T* src = x + (blk * kTileM + i) * static_cast<int64_t>(H);
+    for (int v0 = 0; v0 < nvec; v0 += 32 * 4) {
+      uint4 buf[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int v = v0 + u * 32 + lane;
+        if (v < nvec) buf[u] = reinterpret_cast<const uint4*>(src)[v];
+      }
+      for (int k = 0; k < K; ++k) {
+        const int s = slots[i * K + k];
+        if (s < 0) continue;
+        uint4* dst = reinterpret_cast<uint4*>(x_perm + static_cast<int64_t>(s) * xp_ld);
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int v = v0 + u * 32 + lane;
+          if (v < nvec) dst[v] = buf[u];
+        }
+      }
+    }
+  }
+}
+
+// ---- 4. combine --------------------------------------------------------------------
+// one warp per token; fp32 accumulation in ascending expert order (model.py:339-357)
+template <typename T>
+__global__ void __launch_bounds__(256)
+combine_kernel(const T* __restrict__ y, int64_t y_ld, const int32_t* __restrict__ topk_idx,
+               const float* __restrict__ topk_w, const int* __restrict__ slot_of, int64_t T_tok,
+               int H, int K, T* __restrict__ out) {
+  const int lane = threadIdx.x & 31;
+  const int64_t t = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
+  if (t >= T_tok) return;
+  // the token's K (expert, slot, weight) triples sorted by expert id (K <= 32)
+  int ord_e[32], ord_s[32];
+  float ord_w[32];
+  int n = 0;
+  for (int k = 0; k < K; ++k) {
+    const int e = topk_idx[t * K + k];
+    const int s = slot_of[t * K + k];
+    const float w = topk_w[t * K + k];
+    int j = n++;
+    while (j > 0 && ord_e[j - 1] > e) {
+      ord_e[j] = ord_e[j - 1]; ord_s[j] = ord_s[j - 1]; ord_w[j] = ord_w[j - 1];
+      --j;
+    }
+    ord_e[j] = e; ord_s[j] = s; ord_w[j] = w;
+  }
+  constexpr int V = Vec16<T>::N;
+  const int nvec = H / V;
+  T* orow = out + t * static_cast<int64_t>(H);
+  for (int v = lane; v < nvec; v += 32) {
+    float acc[V];
+#pragma unroll
+    for (int i = 0; i < V; ++i) acc[i] = 0.f;
+    for (int j = 0; j < n; ++j) {
+      if (ord_s[j] < 0) continue;  // dropped by capacity
+      float f[V];
+      load16_to_f(y + static_cast<int64_t>(ord_s[j]) * y_ld + v * V, f);
+      const float w = ord_w[j];
+#pragma unroll
+      for (int i = 0; i < V; ++i) acc[i] = __fadd_rn(acc[i], __fmul_rn(f[i], w));  // (y*w) then add
+    }
+    store16_from_f(orow + v * V, acc);
+  }
+}
+
+}  // namespace
+
+cudaError_t launch_scan_blocks(const int* hist, const float* psum, int nblk, int E, int* excl,
+                               int* counts, float* psum_tot, cudaStream_t s) {
+  scan_blocks_kernel<<<E, 256, 0, s>>>(hist, psum, nblk, E, excl, counts, psum_tot);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_plan(const int* counts, const float* psum_tot, int64_t T, int E, int K,
+                        int64_t capacity, int* offs, int* tile_expert, int* num_tiles,
+                        float* aux, int32_t* counts_out, cudaStream_t s) {
+  plan_kernel<<<1, 1024, 0, s>>>(counts, psum_tot, T, E, K, capacity, offs, tile_expert,
+                                 num_tiles, aux, counts_out);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_dispatch(int dtype, const void* x, const int32_t* topk_idx, const int* excl,
+                            const int* offs, int64_t T, int H, int E, int K, int64_t capacity,
+                            int* slot_of, void* x_perm, int64_t xp_ld, int* status,
+                            cudaStream_t s) {
+  const unsigned nblk = static_cast<unsigned>((T + kTileM - 1) / kTileM);
+  const size_t smem = (8 * static_cast<size_t>(E) + static_cast<size_t>(kTileM) * K) * 4;
+  if (dtype == kF32) {
+    auto kern = dispatch_kernel<float>;
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    kern<<<nblk, 128, smem, s>>>(static_cast<const float*>(x), topk_idx, excl, offs, T, H, E, K,
+                                 capacity, slot_of, static_cast<float*>(x_perm), xp_ld, status);
+  } else {
+    auto kern = dispatch_kernel<__nv_bfloat16>;
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    kern<<<nblk, 128, smem, s>>>(static_cast<const __nv_bfloat16*>(x), topk_idx, excl, offs, T, H,
+                                 E, K, capacity, slot_of, static_cast<__nv_bfloat16*>(x_perm),
+                                 xp_ld, status);
+  }
+  return cudaGetLastError();
+}
+
+cudaError_t launch_combine(int dtype, const void* y, int64_t y_ld, const int32_t* topk_idx,
+                           const float* topk_w, const int* slot_of, int64_t T, int H, int K,
+                           void* out, cudaStream_t s) {
+  const unsigned grid = static_cast<unsigned>((T + 7) / 8);
+  if (dtype == kF32) {
+    combine_kernel<float><<<grid, 256, 0, s>>>(static_cast<const float*>(y), y_ld, topk_idx,
+                                               topk_w, slot_of, T, H, K, static_cast<float*>(out));
+  } else {
+    combine_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>(
+        static_cast<const __nv_bfloat16*>(y), y_ld, topk_idx, topk_w, slot_of, T, H, K,
+        static_cast<__nv_bfloat16*>(out));
+  }
+  return cudaGetLastError();
+}
+
+}  // namespace vmoe

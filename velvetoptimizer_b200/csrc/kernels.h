@@ -1,0 +1,117 @@
+// Internal launcher interface between the C-ABI host code and the CUDA kernels.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+namespace vmoe {
+
+enum Dtype { kF32 = 0, kBF16 = 1 };
+
+// Rows per routing block and per grouped-GEMM M tile: every expert segment of the
+// permuted buffer is padded to a multiple of this, so each M tile has one expert.
+constexpr int kTileM = 128;
+
+inline size_t dtype_bytes(int dt) { return dt == kF32 ? 4 : 2; }
+
+// ---- routing ------------------------------------------------------------------------
+// Router GEMM + softmax + top-K (lowest-index tie-break) + renormalise, per 128-token
+// block also the expert histogram hist[blk][E] and probability sums psum[blk][E].
+cudaError_t launch_router(int dtype, const void* x, const void* w_r, const float* b_r, int64_t T,
+                          int H, int E, int K, float* logits, int32_t* topk_idx, float* topk_w,
+                          int* hist, float* psum, cudaStream_t s);
+
+// Per expert: exclusive prefix of hist over blocks (excl[blk][E]), counts, prob sums.
+cudaError_t launch_scan_blocks(const int* hist, const float* psum, int nblk, int E, int* excl,
+                               int* counts, float* psum_tot, cudaStream_t s);
+
+// Padded expert offsets, M-tile -> expert map, tile count, aux loss, caller counts.
+cudaError_t launch_plan(const int* counts, const float* psum_tot, int64_t T, int E, int K,
+                        int64_t capacity, int* offs, int* tile_expert, int* num_tiles,
+                        float* aux, int32_t* counts_out, cudaStream_t s);
+
+// Stable expert-major slots for every (token, k) and the row gather x -> x_perm.
+cudaError_t launch_dispatch(int dtype, const void* x, const int32_t* topk_idx, const int* excl,
+                            const int* offs, int64_t T, int H, int E, int K, int64_t capacity,
+                            int* slot_of, void* x_perm, int64_t xp_ld, int* status,
+                            cudaStream_t s);
+
+// out[t] = sum over the token's experts in ascending id of w * y[slot]  (fp32 sum).
+cudaError_t launch_combine(int dtype, const void* y, int64_t y_ld, const int32_t* topk_idx,
+                           const float* topk_w, const int* slot_of, int64_t T, int H, int K,
+                           void* out, cudaStream_t s);
+
+// ---- fp32 expert GEMMs (CUDA cores; the fp32 correctness path) ------------------------
+// h = ERA(A Wg^T + bg) * (A Wu^T + bu) per M tile's expert.
+cudaError_t launch_simt_gemm1(const float* a, int64_t lda, const float* wg, const float* wu,
+                              const float* bg, const float* bu, float* h, int64_t ldh, int N,
+                              int K, float gamma, const int* tile_expert, const int* num_tiles,
+                              int64_t max_tiles, cudaStream_t s);
+// y = A Wd^T + bd per M tile's expert.
+cudaError_t launch_simt_gemm2(const float* a, int64_t lda, const float* wd, const float* bd,
+                              float* y, int64_t ldy, int N, int K, const int* tile_expert,
+                              const int* num_tiles, int64_t max_tiles, cudaStream_t s);
+
+// ---- bf16 expert GEMMs (tcgen05 + TMEM + TMA) ----------------------------------------
+struct TcGemmArgs {
+  const int* num_m_tiles;   // device scalar
+  const int* tile_expert;   // [max_tiles]
+  int n_tiles;              // output tiles per expert along N
+  int k_blocks;             // ceil(K / 64)
+  int b_rows_per_expert;    // rows of the 2-D weight view per expert
+  void* out;                // bf16 output
+  int64_t ldo;              // elements
+  const float* bias;        // fp32, per expert
+  int64_t bias_ld;          // elements per expert
+  float gamma;              // ERA gamma (gated epilogue)
+  int* status;
+};
+// gated = true : B tile = [128 gate rows | 128 up rows], h = ERA(gate) * up (128 cols)
+// gated = false: plain bias epilogue, 256 output columns per tile
+cudaError_t launch_tc_gemm(bool gated, const CUtensorMap& a_map, const CUtensorMap& b_map,
+                           const TcGemmArgs& args, int64_t max_tiles, int num_sms,
+                           cudaStream_t s);
+
+// Build a 2-D bf16 tensor map: [rows, cols] row-major with `ld` elements per row, box
+// {64 cols, box_rows rows}, 128-byte swizzle.  Returns false on failure.
+bool make_tmap_bf16(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols,
+                    uint64_t ld, uint32_t box_rows, char* err, size_t err_len);
+
+// ---- weight packing ------------------------------------------------------------------
+// dst[e][map(o)][k] = src[e][o][k] + s * sum_r lu[e][o][r] * ld[e][r][k]  (0 when padded)
+struct PackArgs {
+  int dtype;                 // of src / lora tensors and dst
+  const void* src;           // [E, O, Kin]
+  const void* lora_down;     // [E, R, Kin] or null
+  const void* lora_up;       // [E, O, R] or null
+  int R;
+  float scaling;
+  int E, O, Kin;
+  void* dst;                 // [E, Opad_rows, Kpad] (row map below)
+  int Kpad;                  // dst row length
+  int dst_rows_per_expert;
+  int interleave;            // 0: row o -> o;  >0: block-interleave two matrices (see pack.cu)
+  int which;                 // 0 = gate / first, 1 = up / second (interleave only)
+};
+cudaError_t launch_pack_weight(const PackArgs& a, cudaStream_t s);
+
+// bias: dst[e][map(o)] = b[e][o] + s * (sum_r lu[e][o][r] * bd[e][r] + bu[e][o])  (fp32 out)
+struct PackBiasArgs {
+  int dtype;
+  const void* b;             // [E, O] or null
+  const void* lora_up;       // [E, O, R] or null
+  const void* lora_down_b;   // [E, R] or null
+  const void* lora_up_b;     // [E, O] or null
+  int R;
+  float scaling;
+  int E, O;
+  float* dst;
+  int dst_per_expert;
+  int interleave;
+  int which;
+};
+cudaError_t launch_pack_bias(const PackBiasArgs& a, cudaStream_t s);
+
+}  // namespace vmoe

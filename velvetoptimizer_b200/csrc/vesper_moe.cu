@@ -1,0 +1,641 @@
+// C-ABI host side of the MoE FFN forward (include/vesper_moe.h).
+//
+// Owns: argument validation (VesperConfig.validate, python/vesper/config.py:89-94), the
+// packed weights, the workspace plan, and the launch sequence that replaces
+// MoELayer.forward (python/vesper/model.py:317-364):
+//
+//   router -> scan_blocks -> plan -> dispatch -> gemm1 (gate|up, ERA*up) -> gemm2 (down)
+//   -> combine
+//
+// No host synchronisation and no allocation happen inside vmoe_forward.
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdarg.h>
+#include <stdio.h>
+#include <string.h>
+
+#include <new>
+#include <string>
+#include <vector>
+
+#include "../../include/vesper_moe.h"
+#include "kernels.h"
+
+using namespace vmoe;
+
+namespace {
+
+constexpr int kStages = 7;
+const char* const kStageNames[kStages] = {"router", "scan", "plan", "dispatch",
+                                          "gemm1_gate_up_era", "gemm2_down", "combine"};
+constexpr int kGateUpInterleave = 128;  // rows of gate (then up) per 256-row B tile
+constexpr int kDownTileN = 256;         // N tile of the down projection
+
+int64_t round_up(int64_t v, int64_t m) { return (v + m - 1) / m * m; }
+
+struct DeviceGuard {
+  int prev = -1;
+  explicit DeviceGuard(int dev) {
+    if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+    if (prev != dev) cudaSetDevice(dev);
+  }
+  ~DeviceGuard() {
+    int cur = -1;
+    if (prev >= 0 && cudaGetDevice(&cur) == cudaSuccess && cur != prev) cudaSetDevice(prev);
+  }
+};
+
+struct Plan {
+  int nblk = 0;
+  int64_t max_tiles = 0, max_rows = 0;
+  size_t idx = 0, w = 0, hist = 0, psum = 0, excl = 0, counts = 0, psum_tot = 0, offs = 0,
+         tiles = 0, ntiles = 0, aux = 0, slot = 0, xp = 0, h = 0, y = 0, total = 0;
+};
+
+}  // namespace
+
+struct vmoe_handle {
+  vmoe_config cfg{};
+  int device = 0;
+  int num_sms = 148;
+  int dtype = kF32;
+  int64_t H = 0, I = 0, E = 0, K = 0;
+  int64_t Ipad = 0, Hpad = 0;
+  // packed weights (library-owned)
+  void* w_r = nullptr;
+  float* b_r = nullptr;
+  void* w_g = nullptr;  // f32: [E, I, H]; bf16: interleaved gate|up [E, 2*Ipad, H]
+  void* w_u = nullptr;  // f32 only
+  float* b_g = nullptr; // f32: [E, I]; bf16: interleaved [E, 2*Ipad]
+  float* b_u = nullptr;
+  void* w_d = nullptr;  // [E, Hpad, Ipad]
+  float* b_d = nullptr; // [E, Hpad]
+  int* status = nullptr;
+  CUtensorMap map_wgu{}, map_wd{};
+  bool ready = false;
+  // profiling ring: prof_slots forwards x (kStages + 1) events
+  int prof_slots = 0;
+  int prof_count = 0;
+  std::vector<cudaEvent_t> prof_ev;
+  int last_launches = 0;
+  std::string err;
+};
+
+namespace {
+
+int fail(vmoe_handle* h, int code, const char* fmt, ...) {
+  if (h) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof(buf), fmt, ap);
+    va_end(ap);
+    h->err = buf;
+  }
+  return code;
+}
+
+int cuda_fail(vmoe_handle* h, cudaError_t e, const char* what) {
+  return fail(h, VMOE_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+Plan make_plan(const vmoe_handle* h, int64_t T) {
+  Plan p;
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    const size_t o = off;
+    off += (bytes + 255) & ~static_cast<size_t>(255);
+    return o;
+  };
+  const int64_t E = h->E, K = h->K;
+  const size_t elt = dtype_bytes(h->dtype);
+  p.nblk = static_cast<int>((T + kTileM - 1) / kTileM);
+  int64_t rows_bound = T * K + E * (kTileM - 1);
+  if (h->cfg.capacity > 0) {
+    const int64_t cap_rows = E * round_up(h->cfg.capacity, kTileM);
+    if (cap_rows < rows_bound) rows_bound = cap_rows;
+  }
+  p.max_tiles = (rows_bound + kTileM - 1) / kTileM;
+  if (p.max_tiles < 1) p.max_tiles = 1;
+  p.max_rows = p.max_tiles * kTileM;
+  p.idx = take(T * K * 4);
+  p.w = take(T * K * 4);
+  p.hist = take(static_cast<size_t>(p.nblk) * E * 4);
+  p.psum = take(static_cast<size_t>(p.nblk) * E * 4);
+  p.excl = take(static_cast<size_t>(p.nblk) * E * 4);
+  p.counts = take(E * 4);
+  p.psum_tot = take(E * 4);
+  p.offs = take((E + 1) * 4);
+  p.tiles = take(p.max_tiles * 4);
+  p.ntiles = take(4);
+  p.aux = take(4);
+  p.slot = take(T * K * 4);
+  p.xp = take(static_cast<size_t>(p.max_rows) * h->H * elt);
+  p.h = take(static_cast<size_t>(p.max_rows) * h->Ipad * elt);
+  p.y = take(static_cast<size_t>(p.max_rows) * h->Hpad * elt);
+  p.total = off;
+  return p;
+}
+
+void free_weights(vmoe_handle* h) {
+  void* bufs[] = {h->w_r, h->b_r, h->w_g, h->w_u, h->b_g, h->b_u, h->w_d, h->b_d};
+  for (void* b : bufs)
+    if (b) cudaFree(b);
+  h->w_r = h->w_g = h->w_u = h->w_d = nullptr;
+  h->b_r = h->b_g = h->b_u = h->b_d = nullptr;
+  h->ready = false;
+}
+
+int validate_config(const vmoe_config* c, char* why, size_t n) {
+  if (c->hidden <= 0 || c->inter <= 0) {
+    snprintf(why, n, "hidden (%lld) and inter (%lld) must be positive",
+             static_cast<long long>(c->hidden), static_cast<long long>(c->inter));
+    return VMOE_ERR_INVALID_ARG;
+  }
+  if (c->num_experts < 2) {  // config.py:94
+    snprintf(why, n, "num_experts must be >= 2 (got %d)", c->num_experts);
+    return VMOE_ERR_INVALID_ARG;
+  }
+  if (c->top_k < 1 || c->top_k > c->num_experts) {  // config.py:92
+    snprintf(why, n, "top_k must satisfy 1 <= top_k <= num_experts (got top_k=%d, E=%d)",
+             c->top_k, c->num_experts);
+    return VMOE_ERR_INVALID_ARG;
+  }
+  if (c->dtype != VMOE_F32 && c->dtype != VMOE_BF16) {
+    snprintf(why, n, "dtype must be VMOE_F32 or VMOE_BF16 (got %d)", c->dtype);
+    return VMOE_ERR_INVALID_ARG;
+  }
+  if (c->capacity < 0 || c->lora_rank < 0) {
+    snprintf(why, n, "capacity and lora_rank must be >= 0");
+    return VMOE_ERR_INVALID_ARG;
+  }
+  if (c->num_experts > 256) {
+    snprintf(why, n, "num_experts > 256 is not supported by this build (got %d)", c->num_experts);
+    return VMOE_ERR_UNSUPPORTED_SHAPE;
+  }
+  if (c->top_k > 32) {
+    snprintf(why, n, "top_k > 32 is not supported by this build (got %d)", c->top_k);
+    return VMOE_ERR_UNSUPPORTED_SHAPE;
+  }
+  if (c->hidden % 8 || c->inter % 8) {
+    snprintf(why, n, "hidden and inter must be multiples of 8 (got %lld, %lld)",
+             static_cast<long long>(c->hidden), static_cast<long long>(c->inter));
+    return VMOE_ERR_UNSUPPORTED_SHAPE;
+  }
+  if (c->lora_rank > 1024) {
+    snprintf(why, n, "lora_rank > 1024 is not supported (got %d)", c->lora_rank);
+    return VMOE_ERR_UNSUPPORTED_SHAPE;
+  }
+  return VMOE_OK;
+}
+
+template <typename T>
+int alloc(vmoe_handle* h, T** p, size_t bytes, const char* what) {
+  cudaError_t e = cudaMalloc(reinterpret_cast<void**>(p), bytes);
+  if (e != cudaSuccess) return cuda_fail(h, e, what);
+  return VMOE_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int vmoe_abi_version(void) { return VMOE_ABI_VERSION; }
+
+const char* vmoe_status_string(int status) {
+  switch (status) {
+    case VMOE_OK: return "ok";
+    case VMOE_ERR_INVALID_ARG: return "invalid argument";
+    case VMOE_ERR_UNSUPPORTED_SHAPE: return "unsupported shape";
+    case VMOE_ERR_CUDA: return "CUDA error";
+    case VMOE_ERR_NCCL: return "NCCL error";
+    case VMOE_ERR_TIMEOUT: return "device wait timed out";
+    case VMOE_ERR_DEVICE_STATUS: return "device reported an error";
+    case VMOE_ERR_NOT_READY: return "weights not set";
+    case VMOE_ERR_WORKSPACE: return "workspace too small or misaligned";
+    default: return "unknown status";
+  }
+}
+
+const char* vmoe_last_error(const vmoe_handle* h) { return h ? h->err.c_str() : ""; }
+
+const char* vmoe_stage_name(int stage) {
+  return (stage >= 0 && stage < kStages) ? kStageNames[stage] : "";
+}
+
+int vmoe_create(const vmoe_config* cfg, int device, vmoe_handle** out) {
+  if (!cfg || !out) return VMOE_ERR_INVALID_ARG;
+  *out = nullptr;
+  char why[256];
+  const int v = validate_config(cfg, why, sizeof(why));
+  if (v != VMOE_OK) {
+    fprintf(stderr, "vmoe_create: %s\n", why);
+    return v;
+  }
+  int ndev = 0;
+  if (cudaGetDeviceCount(&ndev) != cudaSuccess || device < 0 || device >= ndev) {
+    cudaGetLastError();
+    fprintf(stderr, "vmoe_create: CUDA device %d is not available\n", device);
+    return VMOE_ERR_CUDA;
+  }
+  vmoe_handle* h = new (std::nothrow) vmoe_handle();
+  if (!h) return VMOE_ERR_CUDA;
+  h->cfg = *cfg;
+  h->device = device;
+  h->dtype = cfg->dtype;
+  h->H = cfg->hidden;
+  h->I = cfg->inter;
+  h->E = cfg->num_experts;
+  h->K = cfg->top_k;
+  if (h->dtype == kBF16) {
+    h->Ipad = round_up(h->I, kGateUpInterleave);
+    h->Hpad = round_up(h->H, kDownTileN);
+  } else {
+    h->Ipad = h->I;
+    h->Hpad = h->H;
+  }
+  DeviceGuard g(device);
+  cudaDeviceGetAttribute(&h->num_sms, cudaDevAttrMultiProcessorCount, device);
+  if (h->dtype == kBF16) {
+    int major = 0, minor = 0;
+    cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, device);
+    cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, device);
+    if (major != 10 || minor != 0) {
+      fprintf(stderr, "vmoe_create: the bf16 path needs an sm_100 GPU (got sm_%d%d)\n", major,
+              minor);
+      delete h;
+      return VMOE_ERR_UNSUPPORTED_SHAPE;
+    }
+  }
+  cudaError_t e = cudaMalloc(&h->status, sizeof(int));
+  if (e == cudaSuccess) e = cudaMemset(h->status, 0, sizeof(int));
+  if (e != cudaSuccess) {
+    fprintf(stderr, "vmoe_create: %s\n", cudaGetErrorString(e));
+    vmoe_destroy(h);
+    return VMOE_ERR_CUDA;
+  }
+  *out = h;
+  return VMOE_OK;
+}
+
+int vmoe_destroy(vmoe_handle* h) {
+  if (!h) return VMOE_ERR_INVALID_ARG;
+  {
+    DeviceGuard g(h->device);
+    free_weights(h);
+    if (h->status) cudaFree(h->status);
+    for (cudaEvent_t ev : h->prof_ev) cudaEventDestroy(ev);
+  }
+  delete h;
+  return VMOE_OK;
+}
+
+int vmoe_set_weights(vmoe_handle* h, const vmoe_weights* w, void* stream) {
+  if (!h) return VMOE_ERR_INVALID_ARG;
+  if (!w) return fail(h, VMOE_ERR_INVALID_ARG, "weights is NULL");
+  if (!w->router_w || !w->gate_w || !w->up_w || !w->down_w)
+    return fail(h, VMOE_ERR_INVALID_ARG, "router_w, gate_w, up_w and down_w are required");
+  DeviceGuard g(h->device);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  free_weights(h);
+  const int64_t E = h->E, H = h->H, I = h->I, Ipad = h->Ipad, Hpad = h->Hpad;
+  const size_t elt = dtype_bytes(h->dtype);
+  const bool bf16 = h->dtype == kBF16;
+  const int R = h->cfg.lora_rank;
+  int rc;
+  if ((rc = alloc(h, &h->w_r, E * H * elt, "router weight")) != VMOE_OK) return rc;
+  if ((rc = alloc(h, &h->b_r, E * 4, "router bias")) != VMOE_OK) return rc;
+  const int64_t gu_rows = bf16 ? 2 * Ipad : I;
+  if ((rc = alloc(h, &h->w_g, E * gu_rows * H * elt, "gate weight")) != VMOE_OK) return rc;
+  if ((rc = alloc(h, &h->b_g, E * gu_rows * 4, "gate bias")) != VMOE_OK) return rc;
+  if (!bf16) {
+    if ((rc = alloc(h, &h->w_u, E * I * H * elt, "up weight")) != VMOE_OK) return rc;
+    if ((rc = alloc(h, &h->b_u, E * I * 4, "up bias")) != VMOE_OK) return rc;
+  }
+  if ((rc = alloc(h, &h->w_d, E * Hpad * Ipad * elt, "down weight")) != VMOE_OK) return rc;
+  if ((rc = alloc(h, &h->b_d, E * Hpad * 4, "down bias")) != VMOE_OK) return rc;
+
+  cudaError_t e;
+  // router: plain copy of W_r, bias to fp32
+  e = cudaMemcpyAsync(h->w_r, w->router_w, E * H * elt, cudaMemcpyDeviceToDevice, s);
+  if (e != cudaSuccess) return cuda_fail(h, e, "router weight copy");
+  {
+    PackBiasArgs b{h->dtype, w->router_b, nullptr, nullptr, nullptr, 0, 0.f,
+                   static_cast<int>(1), static_cast<int>(E), h->b_r, static_cast<int>(E), 0, 0};
+    if ((e = launch_pack_bias(b, s)) != cudaSuccess) return cuda_fail(h, e, "router bias pack");
+  }
+  // gate / up with the FlyLoRA fold
+  const bool lora_g = R > 0 && w->gate_lora_down_w && w->gate_lora_up_w;
+  const bool lora_u = R > 0 && w->up_lora_down_w && w->up_lora_up_w;
+  for (int which = 0; which < 2; ++which) {
+    const bool lo = which == 0 ? lora_g : lora_u;
+    PackArgs p{};
+    p.dtype = h->dtype;
+    p.src = which == 0 ? w->gate_w : w->up_w;
+    p.lora_down = lo ? (which == 0 ? w->gate_lora_down_w : w->up_lora_down_w) : nullptr;
+    p.lora_up = lo ? (which == 0 ? w->gate_lora_up_w : w->up_lora_up_w) : nullptr;
+    p.R = lo ? R : 0;
+    p.scaling = h->cfg.lora_scaling;
+    p.E = static_cast<int>(E);
+    p.O = static_cast<int>(I);
+    p.Kin = static_cast<int>(H);
+    p.Kpad = static_cast<int>(H);
+    if (bf16) {
+      p.dst = h->w_g;
+      p.dst_rows_per_expert = static_cast<int>(2 * Ipad);
+      p.interleave = kGateUpInterleave;
+      p.which = which;
+    } else {
+      p.dst = which == 0 ? h->w_g : h->w_u;
+      p.dst_rows_per_expert = static_cast<int>(I);
+      p.interleave = 0;
+      p.which = 0;
+    }
+    if ((e = launch_pack_weight(p, s)) != cudaSuccess) return cuda_fail(h, e, "gate/up pack");
+    PackBiasArgs b{};
+    b.dtype = h->dtype;
+    b.b = which == 0 ? w->gate_b : w->up_b;
+    b.lora_up = p.lora_up;
+    b.lora_down_b = lo ? (which == 0 ? w->gate_lora_down_b : w->up_lora_down_b) : nullptr;
+    b.lora_up_b = lo ? (which == 0 ? w->gate_lora_up_b : w->up_lora_up_b) : nullptr;
+    b.R = p.R;
+    b.scaling = p.scaling;
+    b.E = p.E;
+    b.O = p.O;
+    b.dst = bf16 ? h->b_g : (which == 0 ? h->b_g : h->b_u);
+    b.dst_per_expert = p.dst_rows_per_expert;
+    b.interleave = p.interleave;
+    b.which = p.which;
+    if ((e = launch_pack_bias(b, s)) != cudaSuccess) return cuda_fail(h, e, "gate/up bias pack");
+  }
+  // down projection, zero padded to [E, Hpad, Ipad]
+  {
+    PackArgs p{};
+    p.dtype = h->dtype;
+    p.src = w->down_w;
+    p.E = static_cast<int>(E);
+    p.O = static_cast<int>(H);
+    p.Kin = static_cast<int>(I);
+    p.Kpad = static_cast<int>(Ipad);
+    p.dst = h->w_d;
+    p.dst_rows_per_expert = static_cast<int>(Hpad);
+    if ((e = launch_pack_weight(p, s)) != cudaSuccess) return cuda_fail(h, e, "down pack");
+    PackBiasArgs b{};
+    b.dtype = h->dtype;
+    b.b = w->down_b;
+    b.E = p.E;
+    b.O = p.O;
+    b.dst = h->b_d;
+    b.dst_per_expert = static_cast<int>(Hpad);
+    if ((e = launch_pack_bias(b, s)) != cudaSuccess) return cuda_fail(h, e, "down bias pack");
+  }
+  if (bf16) {
+    char why[256];
+    if (!make_tmap_bf16(&h->map_wgu, h->w_g, E * 2 * Ipad, H, H, 256, why, sizeof(why)))
+      return fail(h, VMOE_ERR_CUDA, "gate/up tensor map: %s", why);
+    if (!make_tmap_bf16(&h->map_wd, h->w_d, E * Hpad, Ipad, Ipad, 256, why, sizeof(why)))
+      return fail(h, VMOE_ERR_CUDA, "down tensor map: %s", why);
+  }
+  h->ready = true;
+  h->err.clear();
+  return VMOE_OK;
+}
+
+int vmoe_workspace_size(const vmoe_handle* h, int64_t tokens, size_t* bytes) {
+  if (!h || !bytes || tokens < 0) return VMOE_ERR_INVALID_ARG;
+  *bytes = make_plan(h, tokens).total;
+  return VMOE_OK;
+}
+
+int vmoe_workspace_layout(const vmoe_handle* h, int64_t tokens, vmoe_ws_layout* out) {
+  if (!h || !out || tokens < 0) return VMOE_ERR_INVALID_ARG;
+  const Plan p = make_plan(h, tokens);
+  out->slot_of = p.slot;
+  out->expert_offsets = p.offs;
+  out->num_tiles = p.ntiles;
+  out->x_perm = p.xp;
+  out->h = p.h;
+  out->y = p.y;
+  out->max_rows = p.max_rows;
+  out->h_ld = h->Ipad;
+  out->y_ld = h->Hpad;
+  out->total = p.total;
+  return VMOE_OK;
+}
+
+int vmoe_forward(vmoe_handle* h, const void* x, int64_t tokens, void* out, float* router_logits,
+                 int32_t* topk_idx, float* topk_w, int32_t* expert_counts, float* aux_loss,
+                 void* workspace, size_t workspace_bytes, void* stream) {
+  if (!h) return VMOE_ERR_INVALID_ARG;
+  h->last_launches = 0;
+  if (!h->ready) return fail(h, VMOE_ERR_NOT_READY, "vmoe_set_weights has not been called");
+  if (tokens < 0) return fail(h, VMOE_ERR_INVALID_ARG, "tokens must be >= 0 (got %lld)",
+                              static_cast<long long>(tokens));
+  const int64_t E = h->E, K = h->K, H = h->H, T = tokens;
+  if (T * K + E * kTileM >= (static_cast<int64_t>(1) << 31))
+    return fail(h, VMOE_ERR_UNSUPPORTED_SHAPE, "tokens * top_k too large (%lld)",
+                static_cast<long long>(T * K));
+  DeviceGuard g(h->device);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  cudaError_t e;
+  if (T == 0) {
+    // An empty batch: no output rows; the reference's mean over zero tokens makes aux NaN.
+    if (aux_loss) {
+      const float nan = __builtin_nanf("");
+      if ((e = cudaMemcpyAsync(aux_loss, &nan, 4, cudaMemcpyHostToDevice, s)) != cudaSuccess)
+        return cuda_fail(h, e, "aux write");
+    }
+    if (expert_counts && (e = cudaMemsetAsync(expert_counts, 0, E * 4, s)) != cudaSuccess)
+      return cuda_fail(h, e, "counts write");
+    return VMOE_OK;
+  }
+  if (!x || !out) return fail(h, VMOE_ERR_INVALID_ARG, "x and out are required");
+  if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(out)) & 15u)
+    return fail(h, VMOE_ERR_INVALID_ARG, "x and out must be 16-byte aligned");
+  const Plan p = make_plan(h, T);
+  if (!workspace || workspace_bytes < p.total)
+    return fail(h, VMOE_ERR_WORKSPACE, "workspace needs %zu bytes (got %zu)", p.total,
+                workspace ? workspace_bytes : static_cast<size_t>(0));
+  if (reinterpret_cast<uintptr_t>(workspace) & 255u)
+    return fail(h, VMOE_ERR_WORKSPACE, "workspace must be 256-byte aligned");
+
+  char* ws = static_cast<char*>(workspace);
+  int32_t* idx = topk_idx ? topk_idx : reinterpret_cast<int32_t*>(ws + p.idx);
+  float* tw = topk_w ? topk_w : reinterpret_cast<float*>(ws + p.w);
+  int* hist = reinterpret_cast<int*>(ws + p.hist);
+  float* psum = reinterpret_cast<float*>(ws + p.psum);
+  int* excl = reinterpret_cast<int*>(ws + p.excl);
+  int* counts = reinterpret_cast<int*>(ws + p.counts);
+  float* psum_tot = reinterpret_cast<float*>(ws + p.psum_tot);
+  int* offs = reinterpret_cast<int*>(ws + p.offs);
+  int* tiles = reinterpret_cast<int*>(ws + p.tiles);
+  int* ntiles = reinterpret_cast<int*>(ws + p.ntiles);
+  float* aux = aux_loss ? aux_loss : reinterpret_cast<float*>(ws + p.aux);
+  int* slot = reinterpret_cast<int*>(ws + p.slot);
+  void* xp = ws + p.xp;
+  void* hb = ws + p.h;
+  void* yb = ws + p.y;
+
+  const bool prof = h->prof_count < h->prof_slots;
+  cudaEvent_t* ev = prof ? &h->prof_ev[static_cast<size_t>(h->prof_count) * (kStages + 1)] : nullptr;
+  int stage = 0;
+  auto mark = [&]() {
+    if (prof) cudaEventRecord(ev[stage], s);
+    ++stage;
+  };
+  auto check = [&](cudaError_t err, const char* what) -> int {
+    if (err != cudaSuccess) return cuda_fail(h, err, what);
+    ++h->last_launches;
+    return VMOE_OK;
+  };
+  int rc;
+  mark();
+  if ((rc = check(launch_router(h->dtype, x, h->w_r, h->b_r, T, static_cast<int>(H),
+                                static_cast<int>(E), static_cast<int>(K), router_logits, idx, tw,
+                                hist, psum, s),
+                  "router")) != VMOE_OK)
+    return rc;
+  mark();
+  if ((rc = check(launch_scan_blocks(hist, psum, p.nblk, static_cast<int>(E), excl, counts,
+                                     psum_tot, s),
+                  "scan")) != VMOE_OK)
+    return rc;
+  mark();
+  if ((rc = check(launch_plan(counts, psum_tot, T, static_cast<int>(E), static_cast<int>(K),
+                              h->cfg.capacity, offs, tiles, ntiles, aux, expert_counts, s),
+                  "plan")) != VMOE_OK)
+    return rc;
+  mark();
+  if ((rc = check(launch_dispatch(h->dtype, x, idx, excl, offs, T, static_cast<int>(H),
+                                  static_cast<int>(E), static_cast<int>(K), h->cfg.capacity, slot,
+                                  xp, H, h->status, s),
+                  "dispatch")) != VMOE_OK)
+    return rc;
+  mark();
+  if (h->dtype == kF32) {
+    if ((rc = check(launch_simt_gemm1(static_cast<float*>(xp), H, static_cast<float*>(h->w_g),
+                                      static_cast<float*>(h->w_u), h->b_g, h->b_u,
+                                      static_cast<float*>(hb), h->Ipad, static_cast<int>(h->I),
+                                      static_cast<int>(H), h->cfg.era_gamma, tiles, ntiles,
+                                      p.max_tiles, s),
+                    "gemm1")) != VMOE_OK)
+      return rc;
+    mark();
+    if ((rc = check(launch_simt_gemm2(static_cast<float*>(hb), h->Ipad,
+                                      static_cast<float*>(h->w_d), h->b_d,
+                                      static_cast<float*>(yb), h->Hpad, static_cast<int>(H),
+                                      static_cast<int>(h->Ipad), tiles, ntiles, p.max_tiles, s),
+                    "gemm2")) != VMOE_OK)
+      return rc;
+  } else {
+    char why[256];
+    CUtensorMap map_x, map_h;
+    if (!make_tmap_bf16(&map_x, xp, p.max_rows, H, H, kTileM, why, sizeof(why)))
+      return fail(h, VMOE_ERR_CUDA, "x_perm tensor map: %s", why);
+    if (!make_tmap_bf16(&map_h, hb, p.max_rows, h->Ipad, h->Ipad, kTileM, why, sizeof(why)))
+      return fail(h, VMOE_ERR_CUDA, "h tensor map: %s", why);
+    TcGemmArgs a1{};
+    a1.num_m_tiles = ntiles;
+    a1.tile_expert = tiles;
+    a1.n_tiles = static_cast<int>(h->Ipad / kGateUpInterleave);
+    a1.k_blocks = static_cast<int>((H + 63) / 64);
+    a1.b_rows_per_expert = static_cast<int>(2 * h->Ipad);
+    a1.out = hb;
+    a1.ldo = h->Ipad;
+    a1.bias = h->b_g;
+    a1.bias_ld = 2 * h->Ipad;
+    a1.gamma = h->cfg.era_gamma;
+    a1.status = h->status;
+    if ((rc = check(launch_tc_gemm(true, map_x, h->map_wgu, a1, p.max_tiles, h->num_sms, s),
+                    "gemm1")) != VMOE_OK)
+      return rc;
+    mark();
+    TcGemmArgs a2{};
+    a2.num_m_tiles = ntiles;
+    a2.tile_expert = tiles;
+    a2.n_tiles = static_cast<int>(h->Hpad / kDownTileN);
+    a2.k_blocks = static_cast<int>(h->Ipad / 64);
+    a2.b_rows_per_expert = static_cast<int>(h->Hpad);
+    a2.out = yb;
+    a2.ldo = h->Hpad;
+    a2.bias = h->b_d;
+    a2.bias_ld = h->Hpad;
+    a2.gamma = 0.f;
+    a2.status = h->status;
+    if ((rc = check(launch_tc_gemm(false, map_h, h->map_wd, a2, p.max_tiles, h->num_sms, s),
+                    "gemm2")) != VMOE_OK)
+      return rc;
+  }
+  mark();
+  if ((rc = check(launch_combine(h->dtype, yb, h->Hpad, idx, tw, slot, T, static_cast<int>(H),
+                                 static_cast<int>(K), out, s),
+                  "combine")) != VMOE_OK)
+    return rc;
+  mark();
+  if (prof) ++h->prof_count;
+  return VMOE_OK;
+}
+
+int vmoe_device_status(vmoe_handle* h, int32_t* code, void* stream) {
+  if (!h || !code) return VMOE_ERR_INVALID_ARG;
+  DeviceGuard g(h->device);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int v = 0;
+  cudaError_t e = cudaMemcpyAsync(&v, h->status, sizeof(int), cudaMemcpyDeviceToHost, s);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  if (e == cudaSuccess) e = cudaMemsetAsync(h->status, 0, sizeof(int), s);
+  if (e != cudaSuccess) return cuda_fail(h, e, "status read");
+  *code = v;
+  if (v == 0) return VMOE_OK;
+  if (v >= 0x101 && v <= 0x1FF)
+    return fail(h, VMOE_ERR_TIMEOUT, "a bounded device wait gave up (status 0x%x)", v);
+  return fail(h, VMOE_ERR_DEVICE_STATUS, "device status 0x%x", v);
+}
+
+int vmoe_set_profiling(vmoe_handle* h, int n) {
+  if (!h || n < 0) return VMOE_ERR_INVALID_ARG;
+  DeviceGuard g(h->device);
+  for (cudaEvent_t ev : h->prof_ev) cudaEventDestroy(ev);
+  h->prof_ev.clear();
+  h->prof_slots = 0;
+  h->prof_count = 0;
+  if (n == 0) return VMOE_OK;
+  h->prof_ev.resize(static_cast<size_t>(n) * (kStages + 1));
+  for (auto& ev : h->prof_ev) {
+    cudaError_t e = cudaEventCreate(&ev);
+    if (e != cudaSuccess) {
+      ev = nullptr;
+      return cuda_fail(h, e, "profiling events");
+    }
+  }
+  h->prof_slots = n;
+  return VMOE_OK;
+}
+
+int vmoe_stage_times(vmoe_handle* h, float* ms, int n, int* n_out, int* forwards) {
+  if (!h || !ms || n < 0) return VMOE_ERR_INVALID_ARG;
+  if (h->prof_count == 0) return fail(h, VMOE_ERR_NOT_READY, "no profiled forward recorded");
+  DeviceGuard g(h->device);
+  const int m = n < kStages ? n : kStages;
+  for (int i = 0; i < m; ++i) ms[i] = 0.f;
+  for (int f = 0; f < h->prof_count; ++f) {
+    cudaEvent_t* ev = &h->prof_ev[static_cast<size_t>(f) * (kStages + 1)];
+    cudaError_t e = cudaEventSynchronize(ev[kStages]);
+    if (e != cudaSuccess) return cuda_fail(h, e, "stage timing");
+    for (int i = 0; i < m; ++i) {
+      float t = 0.f;
+      e = cudaEventElapsedTime(&t, ev[i], ev[i + 1]);
+      if (e != cudaSuccess) return cuda_fail(h, e, "stage timing");
+      ms[i] += t;
+    }
+  }
+  for (int i = 0; i < m; ++i) ms[i] /= static_cast<float>(h->prof_count);
+  if (n_out) *n_out = m;
+  if (forwards) *forwards = h->prof_count;
+  h->prof_count = 0;
+  return VMOE_OK;
+}
+
+int vmoe_last_launch_count(const vmoe_handle* h) { return h ? h->last_launches : 0; }
+
+}  // extern "C"

@@ -1,0 +1,224 @@
+"""Drop-in MoE layer for VelvetOptimizer's ``MoELayer`` (python/vesper/model.py:305-385).
+
+``MoELayer(config)`` has the reference's submodule names, so its ``state_dict`` keys are
+the reference's (``router.*``, ``experts.{e}.{gate_proj,up_proj}.{base,lora_down,lora_up}.*``,
+``experts.{e}.{gate_proj,up_proj}.proj_a``, ``experts.{e}.down_proj.*``) and a reference
+checkpoint loads unchanged.  ``forward(x[B,S,H]) -> (out[B,S,H], aux_loss[])`` keeps the
+reference's return signature so ``TransformerLayer`` (model.py:419-420) does not change;
+``return_router_logits=True`` also returns the router logits.
+
+The forward runs through ``torch.ops.vesper_moe.forward``, a custom op whose body calls
+the C ABI (include/vesper_moe.h) on torch's current stream.  There is no CPU or eager
+fallback: CPU tensors, a missing library or an unsupported dtype raise.
+"""
+from __future__ import annotations
+
+import ctypes
+import itertools
+import math
+
+import torch
+import torch.nn as nn
+
+from . import _lib
+from .config import MoEConfig
+
+_DTYPES = {torch.float32: _lib.VMOE_F32, torch.bfloat16: _lib.VMOE_BF16}
+
+
+class FlyLoRALinear(nn.Module):
+    """Parameter container with the reference FlyLoRALinear's names (model.py:83-121).
+
+    ``base`` [out,in], ``lora_down`` [r,in], ``lora_up`` [out,r] (zero-initialised, so the
+    branch starts switched off, model.py:120) and the unused ``proj_a`` buffer [in,r]
+    (model.py:107-113).  Its math runs inside the fused op, folded into ``base``.
+    """
+
+    def __init__(self, in_features: int, out_features: int, rank: int = 16,
+                 alpha: float = 32.0, sparsity: float = 0.25):
+        super().__init__()
+        self.in_features, self.out_features, self.rank = in_features, out_features, rank
+        self.scaling = alpha / rank
+        self.base = nn.Linear(in_features, out_features)
+        proj = torch.randn(in_features, rank)
+        proj = proj * (torch.rand_like(proj) > sparsity).float()
+        self.register_buffer("proj_a", proj / proj.norm(dim=0, keepdim=True).clamp(min=1e-8))
+        self.lora_down = nn.Linear(in_features, rank, bias=True)
+        self.lora_up = nn.Linear(rank, out_features, bias=True)
+        nn.init.kaiming_uniform_(self.lora_down.weight, a=math.sqrt(5))
+        nn.init.zeros_(self.lora_up.weight)
+
+    def forward(self, x):  # pragma: no cover - the fused op is the only compute path
+        raise RuntimeError("FlyLoRALinear is evaluated inside the fused MoE op")
+
+
+class ExpertFFN(nn.Module):
+    """Parameter container with the reference ExpertFFN's names (model.py:277-293)."""
+
+    def __init__(self, cfg: MoEConfig):
+        super().__init__()
+        args = (cfg.hidden_size, cfg.intermediate_size, cfg.flylora_rank, cfg.flylora_alpha,
+                cfg.flylora_sparsity)
+        self.gate_proj = FlyLoRALinear(*args)
+        self.up_proj = FlyLoRALinear(*args)
+        self.down_proj = nn.Linear(cfg.intermediate_size, cfg.hidden_size)
+
+    def forward(self, x):  # pragma: no cover
+        raise RuntimeError("ExpertFFN is evaluated inside the fused MoE op")
+
+
+# ---------------------------------------------------------------------------------------
+# handle registry + custom op
+# ---------------------------------------------------------------------------------------
+_HANDLES: dict[int, "_Packed"] = {}
+_ids = itertools.count(1)
+
+
+class _Packed:
+    """A C-ABI handle with packed weights plus a growable workspace."""
+
+    def __init__(self, handle: _lib.Handle, key):
+        self.handle = handle
+        self.key = key
+        self.ws: torch.Tensor | None = None
+        self.id = next(_ids)
+        _HANDLES[self.id] = self
+
+    def workspace(self, tokens: int, device) -> torch.Tensor:
+        need = self.handle.workspace_size(tokens)
+        if self.ws is None or self.ws.numel() < need:
+            self.ws = torch.empty(max(need, 256), dtype=torch.uint8, device=device)
+        return self.ws
+
+    def release(self):
+        _HANDLES.pop(self.id, None)
+        self.handle.close()
+
+
+def _ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+@torch.library.custom_op("vesper_moe::forward", mutates_args=(), device_types="cuda")
+def moe_forward_op(x: torch.Tensor, handle_id: int, want_logits: bool) -> tuple[
+        torch.Tensor, torch.Tensor, torch.Tensor]:
+    """out[T,H], router_logits[T,E] (empty unless want_logits), aux[] for x[T,H]."""
+    packed = _HANDLES[handle_id]
+    h = packed.handle
+    T, H = x.shape
+    E = h.cfg.num_experts
+    x = x.contiguous()
+    out = torch.empty_like(x)
+    aux = torch.empty((), dtype=torch.float32, device=x.device)
+    logits = torch.empty((T, E) if want_logits else (0, E), dtype=torch.float32, device=x.device)
+    ws = packed.workspace(T, x.device)
+    stream = torch.cuda.current_stream(x.device).cuda_stream
+    h.forward(x.data_ptr(), T, out.data_ptr(), logits.data_ptr() if want_logits else None,
+              None, None, None, aux.data_ptr(), ws.data_ptr(), ws.numel(), stream)
+    return out, logits, aux
+
+
+@moe_forward_op.register_fake
+def _(x, handle_id, want_logits):
+    T, _ = x.shape
+    E = _HANDLES[handle_id].handle.cfg.num_experts if handle_id in _HANDLES else 1
+    return (torch.empty_like(x), x.new_empty((T, E) if want_logits else (0, E), dtype=torch.float32),
+            x.new_empty((), dtype=torch.float32))
+
+
+# ---------------------------------------------------------------------------------------
+# the layer
+# ---------------------------------------------------------------------------------------
+class MoELayer(nn.Module):
+    """Mixture of Experts with top-K routing and the Switch load-balancing loss.
+
+    Same constructor argument (a VesperConfig-like object), parameters, state_dict keys
+    and ``forward`` contract as the reference ``MoELayer``.
+    """
+
+    def __init__(self, config):
+        super().__init__()
+        cfg = MoEConfig.from_any(config)
+        cfg.validate()
+        self.config = cfg
+        self.num_experts = cfg.moe_num_experts
+        self.top_k = cfg.moe_top_k
+        self.aux_loss_weight = cfg.moe_aux_loss_weight
+        self.router = nn.Linear(cfg.hidden_size, cfg.moe_num_experts)
+        self.experts = nn.ModuleList([ExpertFFN(cfg) for _ in range(cfg.moe_num_experts)])
+        self._packed: dict[tuple, _Packed] = {}
+
+    # -- weights ---------------------------------------------------------------------
+    def _weight_key(self):
+        return tuple((p.data_ptr(), p._version) for p in self.parameters())
+
+    def stacked_weights(self, dtype: torch.dtype) -> dict[str, torch.Tensor]:
+        """The per-expert parameters stacked on a leading expert axis, in ``dtype``."""
+        ex = self.experts
+
+        def st(get):
+            return torch.stack([get(e).detach() for e in ex]).to(dtype).contiguous()
+
+        w = {"router_w": self.router.weight.detach().to(dtype).contiguous(),
+             "router_b": self.router.bias.detach().to(dtype).contiguous()}
+        for name, attr in (("gate", "gate_proj"), ("up", "up_proj")):
+            w[f"{name}_w"] = st(lambda e: getattr(e, attr).base.weight)
+            w[f"{name}_b"] = st(lambda e: getattr(e, attr).base.bias)
+            w[f"{name}_lora_down_w"] = st(lambda e: getattr(e, attr).lora_down.weight)
+            w[f"{name}_lora_down_b"] = st(lambda e: getattr(e, attr).lora_down.bias)
+            w[f"{name}_lora_up_w"] = st(lambda e: getattr(e, attr).lora_up.weight)
+            w[f"{name}_lora_up_b"] = st(lambda e: getattr(e, attr).lora_up.bias)
+        w["down_w"] = st(lambda e: e.down_proj.weight)
+        w["down_b"] = st(lambda e: e.down_proj.bias)
+        return w
+
+    def _abi_config(self, dtype: torch.dtype) -> _lib.VmoeConfig:
+        c = self.config
+        return _lib.VmoeConfig(hidden=c.hidden_size, inter=c.intermediate_size,
+                               num_experts=c.moe_num_experts, top_k=c.moe_top_k,
+                               lora_rank=c.flylora_rank, lora_scaling=c.lora_scaling,
+                               era_gamma=c.era_gamma, dtype=_DTYPES[dtype],
+                               capacity=c.moe_capacity)
+
+    def packed_for(self, device: torch.device, dtype: torch.dtype) -> _Packed:
+        """The handle for (device, dtype), repacking if any parameter changed."""
+        if dtype not in _DTYPES:
+            raise TypeError(f"vesper_moe supports float32 and bfloat16 inputs, not {dtype}")
+        if device.type != "cuda":
+            raise RuntimeError("velvetoptimizer_b200.MoELayer runs on CUDA tensors only "
+                               "(there is no CPU path)")
+        dev = device.index if device.index is not None else torch.cuda.current_device()
+        slot = (dev, dtype)
+        key = self._weight_key()
+        packed = self._packed.get(slot)
+        if packed is not None and packed.key == key:
+            return packed
+        if packed is None:
+            packed = _Packed(_lib.Handle(self._abi_config(dtype), dev), key)
+            self._packed[slot] = packed
+        with torch.cuda.device(dev):
+            w = {k: v.to(device) for k, v in self.stacked_weights(dtype).items()}
+            vw = _lib.VmoeWeights(**{k: ctypes.c_void_p(v.data_ptr()) for k, v in w.items()})
+            stream = torch.cuda.current_stream(dev)
+            packed.handle.set_weights(vw, stream.cuda_stream)
+            # the stacked temporaries must outlive the enqueued copies
+            stream.synchronize()
+        packed.key = key
+        return packed
+
+    # -- forward ---------------------------------------------------------------------
+    def forward(self, x: torch.Tensor, return_router_logits: bool = False):
+        """(out[B,S,H], aux_loss[]) — or (out, aux_loss, router_logits[B,S,E])."""
+        B, S, H = x.shape
+        packed = self.packed_for(x.device, x.dtype)
+        out, logits, aux = torch.ops.vesper_moe.forward(
+            x.reshape(B * S, H), packed.id, bool(return_router_logits))
+        out = out.reshape(B, S, H)
+        if return_router_logits:
+            return out, aux, logits.reshape(B, S, self.num_experts)
+        return out, aux
+
+    def close(self) -> None:
+        for p in self._packed.values():
+            p.release()
+        self._packed.clear()
