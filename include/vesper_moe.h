@@ -112,6 +112,24 @@ VMOE_API int vmoe_set_weights(vmoe_handle* h, const vmoe_weights* w, void* strea
 /* Bytes of device workspace vmoe_forward needs for `tokens` tokens (256-byte aligned). */
 VMOE_API int vmoe_workspace_size(const vmoe_handle* h, int64_t tokens, size_t* bytes);
 
+/* Allocation-free forward.  This entry point has no counterpart in the reference.  It is
+ * for callers that cannot allocate device memory when they run the layer (a serving thread
+ * under a fixed memory budget, a real-time loop that must not stall on an allocator, an
+ * engine without a caching allocator): it behaves exactly like vmoe_forward but takes its
+ * scratch from one static device array of VMOE_NO_ALLOC_WORKSPACE_BYTES that every GPU
+ * loading this library reserves until the process exits.  It calls no allocator.
+ *  - tokens whose vmoe_workspace_size exceeds that size are rejected with
+ *    VMOE_ERR_WORKSPACE (e.g. 64 decode tokens at H 2048, I 8192, E 8, K 2 need
+ *    about 27 MiB);
+ *  - the first call on each device looks up the array's device address
+ *    (cudaGetSymbolAddress) -- make that first call before any stream capture;
+ *  - all calls share the array: calls whose GPU work overlaps race and corrupt each
+ *    other; serialise them.  Nothing needs clearing between calls. */
+#define VMOE_NO_ALLOC_WORKSPACE_BYTES (64ull << 20)
+VMOE_API int vmoe_forward_no_alloc(vmoe_handle* h, const void* x, int64_t tokens, void* out,
+                                   float* router_logits, int32_t* topk_idx, float* topk_w,
+                                   int32_t* expert_counts, float* aux_loss, void* stream);
+
 /* Where vmoe_forward keeps its intermediates inside the workspace (byte offsets), so a
  * caller can inspect the dispatch: for token t and slot k, slot_of[t*K + k] is the row of
  * the expert-major permuted buffer that holds x[t] (-1 when capacity dropped it); expert

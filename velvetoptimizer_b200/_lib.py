@@ -24,10 +24,13 @@ VMOE_ERR_WORKSPACE = 8
 VMOE_F32 = 0
 VMOE_BF16 = 1
 
+# size of the static scratch array behind vmoe_forward_no_alloc
+VMOE_NO_ALLOC_WORKSPACE_BYTES = 64 << 20
+
 # every symbol include/vesper_moe.h declares
 EXPORTED = (
     "vmoe_create", "vmoe_destroy", "vmoe_set_weights", "vmoe_workspace_size",
-    "vmoe_workspace_layout", "vmoe_forward",
+    "vmoe_workspace_layout", "vmoe_forward", "vmoe_forward_no_alloc",
     "vmoe_device_status", "vmoe_set_profiling", "vmoe_stage_times", "vmoe_stage_name",
     "vmoe_last_launch_count", "vmoe_last_error", "vmoe_status_string", "vmoe_abi_version",
 )
@@ -94,6 +97,9 @@ def load() -> ctypes.CDLL:
     lib.vmoe_forward.argtypes = [H, c_void_p, c_int64, c_void_p, c_void_p, c_void_p, c_void_p,
                                  c_void_p, c_void_p, c_void_p, c_size_t, c_void_p]
     lib.vmoe_forward.restype = c_int
+    lib.vmoe_forward_no_alloc.argtypes = [H, c_void_p, c_int64, c_void_p, c_void_p, c_void_p,
+                                          c_void_p, c_void_p, c_void_p, c_void_p]
+    lib.vmoe_forward_no_alloc.restype = c_int
     lib.vmoe_device_status.argtypes = [H, POINTER(c_int32), c_void_p]
     lib.vmoe_device_status.restype = c_int
     lib.vmoe_set_profiling.argtypes = [H, c_int]

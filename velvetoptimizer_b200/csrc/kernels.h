@@ -115,3 +115,10 @@ struct PackBiasArgs {
 cudaError_t launch_pack_bias(const PackBiasArgs& a, cudaStream_t s);
 
 }  // namespace vmoe
+
+// Internal accessors of the opaque handle (defined in vesper_moe.cu).
+struct vmoe_handle;
+namespace vmoe {
+int handle_device(const vmoe_handle* h);
+int set_handle_error(vmoe_handle* h, int code, const char* msg);
+}  // namespace vmoe

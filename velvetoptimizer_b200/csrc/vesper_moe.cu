@@ -198,6 +198,11 @@ int alloc(vmoe_handle* h, T** p, size_t bytes, const char* what) {
 
 }  // namespace
 
+namespace vmoe {
+int handle_device(const vmoe_handle* h) { return h ? h->device : -1; }
+int set_handle_error(vmoe_handle* h, int code, const char* msg) { return fail(h, code, "%s", msg); }
+}  // namespace vmoe
+
 extern "C" {
 
 int vmoe_abi_version(void) { return VMOE_ABI_VERSION; }
