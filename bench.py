@@ -161,6 +161,27 @@ def build_layer(w, device, seed=0):
     return layer
 
 
+def global_weights(w, device, seed=0):
+    """Stacked weights of all E experts (bf16), drawn like build_layer's, on `device`."""
+    import torch
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+    E, H, I, r = w["experts"], w["hidden"], w["inter"], 16
+    n = lambda *s: (torch.randn(*s, generator=g, device=device) * 0.02).to(torch.bfloat16)  # noqa: E731
+    z = lambda *s: torch.zeros(*s, dtype=torch.bfloat16, device=device)  # noqa: E731
+    out = {"router_w": n(E, H), "router_b": z(E), "down_w": n(E, H, I), "down_b": z(E, H)}
+    for p in ("gate", "up"):
+        out[f"{p}_w"], out[f"{p}_b"] = n(E, I, H), z(E, I)
+        out[f"{p}_lora_down_w"], out[f"{p}_lora_down_b"] = n(E, r, H), z(E, r)
+        out[f"{p}_lora_up_w"] = n(E, I, r) if w.get("lora_on") else z(E, I, r)
+        out[f"{p}_lora_up_b"] = z(E, I)
+    if w.get("zipf_alpha"):
+        ranks = torch.arange(1, E + 1, dtype=torch.float64)
+        pmf = ranks ** (-w["zipf_alpha"])
+        out["router_b"] = torch.log(pmf / pmf.sum()).to(device=device, dtype=torch.bfloat16)
+    return out
+
+
 def cpu_baseline(layer, x_dev, w, seconds):
     """Time the oracle (CPU restatement of the reference, numpy fp32) on a token sample."""
     import numpy as np
@@ -205,12 +226,52 @@ def run_ours(args, rank, world, local_rank):
     dev = torch.device("cuda", local_rank)
     w = dict(WORKLOADS[args.workload])
     T, H, E, K = w["tokens"], w["hidden"], w["experts"], w["top_k"]
-    layer = build_layer(w, dev, seed=0)
     g = torch.Generator(device=dev)
     g.manual_seed(1000 + rank)
     x = torch.randn(T, H, generator=g, device=dev).to(torch.bfloat16).reshape(
         w["batch"], T // w["batch"], H)
-    packed = layer.packed_for(dev, torch.bfloat16)
+
+    if world == 1:
+        # the drop-in module (python/vesper/model.py MoELayer interface) on one GPU
+        layer = build_layer(w, dev, seed=0)
+        packed = layer.packed_for(dev, torch.bfloat16)
+
+        def fwd(inp):
+            return layer(inp)
+
+        def start_profile():
+            packed.handle.set_profiling(args.steps)
+
+        def read_profile():
+            return packed.handle.stage_times()
+
+        def launches_of_last():
+            return packed.handle.last_launch_count()
+    else:
+        # experts sharded over the ranks, rows exchanged with NCCL all-to-all-v
+        from velvetoptimizer_b200 import MoEConfig
+        from velvetoptimizer_b200.ep import ExpertParallelMoE
+        cfg = MoEConfig(hidden_size=H, intermediate_size=w["inter"], moe_num_experts=E,
+                        moe_top_k=K, flylora_rank=16, flylora_alpha=32.0, era_gamma=0.1)
+        gw = global_weights(w, dev, seed=0)
+        layer = ExpertParallelMoE(cfg, gw, dev, torch.bfloat16)
+        del gw
+        torch.cuda.empty_cache()
+
+        def fwd(inp):
+            out, aux = layer(inp.reshape(-1, H))
+            return out.reshape(inp.shape), aux
+
+        def start_profile():
+            layer.stage_events = []
+
+        def read_profile():
+            recs = layer.stage_events
+            layer.stage_events = None
+            return ExpertParallelMoE.stage_ms(recs), len(recs)
+
+        def launches_of_last():
+            return layer.launches
 
     def barrier():
         if world > 1:
@@ -218,7 +279,7 @@ def run_ours(args, rank, world, local_rank):
 
     # warm-up
     for _ in range(args.warmup):
-        out, aux = layer(x)
+        out, aux = fwd(x)
     torch.cuda.synchronize()
 
     # ---- device-resident timed region ----
@@ -226,7 +287,7 @@ def run_ours(args, rank, world, local_rank):
     gpu_id = str(getattr(props, "uuid", "") or local_rank)
     if gpu_id and not gpu_id.startswith("GPU-") and len(gpu_id) > 8:
         gpu_id = "GPU-" + gpu_id
-    packed.handle.set_profiling(args.steps)
+    start_profile()
     stream = torch.cuda.current_stream(dev)
     t_start = torch.cuda.Event(enable_timing=True)
     t_end = torch.cuda.Event(enable_timing=True)
@@ -237,16 +298,15 @@ def run_ours(args, rank, world, local_rank):
     launches = 0
     t_start.record(stream)
     for _ in range(args.steps):
-        out, aux = layer(x)
-        launches += packed.handle.last_launch_count()
+        out, aux = fwd(x)
+        launches += launches_of_last()
     t_end.record(stream)
     t_end.synchronize()
     barrier()
     torch.cuda.synchronize()
     clocks = sampler.stop()
     ms = t_start.elapsed_time(t_end) / args.steps
-    stages, nprof = packed.handle.stage_times()
-    packed.handle.set_profiling(0)
+    stages, nprof = read_profile()
     ms_t = torch.tensor([ms], device=dev)
     if world > 1:
         dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
@@ -260,7 +320,7 @@ def run_ours(args, rank, world, local_rank):
     aux_host = torch.empty((), dtype=torch.float32, pin_memory=True)
     for _ in range(2):
         xd = x_host.to(dev, non_blocking=True)
-        o, a = layer(xd)
+        o, a = fwd(xd)
         out_host.copy_(o, non_blocking=True)
         aux_host.copy_(a, non_blocking=True)
     barrier()
@@ -270,7 +330,7 @@ def run_ours(args, rank, world, local_rank):
     e0.record(stream)
     for _ in range(args.steps):
         xd = x_host.to(dev, non_blocking=True)
-        o, a = layer(xd)
+        o, a = fwd(xd)
         out_host.copy_(o, non_blocking=True)
         aux_host.copy_(a, non_blocking=True)
     e1.record(stream)
@@ -286,8 +346,18 @@ def run_ours(args, rank, world, local_rank):
 
     pk = peaks()
     alg = algorithmic(w)
-    g1 = stages.get("gemm1_gate_up_era", float("nan"))
-    achieved = alg["gemm1_flop"] / (g1 * 1e-3) / 1e12
+    if world == 1:
+        g1 = stages.get("gemm1_gate_up_era", float("nan"))
+        achieved = alg["gemm1_flop"] / (g1 * 1e-3) / 1e12
+        roof_kernel = "gemm1_gate_up_era (tcgen05 grouped GEMM, fused ERA*up)"
+        roof_flop = alg["gemm1_flop"]
+    else:
+        # both expert GEMMs of this rank's local experts over the rows it received
+        rows = layer.last_plan.recv_counts.sum()
+        g1 = stages.get("experts_gemm1_gemm2", float("nan"))
+        roof_flop = 6.0 * float(rows) * H * w["inter"]
+        achieved = roof_flop / (g1 * 1e-3) / 1e12
+        roof_kernel = "gemm1_gate_up_era + gemm2_down on rank 0's local experts"
     stage_report = {}
     for name, t_ms in stages.items():
         rec = {"ms": round(t_ms, 4), "share": round(t_ms / max(sum(stages.values()), 1e-9), 4)}
@@ -318,17 +388,20 @@ def run_ours(args, rank, world, local_rank):
         "config": {"workload": f"{args.workload}: MoE FFN layer fwd, {T} tokens/GPU, d_model {H}, "
                                f"expert d_ff {w['inter']}, {E} experts, top-{K}",
                    "tokens_per_gpu": T, "hidden": H, "inter": w["inter"], "experts": E,
-                   "top_k": K, "parallelism": "single GPU" if world == 1 else f"replicas x{world}",
+                   "top_k": K,
+                   "parallelism": "single GPU" if world == 1 else
+                   f"expert parallel ep{world}: {E // world} experts/GPU, NCCL all-to-all-v",
                    "l2": "inputs larger than L2 (x 512 MiB, weights 3.2 GiB); no flush"},
         "e2e": {"value": round(e2e_value, 1), "unit": "tokens/s",
                 "h2d_bytes_per_step": int(x.numel() * x.element_size()),
                 "d2h_bytes_per_step": int(x.numel() * x.element_size() + 4),
-                "api": "velvetoptimizer_b200.MoELayer.forward"},
-        "roofline": {"kernel": "gemm1_gate_up_era (tcgen05 grouped GEMM, fused ERA*up)",
+                "api": "velvetoptimizer_b200.MoELayer.forward" if world == 1 else
+                       "velvetoptimizer_b200.ep.ExpertParallelMoE.forward"},
+        "roofline": {"kernel": roof_kernel,
                      "bound": "tensor", "achieved": round(achieved, 1),
                      "peak": pk["bf16_tflops"], "peak_source": pk["source"] + " bf16 burst",
                      "unit": "TFLOP/s", "frac": round(achieved / pk["bf16_tflops"], 4),
-                     "traffic": None, "flop_per_launch": alg["gemm1_flop"],
+                     "traffic": None, "flop_per_launch": roof_flop,
                      "avg_launch_ms": round(g1, 4), "launches_timed": nprof},
         "stages": stage_report,
         "gpu_launches": launches,

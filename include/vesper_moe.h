@@ -167,6 +167,43 @@ VMOE_API int vmoe_forward(vmoe_handle* h, const void* x, int64_t tokens, void* o
                  int32_t* expert_counts, float* aux_loss,
                  void* workspace, size_t workspace_bytes, void* stream);
 
+/* ---- Expert parallelism -------------------------------------------------------------
+ * The reference has no distributed code (no collective anywhere in the project); the
+ * path's specification partitions this layer expert-parallel: with G ranks, rank r holds
+ * experts [r*E/G, (r+1)*E/G) and routes its own tokens.  One forward is three calls with
+ * the caller's row exchange (e.g. NCCL all-to-all-v over NVLink) between them:
+ *   1. vmoe_ep_route: router over all E experts; each routed (token, k) row of x is
+ *      written to send_rows [T*K, H] in expert-major order, unpadded -- so the rows for
+ *      destination rank d are contiguous -- and expert_counts[E] (device) says how many;
+ *   2. the caller exchanges counts and rows: rank r gathers, for each of its local experts
+ *      e, the rows from every source rank into one segment of recv_rows, segments padded
+ *      to 128-row tiles; tile_expert[t] = local expert of tile t, *num_tiles = tiles used;
+ *   3. vmoe_ep_experts: the local experts' gate|up GEMM with ERA * up and the down GEMM,
+ *      recv_rows -> out_rows (same layout);
+ *   4. the caller returns each row to its source rank, into back_rows at the position it
+ *      had in send_rows;
+ *   5. vmoe_ep_combine: out[t] = sum over the token's K rows, ascending expert id, of
+ *      w * row, in fp32 -- the same order and arithmetic as vmoe_forward, so each token's
+ *      output is bit-identical to the single-GPU forward.
+ * Workspaces: vmoe_ep_route and vmoe_ep_combine share one workspace of
+ * vmoe_ep_workspace_size(h, tokens, 0) bytes (it carries the routing between them);
+ * vmoe_ep_experts takes a different one of vmoe_ep_workspace_size(h, 0, recv_rows_cap)
+ * bytes (the received row count is known only after routing).  The aux loss is that of
+ * this rank's tokens.  bf16 needs H % 256 == 0; capacity must be 0. */
+VMOE_API int vmoe_create_ep(const vmoe_config* cfg, int device, int ep_size, int ep_rank,
+                            vmoe_handle** out);
+VMOE_API int vmoe_ep_workspace_size(const vmoe_handle* h, int64_t tokens, int64_t recv_rows_cap,
+                                    size_t* bytes);
+VMOE_API int vmoe_ep_route(vmoe_handle* h, const void* x, int64_t tokens, void* send_rows,
+                           int32_t* expert_counts, float* router_logits, float* aux_loss,
+                           void* workspace, size_t workspace_bytes, void* stream);
+VMOE_API int vmoe_ep_experts(vmoe_handle* h, const void* recv_rows, int64_t recv_rows_cap,
+                             const int32_t* tile_expert, const int32_t* num_tiles,
+                             void* out_rows, void* workspace, size_t workspace_bytes,
+                             void* stream);
+VMOE_API int vmoe_ep_combine(vmoe_handle* h, const void* back_rows, int64_t tokens, void* out,
+                             void* workspace, size_t workspace_bytes, void* stream);
+
 /* Read (and clear) the device status word the kernels write when a bounded wait gives
  * up or an index check fails.  Synchronises `stream`.  *code = 0 when all is well. */
 VMOE_API int vmoe_device_status(vmoe_handle* h, int32_t* code, void* stream);

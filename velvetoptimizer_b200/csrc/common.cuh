@@ -20,6 +20,7 @@ enum DeviceStatus : int {
   kStatusTimeoutDrain = 0x104,
   kStatusBadExpert = 0x201,
   kStatusBadSlot = 0x202,
+  kStatusBadTileCount = 0x203,
 };
 
 // Upper bound on any single spin-wait inside a kernel (ns of %globaltimer).

@@ -70,15 +70,16 @@ scan_blocks_kernel(const int* __restrict__ hist, const float* __restrict__ psum,
 // one block of 1024 threads (E <= 1024)
 __global__ void __launch_bounds__(1024)
 plan_kernel(const int* __restrict__ counts, const float* __restrict__ psum_tot, int64_t T, int E,
-            int K, int64_t capacity, int* __restrict__ offs, int* __restrict__ tile_expert,
-            int* __restrict__ num_tiles, float* __restrict__ aux, int32_t* __restrict__ counts_out) {
+            int K, int64_t capacity, int row_align, int* __restrict__ offs,
+            int* __restrict__ tile_expert, int* __restrict__ num_tiles, float* __restrict__ aux,
+            int32_t* __restrict__ counts_out) {
   __shared__ int pad_s[1024];
   __shared__ int off_s[1025];
   const int tid = threadIdx.x;
   if (tid < E) {
     int kept = counts[tid];
     if (capacity > 0 && kept > capacity) kept = static_cast<int>(capacity);
-    pad_s[tid] = (kept + kTileM - 1) / kTileM * kTileM;
+    pad_s[tid] = (kept + row_align - 1) / row_align * row_align;
     if (counts_out) counts_out[tid] = counts[tid];
   }
   __syncthreads();
@@ -86,7 +87,7 @@ plan_kernel(const int* __restrict__ counts, const float* __restrict__ psum_tot, 
     int run = 0;
     for (int e = 0; e < E; ++e) { off_s[e] = run; run += pad_s[e]; }
     off_s[E] = run;
-    *num_tiles = run / kTileM;
+    if (num_tiles) *num_tiles = run / kTileM;
     // Switch load-balancing loss (model.py:366-385), fixed summation order
     const float inv_tk = 1.0f / static_cast<float>(T * K);
     const float inv_t = 1.0f / static_cast<float>(T);
@@ -100,7 +101,7 @@ plan_kernel(const int* __restrict__ counts, const float* __restrict__ psum_tot, 
   }
   __syncthreads();
   for (int e = tid; e <= E; e += blockDim.x) offs[e] = off_s[e];
-  if (tid < E) {
+  if (tile_expert && tid < E) {
     const int t0 = off_s[tid] / kTileM, nt = pad_s[tid] / kTileM;
     for (int j = 0; j < nt; ++j) tile_expert[t0 + j] = tid;
   }
@@ -230,10 +231,10 @@ cudaError_t launch_scan_blocks(const int* hist, const float* psum, int nblk, int
 }
 
 cudaError_t launch_plan(const int* counts, const float* psum_tot, int64_t T, int E, int K,
-                        int64_t capacity, int* offs, int* tile_expert, int* num_tiles,
-                        float* aux, int32_t* counts_out, cudaStream_t s) {
-  plan_kernel<<<1, 1024, 0, s>>>(counts, psum_tot, T, E, K, capacity, offs, tile_expert,
-                                 num_tiles, aux, counts_out);
+                        int64_t capacity, int row_align, int* offs, int* tile_expert,
+                        int* num_tiles, float* aux, int32_t* counts_out, cudaStream_t s) {
+  plan_kernel<<<1, 1024, 0, s>>>(counts, psum_tot, T, E, K, capacity, row_align, offs,
+                                 tile_expert, num_tiles, aux, counts_out);
   return cudaGetLastError();
 }
 

@@ -19,10 +19,15 @@ __global__ void __launch_bounds__(256)
 simt_gemm_kernel(const float* __restrict__ a, int64_t lda, const float* __restrict__ w0,
                  const float* __restrict__ w1, const float* __restrict__ b0,
                  const float* __restrict__ b1, float* __restrict__ c, int64_t ldc, int N, int K,
-                 float gamma, const int* __restrict__ tile_expert, const int* __restrict__ num_tiles) {
+                 float gamma, const int* __restrict__ tile_expert, const int* __restrict__ num_tiles,
+                 int num_experts, int* status) {
   const int mt = blockIdx.y / (kTileM / BM);
   if (mt >= *num_tiles) return;
-  const int e = tile_expert[mt];
+  int e = tile_expert[mt];
+  if (static_cast<unsigned>(e) >= static_cast<unsigned>(num_experts)) {
+    if (threadIdx.x == 0) report(status, kStatusBadExpert);
+    return;
+  }
   const int64_t row0 = static_cast<int64_t>(blockIdx.y) * BM;
   const int n0 = blockIdx.x * BN;
   const float* wa = w0 + static_cast<int64_t>(e) * N * K;
@@ -102,19 +107,20 @@ simt_gemm_kernel(const float* __restrict__ a, int64_t lda, const float* __restri
 cudaError_t launch_simt_gemm1(const float* a, int64_t lda, const float* wg, const float* wu,
                               const float* bg, const float* bu, float* h, int64_t ldh, int N,
                               int K, float gamma, const int* tile_expert, const int* num_tiles,
-                              int64_t max_tiles, cudaStream_t s) {
+                              int64_t max_tiles, int num_experts, int* status, cudaStream_t s) {
   dim3 grid((N + BN - 1) / BN, static_cast<unsigned>(max_tiles * (kTileM / BM)));
   simt_gemm_kernel<true><<<grid, 256, 0, s>>>(a, lda, wg, wu, bg, bu, h, ldh, N, K, gamma,
-                                              tile_expert, num_tiles);
+                                              tile_expert, num_tiles, num_experts, status);
   return cudaGetLastError();
 }
 
 cudaError_t launch_simt_gemm2(const float* a, int64_t lda, const float* wd, const float* bd,
                               float* y, int64_t ldy, int N, int K, const int* tile_expert,
-                              const int* num_tiles, int64_t max_tiles, cudaStream_t s) {
+                              const int* num_tiles, int64_t max_tiles, int num_experts,
+                              int* status, cudaStream_t s) {
   dim3 grid((N + BN - 1) / BN, static_cast<unsigned>(max_tiles * (kTileM / BM)));
   simt_gemm_kernel<false><<<grid, 256, 0, s>>>(a, lda, wd, nullptr, bd, nullptr, y, ldy, N, K,
-                                               0.f, tile_expert, num_tiles);
+                                               0.f, tile_expert, num_tiles, num_experts, status);
   return cudaGetLastError();
 }
 

@@ -57,6 +57,14 @@ __device__ __forceinline__ void set_abort(TcShared* sh, int* status, int code) {
   report(status, code);
 }
 
+// Expert of M tile m, clamped into range (a bad map only produces a status code).
+__device__ __forceinline__ int expert_of(const TcGemmArgs& args, int m) {
+  const int e = args.tile_expert[m];
+  if (static_cast<unsigned>(e) < static_cast<unsigned>(args.num_experts)) return e;
+  report(args.status, kStatusBadExpert);
+  return 0;
+}
+
 template <bool GATED>
 __global__ void __launch_bounds__(192, 1)
 tc_gemm_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_constant__ CUtensorMap b_map,
@@ -95,7 +103,12 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_constant_
   const uint32_t tmem = sh->tmem_base;
 
   const int n_tiles = args.n_tiles, k_blocks = args.k_blocks;
-  const int total = *args.num_m_tiles * n_tiles;
+  int num_m = *args.num_m_tiles;
+  if (num_m > args.max_m_tiles || num_m < 0) {  // never write past the output buffer
+    if (threadIdx.x == 0) report(args.status, kStatusBadTileCount);
+    num_m = num_m < 0 ? 0 : args.max_m_tiles;
+  }
+  const int total = num_m * n_tiles;
 
   if (warp == 0) {
     // ---------------- TMA producer ----------------
@@ -103,7 +116,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_constant_
       int it = 0;
       for (int tile = blockIdx.x; tile < total; tile += gridDim.x) {
         const int m = tile / n_tiles, n = tile - m * n_tiles;
-        const int e = args.tile_expert[m];
+        const int e = expert_of(args, m);
         const int a_row = m * kTileM;
         const int b_row = e * args.b_rows_per_expert + n * BN;
         bool ok = true;
@@ -180,7 +193,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_constant_
       }
       tc_fence_after();
       const int m = tile / n_tiles, n = tile - m * n_tiles;
-      const int e = args.tile_expert[m];
+      const int e = expert_of(args, m);
       const int64_t row = static_cast<int64_t>(m) * kTileM + q * 32 + lane;
       const uint32_t t_row = tmem + (static_cast<uint32_t>(q * 32) << 16) + acc * BN;
       __nv_bfloat16* outp = static_cast<__nv_bfloat16*>(args.out) + row * args.ldo;

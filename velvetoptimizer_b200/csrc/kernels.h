@@ -27,10 +27,12 @@ cudaError_t launch_router(int dtype, const void* x, const void* w_r, const float
 cudaError_t launch_scan_blocks(const int* hist, const float* psum, int nblk, int E, int* excl,
                                int* counts, float* psum_tot, cudaStream_t s);
 
-// Padded expert offsets, M-tile -> expert map, tile count, aux loss, caller counts.
+// Expert offsets padded to `row_align` rows (kTileM for the local GEMMs, 1 for an
+// expert-parallel send buffer), M-tile -> expert map (when tile_expert != null), tile
+// count, aux loss, caller counts.
 cudaError_t launch_plan(const int* counts, const float* psum_tot, int64_t T, int E, int K,
-                        int64_t capacity, int* offs, int* tile_expert, int* num_tiles,
-                        float* aux, int32_t* counts_out, cudaStream_t s);
+                        int64_t capacity, int row_align, int* offs, int* tile_expert,
+                        int* num_tiles, float* aux, int32_t* counts_out, cudaStream_t s);
 
 // Stable expert-major slots for every (token, k) and the row gather x -> x_perm.
 cudaError_t launch_dispatch(int dtype, const void* x, const int32_t* topk_idx, const int* excl,
@@ -48,16 +50,19 @@ cudaError_t launch_combine(int dtype, const void* y, int64_t y_ld, const int32_t
 cudaError_t launch_simt_gemm1(const float* a, int64_t lda, const float* wg, const float* wu,
                               const float* bg, const float* bu, float* h, int64_t ldh, int N,
                               int K, float gamma, const int* tile_expert, const int* num_tiles,
-                              int64_t max_tiles, cudaStream_t s);
+                              int64_t max_tiles, int num_experts, int* status, cudaStream_t s);
 // y = A Wd^T + bd per M tile's expert.
 cudaError_t launch_simt_gemm2(const float* a, int64_t lda, const float* wd, const float* bd,
                               float* y, int64_t ldy, int N, int K, const int* tile_expert,
-                              const int* num_tiles, int64_t max_tiles, cudaStream_t s);
+                              const int* num_tiles, int64_t max_tiles, int num_experts,
+                              int* status, cudaStream_t s);
 
 // ---- bf16 expert GEMMs (tcgen05 + TMEM + TMA) ----------------------------------------
 struct TcGemmArgs {
   const int* num_m_tiles;   // device scalar
   const int* tile_expert;   // [max_tiles]
+  int max_m_tiles;          // tiles the output buffer holds (bounds num_m_tiles)
+  int num_experts;          // experts the weights hold (bounds tile_expert)
   int n_tiles;              // output tiles per expert along N
   int k_blocks;             // ceil(K / 64)
   int b_rows_per_expert;    // rows of the 2-D weight view per expert

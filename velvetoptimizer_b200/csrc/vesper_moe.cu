@@ -61,6 +61,9 @@ struct vmoe_handle {
   int dtype = kF32;
   int64_t H = 0, I = 0, E = 0, K = 0;
   int64_t Ipad = 0, Hpad = 0;
+  // expert parallelism: this handle holds experts [ep_rank*E_local, (ep_rank+1)*E_local)
+  int ep_size = 1, ep_rank = 0;
+  int64_t E_local = 0;
   // packed weights (library-owned)
   void* w_r = nullptr;
   float* b_r = nullptr;
@@ -137,6 +140,39 @@ Plan make_plan(const vmoe_handle* h, int64_t T) {
   return p;
 }
 
+// Workspace of the expert-parallel stages: routing tables (route -> combine) and the
+// gate|up activations of up to `recv_rows` received rows.
+struct EpPlan {
+  int nblk = 0;
+  size_t idx = 0, w = 0, hist = 0, psum = 0, excl = 0, counts = 0, psum_tot = 0, offs = 0,
+         aux = 0, slot = 0, h = 0, total = 0;
+};
+
+EpPlan make_ep_plan(const vmoe_handle* h, int64_t T, int64_t recv_rows) {
+  EpPlan p;
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    const size_t o = off;
+    off += (bytes + 255) & ~static_cast<size_t>(255);
+    return o;
+  };
+  const int64_t E = h->E, K = h->K;
+  p.nblk = static_cast<int>((T + kTileM - 1) / kTileM);
+  p.idx = take(T * K * 4);
+  p.w = take(T * K * 4);
+  p.hist = take(static_cast<size_t>(p.nblk) * E * 4);
+  p.psum = take(static_cast<size_t>(p.nblk) * E * 4);
+  p.excl = take(static_cast<size_t>(p.nblk) * E * 4);
+  p.counts = take(E * 4);
+  p.psum_tot = take(E * 4);
+  p.offs = take((E + 1) * 4);
+  p.aux = take(4);
+  p.slot = take(T * K * 4);
+  p.h = take(static_cast<size_t>(recv_rows) * h->Ipad * dtype_bytes(h->dtype));
+  p.total = off;
+  return p;
+}
+
 void free_weights(vmoe_handle* h) {
   void* bufs[] = {h->w_r, h->b_r, h->w_g, h->w_u, h->b_g, h->b_u, h->w_d, h->b_d};
   for (void* b : bufs)
@@ -196,6 +232,71 @@ int alloc(vmoe_handle* h, T** p, size_t bytes, const char* what) {
   return VMOE_OK;
 }
 
+
+// gate|up GEMM (+ ERA * up) then down GEMM over an expert-major buffer of `max_rows`
+// rows (a multiple of 128) whose M tiles map to experts through tiles / ntiles.
+template <typename Mark, typename Check>
+int run_expert_gemms(vmoe_handle* h, void* xp, int64_t max_rows, const int* tiles,
+                     const int* ntiles, void* hb, void* yb, int64_t y_ld, cudaStream_t s,
+                     Mark&& mark, Check&& check) {
+  const int64_t H = h->H, max_tiles = max_rows / kTileM;
+  int rc;
+  if (h->dtype == kF32) {
+    if ((rc = check(launch_simt_gemm1(static_cast<float*>(xp), H, static_cast<float*>(h->w_g),
+                                      static_cast<float*>(h->w_u), h->b_g, h->b_u,
+                                      static_cast<float*>(hb), h->Ipad, static_cast<int>(h->I),
+                                      static_cast<int>(H), h->cfg.era_gamma, tiles, ntiles,
+                                      max_tiles, static_cast<int>(h->E_local), h->status, s),
+                    "gemm1")) != VMOE_OK)
+      return rc;
+    mark();
+    return check(launch_simt_gemm2(static_cast<float*>(hb), h->Ipad, static_cast<float*>(h->w_d),
+                                   h->b_d, static_cast<float*>(yb), y_ld, static_cast<int>(H),
+                                   static_cast<int>(h->Ipad), tiles, ntiles, max_tiles,
+                                   static_cast<int>(h->E_local), h->status, s),
+                 "gemm2");
+  }
+  char why[256];
+  CUtensorMap map_x, map_h;
+  if (!make_tmap_bf16(&map_x, xp, max_rows, H, H, kTileM, why, sizeof(why)))
+    return fail(h, VMOE_ERR_CUDA, "x_perm tensor map: %s", why);
+  if (!make_tmap_bf16(&map_h, hb, max_rows, h->Ipad, h->Ipad, kTileM, why, sizeof(why)))
+    return fail(h, VMOE_ERR_CUDA, "h tensor map: %s", why);
+  TcGemmArgs a1{};
+  a1.num_m_tiles = ntiles;
+  a1.tile_expert = tiles;
+  a1.max_m_tiles = static_cast<int>(max_tiles);
+  a1.num_experts = static_cast<int>(h->E_local);
+  a1.n_tiles = static_cast<int>(h->Ipad / kGateUpInterleave);
+  a1.k_blocks = static_cast<int>((H + 63) / 64);
+  a1.b_rows_per_expert = static_cast<int>(2 * h->Ipad);
+  a1.out = hb;
+  a1.ldo = h->Ipad;
+  a1.bias = h->b_g;
+  a1.bias_ld = 2 * h->Ipad;
+  a1.gamma = h->cfg.era_gamma;
+  a1.status = h->status;
+  if ((rc = check(launch_tc_gemm(true, map_x, h->map_wgu, a1, max_tiles, h->num_sms, s),
+                  "gemm1")) != VMOE_OK)
+    return rc;
+  mark();
+  TcGemmArgs a2{};
+  a2.num_m_tiles = ntiles;
+  a2.tile_expert = tiles;
+  a2.max_m_tiles = static_cast<int>(max_tiles);
+  a2.num_experts = static_cast<int>(h->E_local);
+  a2.n_tiles = static_cast<int>(h->Hpad / kDownTileN);
+  a2.k_blocks = static_cast<int>(h->Ipad / 64);
+  a2.b_rows_per_expert = static_cast<int>(h->Hpad);
+  a2.out = yb;
+  a2.ldo = y_ld;
+  a2.bias = h->b_d;
+  a2.bias_ld = h->Hpad;
+  a2.gamma = 0.f;
+  a2.status = h->status;
+  return check(launch_tc_gemm(false, map_h, h->map_wd, a2, max_tiles, h->num_sms, s), "gemm2");
+}
+
 }  // namespace
 
 namespace vmoe {
@@ -251,6 +352,7 @@ int vmoe_create(const vmoe_config* cfg, int device, vmoe_handle** out) {
   h->H = cfg->hidden;
   h->I = cfg->inter;
   h->E = cfg->num_experts;
+  h->E_local = cfg->num_experts;
   h->K = cfg->top_k;
   if (h->dtype == kBF16) {
     h->Ipad = round_up(h->I, kGateUpInterleave);
@@ -304,6 +406,7 @@ int vmoe_set_weights(vmoe_handle* h, const vmoe_weights* w, void* stream) {
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   free_weights(h);
   const int64_t E = h->E, H = h->H, I = h->I, Ipad = h->Ipad, Hpad = h->Hpad;
+  const int64_t El = h->E_local;  // experts held by this handle (E without expert parallelism)
   const size_t elt = dtype_bytes(h->dtype);
   const bool bf16 = h->dtype == kBF16;
   const int R = h->cfg.lora_rank;
@@ -311,14 +414,14 @@ int vmoe_set_weights(vmoe_handle* h, const vmoe_weights* w, void* stream) {
   if ((rc = alloc(h, &h->w_r, E * H * elt, "router weight")) != VMOE_OK) return rc;
   if ((rc = alloc(h, &h->b_r, E * 4, "router bias")) != VMOE_OK) return rc;
   const int64_t gu_rows = bf16 ? 2 * Ipad : I;
-  if ((rc = alloc(h, &h->w_g, E * gu_rows * H * elt, "gate weight")) != VMOE_OK) return rc;
-  if ((rc = alloc(h, &h->b_g, E * gu_rows * 4, "gate bias")) != VMOE_OK) return rc;
+  if ((rc = alloc(h, &h->w_g, El * gu_rows * H * elt, "gate weight")) != VMOE_OK) return rc;
+  if ((rc = alloc(h, &h->b_g, El * gu_rows * 4, "gate bias")) != VMOE_OK) return rc;
   if (!bf16) {
-    if ((rc = alloc(h, &h->w_u, E * I * H * elt, "up weight")) != VMOE_OK) return rc;
-    if ((rc = alloc(h, &h->b_u, E * I * 4, "up bias")) != VMOE_OK) return rc;
+    if ((rc = alloc(h, &h->w_u, El * I * H * elt, "up weight")) != VMOE_OK) return rc;
+    if ((rc = alloc(h, &h->b_u, El * I * 4, "up bias")) != VMOE_OK) return rc;
   }
-  if ((rc = alloc(h, &h->w_d, E * Hpad * Ipad * elt, "down weight")) != VMOE_OK) return rc;
-  if ((rc = alloc(h, &h->b_d, E * Hpad * 4, "down bias")) != VMOE_OK) return rc;
+  if ((rc = alloc(h, &h->w_d, El * Hpad * Ipad * elt, "down weight")) != VMOE_OK) return rc;
+  if ((rc = alloc(h, &h->b_d, El * Hpad * 4, "down bias")) != VMOE_OK) return rc;
 
   cudaError_t e;
   // router: plain copy of W_r, bias to fp32
@@ -341,7 +444,7 @@ int vmoe_set_weights(vmoe_handle* h, const vmoe_weights* w, void* stream) {
     p.lora_up = lo ? (which == 0 ? w->gate_lora_up_w : w->up_lora_up_w) : nullptr;
     p.R = lo ? R : 0;
     p.scaling = h->cfg.lora_scaling;
-    p.E = static_cast<int>(E);
+    p.E = static_cast<int>(El);
     p.O = static_cast<int>(I);
     p.Kin = static_cast<int>(H);
     p.Kpad = static_cast<int>(H);
@@ -378,7 +481,7 @@ int vmoe_set_weights(vmoe_handle* h, const vmoe_weights* w, void* stream) {
     PackArgs p{};
     p.dtype = h->dtype;
     p.src = w->down_w;
-    p.E = static_cast<int>(E);
+    p.E = static_cast<int>(El);
     p.O = static_cast<int>(H);
     p.Kin = static_cast<int>(I);
     p.Kpad = static_cast<int>(Ipad);
@@ -396,9 +499,9 @@ int vmoe_set_weights(vmoe_handle* h, const vmoe_weights* w, void* stream) {
   }
   if (bf16) {
     char why[256];
-    if (!make_tmap_bf16(&h->map_wgu, h->w_g, E * 2 * Ipad, H, H, 256, why, sizeof(why)))
+    if (!make_tmap_bf16(&h->map_wgu, h->w_g, El * 2 * Ipad, H, H, 256, why, sizeof(why)))
       return fail(h, VMOE_ERR_CUDA, "gate/up tensor map: %s", why);
-    if (!make_tmap_bf16(&h->map_wd, h->w_d, E * Hpad, Ipad, Ipad, 256, why, sizeof(why)))
+    if (!make_tmap_bf16(&h->map_wd, h->w_d, El * Hpad, Ipad, Ipad, 256, why, sizeof(why)))
       return fail(h, VMOE_ERR_CUDA, "down tensor map: %s", why);
   }
   h->ready = true;
@@ -434,6 +537,9 @@ int vmoe_forward(vmoe_handle* h, const void* x, int64_t tokens, void* out, float
   if (!h) return VMOE_ERR_INVALID_ARG;
   h->last_launches = 0;
   if (!h->ready) return fail(h, VMOE_ERR_NOT_READY, "vmoe_set_weights has not been called");
+  if (h->ep_size > 1)
+    return fail(h, VMOE_ERR_INVALID_ARG,
+                "an expert-parallel handle runs through vmoe_ep_route/experts/combine");
   if (tokens < 0) return fail(h, VMOE_ERR_INVALID_ARG, "tokens must be >= 0 (got %lld)",
                               static_cast<long long>(tokens));
   const int64_t E = h->E, K = h->K, H = h->H, T = tokens;
@@ -507,7 +613,7 @@ int vmoe_forward(vmoe_handle* h, const void* x, int64_t tokens, void* out, float
     return rc;
   mark();
   if ((rc = check(launch_plan(counts, psum_tot, T, static_cast<int>(E), static_cast<int>(K),
-                              h->cfg.capacity, offs, tiles, ntiles, aux, expert_counts, s),
+                              h->cfg.capacity, kTileM, offs, tiles, ntiles, aux, expert_counts, s),
                   "plan")) != VMOE_OK)
     return rc;
   mark();
@@ -517,60 +623,9 @@ int vmoe_forward(vmoe_handle* h, const void* x, int64_t tokens, void* out, float
                   "dispatch")) != VMOE_OK)
     return rc;
   mark();
-  if (h->dtype == kF32) {
-    if ((rc = check(launch_simt_gemm1(static_cast<float*>(xp), H, static_cast<float*>(h->w_g),
-                                      static_cast<float*>(h->w_u), h->b_g, h->b_u,
-                                      static_cast<float*>(hb), h->Ipad, static_cast<int>(h->I),
-                                      static_cast<int>(H), h->cfg.era_gamma, tiles, ntiles,
-                                      p.max_tiles, s),
-                    "gemm1")) != VMOE_OK)
-      return rc;
-    mark();
-    if ((rc = check(launch_simt_gemm2(static_cast<float*>(hb), h->Ipad,
-                                      static_cast<float*>(h->w_d), h->b_d,
-                                      static_cast<float*>(yb), h->Hpad, static_cast<int>(H),
-                                      static_cast<int>(h->Ipad), tiles, ntiles, p.max_tiles, s),
-                    "gemm2")) != VMOE_OK)
-      return rc;
-  } else {
-    char why[256];
-    CUtensorMap map_x, map_h;
-    if (!make_tmap_bf16(&map_x, xp, p.max_rows, H, H, kTileM, why, sizeof(why)))
-      return fail(h, VMOE_ERR_CUDA, "x_perm tensor map: %s", why);
-    if (!make_tmap_bf16(&map_h, hb, p.max_rows, h->Ipad, h->Ipad, kTileM, why, sizeof(why)))
-      return fail(h, VMOE_ERR_CUDA, "h tensor map: %s", why);
-    TcGemmArgs a1{};
-    a1.num_m_tiles = ntiles;
-    a1.tile_expert = tiles;
-    a1.n_tiles = static_cast<int>(h->Ipad / kGateUpInterleave);
-    a1.k_blocks = static_cast<int>((H + 63) / 64);
-    a1.b_rows_per_expert = static_cast<int>(2 * h->Ipad);
-    a1.out = hb;
-    a1.ldo = h->Ipad;
-    a1.bias = h->b_g;
-    a1.bias_ld = 2 * h->Ipad;
-    a1.gamma = h->cfg.era_gamma;
-    a1.status = h->status;
-    if ((rc = check(launch_tc_gemm(true, map_x, h->map_wgu, a1, p.max_tiles, h->num_sms, s),
-                    "gemm1")) != VMOE_OK)
-      return rc;
-    mark();
-    TcGemmArgs a2{};
-    a2.num_m_tiles = ntiles;
-    a2.tile_expert = tiles;
-    a2.n_tiles = static_cast<int>(h->Hpad / kDownTileN);
-    a2.k_blocks = static_cast<int>(h->Ipad / 64);
-    a2.b_rows_per_expert = static_cast<int>(h->Hpad);
-    a2.out = yb;
-    a2.ldo = h->Hpad;
-    a2.bias = h->b_d;
-    a2.bias_ld = h->Hpad;
-    a2.gamma = 0.f;
-    a2.status = h->status;
-    if ((rc = check(launch_tc_gemm(false, map_h, h->map_wd, a2, p.max_tiles, h->num_sms, s),
-                    "gemm2")) != VMOE_OK)
-      return rc;
-  }
+  if ((rc = run_expert_gemms(h, xp, p.max_rows, tiles, ntiles, hb, yb, h->Hpad, s, mark,
+                             check)) != VMOE_OK)
+    return rc;
   mark();
   if ((rc = check(launch_combine(h->dtype, yb, h->Hpad, idx, tw, slot, T, static_cast<int>(H),
                                  static_cast<int>(K), out, s),
@@ -578,6 +633,169 @@ int vmoe_forward(vmoe_handle* h, const void* x, int64_t tokens, void* out, float
     return rc;
   mark();
   if (prof) ++h->prof_count;
+  return VMOE_OK;
+}
+
+int vmoe_create_ep(const vmoe_config* cfg, int device, int ep_size, int ep_rank,
+                   vmoe_handle** out) {
+  if (!cfg || !out) return VMOE_ERR_INVALID_ARG;
+  *out = nullptr;
+  if (ep_size < 1 || ep_rank < 0 || ep_rank >= ep_size || cfg->num_experts % ep_size) {
+    fprintf(stderr, "vmoe_create_ep: need 0 <= ep_rank < ep_size and num_experts %% ep_size == 0"
+            " (E=%d, ep_size=%d, ep_rank=%d)\n", cfg->num_experts, ep_size, ep_rank);
+    return VMOE_ERR_INVALID_ARG;
+  }
+  if (cfg->capacity != 0) {
+    fprintf(stderr, "vmoe_create_ep: capacity is not supported with expert parallelism\n");
+    return VMOE_ERR_UNSUPPORTED_SHAPE;
+  }
+  if (cfg->dtype == VMOE_BF16 && cfg->hidden % kDownTileN) {
+    fprintf(stderr, "vmoe_create_ep: bf16 expert parallelism needs hidden %% %d == 0\n",
+            kDownTileN);
+    return VMOE_ERR_UNSUPPORTED_SHAPE;
+  }
+  vmoe_handle* h = nullptr;
+  const int rc = vmoe_create(cfg, device, &h);
+  if (rc != VMOE_OK) return rc;
+  h->ep_size = ep_size;
+  h->ep_rank = ep_rank;
+  h->E_local = cfg->num_experts / ep_size;
+  *out = h;
+  return VMOE_OK;
+}
+
+int vmoe_ep_workspace_size(const vmoe_handle* h, int64_t tokens, int64_t recv_rows_cap,
+                           size_t* bytes) {
+  if (!h || !bytes || tokens < 0 || recv_rows_cap < 0) return VMOE_ERR_INVALID_ARG;
+  *bytes = make_ep_plan(h, tokens, recv_rows_cap).total;
+  return VMOE_OK;
+}
+
+namespace {
+int ep_common_checks(vmoe_handle* h, void* workspace, size_t workspace_bytes, size_t need) {
+  if (!h->ready) return fail(h, VMOE_ERR_NOT_READY, "vmoe_set_weights has not been called");
+  if (!workspace || workspace_bytes < need)
+    return fail(h, VMOE_ERR_WORKSPACE, "workspace needs %zu bytes (got %zu)", need,
+                workspace ? workspace_bytes : static_cast<size_t>(0));
+  if (reinterpret_cast<uintptr_t>(workspace) & 255u)
+    return fail(h, VMOE_ERR_WORKSPACE, "workspace must be 256-byte aligned");
+  return VMOE_OK;
+}
+}  // namespace
+
+int vmoe_ep_route(vmoe_handle* h, const void* x, int64_t tokens, void* send_rows,
+                  int32_t* expert_counts, float* router_logits, float* aux_loss, void* workspace,
+                  size_t workspace_bytes, void* stream) {
+  if (!h) return VMOE_ERR_INVALID_ARG;
+  h->last_launches = 0;
+  const int64_t E = h->E, K = h->K, H = h->H, T = tokens;
+  if (T < 0 || T * K + E >= (static_cast<int64_t>(1) << 31))
+    return fail(h, VMOE_ERR_INVALID_ARG, "bad token count %lld", static_cast<long long>(T));
+  if (!expert_counts) return fail(h, VMOE_ERR_INVALID_ARG, "expert_counts is required");
+  const EpPlan p = make_ep_plan(h, T, 0);
+  int rc = ep_common_checks(h, workspace, workspace_bytes, p.total);
+  if (rc != VMOE_OK) return rc;
+  DeviceGuard g(h->device);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  cudaError_t e;
+  if (T == 0) {
+    if ((e = cudaMemsetAsync(expert_counts, 0, E * 4, s)) != cudaSuccess)
+      return cuda_fail(h, e, "counts write");
+    if (aux_loss) {
+      const float nan = __builtin_nanf("");
+      if ((e = cudaMemcpyAsync(aux_loss, &nan, 4, cudaMemcpyHostToDevice, s)) != cudaSuccess)
+        return cuda_fail(h, e, "aux write");
+    }
+    return VMOE_OK;
+  }
+  if (!x || !send_rows) return fail(h, VMOE_ERR_INVALID_ARG, "x and send_rows are required");
+  if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(send_rows)) & 15u)
+    return fail(h, VMOE_ERR_INVALID_ARG, "x and send_rows must be 16-byte aligned");
+  char* ws = static_cast<char*>(workspace);
+  int32_t* idx = reinterpret_cast<int32_t*>(ws + p.idx);
+  float* tw = reinterpret_cast<float*>(ws + p.w);
+  int* hist = reinterpret_cast<int*>(ws + p.hist);
+  float* psum = reinterpret_cast<float*>(ws + p.psum);
+  int* excl = reinterpret_cast<int*>(ws + p.excl);
+  int* counts = reinterpret_cast<int*>(ws + p.counts);
+  float* psum_tot = reinterpret_cast<float*>(ws + p.psum_tot);
+  int* offs = reinterpret_cast<int*>(ws + p.offs);
+  float* aux = aux_loss ? aux_loss : reinterpret_cast<float*>(ws + p.aux);
+  int* slot = reinterpret_cast<int*>(ws + p.slot);
+  auto check = [&](cudaError_t err, const char* what) -> int {
+    if (err != cudaSuccess) return cuda_fail(h, err, what);
+    ++h->last_launches;
+    return VMOE_OK;
+  };
+  if ((rc = check(launch_router(h->dtype, x, h->w_r, h->b_r, T, static_cast<int>(H),
+                                static_cast<int>(E), static_cast<int>(K), router_logits, idx, tw,
+                                hist, psum, s), "router")) != VMOE_OK)
+    return rc;
+  if ((rc = check(launch_scan_blocks(hist, psum, p.nblk, static_cast<int>(E), excl, counts,
+                                     psum_tot, s), "scan")) != VMOE_OK)
+    return rc;
+  if ((rc = check(launch_plan(counts, psum_tot, T, static_cast<int>(E), static_cast<int>(K), 0,
+                              1, offs, nullptr, nullptr, aux, expert_counts, s), "plan")) != VMOE_OK)
+    return rc;
+  return check(launch_dispatch(h->dtype, x, idx, excl, offs, T, static_cast<int>(H),
+                               static_cast<int>(E), static_cast<int>(K), 0, slot, send_rows, H,
+                               h->status, s), "dispatch");
+}
+
+int vmoe_ep_experts(vmoe_handle* h, const void* recv_rows, int64_t recv_rows_cap,
+                    const int32_t* tile_expert, const int32_t* num_tiles, void* out_rows,
+                    void* workspace, size_t workspace_bytes, void* stream) {
+  if (!h) return VMOE_ERR_INVALID_ARG;
+  h->last_launches = 0;
+  if (recv_rows_cap < 0 || recv_rows_cap % kTileM)
+    return fail(h, VMOE_ERR_INVALID_ARG, "recv_rows_cap must be a multiple of %d (got %lld)",
+                kTileM, static_cast<long long>(recv_rows_cap));
+  const EpPlan p = make_ep_plan(h, 0, recv_rows_cap);
+  int rc = ep_common_checks(h, workspace, workspace_bytes, p.total);
+  if (rc != VMOE_OK) return rc;
+  if (recv_rows_cap == 0) return VMOE_OK;
+  if (!recv_rows || !out_rows || !tile_expert || !num_tiles)
+    return fail(h, VMOE_ERR_INVALID_ARG, "recv_rows, out_rows, tile_expert, num_tiles required");
+  if ((reinterpret_cast<uintptr_t>(recv_rows) | reinterpret_cast<uintptr_t>(out_rows)) & 15u)
+    return fail(h, VMOE_ERR_INVALID_ARG, "row buffers must be 16-byte aligned");
+  if (h->Hpad != h->H)
+    return fail(h, VMOE_ERR_UNSUPPORTED_SHAPE, "expert parallelism needs hidden %% %d == 0",
+                kDownTileN);
+  DeviceGuard g(h->device);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  char* ws = static_cast<char*>(workspace);
+  auto mark = []() {};
+  auto check = [&](cudaError_t err, const char* what) -> int {
+    if (err != cudaSuccess) return cuda_fail(h, err, what);
+    ++h->last_launches;
+    return VMOE_OK;
+  };
+  return run_expert_gemms(h, const_cast<void*>(recv_rows), recv_rows_cap, tile_expert, num_tiles,
+                          ws + p.h, out_rows, h->H, s, mark, check);
+}
+
+int vmoe_ep_combine(vmoe_handle* h, const void* back_rows, int64_t tokens, void* out,
+                    void* workspace, size_t workspace_bytes, void* stream) {
+  if (!h) return VMOE_ERR_INVALID_ARG;
+  h->last_launches = 0;
+  if (tokens < 0) return fail(h, VMOE_ERR_INVALID_ARG, "tokens must be >= 0");
+  const EpPlan p = make_ep_plan(h, tokens, 0);
+  int rc = ep_common_checks(h, workspace, workspace_bytes, p.total);
+  if (rc != VMOE_OK) return rc;
+  if (tokens == 0) return VMOE_OK;
+  if (!back_rows || !out) return fail(h, VMOE_ERR_INVALID_ARG, "back_rows and out are required");
+  if ((reinterpret_cast<uintptr_t>(back_rows) | reinterpret_cast<uintptr_t>(out)) & 15u)
+    return fail(h, VMOE_ERR_INVALID_ARG, "back_rows and out must be 16-byte aligned");
+  DeviceGuard g(h->device);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  char* ws = static_cast<char*>(workspace);
+  const cudaError_t e = launch_combine(h->dtype, back_rows, h->H,
+                                       reinterpret_cast<int32_t*>(ws + p.idx),
+                                       reinterpret_cast<float*>(ws + p.w),
+                                       reinterpret_cast<int*>(ws + p.slot), tokens,
+                                       static_cast<int>(h->H), static_cast<int>(h->K), out, s);
+  if (e != cudaSuccess) return cuda_fail(h, e, "combine");
+  h->last_launches = 1;
   return VMOE_OK;
 }
 
