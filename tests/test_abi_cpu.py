@@ -69,6 +69,22 @@ def test_create_rejects_bad_config(kw, code):
     assert not h.value
 
 
+@pytest.mark.parametrize("ep_size,ep_rank,kw,code", [
+    (3, 0, {}, _lib.VMOE_ERR_INVALID_ARG),          # 4 experts over 3 ranks
+    (2, 2, {}, _lib.VMOE_ERR_INVALID_ARG),          # rank out of range
+    (2, 0, dict(capacity=8), _lib.VMOE_ERR_UNSUPPORTED_SHAPE),
+    (2, 0, dict(dtype=_lib.VMOE_BF16, hidden=128), _lib.VMOE_ERR_UNSUPPORTED_SHAPE),
+])
+def test_create_ep_rejects_bad_partition(ep_size, ep_rank, kw, code):
+    base = dict(hidden=64, inter=128, num_experts=4, top_k=2, lora_rank=16, lora_scaling=2.0,
+                era_gamma=0.1, dtype=_lib.VMOE_F32, capacity=0)
+    base.update(kw)
+    cfg = _lib.VmoeConfig(**base)
+    h = ctypes.c_void_p()
+    assert _lib.load().vmoe_create_ep(ctypes.byref(cfg), 0, ep_size, ep_rank, ctypes.byref(h)) == code
+    assert not h.value
+
+
 def test_null_arguments_rejected():
     lib = _lib.load()
     assert lib.vmoe_create(None, 0, None) == _lib.VMOE_ERR_INVALID_ARG

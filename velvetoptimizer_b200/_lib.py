@@ -33,6 +33,8 @@ EXPORTED = (
     "vmoe_workspace_layout", "vmoe_forward", "vmoe_forward_no_alloc",
     "vmoe_device_status", "vmoe_set_profiling", "vmoe_stage_times", "vmoe_stage_name",
     "vmoe_last_launch_count", "vmoe_last_error", "vmoe_status_string", "vmoe_abi_version",
+    "vmoe_create_ep", "vmoe_ep_workspace_size", "vmoe_ep_route", "vmoe_ep_experts",
+    "vmoe_ep_combine",
 )
 
 
@@ -100,6 +102,18 @@ def load() -> ctypes.CDLL:
     lib.vmoe_forward_no_alloc.argtypes = [H, c_void_p, c_int64, c_void_p, c_void_p, c_void_p,
                                           c_void_p, c_void_p, c_void_p, c_void_p]
     lib.vmoe_forward_no_alloc.restype = c_int
+    lib.vmoe_create_ep.argtypes = [POINTER(VmoeConfig), c_int, c_int, c_int, POINTER(H)]
+    lib.vmoe_create_ep.restype = c_int
+    lib.vmoe_ep_workspace_size.argtypes = [H, c_int64, c_int64, POINTER(c_size_t)]
+    lib.vmoe_ep_workspace_size.restype = c_int
+    lib.vmoe_ep_route.argtypes = [H, c_void_p, c_int64, c_void_p, c_void_p, c_void_p, c_void_p,
+                                  c_void_p, c_size_t, c_void_p]
+    lib.vmoe_ep_route.restype = c_int
+    lib.vmoe_ep_experts.argtypes = [H, c_void_p, c_int64, c_void_p, c_void_p, c_void_p,
+                                    c_void_p, c_size_t, c_void_p]
+    lib.vmoe_ep_experts.restype = c_int
+    lib.vmoe_ep_combine.argtypes = [H, c_void_p, c_int64, c_void_p, c_void_p, c_size_t, c_void_p]
+    lib.vmoe_ep_combine.restype = c_int
     lib.vmoe_device_status.argtypes = [H, POINTER(c_int32), c_void_p]
     lib.vmoe_device_status.restype = c_int
     lib.vmoe_set_profiling.argtypes = [H, c_int]
