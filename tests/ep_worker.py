@@ -72,31 +72,40 @@ def main():
             (torch.float32, MoEConfig(hidden_size=128, intermediate_size=192, moe_num_experts=8,
                                       moe_top_k=3), 300),
         ]
-        for dtype, cfg, T in cases:
-            w = global_weights(cfg, dev, dtype, seed=7)
-            g = torch.Generator(device=dev)
-            g.manual_seed(1000 + rank)
-            x = torch.randn(T, cfg.hidden_size, generator=g, device=dev).to(dtype)
-            layer = ExpertParallelMoE(cfg, w, dev, dtype)
-            out, aux = layer(x)
-            out2, aux2 = layer(x)  # a second call reuses nothing stale
-            torch.cuda.synchronize()
-            ref, ref_aux = single_gpu(cfg, w, x, dtype)
-            tag = f"rank {rank} {dtype} E{cfg.moe_num_experts} K{cfg.moe_top_k}"
-            if not torch.equal(out, ref):
-                d = (out.float() - ref.float()).abs().max().item()
-                failures.append(f"{tag}: EP output differs from single GPU (max abs {d:.3e})")
-            if not torch.equal(out, out2):
-                failures.append(f"{tag}: EP output not deterministic")
-            if abs(aux.item() - ref_aux.item()) > 1e-6 * abs(ref_aux.item()) or aux.item() != aux2.item():
-                failures.append(f"{tag}: aux {aux.item()} vs {ref_aux.item()}")
-            rows = int(layer.last_plan.recv_counts.sum())
-            tot = torch.tensor([rows], device=dev)
-            dist.all_reduce(tot)
-            if int(tot.item()) != world * T * cfg.moe_top_k:
-                failures.append(f"{tag}: {int(tot.item())} rows exchanged")
-            layer.close()
-            dist.barrier()
+        for transport in ("nccl", "p2p"):
+            for dtype, cfg, T0 in cases:
+                T = T0 - 37 * rank  # ranks route different token counts
+                w = global_weights(cfg, dev, dtype, seed=7)
+                layer = ExpertParallelMoE(cfg, w, dev, dtype, transport=transport, max_tokens=T0)
+                tag = f"{transport} rank {rank} {dtype} E{cfg.moe_num_experts} K{cfg.moe_top_k}"
+                for it in range(3):  # several forwards: epochs advance, buffers are reused
+                    g = torch.Generator(device=dev)
+                    g.manual_seed(1000 + 10 * rank + it)
+                    x = torch.randn(T, cfg.hidden_size, generator=g, device=dev).to(dtype)
+                    out, aux = layer(x)
+                    out2, aux2 = layer(x)
+                    torch.cuda.synchronize()
+                    status = layer.device_status()
+                    if status:
+                        failures.append(f"{tag}: device status 0x{status:x}")
+                    ref, ref_aux = single_gpu(cfg, w, x, dtype)
+                    if not torch.equal(out, ref):
+                        d = (out.float() - ref.float()).abs().max().item()
+                        failures.append(f"{tag} it{it}: EP output differs from single GPU (max abs {d:.3e})")
+                    if not torch.equal(out, out2):
+                        failures.append(f"{tag} it{it}: EP output not deterministic")
+                    if (abs(aux.item() - ref_aux.item()) > 1e-6 * abs(ref_aux.item())
+                            or aux.item() != aux2.item()):
+                        failures.append(f"{tag} it{it}: aux {aux.item()} vs {ref_aux.item()}")
+                if transport == "nccl":
+                    rows = int(layer.last_plan.recv_counts.sum())
+                    tot = torch.tensor([rows], device=dev)
+                    dist.all_reduce(tot)
+                    want = sum(T0 - 37 * r for r in range(world)) * cfg.moe_top_k
+                    if int(tot.item()) != want:
+                        failures.append(f"{tag}: {int(tot.item())} rows exchanged, want {want}")
+                layer.close()
+                dist.barrier()
     finally:
         dist.destroy_process_group()
     if failures:

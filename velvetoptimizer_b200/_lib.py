@@ -34,7 +34,8 @@ EXPORTED = (
     "vmoe_device_status", "vmoe_set_profiling", "vmoe_stage_times", "vmoe_stage_name",
     "vmoe_last_launch_count", "vmoe_last_error", "vmoe_status_string", "vmoe_abi_version",
     "vmoe_create_ep", "vmoe_ep_workspace_size", "vmoe_ep_route", "vmoe_ep_experts",
-    "vmoe_ep_combine",
+    "vmoe_ep_combine", "vmoe_ep_p2p_setup", "vmoe_ep_p2p_connect", "vmoe_ep_p2p_workspace_size",
+    "vmoe_ep_p2p_forward",
 )
 
 
@@ -114,6 +115,15 @@ def load() -> ctypes.CDLL:
     lib.vmoe_ep_experts.restype = c_int
     lib.vmoe_ep_combine.argtypes = [H, c_void_p, c_int64, c_void_p, c_void_p, c_size_t, c_void_p]
     lib.vmoe_ep_combine.restype = c_int
+    lib.vmoe_ep_p2p_setup.argtypes = [H, c_int64, c_void_p]
+    lib.vmoe_ep_p2p_setup.restype = c_int
+    lib.vmoe_ep_p2p_connect.argtypes = [H, c_void_p]
+    lib.vmoe_ep_p2p_connect.restype = c_int
+    lib.vmoe_ep_p2p_workspace_size.argtypes = [H, c_int64, POINTER(c_size_t)]
+    lib.vmoe_ep_p2p_workspace_size.restype = c_int
+    lib.vmoe_ep_p2p_forward.argtypes = [H, c_void_p, c_int64, c_void_p, c_void_p, c_void_p,
+                                        c_void_p, c_size_t, c_void_p]
+    lib.vmoe_ep_p2p_forward.restype = c_int
     lib.vmoe_device_status.argtypes = [H, POINTER(c_int32), c_void_p]
     lib.vmoe_device_status.restype = c_int
     lib.vmoe_set_profiling.argtypes = [H, c_int]

@@ -18,6 +18,8 @@ enum DeviceStatus : int {
   kStatusTimeoutMma = 0x102,
   kStatusTimeoutEpilogue = 0x103,
   kStatusTimeoutDrain = 0x104,
+  kStatusTimeoutPeer = 0x105,
+  kStatusCapacity = 0x204,
   kStatusBadExpert = 0x201,
   kStatusBadSlot = 0x202,
   kStatusBadTileCount = 0x203,

@@ -84,6 +84,30 @@ cudaError_t launch_tc_gemm(bool gated, const CUtensorMap& a_map, const CUtensorM
 bool make_tmap_bf16(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols,
                     uint64_t ld, uint32_t box_rows, char* err, size_t err_len);
 
+// ---- expert parallelism over NVLink peer memory ---------------------------------------
+struct P2PArgs {
+  char* const* peer_base;   // device array [G]: every rank's symmetric region (own included)
+  size_t sig_off, counts_off, recv_off, y_off;
+  int me, G, E, El, K;
+  int64_t H;
+  int64_t cap_rows;         // rows of recv / y
+  unsigned epoch;           // this forward's flag value
+  int* status;
+  int* block_counter;       // local, zero between forwards
+  int32_t* dest_rank;       // [T*K] owner rank of each (token, k) row
+  int32_t* dest_row;        // [T*K] row in the owner's recv / y
+  int* tile_expert;         // this rank's GEMM tile map
+  int* num_tiles;
+};
+cudaError_t launch_p2p_publish(const P2PArgs& a, const int* counts, cudaStream_t s);
+cudaError_t launch_p2p_wait(const P2PArgs& a, int which, cudaStream_t s);
+cudaError_t launch_p2p_signal(const P2PArgs& a, int which, cudaStream_t s);
+cudaError_t launch_p2p_dispatch(int dtype, const P2PArgs& a, const void* x,
+                                const int32_t* topk_idx, const int* excl, int64_t T,
+                                cudaStream_t s);
+cudaError_t launch_p2p_combine(int dtype, const P2PArgs& a, const int32_t* topk_idx,
+                               const float* topk_w, int64_t T, void* out, cudaStream_t s);
+
 // ---- weight packing ------------------------------------------------------------------
 // dst[e][map(o)][k] = src[e][o][k] + s * sum_r lu[e][o][r] * ld[e][r][k]  (0 when padded)
 struct PackArgs {

@@ -64,6 +64,15 @@ struct vmoe_handle {
   // expert parallelism: this handle holds experts [ep_rank*E_local, (ep_rank+1)*E_local)
   int ep_size = 1, ep_rank = 0;
   int64_t E_local = 0;
+  // expert parallelism over NVLink peer memory (vmoe_ep_p2p_*)
+  char* p2p_region = nullptr;
+  size_t p2p_sig_off = 0, p2p_counts_off = 0, p2p_recv_off = 0, p2p_y_off = 0;
+  int64_t p2p_cap_rows = 0, p2p_max_tokens = 0;
+  std::vector<char*> p2p_peers;  // every rank's region as mapped here (own at [ep_rank])
+  char** p2p_peers_dev = nullptr;
+  int* p2p_block_counter = nullptr;
+  unsigned p2p_epoch = 0;
+  bool p2p_connected = false;
   // packed weights (library-owned)
   void* w_r = nullptr;
   float* b_r = nullptr;
@@ -169,6 +178,42 @@ EpPlan make_ep_plan(const vmoe_handle* h, int64_t T, int64_t recv_rows) {
   p.aux = take(4);
   p.slot = take(T * K * 4);
   p.h = take(static_cast<size_t>(recv_rows) * h->Ipad * dtype_bytes(h->dtype));
+  p.total = off;
+  return p;
+}
+
+// Workspace of vmoe_ep_p2p_forward: routing tables, owner rank/row of every routed row,
+// this rank's tile map, and the gate|up activations of its receive buffer.
+struct P2PPlan {
+  int nblk = 0;
+  size_t idx = 0, w = 0, hist = 0, psum = 0, excl = 0, counts = 0, psum_tot = 0, offs = 0,
+         aux = 0, drank = 0, drow = 0, tiles = 0, ntiles = 0, hbuf = 0, total = 0;
+};
+
+P2PPlan make_p2p_plan(const vmoe_handle* h, int64_t T) {
+  P2PPlan p;
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    const size_t o = off;
+    off += (bytes + 255) & ~static_cast<size_t>(255);
+    return o;
+  };
+  const int64_t E = h->E, K = h->K, cap = h->p2p_cap_rows;
+  p.nblk = static_cast<int>((T + kTileM - 1) / kTileM);
+  p.idx = take(T * K * 4);
+  p.w = take(T * K * 4);
+  p.hist = take(static_cast<size_t>(p.nblk) * E * 4);
+  p.psum = take(static_cast<size_t>(p.nblk) * E * 4);
+  p.excl = take(static_cast<size_t>(p.nblk) * E * 4);
+  p.counts = take(E * 4);
+  p.psum_tot = take(E * 4);
+  p.offs = take((E + 1) * 4);
+  p.aux = take(4);
+  p.drank = take(T * K * 4);
+  p.drow = take(T * K * 4);
+  p.tiles = take((cap / kTileM + 1) * 4);
+  p.ntiles = take(4);
+  p.hbuf = take(static_cast<size_t>(cap) * h->Ipad * dtype_bytes(h->dtype));
   p.total = off;
   return p;
 }
@@ -390,6 +435,11 @@ int vmoe_destroy(vmoe_handle* h) {
   {
     DeviceGuard g(h->device);
     free_weights(h);
+    for (size_t r = 0; r < h->p2p_peers.size(); ++r)
+      if (static_cast<int>(r) != h->ep_rank && h->p2p_peers[r]) cudaIpcCloseMemHandle(h->p2p_peers[r]);
+    if (h->p2p_region) cudaFree(h->p2p_region);
+    if (h->p2p_peers_dev) cudaFree(h->p2p_peers_dev);
+    if (h->p2p_block_counter) cudaFree(h->p2p_block_counter);
     if (h->status) cudaFree(h->status);
     for (cudaEvent_t ev : h->prof_ev) cudaEventDestroy(ev);
   }
@@ -796,6 +846,178 @@ int vmoe_ep_combine(vmoe_handle* h, const void* back_rows, int64_t tokens, void*
                                        static_cast<int>(h->H), static_cast<int>(h->K), out, s);
   if (e != cudaSuccess) return cuda_fail(h, e, "combine");
   h->last_launches = 1;
+  return VMOE_OK;
+}
+
+int vmoe_ep_p2p_setup(vmoe_handle* h, int64_t max_tokens, void* ipc_handle) {
+  if (!h || !ipc_handle || max_tokens < 0) return VMOE_ERR_INVALID_ARG;
+  if (h->p2p_region) return fail(h, VMOE_ERR_INVALID_ARG, "vmoe_ep_p2p_setup was already called");
+  if (h->dtype == kBF16 && h->Hpad != h->H)
+    return fail(h, VMOE_ERR_UNSUPPORTED_SHAPE, "bf16 expert parallelism needs hidden %% %d == 0",
+                kDownTileN);
+  const int64_t G = h->ep_size, E = h->E, K = h->K, El = h->E_local, H = h->H;
+  const int64_t cap = round_up(G * max_tokens * K + El * (kTileM - 1), kTileM);
+  if (cap >= (static_cast<int64_t>(1) << 31))
+    return fail(h, VMOE_ERR_UNSUPPORTED_SHAPE, "receive capacity of %lld rows is too large",
+                static_cast<long long>(cap));
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    const size_t o = off;
+    off += (bytes + 255) & ~static_cast<size_t>(255);
+    return o;
+  };
+  h->p2p_sig_off = take(3 * G * 4);
+  h->p2p_counts_off = take(G * E * 4);
+  h->p2p_recv_off = take(static_cast<size_t>(cap) * H * dtype_bytes(h->dtype));
+  h->p2p_y_off = take(static_cast<size_t>(cap) * H * dtype_bytes(h->dtype));
+  DeviceGuard g(h->device);
+  cudaError_t e = cudaMalloc(&h->p2p_region, off);
+  if (e == cudaSuccess) e = cudaMemset(h->p2p_region, 0, h->p2p_recv_off);
+  if (e == cudaSuccess) e = cudaMalloc(&h->p2p_block_counter, sizeof(int));
+  if (e == cudaSuccess) e = cudaMemset(h->p2p_block_counter, 0, sizeof(int));
+  if (e == cudaSuccess) e = cudaMalloc(&h->p2p_peers_dev, G * sizeof(char*));
+  cudaIpcMemHandle_t mh;
+  if (e == cudaSuccess) e = cudaIpcGetMemHandle(&mh, h->p2p_region);
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) return cuda_fail(h, e, "peer-memory region");
+  memcpy(ipc_handle, &mh, sizeof(mh));
+  h->p2p_cap_rows = cap;
+  h->p2p_max_tokens = max_tokens;
+  return VMOE_OK;
+}
+
+int vmoe_ep_p2p_connect(vmoe_handle* h, const void* ipc_handles) {
+  if (!h || !ipc_handles) return VMOE_ERR_INVALID_ARG;
+  if (!h->p2p_region) return fail(h, VMOE_ERR_NOT_READY, "vmoe_ep_p2p_setup has not been called");
+  if (h->p2p_connected) return fail(h, VMOE_ERR_INVALID_ARG, "already connected");
+  DeviceGuard g(h->device);
+  const int G = h->ep_size;
+  h->p2p_peers.assign(G, nullptr);
+  const char* bytes = static_cast<const char*>(ipc_handles);
+  for (int r = 0; r < G; ++r) {
+    if (r == h->ep_rank) {
+      h->p2p_peers[r] = h->p2p_region;
+      continue;
+    }
+    cudaIpcMemHandle_t mh;
+    memcpy(&mh, bytes + static_cast<size_t>(r) * sizeof(mh), sizeof(mh));
+    void* p = nullptr;
+    cudaError_t e = cudaIpcOpenMemHandle(&p, mh, cudaIpcMemLazyEnablePeerAccess);
+    if (e != cudaSuccess) return cuda_fail(h, e, "cudaIpcOpenMemHandle of a peer region");
+    h->p2p_peers[r] = static_cast<char*>(p);
+  }
+  cudaError_t e = cudaMemcpy(h->p2p_peers_dev, h->p2p_peers.data(), G * sizeof(char*),
+                             cudaMemcpyHostToDevice);
+  if (e != cudaSuccess) return cuda_fail(h, e, "peer table");
+  h->p2p_connected = true;
+  return VMOE_OK;
+}
+
+int vmoe_ep_p2p_workspace_size(const vmoe_handle* h, int64_t tokens, size_t* bytes) {
+  if (!h || !bytes || tokens < 0) return VMOE_ERR_INVALID_ARG;
+  *bytes = make_p2p_plan(h, tokens).total;
+  return VMOE_OK;
+}
+
+int vmoe_ep_p2p_forward(vmoe_handle* h, const void* x, int64_t tokens, void* out,
+                        float* router_logits, float* aux_loss, void* workspace,
+                        size_t workspace_bytes, void* stream) {
+  if (!h) return VMOE_ERR_INVALID_ARG;
+  h->last_launches = 0;
+  if (!h->ready) return fail(h, VMOE_ERR_NOT_READY, "vmoe_set_weights has not been called");
+  if (!h->p2p_connected) return fail(h, VMOE_ERR_NOT_READY, "vmoe_ep_p2p_connect has not been called");
+  const int64_t E = h->E, K = h->K, H = h->H, T = tokens;
+  if (T < 0 || T > h->p2p_max_tokens)
+    return fail(h, VMOE_ERR_INVALID_ARG, "tokens must be in [0, %lld] (got %lld)",
+                static_cast<long long>(h->p2p_max_tokens), static_cast<long long>(T));
+  if (T > 0 && (!x || !out)) return fail(h, VMOE_ERR_INVALID_ARG, "x and out are required");
+  if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(out)) & 15u)
+    return fail(h, VMOE_ERR_INVALID_ARG, "x and out must be 16-byte aligned");
+  const P2PPlan p = make_p2p_plan(h, T);
+  if (!workspace || workspace_bytes < p.total)
+    return fail(h, VMOE_ERR_WORKSPACE, "workspace needs %zu bytes (got %zu)", p.total,
+                workspace ? workspace_bytes : static_cast<size_t>(0));
+  if (reinterpret_cast<uintptr_t>(workspace) & 255u)
+    return fail(h, VMOE_ERR_WORKSPACE, "workspace must be 256-byte aligned");
+  DeviceGuard g(h->device);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  char* ws = static_cast<char*>(workspace);
+  int32_t* idx = reinterpret_cast<int32_t*>(ws + p.idx);
+  float* tw = reinterpret_cast<float*>(ws + p.w);
+  int* hist = reinterpret_cast<int*>(ws + p.hist);
+  float* psum = reinterpret_cast<float*>(ws + p.psum);
+  int* excl = reinterpret_cast<int*>(ws + p.excl);
+  int* counts = reinterpret_cast<int*>(ws + p.counts);
+  float* psum_tot = reinterpret_cast<float*>(ws + p.psum_tot);
+  int* offs = reinterpret_cast<int*>(ws + p.offs);
+  float* aux = aux_loss ? aux_loss : reinterpret_cast<float*>(ws + p.aux);
+
+  P2PArgs a{};
+  a.peer_base = h->p2p_peers_dev;
+  a.sig_off = h->p2p_sig_off;
+  a.counts_off = h->p2p_counts_off;
+  a.recv_off = h->p2p_recv_off;
+  a.y_off = h->p2p_y_off;
+  a.me = h->ep_rank;
+  a.G = h->ep_size;
+  a.E = static_cast<int>(E);
+  a.El = static_cast<int>(h->E_local);
+  a.K = static_cast<int>(K);
+  a.H = H;
+  a.cap_rows = h->p2p_cap_rows;
+  a.epoch = ++h->p2p_epoch;
+  a.status = h->status;
+  a.block_counter = h->p2p_block_counter;
+  a.dest_rank = reinterpret_cast<int32_t*>(ws + p.drank);
+  a.dest_row = reinterpret_cast<int32_t*>(ws + p.drow);
+  a.tile_expert = reinterpret_cast<int*>(ws + p.tiles);
+  a.num_tiles = reinterpret_cast<int*>(ws + p.ntiles);
+
+  const bool prof = h->prof_count < h->prof_slots;
+  cudaEvent_t* ev = prof ? &h->prof_ev[static_cast<size_t>(h->prof_count) * (kStages + 1)] : nullptr;
+  int stage = 0;
+  auto mark = [&]() {
+    if (prof) cudaEventRecord(ev[stage], s);
+    ++stage;
+  };
+  auto check = [&](cudaError_t err, const char* what) -> int {
+    if (err != cudaSuccess) return cuda_fail(h, err, what);
+    ++h->last_launches;
+    return VMOE_OK;
+  };
+  int rc;
+  mark();  // router
+  if (T > 0) {
+    if ((rc = check(launch_router(h->dtype, x, h->w_r, h->b_r, T, static_cast<int>(H),
+                                  static_cast<int>(E), static_cast<int>(K), router_logits, idx,
+                                  tw, hist, psum, s), "router")) != VMOE_OK)
+      return rc;
+  }
+  mark();  // scan
+  if ((rc = check(launch_scan_blocks(hist, psum, p.nblk, static_cast<int>(E), excl, counts,
+                                     psum_tot, s), "scan")) != VMOE_OK)
+    return rc;
+  mark();  // plan (aux loss, counts) + publish counts to every rank
+  if ((rc = check(launch_plan(counts, psum_tot, T, static_cast<int>(E), static_cast<int>(K), 0, 1,
+                              offs, nullptr, nullptr, aux, nullptr, s), "plan")) != VMOE_OK)
+    return rc;
+  if ((rc = check(launch_p2p_publish(a, counts, s), "publish")) != VMOE_OK) return rc;
+  mark();  // dispatch over NVLink + wait for every rank's rows
+  if ((rc = check(launch_p2p_dispatch(h->dtype, a, x, idx, excl, T, s), "dispatch")) != VMOE_OK)
+    return rc;
+  if ((rc = check(launch_p2p_wait(a, 1, s), "wait rows")) != VMOE_OK) return rc;
+  mark();  // gemm1 (inside run_expert_gemms: gemm1, mark, gemm2)
+  if ((rc = run_expert_gemms(h, h->p2p_region + h->p2p_recv_off, h->p2p_cap_rows, a.tile_expert,
+                             a.num_tiles, ws + p.hbuf, h->p2p_region + h->p2p_y_off, H, s, mark,
+                             check)) != VMOE_OK)
+    return rc;
+  mark();  // signal outputs ready, wait for every rank's, combine over NVLink
+  if ((rc = check(launch_p2p_signal(a, 2, s), "signal outputs")) != VMOE_OK) return rc;
+  if ((rc = check(launch_p2p_wait(a, 2, s), "wait outputs")) != VMOE_OK) return rc;
+  if ((rc = check(launch_p2p_combine(h->dtype, a, idx, tw, T, out, s), "combine")) != VMOE_OK)
+    return rc;
+  mark();
+  if (prof) ++h->prof_count;
   return VMOE_OK;
 }
 

@@ -110,10 +110,18 @@ class ExpertParallelMoE:
 
     ``weights`` holds the GLOBAL stacked tensors of ``MoELayer.stacked_weights`` (router
     ``[E, H]``, experts ``[E, ...]``); each rank keeps the router and its own slice.
+
+    ``transport``:
+      * ``"p2p"`` (default) -- the exchange runs inside the kernels over NVLink peer memory
+        (``vmoe_ep_p2p_forward``): one call per forward, no host synchronisation; every rank
+        must call ``forward`` the same number of times with at most ``max_tokens`` tokens;
+      * ``"nccl"`` -- the staged path: route, NCCL all-to-all-v, experts, all-to-all-v back,
+        combine.
     """
 
     def __init__(self, config, weights: dict[str, torch.Tensor], device: torch.device,
-                 dtype: torch.dtype = torch.bfloat16, group=None):
+                 dtype: torch.dtype = torch.bfloat16, group=None, transport: str = "p2p",
+                 max_tokens: int | None = None):
         cfg = MoEConfig.from_any(config)
         cfg.validate()
         self.cfg, self.group, self.device, self.dtype = cfg, group, device, dtype
@@ -145,6 +153,26 @@ class ExpertParallelMoE:
         stream.synchronize()
         self.last_plan: ExchangePlan | None = None
         self.launches = 0
+        if transport not in ("p2p", "nccl"):
+            raise ValueError(f"transport must be 'p2p' or 'nccl', not {transport!r}")
+        self.transport = transport
+        self.max_tokens = max_tokens
+        self._p2p_ws = None
+        if transport == "p2p":
+            if max_tokens is None:
+                raise ValueError("transport='p2p' needs max_tokens (tokens per rank per forward)")
+            caps = [None] * self.world
+            dist.all_gather_object(caps, int(max_tokens), group=group)
+            if len(set(caps)) != 1:  # the symmetric regions must have one layout
+                raise ValueError(f"max_tokens differs across ranks: {caps}")
+            handle = ctypes.create_string_buffer(64)
+            _lib.check(self.lib.vmoe_ep_p2p_setup(self.h, int(max_tokens), handle), self.h,
+                       "vmoe_ep_p2p_setup")
+            handles = [None] * self.world
+            dist.all_gather_object(handles, handle.raw, group=group)
+            blob = ctypes.create_string_buffer(b"".join(handles), 64 * self.world)
+            _lib.check(self.lib.vmoe_ep_p2p_connect(self.h, blob), self.h, "vmoe_ep_p2p_connect")
+            dist.barrier(group=group)
         # set to a list to record (stage -> (start, end) CUDA events) for every forward
         self.stage_events: list[dict] | None = None
 
@@ -161,6 +189,48 @@ class ExpertParallelMoE:
 
     def forward(self, x: torch.Tensor):
         """x [T, H] on this rank -> (out [T, H], aux_loss of this rank's tokens)."""
+        if self.transport == "p2p":
+            return self._forward_p2p(x)
+        return self._forward_nccl(x)
+
+    def _forward_p2p(self, x: torch.Tensor):
+        lib, h, dev = self.lib, self.h, self.device
+        T, H = x.shape
+        x = x.contiguous()
+        n = ctypes.c_size_t()
+        _lib.check(lib.vmoe_ep_p2p_workspace_size(h, T, ctypes.byref(n)), h)
+        if self._p2p_ws is None or self._p2p_ws.numel() < n.value:
+            self._p2p_ws = torch.empty(max(n.value, 256), dtype=torch.uint8, device=dev)
+        out = torch.empty_like(x)
+        aux = torch.empty((), dtype=torch.float32, device=dev)
+        stream = ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
+        _lib.check(lib.vmoe_ep_p2p_forward(h, ctypes.c_void_p(x.data_ptr()), T,
+                                           ctypes.c_void_p(out.data_ptr()), None,
+                                           ctypes.c_void_p(aux.data_ptr()),
+                                           ctypes.c_void_p(self._p2p_ws.data_ptr()),
+                                           self._p2p_ws.numel(), stream), h, "vmoe_ep_p2p_forward")
+        self.launches = lib.vmoe_last_launch_count(h)
+        return out, aux
+
+    def set_profiling(self, forwards: int) -> None:
+        _lib.check(self.lib.vmoe_set_profiling(self.h, int(forwards)), self.h)
+
+    def stage_times(self):
+        buf = (ctypes.c_float * 16)()
+        n, f = ctypes.c_int(), ctypes.c_int()
+        _lib.check(self.lib.vmoe_stage_times(self.h, buf, 16, ctypes.byref(n), ctypes.byref(f)), self.h)
+        return {self.lib.vmoe_stage_name(i).decode(): float(buf[i]) for i in range(n.value)}, f.value
+
+    def device_status(self) -> int:
+        """The device status word (0 = fine; timeouts and bad-index codes otherwise); clears it."""
+        code = ctypes.c_int32()
+        rc = self.lib.vmoe_device_status(self.h, ctypes.byref(code),
+                                         ctypes.c_void_p(torch.cuda.current_stream(self.device).cuda_stream))
+        if rc not in (_lib.VMOE_OK, _lib.VMOE_ERR_TIMEOUT, _lib.VMOE_ERR_DEVICE_STATUS):
+            _lib.check(rc, self.h, "vmoe_device_status")
+        return code.value
+
+    def _forward_nccl(self, x: torch.Tensor):
         lib, h, dev = self.lib, self.h, self.device
         rec = {} if self.stage_events is not None else None
         self._mark(rec, "route")
@@ -231,6 +301,11 @@ class ExpertParallelMoE:
     __call__ = forward
 
     def close(self):
+        """Free this rank's handle.  Collective: peers may still be reading this rank's
+        expert outputs (or writing its receive buffer) until every rank is done, so all
+        ranks synchronise their devices and meet at a barrier before anything is freed."""
         if self.h:
+            torch.cuda.synchronize(self.device)
+            dist.barrier(group=self.group)
             self.lib.vmoe_destroy(self.h)
             self.h = ctypes.c_void_p()
