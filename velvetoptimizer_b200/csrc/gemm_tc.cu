@@ -1,24 +1,28 @@
-// bf16 grouped expert GEMMs on the 5th-generation tensor cores (tcgen05 + TMEM + TMA).
+// bf16 GEMMs on the 5th-generation tensor cores (tcgen05 + TMEM + TMA), three epilogues.
 //
 // Reference math (python/vesper/model.py):
-//   gated (gemm1): h = ERA(x_e Wg_e^T + bg_e) * (x_e Wu_e^T + bu_e)   :295-297, ERA :69-76
-//   plain (gemm2): y = h Wd_e^T + bd_e                                :298
+//   kGated  (expert gemm1): h = ERA(x_e Wg_e^T + bg_e) * (x_e Wu_e^T + bu_e)  :295-297, ERA :69-76
+//   kPlain  (expert gemm2): y = h Wd_e^T + bd_e                               :298
+//   kRouter (router)      : logits = x W_r^T + b_r, softmax, top-K, renormalise :322-329, plus
+//                           the per-128-token expert histogram and probability sums the
+//                           dispatch and the load-balancing loss (:366-385) consume
 //
 // Design (one CTA per SM, persistent over (M tile, N tile) work items):
-//   warp 0      TMA producer: A tile [128 x 64] and B tile [256 x 64] per k-block into a
-//               4-stage ring of 128B-swizzled shared-memory buffers;
-//   warp 1      allocates 512 TMEM columns (two 128 x 256 fp32 accumulators) and one
-//               thread issues tcgen05.mma (M=128, N=256, K=16) four times per k-block;
-//   warps 2..5  epilogue: tcgen05.ld of their 32 TMEM lanes, bias + ERA(gate) * up (or
-//               bias only), bf16 convert, store; the accumulator is double-buffered so
-//               the epilogue of tile i overlaps the main loop of tile i+1.
-// The gate/up weights are packed so that one 256-row B tile holds 128 gate rows followed
-// by the 128 up rows of the same output columns: one MMA chain produces both operands
-// of the gated product, and the activation never leaves the SM before it is multiplied.
+//   warp 0      TMA producer: A tile [128 x 64] and B tile [BN x 64] per k-block into a
+//               ring of 128B-swizzled shared-memory stages (4 stages at BN = 256, 8 at <= 64);
+//   warp 1      allocates TMEM (two 128 x BN fp32 accumulators) and one thread issues
+//               tcgen05.mma (M = 128, N = BN, K = 16) four times per k-block;
+//   warps 2..5  epilogue: tcgen05.ld of their 32 TMEM lanes (one row per thread); the
+//               accumulator is double-buffered so the epilogue of tile i overlaps the main
+//               loop of tile i + 1.
+// The gate/up weights are packed so that one 256-row B tile holds 128 gate rows followed by
+// the 128 up rows of the same output columns: one MMA chain produces both operands of the
+// gated product, and the activation never leaves the SM before it is multiplied.  The router
+// keeps each token's E logits in registers: softmax, top-K and the weights never touch HBM.
 //
-// Every mbarrier wait is bounded (kWaitLimitNs); on a timeout the kernel records a code
-// in the status word, stops issuing work, waits (bounded) for its own copies and MMAs in
-// flight, frees TMEM and returns.  No TMA multicast is used.
+// Every mbarrier wait is bounded (kWaitLimitNs); on a timeout the kernel records a code in
+// the status word, stops issuing work, waits (bounded) for its own copies and MMAs in flight,
+// frees TMEM and returns.  No TMA multicast is used.
 #include <cudaTypedefs.h>
 #include <stdio.h>
 
@@ -28,13 +32,22 @@
 namespace vmoe {
 namespace {
 
-constexpr int BN = 256, BK = 64, STAGES = 4;
-constexpr uint32_t A_BYTES = kTileM * BK * 2;  // 16 KB
-constexpr uint32_t B_BYTES = BN * BK * 2;      // 32 KB
-constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
-constexpr uint32_t TMEM_COLS = 2 * BN;         // 512: two accumulators
-constexpr uint32_t IDESC = umma_idesc_bf16(kTileM, BN);
+enum Epi { kPlain = 0, kGated = 1, kRouter = 2 };
 
+constexpr int BK = 64;
+constexpr uint32_t A_BYTES = kTileM * BK * 2;  // 16 KB
+
+template <int BN>
+struct TcCfg {
+  static constexpr uint32_t B_BYTES = BN * BK * 2;
+  static constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int STAGES_FIT = static_cast<int>((200u * 1024u) / STAGE_BYTES);
+  static constexpr int STAGES = STAGES_FIT > 8 ? 8 : STAGES_FIT;
+  static constexpr uint32_t TMEM_COLS = 2 * BN < 32 ? 32 : 2 * BN;  // power of two for BN in {16..256}
+  static constexpr uint32_t IDESC = umma_idesc_bf16(kTileM, BN);
+};
+
+template <int STAGES>
 struct TcShared {
   uint64_t full[STAGES];
   uint64_t empty[STAGES];
@@ -45,37 +58,135 @@ struct TcShared {
   int abort;
   int issued;
   int consumed;
+  // router epilogue scratch (E <= 64)
+  int ep_ok[4];
+  int hist[64];
+  float psum[4][64];
 };
 
-constexpr size_t SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + sizeof(TcShared) + 64;
+template <int BN>
+constexpr size_t tc_smem_bytes() {
+  return 1024 + TcCfg<BN>::STAGES * TcCfg<BN>::STAGE_BYTES + sizeof(TcShared<TcCfg<BN>::STAGES>) + 64;
+}
 
-__device__ __forceinline__ bool aborted(const TcShared* sh) {
+template <int STAGES>
+__device__ __forceinline__ bool aborted(const TcShared<STAGES>* sh) {
   return *reinterpret_cast<const volatile int*>(&sh->abort) != 0;
 }
-__device__ __forceinline__ void set_abort(TcShared* sh, int* status, int code) {
+template <int STAGES>
+__device__ __forceinline__ void set_abort(TcShared<STAGES>* sh, int* status, int code) {
   *reinterpret_cast<volatile int*>(&sh->abort) = 1;
   report(status, code);
 }
 
 // Expert of M tile m, clamped into range (a bad map only produces a status code).
 __device__ __forceinline__ int expert_of(const TcGemmArgs& args, int m) {
+  if (!args.tile_expert) return 0;
   const int e = args.tile_expert[m];
   if (static_cast<unsigned>(e) < static_cast<unsigned>(args.num_experts)) return e;
   report(args.status, kStatusBadExpert);
   return 0;
 }
 
-template <bool GATED>
+__device__ __forceinline__ void epilogue_bar() {  // the 4 epilogue warps only
+  asm volatile("bar.sync 1, 128;" ::: "memory");
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// Router epilogue for one 128-token tile: each thread owns one token's logits.
+template <int BN, int STAGES>
+__device__ __forceinline__ void router_epilogue(const TcGemmArgs& args, TcShared<STAGES>* sh,
+                                                uint32_t t_row, int m, int q, int lane) {
+  float lg[BN];
+#pragma unroll
+  for (int c = 0; c < BN; c += 16) tmem_ld16(t_row + c, lg + c);
+  const int E = args.num_experts, K = args.top_k;
+  const int64_t t = static_cast<int64_t>(m) * kTileM + q * 32 + lane;
+  const bool valid = t < args.tokens;
+#pragma unroll
+  for (int e = 0; e < BN; ++e) lg[e] = e < E ? lg[e] + args.bias[e] : -INFINITY;
+  if (valid && args.logits) {
+    float* dst = args.logits + t * E;
+#pragma unroll
+    for (int e = 0; e < BN; ++e)
+      if (e < E) dst[e] = lg[e];
+  }
+  // softmax (model.py:323): exp(l - max) / sum, summed in ascending expert order
+  float mx = -INFINITY;
+#pragma unroll
+  for (int e = 0; e < BN; ++e) mx = fmaxf(mx, lg[e]);
+  float s = 0.f;
+#pragma unroll
+  for (int e = 0; e < BN; ++e) {
+    const float p = e < E ? expf(lg[e] - mx) : 0.f;
+    lg[e] = p;
+    s += p;
+  }
+#pragma unroll
+  for (int e = 0; e < BN; ++e) lg[e] = lg[e] / s;
+  // top-K by (p desc, index asc) (model.py:326): strict '>' keeps the lowest index
+  int sel[32];
+  float vsum = 0.f;
+  uint64_t taken = 0;
+  for (int k = 0; k < K; ++k) {
+    int best = -1;
+    float bv = -INFINITY;
+#pragma unroll
+    for (int e = 0; e < BN; ++e) {
+      const bool free_e = e < E && !((taken >> e) & 1ull);
+      if (free_e && (best < 0 || lg[e] > bv)) { best = e; bv = lg[e]; }
+    }
+    taken |= 1ull << best;
+    sel[k] = best;
+    vsum += bv;
+  }
+  if (valid) {
+    for (int k = 0; k < K; ++k) {
+      float v = 0.f;
+#pragma unroll
+      for (int e = 0; e < BN; ++e) v = e == sel[k] ? lg[e] : v;
+      args.topk_idx[t * K + k] = sel[k];
+      args.topk_w[t * K + k] = v / vsum;  // model.py:329
+    }
+  }
+  // per-tile histogram and probability column sums, fixed reduction order
+  const int et = q * 32 + lane;  // 0..127 over the four epilogue warps
+  epilogue_bar();                // the previous tile's readers of sh->hist / sh->psum are done
+  if (et < E) sh->hist[et] = 0;
+  epilogue_bar();
+  if (valid)
+    for (int k = 0; k < K; ++k) atomicAdd(&sh->hist[sel[k]], 1);
+#pragma unroll
+  for (int e = 0; e < BN; ++e) {
+    const float v = warp_sum(valid && e < E ? lg[e] : 0.f);
+    if (lane == 0 && e < E) sh->psum[q][e] = v;
+  }
+  epilogue_bar();
+  if (et < E) {
+    args.psum[static_cast<int64_t>(m) * E + et] =
+        ((sh->psum[0][et] + sh->psum[1][et]) + sh->psum[2][et]) + sh->psum[3][et];
+    args.hist[static_cast<int64_t>(m) * E + et] = sh->hist[et];
+  }
+}
+
+template <int EPI, int BN>
 __global__ void __launch_bounds__(192, 1)
 tc_gemm_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_constant__ CUtensorMap b_map,
                const TcGemmArgs args) {
+  using Cfg = TcCfg<BN>;
+  constexpr int STAGES = Cfg::STAGES;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
   uint8_t* gbase = smem_raw + (base - raw);
   const uint32_t a_s = base;
   const uint32_t b_s = base + STAGES * A_BYTES;
-  TcShared* sh = reinterpret_cast<TcShared*>(gbase + STAGES * STAGE_BYTES);
+  auto* sh = reinterpret_cast<TcShared<STAGES>*>(gbase + STAGES * Cfg::STAGE_BYTES);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
@@ -96,14 +207,14 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_constant_
     prefetch_tmap(&a_map);
     prefetch_tmap(&b_map);
   }
-  if (warp == 1) tmem_alloc(smem_u32(&sh->tmem_base), TMEM_COLS);
+  if (warp == 1) tmem_alloc(smem_u32(&sh->tmem_base), Cfg::TMEM_COLS);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = sh->tmem_base;
 
   const int n_tiles = args.n_tiles, k_blocks = args.k_blocks;
-  int num_m = *args.num_m_tiles;
+  int num_m = args.num_m_tiles ? *args.num_m_tiles : args.m_tiles_host;
   if (num_m > args.max_m_tiles || num_m < 0) {  // never write past the output buffer
     if (threadIdx.x == 0) report(args.status, kStatusBadTileCount);
     num_m = num_m < 0 ? 0 : args.max_m_tiles;
@@ -130,9 +241,9 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_constant_
           }
           if (aborted(sh)) { ok = false; break; }
           const uint32_t fb = smem_u32(&sh->full[s]);
-          mbar_arrive_expect_tx(fb, STAGE_BYTES);
+          mbar_arrive_expect_tx(fb, Cfg::STAGE_BYTES);
           tma_load_2d(a_s + s * A_BYTES, &a_map, fb, kb * BK, a_row);
-          tma_load_2d(b_s + s * B_BYTES, &b_map, fb, kb * BK, b_row);
+          tma_load_2d(b_s + s * Cfg::B_BYTES, &b_map, fb, kb * BK, b_row);
           *reinterpret_cast<volatile int*>(&sh->issued) = it + 1;
         }
         if (!ok) break;
@@ -161,11 +272,11 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_constant_
             break;
           }
           tc_fence_after();
-          const uint32_t a_addr = a_s + s * A_BYTES, b_addr = b_s + s * B_BYTES;
+          const uint32_t a_addr = a_s + s * A_BYTES, b_addr = b_s + s * Cfg::B_BYTES;
 #pragma unroll
           for (int k = 0; k < BK / 16; ++k) {
             umma_bf16(d_tmem, umma_desc_sw128(a_addr + k * 32), umma_desc_sw128(b_addr + k * 32),
-                      IDESC, (kb | k) != 0 ? 1u : 0u);
+                      Cfg::IDESC, (kb | k) != 0 ? 1u : 0u);
           }
           umma_commit(smem_u32(&sh->empty[s]));
           *reinterpret_cast<volatile int*>(&sh->consumed) = it + 1;
@@ -187,51 +298,66 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_constant_
       const uint32_t aph = (local >> 1) & 1;
       const bool got = mbar_wait(smem_u32(&sh->tfull[acc]), aph);
       __syncwarp();
-      if (!__all_sync(0xffffffffu, got)) {
+      const bool warp_ok = __all_sync(0xffffffffu, got);
+      if constexpr (EPI == kRouter) {
+        // the router epilogue synchronises the four epilogue warps, so they must agree
+        // on whether to go on (each warp's wait above is bounded)
+        if (lane == 0) sh->ep_ok[q] = warp_ok ? 1 : 0;
+        epilogue_bar();
+        const bool all_ok = sh->ep_ok[0] && sh->ep_ok[1] && sh->ep_ok[2] && sh->ep_ok[3];
+        if (!all_ok) {
+          if (lane == 0 && !warp_ok) set_abort(sh, args.status, kStatusTimeoutEpilogue);
+          break;
+        }
+      } else if (!warp_ok) {
         if (lane == 0) set_abort(sh, args.status, kStatusTimeoutEpilogue);
         break;
       }
       tc_fence_after();
       const int m = tile / n_tiles, n = tile - m * n_tiles;
-      const int e = expert_of(args, m);
-      const int64_t row = static_cast<int64_t>(m) * kTileM + q * 32 + lane;
       const uint32_t t_row = tmem + (static_cast<uint32_t>(q * 32) << 16) + acc * BN;
-      __nv_bfloat16* outp = static_cast<__nv_bfloat16*>(args.out) + row * args.ldo;
-      const float* bias = args.bias + static_cast<int64_t>(e) * args.bias_ld + n * BN;
-      if constexpr (GATED) {
-        outp += n * (BN / 2);
-#pragma unroll 1
-        for (int c = 0; c < BN / 2; c += 32) {
-          float g[32], u[32];
-          tmem_ld32(t_row + c, g);
-          tmem_ld32(t_row + BN / 2 + c, u);
-          uint32_t packed[16];
-#pragma unroll
-          for (int j = 0; j < 32; j += 2) {
-            const float h0 = era_fast(g[j] + bias[c + j], args.gamma) * (u[j] + bias[BN / 2 + c + j]);
-            const float h1 =
-                era_fast(g[j + 1] + bias[c + j + 1], args.gamma) * (u[j + 1] + bias[BN / 2 + c + j + 1]);
-            packed[j / 2] = pack_bf16x2(h0, h1);
-          }
-          uint4* dst = reinterpret_cast<uint4*>(outp + c);
-#pragma unroll
-          for (int v = 0; v < 4; ++v)
-            dst[v] = make_uint4(packed[4 * v], packed[4 * v + 1], packed[4 * v + 2], packed[4 * v + 3]);
-        }
+      if constexpr (EPI == kRouter) {
+        router_epilogue<BN>(args, sh, t_row, m, q, lane);
       } else {
-        outp += n * BN;
+        const int e = expert_of(args, m);
+        const int64_t row = static_cast<int64_t>(m) * kTileM + q * 32 + lane;
+        __nv_bfloat16* outp = static_cast<__nv_bfloat16*>(args.out) + row * args.ldo;
+        const float* bias = args.bias + static_cast<int64_t>(e) * args.bias_ld + n * BN;
+        if constexpr (EPI == kGated) {
+          outp += n * (BN / 2);
 #pragma unroll 1
-        for (int c = 0; c < BN; c += 32) {
-          float v32[32];
-          tmem_ld32(t_row + c, v32);
-          uint32_t packed[16];
+          for (int c = 0; c < BN / 2; c += 32) {
+            float g[32], u[32];
+            tmem_ld32(t_row + c, g);
+            tmem_ld32(t_row + BN / 2 + c, u);
+            uint32_t packed[16];
 #pragma unroll
-          for (int j = 0; j < 32; j += 2)
-            packed[j / 2] = pack_bf16x2(v32[j] + bias[c + j], v32[j + 1] + bias[c + j + 1]);
-          uint4* dst = reinterpret_cast<uint4*>(outp + c);
+            for (int j = 0; j < 32; j += 2) {
+              const float h0 = era_fast(g[j] + bias[c + j], args.gamma) * (u[j] + bias[BN / 2 + c + j]);
+              const float h1 = era_fast(g[j + 1] + bias[c + j + 1], args.gamma) *
+                               (u[j + 1] + bias[BN / 2 + c + j + 1]);
+              packed[j / 2] = pack_bf16x2(h0, h1);
+            }
+            uint4* dst = reinterpret_cast<uint4*>(outp + c);
 #pragma unroll
-          for (int v = 0; v < 4; ++v)
-            dst[v] = make_uint4(packed[4 * v], packed[4 * v + 1], packed[4 * v + 2], packed[4 * v + 3]);
+            for (int v = 0; v < 4; ++v)
+              dst[v] = make_uint4(packed[4 * v], packed[4 * v + 1], packed[4 * v + 2], packed[4 * v + 3]);
+          }
+        } else {
+          outp += n * BN;
+#pragma unroll 1
+          for (int c = 0; c < BN; c += 32) {
+            float v32[32];
+            tmem_ld32(t_row + c, v32);
+            uint32_t packed[16];
+#pragma unroll
+            for (int j = 0; j < 32; j += 2)
+              packed[j / 2] = pack_bf16x2(v32[j] + bias[c + j], v32[j + 1] + bias[c + j + 1]);
+            uint4* dst = reinterpret_cast<uint4*>(outp + c);
+#pragma unroll
+            for (int v = 0; v < 4; ++v)
+              dst[v] = make_uint4(packed[4 * v], packed[4 * v + 1], packed[4 * v + 2], packed[4 * v + 3]);
+          }
         }
       }
       tc_fence_before();
@@ -256,8 +382,22 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_constant_
   if (warp == 1) {
     __syncwarp();
     tc_fence_after();
-    tmem_dealloc(tmem, TMEM_COLS);
+    tmem_dealloc(tmem, Cfg::TMEM_COLS);
   }
+}
+
+template <int EPI, int BN>
+cudaError_t launch_cfg(const CUtensorMap& a_map, const CUtensorMap& b_map, const TcGemmArgs& args,
+                       int64_t work, int num_sms, cudaStream_t s) {
+  constexpr size_t smem = tc_smem_bytes<BN>();
+  static_assert(smem <= 232448, "shared memory budget");
+  const int grid = static_cast<int>(work < num_sms ? (work > 0 ? work : 1) : num_sms);
+  auto kern = tc_gemm_kernel<EPI, BN>;
+  cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(smem));
+  if (err != cudaSuccess) return err;
+  kern<<<grid, 192, smem, s>>>(a_map, b_map, args);
+  return cudaGetLastError();
 }
 
 PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
@@ -306,20 +446,26 @@ cudaError_t launch_tc_gemm(bool gated, const CUtensorMap& a_map, const CUtensorM
                            const TcGemmArgs& args, int64_t max_tiles, int num_sms,
                            cudaStream_t s) {
   const int64_t work = max_tiles * args.n_tiles;
-  const int grid = static_cast<int>(work < num_sms ? (work > 0 ? work : 1) : num_sms);
-  cudaError_t err;
-  if (gated) {
-    err = cudaFuncSetAttribute(tc_gemm_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               static_cast<int>(SMEM_BYTES));
-    if (err != cudaSuccess) return err;
-    tc_gemm_kernel<true><<<grid, 192, SMEM_BYTES, s>>>(a_map, b_map, args);
-  } else {
-    err = cudaFuncSetAttribute(tc_gemm_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               static_cast<int>(SMEM_BYTES));
-    if (err != cudaSuccess) return err;
-    tc_gemm_kernel<false><<<grid, 192, SMEM_BYTES, s>>>(a_map, b_map, args);
+  if (gated) return launch_cfg<kGated, 256>(a_map, b_map, args, work, num_sms, s);
+  return launch_cfg<kPlain, 256>(a_map, b_map, args, work, num_sms, s);
+}
+
+int tc_router_width(int E) {
+  if (E <= 16) return 16;
+  if (E <= 32) return 32;
+  if (E <= 64) return 64;
+  return 0;  // wider routers use the CUDA-core kernel
+}
+
+cudaError_t launch_tc_router(const CUtensorMap& x_map, const CUtensorMap& w_map,
+                             const TcGemmArgs& args, int num_sms, cudaStream_t s) {
+  const int64_t work = args.m_tiles_host;
+  switch (tc_router_width(args.num_experts)) {
+    case 16: return launch_cfg<kRouter, 16>(x_map, w_map, args, work, num_sms, s);
+    case 32: return launch_cfg<kRouter, 32>(x_map, w_map, args, work, num_sms, s);
+    case 64: return launch_cfg<kRouter, 64>(x_map, w_map, args, work, num_sms, s);
+    default: return cudaErrorInvalidValue;
   }
-  return cudaGetLastError();
 }
 
 }  // namespace vmoe

@@ -59,10 +59,19 @@ cudaError_t launch_simt_gemm2(const float* a, int64_t lda, const float* wd, cons
 
 // ---- bf16 expert GEMMs (tcgen05 + TMEM + TMA) ----------------------------------------
 struct TcGemmArgs {
-  const int* num_m_tiles;   // device scalar
-  const int* tile_expert;   // [max_tiles]
+  const int* num_m_tiles;   // device scalar, or null: m_tiles_host is used
+  int m_tiles_host;
+  const int* tile_expert;   // [max_tiles], or null: every tile uses weight block 0
   int max_m_tiles;          // tiles the output buffer holds (bounds num_m_tiles)
-  int num_experts;          // experts the weights hold (bounds tile_expert)
+  int num_experts;          // experts the weights hold (bounds tile_expert); router: E
+  // router epilogue
+  int64_t tokens;           // valid rows of A
+  int top_k;
+  float* logits;            // [T, E] or null
+  int32_t* topk_idx;        // [T, K]
+  float* topk_w;            // [T, K]
+  int* hist;                // [ceil(T/128), E]
+  float* psum;              // [ceil(T/128), E]
   int n_tiles;              // output tiles per expert along N
   int k_blocks;             // ceil(K / 64)
   int b_rows_per_expert;    // rows of the 2-D weight view per expert
@@ -78,6 +87,13 @@ struct TcGemmArgs {
 cudaError_t launch_tc_gemm(bool gated, const CUtensorMap& a_map, const CUtensorMap& b_map,
                            const TcGemmArgs& args, int64_t max_tiles, int num_sms,
                            cudaStream_t s);
+
+// Router on the tensor cores: logits = x W_r^T (+ bias in `args.bias`), softmax, top-K,
+// renormalised weights, per-128-token histogram and probability sums.  E <= 64;
+// tc_router_width(E) is the N tile (16, 32 or 64), 0 when E is too wide.
+int tc_router_width(int E);
+cudaError_t launch_tc_router(const CUtensorMap& x_map, const CUtensorMap& w_map,
+                             const TcGemmArgs& args, int num_sms, cudaStream_t s);
 
 // Build a 2-D bf16 tensor map: [rows, cols] row-major with `ld` elements per row, box
 // {64 cols, box_rows rows}, 128-byte swizzle.  Returns false on failure.

@@ -84,6 +84,8 @@ struct vmoe_handle {
   float* b_d = nullptr; // [E, Hpad]
   int* status = nullptr;
   CUtensorMap map_wgu{}, map_wd{};
+  CUtensorMap map_wr{};   // router weights for the tensor-core router (bf16, E <= 64)
+  int router_bn = 0;      // its N tile; 0 = CUDA-core router
   bool ready = false;
   // profiling ring: prof_slots forwards x (kStages + 1) events
   int prof_slots = 0;
@@ -342,6 +344,45 @@ int run_expert_gemms(vmoe_handle* h, void* xp, int64_t max_rows, const int* tile
   return check(launch_tc_gemm(false, map_h, h->map_wd, a2, max_tiles, h->num_sms, s), "gemm2");
 }
 
+// Router + softmax + top-K + per-block histogram / probability sums: on the tensor cores
+// for bf16 with E <= 64, on CUDA cores otherwise (fp32 parity, or wider routers).
+int run_router(vmoe_handle* h, const void* x, int64_t T, float* logits, int32_t* idx, float* tw,
+               int* hist, float* psum, cudaStream_t s) {
+  const int64_t H = h->H;
+  cudaError_t e;
+  if (h->dtype == kBF16 && h->router_bn > 0) {
+    char why[256];
+    CUtensorMap map_x;
+    if (!make_tmap_bf16(&map_x, x, T, H, H, kTileM, why, sizeof(why)))
+      return fail(h, VMOE_ERR_CUDA, "x tensor map: %s", why);
+    TcGemmArgs a{};
+    a.num_m_tiles = nullptr;
+    a.m_tiles_host = static_cast<int>((T + kTileM - 1) / kTileM);
+    a.tile_expert = nullptr;
+    a.max_m_tiles = a.m_tiles_host;
+    a.num_experts = static_cast<int>(h->E);
+    a.n_tiles = 1;
+    a.k_blocks = static_cast<int>((H + 63) / 64);
+    a.b_rows_per_expert = 0;
+    a.bias = h->b_r;
+    a.status = h->status;
+    a.tokens = T;
+    a.top_k = static_cast<int>(h->K);
+    a.logits = logits;
+    a.topk_idx = idx;
+    a.topk_w = tw;
+    a.hist = hist;
+    a.psum = psum;
+    e = launch_tc_router(map_x, h->map_wr, a, h->num_sms, s);
+  } else {
+    e = launch_router(h->dtype, x, h->w_r, h->b_r, T, static_cast<int>(H), static_cast<int>(h->E),
+                      static_cast<int>(h->K), logits, idx, tw, hist, psum, s);
+  }
+  if (e != cudaSuccess) return cuda_fail(h, e, "router");
+  ++h->last_launches;
+  return VMOE_OK;
+}
+
 }  // namespace
 
 namespace vmoe {
@@ -549,6 +590,11 @@ int vmoe_set_weights(vmoe_handle* h, const vmoe_weights* w, void* stream) {
   }
   if (bf16) {
     char why[256];
+    h->router_bn = tc_router_width(static_cast<int>(E));
+    if (h->router_bn &&
+        !make_tmap_bf16(&h->map_wr, h->w_r, E, H, H, static_cast<uint32_t>(h->router_bn), why,
+                        sizeof(why)))
+      return fail(h, VMOE_ERR_CUDA, "router tensor map: %s", why);
     if (!make_tmap_bf16(&h->map_wgu, h->w_g, El * 2 * Ipad, H, H, 256, why, sizeof(why)))
       return fail(h, VMOE_ERR_CUDA, "gate/up tensor map: %s", why);
     if (!make_tmap_bf16(&h->map_wd, h->w_d, El * Hpad, Ipad, Ipad, 256, why, sizeof(why)))
@@ -651,11 +697,7 @@ int vmoe_forward(vmoe_handle* h, const void* x, int64_t tokens, void* out, float
   };
   int rc;
   mark();
-  if ((rc = check(launch_router(h->dtype, x, h->w_r, h->b_r, T, static_cast<int>(H),
-                                static_cast<int>(E), static_cast<int>(K), router_logits, idx, tw,
-                                hist, psum, s),
-                  "router")) != VMOE_OK)
-    return rc;
+  if ((rc = run_router(h, x, T, router_logits, idx, tw, hist, psum, s)) != VMOE_OK) return rc;
   mark();
   if ((rc = check(launch_scan_blocks(hist, psum, p.nblk, static_cast<int>(E), excl, counts,
                                      psum_tot, s),
@@ -777,10 +819,7 @@ int vmoe_ep_route(vmoe_handle* h, const void* x, int64_t tokens, void* send_rows
     ++h->last_launches;
     return VMOE_OK;
   };
-  if ((rc = check(launch_router(h->dtype, x, h->w_r, h->b_r, T, static_cast<int>(H),
-                                static_cast<int>(E), static_cast<int>(K), router_logits, idx, tw,
-                                hist, psum, s), "router")) != VMOE_OK)
-    return rc;
+  if ((rc = run_router(h, x, T, router_logits, idx, tw, hist, psum, s)) != VMOE_OK) return rc;
   if ((rc = check(launch_scan_blocks(hist, psum, p.nblk, static_cast<int>(E), excl, counts,
                                      psum_tot, s), "scan")) != VMOE_OK)
     return rc;
@@ -987,12 +1026,8 @@ int vmoe_ep_p2p_forward(vmoe_handle* h, const void* x, int64_t tokens, void* out
   };
   int rc;
   mark();  // router
-  if (T > 0) {
-    if ((rc = check(launch_router(h->dtype, x, h->w_r, h->b_r, T, static_cast<int>(H),
-                                  static_cast<int>(E), static_cast<int>(K), router_logits, idx,
-                                  tw, hist, psum, s), "router")) != VMOE_OK)
-      return rc;
-  }
+  if (T > 0 && (rc = run_router(h, x, T, router_logits, idx, tw, hist, psum, s)) != VMOE_OK)
+    return rc;
   mark();  // scan
   if ((rc = check(launch_scan_blocks(hist, psum, p.nblk, static_cast<int>(E), excl, counts,
                                      psum_tot, s), "scan")) != VMOE_OK)
