@@ -120,7 +120,7 @@ VMOE_API int vmoe_workspace_size(const vmoe_handle* h, int64_t tokens, size_t* b
  * loading this library reserves until the process exits.  It calls no allocator.
  *  - tokens whose vmoe_workspace_size exceeds that size are rejected with
  *    VMOE_ERR_WORKSPACE (e.g. 64 decode tokens at H 2048, I 8192, E 8, K 2 need
- *    about 27 MiB);
+ *    about 54 MiB);
  *  - the first call on each device looks up the array's device address
  *    (cudaGetSymbolAddress) -- make that first call before any stream capture;
  *  - all calls share the array: calls whose GPU work overlaps race and corrupt each
@@ -243,6 +243,11 @@ VMOE_API const char* vmoe_stage_name(int stage);
 
 /* Number of kernel launches the last vmoe_forward enqueued. */
 VMOE_API int vmoe_last_launch_count(const vmoe_handle* h);
+
+/* Rows of one grouped-GEMM M tile (128, or 256 when a pair of CTAs shares each tile):
+ * expert segments are padded to this, and vmoe_ep_experts' tile_expert has one entry per
+ * tile of this many rows.  Not part of the reference. */
+VMOE_API int vmoe_gemm_tile_rows(const vmoe_handle* h);
 
 /* Last error message of this handle ("" if none), and a static text per code. */
 VMOE_API const char* vmoe_last_error(const vmoe_handle* h);

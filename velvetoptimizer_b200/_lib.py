@@ -35,7 +35,7 @@ EXPORTED = (
     "vmoe_last_launch_count", "vmoe_last_error", "vmoe_status_string", "vmoe_abi_version",
     "vmoe_create_ep", "vmoe_ep_workspace_size", "vmoe_ep_route", "vmoe_ep_experts",
     "vmoe_ep_combine", "vmoe_ep_p2p_setup", "vmoe_ep_p2p_connect", "vmoe_ep_p2p_workspace_size",
-    "vmoe_ep_p2p_forward",
+    "vmoe_ep_p2p_forward", "vmoe_gemm_tile_rows",
 )
 
 
@@ -134,6 +134,8 @@ def load() -> ctypes.CDLL:
     lib.vmoe_stage_name.restype = c_char_p
     lib.vmoe_last_launch_count.argtypes = [H]
     lib.vmoe_last_launch_count.restype = c_int
+    lib.vmoe_gemm_tile_rows.argtypes = [H]
+    lib.vmoe_gemm_tile_rows.restype = c_int
     lib.vmoe_last_error.argtypes = [H]
     lib.vmoe_last_error.restype = c_char_p
     lib.vmoe_status_string.argtypes = [c_int]

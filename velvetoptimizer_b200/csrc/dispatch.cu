@@ -87,7 +87,7 @@ plan_kernel(const int* __restrict__ counts, const float* __restrict__ psum_tot, 
     int run = 0;
     for (int e = 0; e < E; ++e) { off_s[e] = run; run += pad_s[e]; }
     off_s[E] = run;
-    if (num_tiles) *num_tiles = run / kTileM;
+    if (num_tiles) *num_tiles = run / row_align;
     // Switch load-balancing loss (model.py:366-385), fixed summation order
     const float inv_tk = 1.0f / static_cast<float>(T * K);
     const float inv_t = 1.0f / static_cast<float>(T);
@@ -101,8 +101,8 @@ plan_kernel(const int* __restrict__ counts, const float* __restrict__ psum_tot, 
   }
   __syncthreads();
   for (int e = tid; e <= E; e += blockDim.x) offs[e] = off_s[e];
-  if (tile_expert && tid < E) {
-    const int t0 = off_s[tid] / kTileM, nt = pad_s[tid] / kTileM;
+  if (tile_expert && tid < E) {  // one entry per row_align-row GEMM tile
+    const int t0 = off_s[tid] / row_align, nt = pad_s[tid] / row_align;
     for (int j = 0; j < nt; ++j) tile_expert[t0 + j] = tid;
   }
 }

@@ -115,7 +115,7 @@ p2p_dispatch_kernel(P2PArgs a, const T* __restrict__ x, const int32_t* __restric
       for (int j = 0; j < el; ++j) {
         int64_t n = 0;
         for (int s = 0; s < G; ++s) n += cnt[s * E + d * El + j];
-        off += (n + kTileM - 1) / kTileM * kTileM;
+        off += (n + a.row_align - 1) / a.row_align * a.row_align;
       }
       for (int s = 0; s < a.me; ++s) off += cnt[s * E + e];
       const int64_t end = off + cnt[a.me * E + e];
@@ -132,8 +132,8 @@ p2p_dispatch_kernel(P2PArgs a, const T* __restrict__ x, const int32_t* __restric
       for (int el = 0; el < El; ++el) {
         int64_t n = 0;
         for (int s = 0; s < G; ++s) n += cnt[s * E + a.me * El + el];
-        const int64_t tiles = (n + kTileM - 1) / kTileM;
-        if ((t0 + tiles) * kTileM > a.cap_rows) { report(a.status, kStatusCapacity); break; }
+        const int64_t tiles = (n + a.row_align - 1) / a.row_align;
+        if ((t0 + tiles) * a.row_align > a.cap_rows) { report(a.status, kStatusCapacity); break; }
         for (int64_t j = 0; j < tiles; ++j) a.tile_expert[t0 + j] = el;
         t0 += tiles;
       }

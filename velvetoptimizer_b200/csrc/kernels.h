@@ -88,6 +88,12 @@ cudaError_t launch_tc_gemm(bool gated, const CUtensorMap& a_map, const CUtensorM
                            const TcGemmArgs& args, int64_t max_tiles, int num_sms,
                            cudaStream_t s);
 
+// Same GEMMs on CTA pairs (tcgen05.mma.cta_group::2): 256-row pair tiles, tile_expert
+// holds one expert per 256-row tile, B tensor maps have 128-row boxes (each CTA loads half).
+cudaError_t launch_tc_gemm_pair(bool gated, const CUtensorMap& a_map, const CUtensorMap& b_map,
+                                const TcGemmArgs& args, int64_t max_pair_tiles, int num_sms,
+                                cudaStream_t s);
+
 // Router on the tensor cores: logits = x W_r^T (+ bias in `args.bias`), softmax, top-K,
 // renormalised weights, per-128-token histogram and probability sums.  E <= 64;
 // tc_router_width(E) is the N tile (16, 32 or 64), 0 when E is too wide.
@@ -107,6 +113,7 @@ struct P2PArgs {
   int me, G, E, El, K;
   int64_t H;
   int64_t cap_rows;         // rows of recv / y
+  int row_align;            // GEMM tile rows: expert segments are padded to this
   unsigned epoch;           // this forward's flag value
   int* status;
   int* block_counter;       // local, zero between forwards

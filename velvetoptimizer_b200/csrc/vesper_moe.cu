@@ -12,6 +12,7 @@
 #include <cuda_runtime.h>
 #include <stdarg.h>
 #include <stdio.h>
+#include <stdlib.h>
 #include <string.h>
 
 #include <new>
@@ -84,6 +85,7 @@ struct vmoe_handle {
   float* b_d = nullptr; // [E, Hpad]
   int* status = nullptr;
   CUtensorMap map_wgu{}, map_wd{};
+  int tile_rows = kTileM;  // GEMM M tile: 256 with CTA-pair GEMMs (bf16), else 128
   CUtensorMap map_wr{};   // router weights for the tensor-core router (bf16, E <= 64)
   int router_bn = 0;      // its N tile; 0 = CUDA-core router
   bool ready = false;
@@ -124,14 +126,15 @@ Plan make_plan(const vmoe_handle* h, int64_t T) {
   const int64_t E = h->E, K = h->K;
   const size_t elt = dtype_bytes(h->dtype);
   p.nblk = static_cast<int>((T + kTileM - 1) / kTileM);
-  int64_t rows_bound = T * K + E * (kTileM - 1);
+  const int64_t tr = h->tile_rows;
+  int64_t rows_bound = T * K + E * (tr - 1);
   if (h->cfg.capacity > 0) {
-    const int64_t cap_rows = E * round_up(h->cfg.capacity, kTileM);
+    const int64_t cap_rows = E * round_up(h->cfg.capacity, tr);
     if (cap_rows < rows_bound) rows_bound = cap_rows;
   }
-  p.max_tiles = (rows_bound + kTileM - 1) / kTileM;
+  p.max_tiles = (rows_bound + tr - 1) / tr;
   if (p.max_tiles < 1) p.max_tiles = 1;
-  p.max_rows = p.max_tiles * kTileM;
+  p.max_rows = p.max_tiles * tr;
   p.idx = take(T * K * 4);
   p.w = take(T * K * 4);
   p.hist = take(static_cast<size_t>(p.nblk) * E * 4);
@@ -213,7 +216,7 @@ P2PPlan make_p2p_plan(const vmoe_handle* h, int64_t T) {
   p.aux = take(4);
   p.drank = take(T * K * 4);
   p.drow = take(T * K * 4);
-  p.tiles = take((cap / kTileM + 1) * 4);
+  p.tiles = take((cap / h->tile_rows + 1) * 4);
   p.ntiles = take(4);
   p.hbuf = take(static_cast<size_t>(cap) * h->Ipad * dtype_bytes(h->dtype));
   p.total = off;
@@ -286,7 +289,7 @@ template <typename Mark, typename Check>
 int run_expert_gemms(vmoe_handle* h, void* xp, int64_t max_rows, const int* tiles,
                      const int* ntiles, void* hb, void* yb, int64_t y_ld, cudaStream_t s,
                      Mark&& mark, Check&& check) {
-  const int64_t H = h->H, max_tiles = max_rows / kTileM;
+  const int64_t H = h->H, max_tiles = max_rows / h->tile_rows;
   int rc;
   if (h->dtype == kF32) {
     if ((rc = check(launch_simt_gemm1(static_cast<float*>(xp), H, static_cast<float*>(h->w_g),
@@ -323,7 +326,9 @@ int run_expert_gemms(vmoe_handle* h, void* xp, int64_t max_rows, const int* tile
   a1.bias_ld = 2 * h->Ipad;
   a1.gamma = h->cfg.era_gamma;
   a1.status = h->status;
-  if ((rc = check(launch_tc_gemm(true, map_x, h->map_wgu, a1, max_tiles, h->num_sms, s),
+  const bool pair = h->tile_rows != kTileM;
+  if ((rc = check(pair ? launch_tc_gemm_pair(true, map_x, h->map_wgu, a1, max_tiles, h->num_sms, s)
+                       : launch_tc_gemm(true, map_x, h->map_wgu, a1, max_tiles, h->num_sms, s),
                   "gemm1")) != VMOE_OK)
     return rc;
   mark();
@@ -341,7 +346,9 @@ int run_expert_gemms(vmoe_handle* h, void* xp, int64_t max_rows, const int* tile
   a2.bias_ld = h->Hpad;
   a2.gamma = 0.f;
   a2.status = h->status;
-  return check(launch_tc_gemm(false, map_h, h->map_wd, a2, max_tiles, h->num_sms, s), "gemm2");
+  return check(pair ? launch_tc_gemm_pair(false, map_h, h->map_wd, a2, max_tiles, h->num_sms, s)
+                    : launch_tc_gemm(false, map_h, h->map_wd, a2, max_tiles, h->num_sms, s),
+               "gemm2");
 }
 
 // Router + softmax + top-K + per-block histogram / probability sums: on the tensor cores
@@ -443,6 +450,8 @@ int vmoe_create(const vmoe_config* cfg, int device, vmoe_handle** out) {
   if (h->dtype == kBF16) {
     h->Ipad = round_up(h->I, kGateUpInterleave);
     h->Hpad = round_up(h->H, kDownTileN);
+    const char* pair = getenv("VMOE_PAIR_GEMM");  // "0" selects the single-CTA GEMMs
+    h->tile_rows = (pair && pair[0] == '0') ? kTileM : 2 * kTileM;
   } else {
     h->Ipad = h->I;
     h->Hpad = h->H;
@@ -595,9 +604,11 @@ int vmoe_set_weights(vmoe_handle* h, const vmoe_weights* w, void* stream) {
         !make_tmap_bf16(&h->map_wr, h->w_r, E, H, H, static_cast<uint32_t>(h->router_bn), why,
                         sizeof(why)))
       return fail(h, VMOE_ERR_CUDA, "router tensor map: %s", why);
-    if (!make_tmap_bf16(&h->map_wgu, h->w_g, El * 2 * Ipad, H, H, 256, why, sizeof(why)))
+    // B tiles: 256 rows per CTA, or 128 per CTA of a pair
+    const uint32_t b_box = h->tile_rows == kTileM ? 256u : 128u;
+    if (!make_tmap_bf16(&h->map_wgu, h->w_g, El * 2 * Ipad, H, H, b_box, why, sizeof(why)))
       return fail(h, VMOE_ERR_CUDA, "gate/up tensor map: %s", why);
-    if (!make_tmap_bf16(&h->map_wd, h->w_d, El * Hpad, Ipad, Ipad, 256, why, sizeof(why)))
+    if (!make_tmap_bf16(&h->map_wd, h->w_d, El * Hpad, Ipad, Ipad, b_box, why, sizeof(why)))
       return fail(h, VMOE_ERR_CUDA, "down tensor map: %s", why);
   }
   h->ready = true;
@@ -705,7 +716,8 @@ int vmoe_forward(vmoe_handle* h, const void* x, int64_t tokens, void* out, float
     return rc;
   mark();
   if ((rc = check(launch_plan(counts, psum_tot, T, static_cast<int>(E), static_cast<int>(K),
-                              h->cfg.capacity, kTileM, offs, tiles, ntiles, aux, expert_counts, s),
+                              h->cfg.capacity, static_cast<int>(h->tile_rows), offs, tiles,
+                              ntiles, aux, expert_counts, s),
                   "plan")) != VMOE_OK)
     return rc;
   mark();
@@ -836,9 +848,9 @@ int vmoe_ep_experts(vmoe_handle* h, const void* recv_rows, int64_t recv_rows_cap
                     void* workspace, size_t workspace_bytes, void* stream) {
   if (!h) return VMOE_ERR_INVALID_ARG;
   h->last_launches = 0;
-  if (recv_rows_cap < 0 || recv_rows_cap % kTileM)
+  if (recv_rows_cap < 0 || recv_rows_cap % h->tile_rows)
     return fail(h, VMOE_ERR_INVALID_ARG, "recv_rows_cap must be a multiple of %d (got %lld)",
-                kTileM, static_cast<long long>(recv_rows_cap));
+                h->tile_rows, static_cast<long long>(recv_rows_cap));
   const EpPlan p = make_ep_plan(h, 0, recv_rows_cap);
   int rc = ep_common_checks(h, workspace, workspace_bytes, p.total);
   if (rc != VMOE_OK) return rc;
@@ -895,7 +907,7 @@ int vmoe_ep_p2p_setup(vmoe_handle* h, int64_t max_tokens, void* ipc_handle) {
     return fail(h, VMOE_ERR_UNSUPPORTED_SHAPE, "bf16 expert parallelism needs hidden %% %d == 0",
                 kDownTileN);
   const int64_t G = h->ep_size, E = h->E, K = h->K, El = h->E_local, H = h->H;
-  const int64_t cap = round_up(G * max_tokens * K + El * (kTileM - 1), kTileM);
+  const int64_t cap = round_up(G * max_tokens * K + El * (h->tile_rows - 1), h->tile_rows);
   if (cap >= (static_cast<int64_t>(1) << 31))
     return fail(h, VMOE_ERR_UNSUPPORTED_SHAPE, "receive capacity of %lld rows is too large",
                 static_cast<long long>(cap));
@@ -1004,6 +1016,7 @@ int vmoe_ep_p2p_forward(vmoe_handle* h, const void* x, int64_t tokens, void* out
   a.K = static_cast<int>(K);
   a.H = H;
   a.cap_rows = h->p2p_cap_rows;
+  a.row_align = static_cast<int>(h->tile_rows);
   a.epoch = ++h->p2p_epoch;
   a.status = h->status;
   a.block_counter = h->p2p_block_counter;
@@ -1117,5 +1130,7 @@ int vmoe_stage_times(vmoe_handle* h, float* ms, int n, int* n_out, int* forwards
 }
 
 int vmoe_last_launch_count(const vmoe_handle* h) { return h ? h->last_launches : 0; }
+
+int vmoe_gemm_tile_rows(const vmoe_handle* h) { return h ? h->tile_rows : 0; }
 
 }  // extern "C"

@@ -253,7 +253,8 @@ class ExpertParallelMoE:
         recv_counts = torch.empty((self.world * self.El,), dtype=torch.int32, device=dev)
         dist.all_to_all_single(recv_counts, counts, group=self.group)
         both = torch.cat([counts, recv_counts]).cpu().numpy().astype(np.int64)
-        plan = plan_exchange(both[:self.E], both[self.E:].reshape(self.world, self.El))
+        plan = plan_exchange(both[:self.E], both[self.E:].reshape(self.world, self.El),
+                             align=int(lib.vmoe_gemm_tile_rows(h)))
         self.last_plan = plan
         rows = plan.recv_rows
         recv = torch.empty((rows, H), dtype=self.dtype, device=dev)
