@@ -208,10 +208,12 @@ VMOE_API int vmoe_ep_combine(vmoe_handle* h, const void* back_rows, int64_t toke
  * (no collective library, no host synchronisation inside the forward).  Every rank owns
  * one symmetric device region (flags, all ranks' routing counts, a receive buffer and an
  * expert-output buffer) that every peer maps through CUDA IPC:
- *   vmoe_ep_p2p_setup   allocates this rank's region for up to max_tokens tokens per rank
- *                       per forward and writes its 64-byte CUDA IPC handle to ipc_handle;
- *   (caller)            all-gathers the G handles (any transport: they are plain bytes);
- *   vmoe_ep_p2p_connect maps every peer's region (handles in rank order, G x 64 bytes);
+ *   vmoe_ep_p2p_setup   allocates this rank's regions for up to max_tokens tokens per
+ *                       rank per forward, split into `chunks` (1..4) token chunks that run
+ *                       on internal streams so one chunk's NVLink exchange overlaps another's
+ *                       GEMMs; writes chunks x 64 bytes of CUDA IPC handles to ipc_handles;
+ *   (caller)            all-gathers every rank's handles (plain bytes, any transport);
+ *   vmoe_ep_p2p_connect maps every peer's regions (G x chunks x 64 bytes, rank-major);
  *   vmoe_ep_p2p_forward one forward: route; publish counts to every peer; dispatch rows
  *                       straight into the owners' receive buffers; local grouped GEMMs;
  *                       combine reading the owners' outputs; device-side epoch flags with
@@ -219,7 +221,8 @@ VMOE_API int vmoe_ep_combine(vmoe_handle* h, const void* back_rows, int64_t toke
  * Every rank must call vmoe_ep_p2p_forward the same number of times, each with
  * tokens <= max_tokens.  A bounded wait that gives up (a peer that never arrives) shows up
  * in vmoe_device_status as VMOE_ERR_TIMEOUT. */
-VMOE_API int vmoe_ep_p2p_setup(vmoe_handle* h, int64_t max_tokens, void* ipc_handle);
+VMOE_API int vmoe_ep_p2p_setup(vmoe_handle* h, int64_t max_tokens, int chunks,
+                               void* ipc_handles);
 VMOE_API int vmoe_ep_p2p_connect(vmoe_handle* h, const void* ipc_handles);
 VMOE_API int vmoe_ep_p2p_workspace_size(const vmoe_handle* h, int64_t tokens, size_t* bytes);
 VMOE_API int vmoe_ep_p2p_forward(vmoe_handle* h, const void* x, int64_t tokens, void* out,

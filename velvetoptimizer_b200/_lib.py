@@ -115,7 +115,7 @@ def load() -> ctypes.CDLL:
     lib.vmoe_ep_experts.restype = c_int
     lib.vmoe_ep_combine.argtypes = [H, c_void_p, c_int64, c_void_p, c_void_p, c_size_t, c_void_p]
     lib.vmoe_ep_combine.restype = c_int
-    lib.vmoe_ep_p2p_setup.argtypes = [H, c_int64, c_void_p]
+    lib.vmoe_ep_p2p_setup.argtypes = [H, c_int64, c_int, c_void_p]
     lib.vmoe_ep_p2p_setup.restype = c_int
     lib.vmoe_ep_p2p_connect.argtypes = [H, c_void_p]
     lib.vmoe_ep_p2p_connect.restype = c_int

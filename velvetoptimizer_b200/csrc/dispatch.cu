@@ -222,7 +222,36 @@ combine_kernel(const T* __restrict__ y, int64_t y_ld, const int32_t* __restrict_
   }
 }
 
+// ---- 5. aux loss of a batch routed in chunks -----------------------------------------
+// counts[c] / psum_tot[c] are chunk c's per-expert routed rows and probability sums; the
+// loss of the whole batch is E * sum_e (sum_c counts) / (T*K) * (sum_c psum) / T, summed
+// over chunks and experts in a fixed order (model.py:366-385).
+__global__ void aux_merge_kernel(const char* ws, size_t stride, size_t counts_off,
+                                 size_t psum_off, int chunks, int64_t T, int E, int K, float* aux) {
+  if (threadIdx.x != 0) return;
+  const float inv_tk = 1.0f / static_cast<float>(T * K);
+  const float inv_t = 1.0f / static_cast<float>(T);
+  float s = 0.f;
+  for (int e = 0; e < E; ++e) {
+    int c_e = 0;
+    float p_e = 0.f;
+    for (int c = 0; c < chunks; ++c) {
+      c_e += reinterpret_cast<const int*>(ws + c * stride + counts_off)[e];
+      p_e += reinterpret_cast<const float*>(ws + c * stride + psum_off)[e];
+    }
+    s += (static_cast<float>(c_e) * inv_tk) * (p_e * inv_t);
+  }
+  *aux = static_cast<float>(E) * s;
+}
+
 }  // namespace
+
+cudaError_t launch_aux_merge_ws(const void* ws, size_t stride, size_t counts_off, size_t psum_off,
+                                int chunks, int64_t T, int E, int K, float* aux, cudaStream_t s) {
+  aux_merge_kernel<<<1, 32, 0, s>>>(static_cast<const char*>(ws), stride, counts_off, psum_off,
+                                    chunks, T, E, K, aux);
+  return cudaGetLastError();
+}
 
 cudaError_t launch_scan_blocks(const int* hist, const float* psum, int nblk, int E, int* excl,
                                int* counts, float* psum_tot, cudaStream_t s) {

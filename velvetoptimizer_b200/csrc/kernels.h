@@ -34,6 +34,11 @@ cudaError_t launch_plan(const int* counts, const float* psum_tot, int64_t T, int
                         int64_t capacity, int row_align, int* offs, int* tile_expert,
                         int* num_tiles, float* aux, int32_t* counts_out, cudaStream_t s);
 
+// Aux loss of a batch routed in chunks: chunk c's per-expert counts (int [E]) and
+// probability sums (float [E]) sit at ws + c*stride + counts_off / psum_off.
+cudaError_t launch_aux_merge_ws(const void* ws, size_t stride, size_t counts_off, size_t psum_off,
+                                int chunks, int64_t T, int E, int K, float* aux, cudaStream_t s);
+
 // Stable expert-major slots for every (token, k) and the row gather x -> x_perm.
 cudaError_t launch_dispatch(int dtype, const void* x, const int32_t* topk_idx, const int* excl,
                             const int* offs, int64_t T, int H, int E, int K, int64_t capacity,

@@ -46,6 +46,17 @@ struct DeviceGuard {
   }
 };
 
+constexpr int kMaxChunks = 4;
+
+// One token chunk's symmetric region and its bookkeeping.
+struct P2PChannel {
+  char* region = nullptr;
+  std::vector<char*> peers;  // every rank's region of this channel as mapped here
+  char** peers_dev = nullptr;
+  int* block_counter = nullptr;
+  unsigned epoch = 0;
+};
+
 struct Plan {
   int nblk = 0;
   int64_t max_tiles = 0, max_rows = 0;
@@ -65,14 +76,14 @@ struct vmoe_handle {
   // expert parallelism: this handle holds experts [ep_rank*E_local, (ep_rank+1)*E_local)
   int ep_size = 1, ep_rank = 0;
   int64_t E_local = 0;
-  // expert parallelism over NVLink peer memory (vmoe_ep_p2p_*)
-  char* p2p_region = nullptr;
+  // expert parallelism over NVLink peer memory (vmoe_ep_p2p_*): one channel per token
+  // chunk; every channel has the same region layout
+  std::vector<P2PChannel> p2p;
   size_t p2p_sig_off = 0, p2p_counts_off = 0, p2p_recv_off = 0, p2p_y_off = 0;
-  int64_t p2p_cap_rows = 0, p2p_max_tokens = 0;
-  std::vector<char*> p2p_peers;  // every rank's region as mapped here (own at [ep_rank])
-  char** p2p_peers_dev = nullptr;
-  int* p2p_block_counter = nullptr;
-  unsigned p2p_epoch = 0;
+  int64_t p2p_cap_rows = 0, p2p_max_tokens = 0, p2p_chunk_tokens = 0;
+  cudaStream_t p2p_streams[kMaxChunks] = {};
+  cudaEvent_t p2p_start = nullptr;
+  cudaEvent_t p2p_done[kMaxChunks] = {};
   bool p2p_connected = false;
   // packed weights (library-owned)
   void* w_r = nullptr;
@@ -485,11 +496,18 @@ int vmoe_destroy(vmoe_handle* h) {
   {
     DeviceGuard g(h->device);
     free_weights(h);
-    for (size_t r = 0; r < h->p2p_peers.size(); ++r)
-      if (static_cast<int>(r) != h->ep_rank && h->p2p_peers[r]) cudaIpcCloseMemHandle(h->p2p_peers[r]);
-    if (h->p2p_region) cudaFree(h->p2p_region);
-    if (h->p2p_peers_dev) cudaFree(h->p2p_peers_dev);
-    if (h->p2p_block_counter) cudaFree(h->p2p_block_counter);
+    for (P2PChannel& c : h->p2p) {
+      for (size_t r = 0; r < c.peers.size(); ++r)
+        if (static_cast<int>(r) != h->ep_rank && c.peers[r]) cudaIpcCloseMemHandle(c.peers[r]);
+      if (c.region) cudaFree(c.region);
+      if (c.peers_dev) cudaFree(c.peers_dev);
+      if (c.block_counter) cudaFree(c.block_counter);
+    }
+    for (int i = 0; i < kMaxChunks; ++i) {
+      if (h->p2p_streams[i]) cudaStreamDestroy(h->p2p_streams[i]);
+      if (h->p2p_done[i]) cudaEventDestroy(h->p2p_done[i]);
+    }
+    if (h->p2p_start) cudaEventDestroy(h->p2p_start);
     if (h->status) cudaFree(h->status);
     for (cudaEvent_t ev : h->prof_ev) cudaEventDestroy(ev);
   }
@@ -900,14 +918,17 @@ int vmoe_ep_combine(vmoe_handle* h, const void* back_rows, int64_t tokens, void*
   return VMOE_OK;
 }
 
-int vmoe_ep_p2p_setup(vmoe_handle* h, int64_t max_tokens, void* ipc_handle) {
-  if (!h || !ipc_handle || max_tokens < 0) return VMOE_ERR_INVALID_ARG;
-  if (h->p2p_region) return fail(h, VMOE_ERR_INVALID_ARG, "vmoe_ep_p2p_setup was already called");
+int vmoe_ep_p2p_setup(vmoe_handle* h, int64_t max_tokens, int chunks, void* ipc_handles) {
+  if (!h || !ipc_handles || max_tokens < 0) return VMOE_ERR_INVALID_ARG;
+  if (chunks < 1 || chunks > kMaxChunks)
+    return fail(h, VMOE_ERR_INVALID_ARG, "chunks must be in [1, %d] (got %d)", kMaxChunks, chunks);
+  if (!h->p2p.empty()) return fail(h, VMOE_ERR_INVALID_ARG, "vmoe_ep_p2p_setup was already called");
   if (h->dtype == kBF16 && h->Hpad != h->H)
     return fail(h, VMOE_ERR_UNSUPPORTED_SHAPE, "bf16 expert parallelism needs hidden %% %d == 0",
                 kDownTileN);
   const int64_t G = h->ep_size, E = h->E, K = h->K, El = h->E_local, H = h->H;
-  const int64_t cap = round_up(G * max_tokens * K + El * (h->tile_rows - 1), h->tile_rows);
+  const int64_t chunk_tokens = round_up((max_tokens + chunks - 1) / chunks, kTileM);
+  const int64_t cap = round_up(G * chunk_tokens * K + El * (h->tile_rows - 1), h->tile_rows);
   if (cap >= (static_cast<int64_t>(1) << 31))
     return fail(h, VMOE_ERR_UNSUPPORTED_SHAPE, "receive capacity of %lld rows is too large",
                 static_cast<long long>(cap));
@@ -922,53 +943,154 @@ int vmoe_ep_p2p_setup(vmoe_handle* h, int64_t max_tokens, void* ipc_handle) {
   h->p2p_recv_off = take(static_cast<size_t>(cap) * H * dtype_bytes(h->dtype));
   h->p2p_y_off = take(static_cast<size_t>(cap) * H * dtype_bytes(h->dtype));
   DeviceGuard g(h->device);
-  cudaError_t e = cudaMalloc(&h->p2p_region, off);
-  if (e == cudaSuccess) e = cudaMemset(h->p2p_region, 0, h->p2p_recv_off);
-  if (e == cudaSuccess) e = cudaMalloc(&h->p2p_block_counter, sizeof(int));
-  if (e == cudaSuccess) e = cudaMemset(h->p2p_block_counter, 0, sizeof(int));
-  if (e == cudaSuccess) e = cudaMalloc(&h->p2p_peers_dev, G * sizeof(char*));
-  cudaIpcMemHandle_t mh;
-  if (e == cudaSuccess) e = cudaIpcGetMemHandle(&mh, h->p2p_region);
+  h->p2p.resize(chunks);
+  cudaError_t e = cudaSuccess;
+  for (int c = 0; c < chunks && e == cudaSuccess; ++c) {
+    P2PChannel& ch = h->p2p[c];
+    e = cudaMalloc(&ch.region, off);
+    if (e == cudaSuccess) e = cudaMemset(ch.region, 0, h->p2p_recv_off);
+    if (e == cudaSuccess) e = cudaMalloc(&ch.block_counter, sizeof(int));
+    if (e == cudaSuccess) e = cudaMemset(ch.block_counter, 0, sizeof(int));
+    if (e == cudaSuccess) e = cudaMalloc(&ch.peers_dev, G * sizeof(char*));
+    cudaIpcMemHandle_t mh;
+    if (e == cudaSuccess) e = cudaIpcGetMemHandle(&mh, ch.region);
+    if (e == cudaSuccess)
+      memcpy(static_cast<char*>(ipc_handles) + static_cast<size_t>(c) * sizeof(mh), &mh, sizeof(mh));
+    if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&h->p2p_streams[c], cudaStreamNonBlocking);
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&h->p2p_done[c], cudaEventDisableTiming);
+  }
+  if (e == cudaSuccess) e = cudaEventCreateWithFlags(&h->p2p_start, cudaEventDisableTiming);
   if (e == cudaSuccess) e = cudaDeviceSynchronize();
   if (e != cudaSuccess) return cuda_fail(h, e, "peer-memory region");
-  memcpy(ipc_handle, &mh, sizeof(mh));
   h->p2p_cap_rows = cap;
   h->p2p_max_tokens = max_tokens;
+  h->p2p_chunk_tokens = chunk_tokens;
   return VMOE_OK;
 }
 
 int vmoe_ep_p2p_connect(vmoe_handle* h, const void* ipc_handles) {
   if (!h || !ipc_handles) return VMOE_ERR_INVALID_ARG;
-  if (!h->p2p_region) return fail(h, VMOE_ERR_NOT_READY, "vmoe_ep_p2p_setup has not been called");
+  if (h->p2p.empty()) return fail(h, VMOE_ERR_NOT_READY, "vmoe_ep_p2p_setup has not been called");
   if (h->p2p_connected) return fail(h, VMOE_ERR_INVALID_ARG, "already connected");
   DeviceGuard g(h->device);
-  const int G = h->ep_size;
-  h->p2p_peers.assign(G, nullptr);
+  const int G = h->ep_size, C = static_cast<int>(h->p2p.size());
   const char* bytes = static_cast<const char*>(ipc_handles);
-  for (int r = 0; r < G; ++r) {
-    if (r == h->ep_rank) {
-      h->p2p_peers[r] = h->p2p_region;
-      continue;
+  for (int c = 0; c < C; ++c) {
+    P2PChannel& ch = h->p2p[c];
+    ch.peers.assign(G, nullptr);
+    for (int r = 0; r < G; ++r) {
+      if (r == h->ep_rank) {
+        ch.peers[r] = ch.region;
+        continue;
+      }
+      cudaIpcMemHandle_t mh;
+      memcpy(&mh, bytes + (static_cast<size_t>(r) * C + c) * sizeof(mh), sizeof(mh));
+      void* p = nullptr;
+      cudaError_t e = cudaIpcOpenMemHandle(&p, mh, cudaIpcMemLazyEnablePeerAccess);
+      if (e != cudaSuccess) return cuda_fail(h, e, "cudaIpcOpenMemHandle of a peer region");
+      ch.peers[r] = static_cast<char*>(p);
     }
-    cudaIpcMemHandle_t mh;
-    memcpy(&mh, bytes + static_cast<size_t>(r) * sizeof(mh), sizeof(mh));
-    void* p = nullptr;
-    cudaError_t e = cudaIpcOpenMemHandle(&p, mh, cudaIpcMemLazyEnablePeerAccess);
-    if (e != cudaSuccess) return cuda_fail(h, e, "cudaIpcOpenMemHandle of a peer region");
-    h->p2p_peers[r] = static_cast<char*>(p);
+    cudaError_t e = cudaMemcpy(ch.peers_dev, ch.peers.data(), G * sizeof(char*),
+                               cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) return cuda_fail(h, e, "peer table");
   }
-  cudaError_t e = cudaMemcpy(h->p2p_peers_dev, h->p2p_peers.data(), G * sizeof(char*),
-                             cudaMemcpyHostToDevice);
-  if (e != cudaSuccess) return cuda_fail(h, e, "peer table");
   h->p2p_connected = true;
   return VMOE_OK;
 }
 
+namespace {
+size_t p2p_chunk_stride(const vmoe_handle* h) {
+  return (make_p2p_plan(h, h->p2p_chunk_tokens).total + 255) & ~static_cast<size_t>(255);
+}
+}  // namespace
+
 int vmoe_ep_p2p_workspace_size(const vmoe_handle* h, int64_t tokens, size_t* bytes) {
   if (!h || !bytes || tokens < 0) return VMOE_ERR_INVALID_ARG;
-  *bytes = make_p2p_plan(h, tokens).total;
+  if (h->p2p.empty()) return VMOE_ERR_NOT_READY;
+  *bytes = p2p_chunk_stride(h) * h->p2p.size();
   return VMOE_OK;
 }
+
+namespace {
+// One chunk of the fused forward on stream s (the whole pipeline of ep_p2p.cu).
+int p2p_chunk(vmoe_handle* h, int c, const void* x, int64_t T, void* out, float* logits,
+              char* ws, const P2PPlan& p, cudaStream_t s, bool prof) {
+  const int64_t E = h->E, K = h->K, H = h->H;
+  P2PChannel& ch = h->p2p[c];
+  int32_t* idx = reinterpret_cast<int32_t*>(ws + p.idx);
+  float* tw = reinterpret_cast<float*>(ws + p.w);
+  int* hist = reinterpret_cast<int*>(ws + p.hist);
+  float* psum = reinterpret_cast<float*>(ws + p.psum);
+  int* excl = reinterpret_cast<int*>(ws + p.excl);
+  int* counts = reinterpret_cast<int*>(ws + p.counts);
+  float* psum_tot = reinterpret_cast<float*>(ws + p.psum_tot);
+  int* offs = reinterpret_cast<int*>(ws + p.offs);
+  float* aux = reinterpret_cast<float*>(ws + p.aux);
+  const int nblk = static_cast<int>((T + kTileM - 1) / kTileM);
+
+  P2PArgs a{};
+  a.peer_base = ch.peers_dev;
+  a.sig_off = h->p2p_sig_off;
+  a.counts_off = h->p2p_counts_off;
+  a.recv_off = h->p2p_recv_off;
+  a.y_off = h->p2p_y_off;
+  a.me = h->ep_rank;
+  a.G = h->ep_size;
+  a.E = static_cast<int>(E);
+  a.El = static_cast<int>(h->E_local);
+  a.K = static_cast<int>(K);
+  a.H = H;
+  a.cap_rows = h->p2p_cap_rows;
+  a.row_align = static_cast<int>(h->tile_rows);
+  a.epoch = ++ch.epoch;
+  a.status = h->status;
+  a.block_counter = ch.block_counter;
+  a.dest_rank = reinterpret_cast<int32_t*>(ws + p.drank);
+  a.dest_row = reinterpret_cast<int32_t*>(ws + p.drow);
+  a.tile_expert = reinterpret_cast<int*>(ws + p.tiles);
+  a.num_tiles = reinterpret_cast<int*>(ws + p.ntiles);
+
+  cudaEvent_t* ev = prof ? &h->prof_ev[static_cast<size_t>(h->prof_count) * (kStages + 1)] : nullptr;
+  int stage = 0;
+  auto mark = [&]() {
+    if (prof) cudaEventRecord(ev[stage], s);
+    ++stage;
+  };
+  auto check = [&](cudaError_t err, const char* what) -> int {
+    if (err != cudaSuccess) return cuda_fail(h, err, what);
+    ++h->last_launches;
+    return VMOE_OK;
+  };
+  int rc;
+  mark();  // router
+  if (T > 0 && (rc = run_router(h, x, T, logits, idx, tw, hist, psum, s)) != VMOE_OK) return rc;
+  mark();  // scan
+  if ((rc = check(launch_scan_blocks(hist, psum, nblk, static_cast<int>(E), excl, counts,
+                                     psum_tot, s), "scan")) != VMOE_OK)
+    return rc;
+  mark();  // plan (this chunk's counts) + publish counts to every rank
+  if ((rc = check(launch_plan(counts, psum_tot, T, static_cast<int>(E), static_cast<int>(K), 0, 1,
+                              offs, nullptr, nullptr, aux, nullptr, s), "plan")) != VMOE_OK)
+    return rc;
+  if ((rc = check(launch_p2p_publish(a, counts, s), "publish")) != VMOE_OK) return rc;
+  mark();  // dispatch over NVLink + wait for every rank's rows
+  if ((rc = check(launch_p2p_dispatch(h->dtype, a, x, idx, excl, T, s), "dispatch")) != VMOE_OK)
+    return rc;
+  if ((rc = check(launch_p2p_wait(a, 1, s), "wait rows")) != VMOE_OK) return rc;
+  mark();  // gemm1 (inside run_expert_gemms: gemm1, mark, gemm2)
+  if ((rc = run_expert_gemms(h, ch.region + h->p2p_recv_off, h->p2p_cap_rows, a.tile_expert,
+                             a.num_tiles, ws + p.hbuf, ch.region + h->p2p_y_off, H, s, mark,
+                             check)) != VMOE_OK)
+    return rc;
+  mark();  // signal outputs ready, wait for every rank's, combine over NVLink
+  if ((rc = check(launch_p2p_signal(a, 2, s), "signal outputs")) != VMOE_OK) return rc;
+  if ((rc = check(launch_p2p_wait(a, 2, s), "wait outputs")) != VMOE_OK) return rc;
+  if ((rc = check(launch_p2p_combine(h->dtype, a, idx, tw, T, out, s), "combine")) != VMOE_OK)
+    return rc;
+  mark();
+  return VMOE_OK;
+}
+}  // namespace
 
 int vmoe_ep_p2p_forward(vmoe_handle* h, const void* x, int64_t tokens, void* out,
                         float* router_logits, float* aux_loss, void* workspace,
@@ -984,87 +1106,49 @@ int vmoe_ep_p2p_forward(vmoe_handle* h, const void* x, int64_t tokens, void* out
   if (T > 0 && (!x || !out)) return fail(h, VMOE_ERR_INVALID_ARG, "x and out are required");
   if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(out)) & 15u)
     return fail(h, VMOE_ERR_INVALID_ARG, "x and out must be 16-byte aligned");
-  const P2PPlan p = make_p2p_plan(h, T);
-  if (!workspace || workspace_bytes < p.total)
-    return fail(h, VMOE_ERR_WORKSPACE, "workspace needs %zu bytes (got %zu)", p.total,
+  const int C = static_cast<int>(h->p2p.size());
+  const size_t stride = p2p_chunk_stride(h);
+  if (!workspace || workspace_bytes < stride * C)
+    return fail(h, VMOE_ERR_WORKSPACE, "workspace needs %zu bytes (got %zu)", stride * C,
                 workspace ? workspace_bytes : static_cast<size_t>(0));
   if (reinterpret_cast<uintptr_t>(workspace) & 255u)
     return fail(h, VMOE_ERR_WORKSPACE, "workspace must be 256-byte aligned");
   DeviceGuard g(h->device);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   char* ws = static_cast<char*>(workspace);
-  int32_t* idx = reinterpret_cast<int32_t*>(ws + p.idx);
-  float* tw = reinterpret_cast<float*>(ws + p.w);
-  int* hist = reinterpret_cast<int*>(ws + p.hist);
-  float* psum = reinterpret_cast<float*>(ws + p.psum);
-  int* excl = reinterpret_cast<int*>(ws + p.excl);
-  int* counts = reinterpret_cast<int*>(ws + p.counts);
-  float* psum_tot = reinterpret_cast<float*>(ws + p.psum_tot);
-  int* offs = reinterpret_cast<int*>(ws + p.offs);
-  float* aux = aux_loss ? aux_loss : reinterpret_cast<float*>(ws + p.aux);
-
-  P2PArgs a{};
-  a.peer_base = h->p2p_peers_dev;
-  a.sig_off = h->p2p_sig_off;
-  a.counts_off = h->p2p_counts_off;
-  a.recv_off = h->p2p_recv_off;
-  a.y_off = h->p2p_y_off;
-  a.me = h->ep_rank;
-  a.G = h->ep_size;
-  a.E = static_cast<int>(E);
-  a.El = static_cast<int>(h->E_local);
-  a.K = static_cast<int>(K);
-  a.H = H;
-  a.cap_rows = h->p2p_cap_rows;
-  a.row_align = static_cast<int>(h->tile_rows);
-  a.epoch = ++h->p2p_epoch;
-  a.status = h->status;
-  a.block_counter = h->p2p_block_counter;
-  a.dest_rank = reinterpret_cast<int32_t*>(ws + p.drank);
-  a.dest_row = reinterpret_cast<int32_t*>(ws + p.drow);
-  a.tile_expert = reinterpret_cast<int*>(ws + p.tiles);
-  a.num_tiles = reinterpret_cast<int*>(ws + p.ntiles);
-
+  const P2PPlan p = make_p2p_plan(h, h->p2p_chunk_tokens);
+  const size_t elt = dtype_bytes(h->dtype);
   const bool prof = h->prof_count < h->prof_slots;
-  cudaEvent_t* ev = prof ? &h->prof_ev[static_cast<size_t>(h->prof_count) * (kStages + 1)] : nullptr;
-  int stage = 0;
-  auto mark = [&]() {
-    if (prof) cudaEventRecord(ev[stage], s);
-    ++stage;
-  };
-  auto check = [&](cudaError_t err, const char* what) -> int {
-    if (err != cudaSuccess) return cuda_fail(h, err, what);
-    ++h->last_launches;
-    return VMOE_OK;
-  };
+  cudaError_t e;
   int rc;
-  mark();  // router
-  if (T > 0 && (rc = run_router(h, x, T, router_logits, idx, tw, hist, psum, s)) != VMOE_OK)
-    return rc;
-  mark();  // scan
-  if ((rc = check(launch_scan_blocks(hist, psum, p.nblk, static_cast<int>(E), excl, counts,
-                                     psum_tot, s), "scan")) != VMOE_OK)
-    return rc;
-  mark();  // plan (aux loss, counts) + publish counts to every rank
-  if ((rc = check(launch_plan(counts, psum_tot, T, static_cast<int>(E), static_cast<int>(K), 0, 1,
-                              offs, nullptr, nullptr, aux, nullptr, s), "plan")) != VMOE_OK)
-    return rc;
-  if ((rc = check(launch_p2p_publish(a, counts, s), "publish")) != VMOE_OK) return rc;
-  mark();  // dispatch over NVLink + wait for every rank's rows
-  if ((rc = check(launch_p2p_dispatch(h->dtype, a, x, idx, excl, T, s), "dispatch")) != VMOE_OK)
-    return rc;
-  if ((rc = check(launch_p2p_wait(a, 1, s), "wait rows")) != VMOE_OK) return rc;
-  mark();  // gemm1 (inside run_expert_gemms: gemm1, mark, gemm2)
-  if ((rc = run_expert_gemms(h, h->p2p_region + h->p2p_recv_off, h->p2p_cap_rows, a.tile_expert,
-                             a.num_tiles, ws + p.hbuf, h->p2p_region + h->p2p_y_off, H, s, mark,
-                             check)) != VMOE_OK)
-    return rc;
-  mark();  // signal outputs ready, wait for every rank's, combine over NVLink
-  if ((rc = check(launch_p2p_signal(a, 2, s), "signal outputs")) != VMOE_OK) return rc;
-  if ((rc = check(launch_p2p_wait(a, 2, s), "wait outputs")) != VMOE_OK) return rc;
-  if ((rc = check(launch_p2p_combine(h->dtype, a, idx, tw, T, out, s), "combine")) != VMOE_OK)
-    return rc;
-  mark();
+  if (C == 1) {
+    if ((rc = p2p_chunk(h, 0, x, T, out, router_logits, ws, p, s, prof)) != VMOE_OK) return rc;
+  } else {
+    // chunk c on its own stream: its dispatch and combine overlap the other chunks' GEMMs
+    if ((e = cudaEventRecord(h->p2p_start, s)) != cudaSuccess) return cuda_fail(h, e, "event");
+    for (int c = 0; c < C; ++c) {
+      cudaStream_t sc = h->p2p_streams[c];
+      if ((e = cudaStreamWaitEvent(sc, h->p2p_start, 0)) != cudaSuccess) return cuda_fail(h, e, "wait");
+      const int64_t t0 = c * h->p2p_chunk_tokens;
+      int64_t tc = T - t0;
+      tc = tc < 0 ? 0 : (tc > h->p2p_chunk_tokens ? h->p2p_chunk_tokens : tc);
+      const char* xc = static_cast<const char*>(x) + (tc > 0 ? t0 * H * elt : 0);
+      char* oc = static_cast<char*>(out) + (tc > 0 ? t0 * H * elt : 0);
+      float* lc = router_logits && tc > 0 ? router_logits + t0 * E : nullptr;
+      if ((rc = p2p_chunk(h, c, tc > 0 ? xc : nullptr, tc, tc > 0 ? oc : nullptr, lc,
+                          ws + c * stride, p, sc, prof && c == 0)) != VMOE_OK)
+        return rc;
+      if ((e = cudaEventRecord(h->p2p_done[c], sc)) != cudaSuccess) return cuda_fail(h, e, "event");
+    }
+    for (int c = 0; c < C; ++c)
+      if ((e = cudaStreamWaitEvent(s, h->p2p_done[c], 0)) != cudaSuccess) return cuda_fail(h, e, "wait");
+  }
+  if (aux_loss) {  // the loss of the whole batch from every chunk's counts and sums
+    if ((e = launch_aux_merge_ws(ws, stride, p.counts, p.psum_tot, C, T, static_cast<int>(E),
+                                 static_cast<int>(K), aux_loss, s)) != cudaSuccess)
+      return cuda_fail(h, e, "aux merge");
+    ++h->last_launches;
+  }
   if (prof) ++h->prof_count;
   return VMOE_OK;
 }

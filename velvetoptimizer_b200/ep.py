@@ -115,13 +115,15 @@ class ExpertParallelMoE:
       * ``"p2p"`` (default) -- the exchange runs inside the kernels over NVLink peer memory
         (``vmoe_ep_p2p_forward``): one call per forward, no host synchronisation; every rank
         must call ``forward`` the same number of times with at most ``max_tokens`` tokens;
+        ``chunks`` token chunks run on internal streams so that the NVLink traffic of one
+        overlaps the GEMMs of another;
       * ``"nccl"`` -- the staged path: route, NCCL all-to-all-v, experts, all-to-all-v back,
         combine.
     """
 
     def __init__(self, config, weights: dict[str, torch.Tensor], device: torch.device,
                  dtype: torch.dtype = torch.bfloat16, group=None, transport: str = "p2p",
-                 max_tokens: int | None = None):
+                 max_tokens: int | None = None, chunks: int = 2):
         cfg = MoEConfig.from_any(config)
         cfg.validate()
         self.cfg, self.group, self.device, self.dtype = cfg, group, device, dtype
@@ -165,12 +167,13 @@ class ExpertParallelMoE:
             dist.all_gather_object(caps, int(max_tokens), group=group)
             if len(set(caps)) != 1:  # the symmetric regions must have one layout
                 raise ValueError(f"max_tokens differs across ranks: {caps}")
-            handle = ctypes.create_string_buffer(64)
-            _lib.check(self.lib.vmoe_ep_p2p_setup(self.h, int(max_tokens), handle), self.h,
-                       "vmoe_ep_p2p_setup")
+            self.chunks = int(chunks)
+            handle = ctypes.create_string_buffer(64 * self.chunks)
+            _lib.check(self.lib.vmoe_ep_p2p_setup(self.h, int(max_tokens), self.chunks, handle),
+                       self.h, "vmoe_ep_p2p_setup")
             handles = [None] * self.world
             dist.all_gather_object(handles, handle.raw, group=group)
-            blob = ctypes.create_string_buffer(b"".join(handles), 64 * self.world)
+            blob = ctypes.create_string_buffer(b"".join(handles), 64 * self.chunks * self.world)
             _lib.check(self.lib.vmoe_ep_p2p_connect(self.h, blob), self.h, "vmoe_ep_p2p_connect")
             dist.barrier(group=group)
         # set to a list to record (stage -> (start, end) CUDA events) for every forward
