@@ -84,6 +84,7 @@ struct vmoe_handle {
   cudaStream_t p2p_streams[kMaxChunks] = {};
   cudaEvent_t p2p_start = nullptr;
   cudaEvent_t p2p_done[kMaxChunks] = {};
+  cudaEvent_t p2p_gemm_done[kMaxChunks] = {};  // orders the chunks' GEMMs one after another
   bool p2p_connected = false;
   // packed weights (library-owned)
   void* w_r = nullptr;
@@ -506,6 +507,7 @@ int vmoe_destroy(vmoe_handle* h) {
     for (int i = 0; i < kMaxChunks; ++i) {
       if (h->p2p_streams[i]) cudaStreamDestroy(h->p2p_streams[i]);
       if (h->p2p_done[i]) cudaEventDestroy(h->p2p_done[i]);
+      if (h->p2p_gemm_done[i]) cudaEventDestroy(h->p2p_gemm_done[i]);
     }
     if (h->p2p_start) cudaEventDestroy(h->p2p_start);
     if (h->status) cudaFree(h->status);
@@ -958,6 +960,7 @@ int vmoe_ep_p2p_setup(vmoe_handle* h, int64_t max_tokens, int chunks, void* ipc_
       memcpy(static_cast<char*>(ipc_handles) + static_cast<size_t>(c) * sizeof(mh), &mh, sizeof(mh));
     if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&h->p2p_streams[c], cudaStreamNonBlocking);
     if (e == cudaSuccess) e = cudaEventCreateWithFlags(&h->p2p_done[c], cudaEventDisableTiming);
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&h->p2p_gemm_done[c], cudaEventDisableTiming);
   }
   if (e == cudaSuccess) e = cudaEventCreateWithFlags(&h->p2p_start, cudaEventDisableTiming);
   if (e == cudaSuccess) e = cudaDeviceSynchronize();
@@ -1077,11 +1080,18 @@ int p2p_chunk(vmoe_handle* h, int c, const void* x, int64_t T, void* out, float*
   if ((rc = check(launch_p2p_dispatch(h->dtype, a, x, idx, excl, T, s), "dispatch")) != VMOE_OK)
     return rc;
   if ((rc = check(launch_p2p_wait(a, 1, s), "wait rows")) != VMOE_OK) return rc;
+  // the chunks' GEMMs run one after another (each fills every SM); what overlaps them is
+  // the other chunks' dispatch and combine traffic
+  cudaError_t e;
+  if (c > 0 && (e = cudaStreamWaitEvent(s, h->p2p_gemm_done[c - 1], 0)) != cudaSuccess)
+    return cuda_fail(h, e, "gemm order");
   mark();  // gemm1 (inside run_expert_gemms: gemm1, mark, gemm2)
   if ((rc = run_expert_gemms(h, ch.region + h->p2p_recv_off, h->p2p_cap_rows, a.tile_expert,
                              a.num_tiles, ws + p.hbuf, ch.region + h->p2p_y_off, H, s, mark,
                              check)) != VMOE_OK)
     return rc;
+  if (h->p2p.size() > 1 && (e = cudaEventRecord(h->p2p_gemm_done[c], s)) != cudaSuccess)
+    return cuda_fail(h, e, "gemm order");
   mark();  // signal outputs ready, wait for every rank's, combine over NVLink
   if ((rc = check(launch_p2p_signal(a, 2, s), "signal outputs")) != VMOE_OK) return rc;
   if ((rc = check(launch_p2p_wait(a, 2, s), "wait outputs")) != VMOE_OK) return rc;
