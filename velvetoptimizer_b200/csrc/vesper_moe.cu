@@ -85,6 +85,7 @@ struct vmoe_handle {
   cudaEvent_t p2p_start = nullptr;
   cudaEvent_t p2p_done[kMaxChunks] = {};
   cudaEvent_t p2p_gemm_done[kMaxChunks] = {};  // orders the chunks' GEMMs one after another
+  cudaEvent_t p2p_sent[kMaxChunks] = {};       // and their dispatches
   bool p2p_connected = false;
   // packed weights (library-owned)
   void* w_r = nullptr;
@@ -508,6 +509,7 @@ int vmoe_destroy(vmoe_handle* h) {
       if (h->p2p_streams[i]) cudaStreamDestroy(h->p2p_streams[i]);
       if (h->p2p_done[i]) cudaEventDestroy(h->p2p_done[i]);
       if (h->p2p_gemm_done[i]) cudaEventDestroy(h->p2p_gemm_done[i]);
+      if (h->p2p_sent[i]) cudaEventDestroy(h->p2p_sent[i]);
     }
     if (h->p2p_start) cudaEventDestroy(h->p2p_start);
     if (h->status) cudaFree(h->status);
@@ -961,6 +963,7 @@ int vmoe_ep_p2p_setup(vmoe_handle* h, int64_t max_tokens, int chunks, void* ipc_
     if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&h->p2p_streams[c], cudaStreamNonBlocking);
     if (e == cudaSuccess) e = cudaEventCreateWithFlags(&h->p2p_done[c], cudaEventDisableTiming);
     if (e == cudaSuccess) e = cudaEventCreateWithFlags(&h->p2p_gemm_done[c], cudaEventDisableTiming);
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&h->p2p_sent[c], cudaEventDisableTiming);
   }
   if (e == cudaSuccess) e = cudaEventCreateWithFlags(&h->p2p_start, cudaEventDisableTiming);
   if (e == cudaSuccess) e = cudaDeviceSynchronize();
@@ -1076,13 +1079,19 @@ int p2p_chunk(vmoe_handle* h, int c, const void* x, int64_t T, void* out, float*
                               offs, nullptr, nullptr, aux, nullptr, s), "plan")) != VMOE_OK)
     return rc;
   if ((rc = check(launch_p2p_publish(a, counts, s), "publish")) != VMOE_OK) return rc;
+  // The chunks' dispatches run one after another (they share the links) and so do their
+  // GEMMs (each fills every SM): chunk c's GEMMs can start as soon as its own rows arrived,
+  // while chunk c+1's rows are still in flight and chunk c-1's outputs are combined.
+  cudaError_t e;
+  const bool chained = h->p2p.size() > 1;
+  if (c > 0 && (e = cudaStreamWaitEvent(s, h->p2p_sent[c - 1], 0)) != cudaSuccess)
+    return cuda_fail(h, e, "dispatch order");
   mark();  // dispatch over NVLink + wait for every rank's rows
   if ((rc = check(launch_p2p_dispatch(h->dtype, a, x, idx, excl, T, s), "dispatch")) != VMOE_OK)
     return rc;
+  if (chained && (e = cudaEventRecord(h->p2p_sent[c], s)) != cudaSuccess)
+    return cuda_fail(h, e, "dispatch order");
   if ((rc = check(launch_p2p_wait(a, 1, s), "wait rows")) != VMOE_OK) return rc;
-  // the chunks' GEMMs run one after another (each fills every SM); what overlaps them is
-  // the other chunks' dispatch and combine traffic
-  cudaError_t e;
   if (c > 0 && (e = cudaStreamWaitEvent(s, h->p2p_gemm_done[c - 1], 0)) != cudaSuccess)
     return cuda_fail(h, e, "gemm order");
   mark();  // gemm1 (inside run_expert_gemms: gemm1, mark, gemm2)
@@ -1090,7 +1099,7 @@ int p2p_chunk(vmoe_handle* h, int c, const void* x, int64_t T, void* out, float*
                              a.num_tiles, ws + p.hbuf, ch.region + h->p2p_y_off, H, s, mark,
                              check)) != VMOE_OK)
     return rc;
-  if (h->p2p.size() > 1 && (e = cudaEventRecord(h->p2p_gemm_done[c], s)) != cudaSuccess)
+  if (chained && (e = cudaEventRecord(h->p2p_gemm_done[c], s)) != cudaSuccess)
     return cuda_fail(h, e, "gemm order");
   mark();  // signal outputs ready, wait for every rank's, combine over NVLink
   if ((rc = check(launch_p2p_signal(a, 2, s), "signal outputs")) != VMOE_OK) return rc;
