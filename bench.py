@@ -57,7 +57,7 @@ def parse_args():
     p.add_argument("--cpu-seconds", type=float, default=10.0,
                    help="target CPU time of the cpu_baseline sample")
     p.add_argument("--no-cpu-baseline", action="store_true")
-    p.add_argument("--ep-chunks", type=int, default=2,
+    p.add_argument("--ep-chunks", type=int, default=4,
                    help="token chunks of the fused expert-parallel forward (overlap)")
     return p.parse_args()
 
