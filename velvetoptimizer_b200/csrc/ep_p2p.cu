@@ -275,10 +275,11 @@ size_t p2p_dispatch_smem(int E, int K, int G) {
 
 cudaError_t launch_p2p_dispatch(int dtype, const P2PArgs& a, const void* x,
                                 const int32_t* topk_idx, const int* excl, int64_t T,
-                                cudaStream_t s) {
+                                size_t min_smem, cudaStream_t s) {
   const unsigned nblk = static_cast<unsigned>((T + kTileM - 1) / kTileM);
   const unsigned grid = nblk > 0 ? nblk : 1;
-  const size_t smem = p2p_dispatch_smem(a.E, a.K, a.G);
+  size_t smem = p2p_dispatch_smem(a.E, a.K, a.G);
+  if (smem < min_smem) smem = min_smem;  // see launch_p2p_combine
   if (dtype == kF32) {
     auto kern = p2p_dispatch_kernel<float>;
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
@@ -291,15 +292,23 @@ cudaError_t launch_p2p_dispatch(int dtype, const P2PArgs& a, const void* x,
   return cudaGetLastError();
 }
 
+// `min_smem` > 0 makes each block claim that much shared memory (unused by the kernel) so
+// the transfer kernels cannot share an SM with a GEMM CTA and run only on the SMs the GEMMs
+// leave free: the GEMMs keep full speed while the links are busy.
 cudaError_t launch_p2p_combine(int dtype, const P2PArgs& a, const int32_t* topk_idx,
-                               const float* topk_w, int64_t T, void* out, cudaStream_t s) {
+                               const float* topk_w, int64_t T, void* out, size_t min_smem,
+                               cudaStream_t s) {
   if (T == 0) return cudaSuccess;
   const unsigned grid = static_cast<unsigned>((T + 7) / 8);
-  if (dtype == kF32)
-    p2p_combine_kernel<float><<<grid, 256, 0, s>>>(a, topk_idx, topk_w, T, static_cast<float*>(out));
-  else
-    p2p_combine_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>(a, topk_idx, topk_w, T,
-                                                           static_cast<__nv_bfloat16*>(out));
+  if (dtype == kF32) {
+    auto kern = p2p_combine_kernel<float>;
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(min_smem));
+    kern<<<grid, 256, min_smem, s>>>(a, topk_idx, topk_w, T, static_cast<float*>(out));
+  } else {
+    auto kern = p2p_combine_kernel<__nv_bfloat16>;
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(min_smem));
+    kern<<<grid, 256, min_smem, s>>>(a, topk_idx, topk_w, T, static_cast<__nv_bfloat16*>(out));
+  }
   return cudaGetLastError();
 }
 

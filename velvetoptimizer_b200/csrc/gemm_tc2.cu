@@ -284,7 +284,9 @@ cudaError_t launch_tc_gemm_pair(bool gated, const CUtensorMap& a_map, const CUte
   if (max_clusters < 1) return cudaErrorInvalidConfiguration;
   int64_t work = max_pair_tiles * args.n_tiles;
   if (work < 1) work = 1;
-  const int64_t pairs = work < max_clusters ? work : max_clusters;
+  int64_t pairs = work < max_clusters ? work : max_clusters;
+  if (pairs > num_sms / 2) pairs = num_sms / 2;  // the caller's SM budget
+  if (pairs < 1) pairs = 1;
   cfg.gridDim = dim3(static_cast<unsigned>(2 * pairs), 1, 1);
   if (gated)
     err = cudaLaunchKernelEx(&cfg, tc_gemm_pair_kernel<true>, a_map, b_map, args);

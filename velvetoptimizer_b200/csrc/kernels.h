@@ -132,9 +132,10 @@ cudaError_t launch_p2p_wait(const P2PArgs& a, int which, cudaStream_t s);
 cudaError_t launch_p2p_signal(const P2PArgs& a, int which, cudaStream_t s);
 cudaError_t launch_p2p_dispatch(int dtype, const P2PArgs& a, const void* x,
                                 const int32_t* topk_idx, const int* excl, int64_t T,
-                                cudaStream_t s);
+                                size_t min_smem, cudaStream_t s);
 cudaError_t launch_p2p_combine(int dtype, const P2PArgs& a, const int32_t* topk_idx,
-                               const float* topk_w, int64_t T, void* out, cudaStream_t s);
+                               const float* topk_w, int64_t T, void* out, size_t min_smem,
+                               cudaStream_t s);
 
 // ---- weight packing ------------------------------------------------------------------
 // dst[e][map(o)][k] = src[e][o][k] + s * sum_r lu[e][o][r] * ld[e][r][k]  (0 when padded)

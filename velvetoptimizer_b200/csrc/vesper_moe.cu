@@ -87,6 +87,7 @@ struct vmoe_handle {
   cudaEvent_t p2p_gemm_done[kMaxChunks] = {};  // orders the chunks' GEMMs one after another
   cudaEvent_t p2p_sent[kMaxChunks] = {};       // and their dispatches
   bool p2p_connected = false;
+  int p2p_reserve_sms = 0;  // SMs the chunked GEMMs leave to the transfer kernels
   // packed weights (library-owned)
   void* w_r = nullptr;
   float* b_r = nullptr;
@@ -301,7 +302,8 @@ int alloc(vmoe_handle* h, T** p, size_t bytes, const char* what) {
 template <typename Mark, typename Check>
 int run_expert_gemms(vmoe_handle* h, void* xp, int64_t max_rows, const int* tiles,
                      const int* ntiles, void* hb, void* yb, int64_t y_ld, cudaStream_t s,
-                     Mark&& mark, Check&& check) {
+                     Mark&& mark, Check&& check, int gemm_sms = 0) {
+  const int sms = gemm_sms > 0 ? gemm_sms : h->num_sms;  // persistent GEMM grid bound
   const int64_t H = h->H, max_tiles = max_rows / h->tile_rows;
   int rc;
   if (h->dtype == kF32) {
@@ -340,8 +342,8 @@ int run_expert_gemms(vmoe_handle* h, void* xp, int64_t max_rows, const int* tile
   a1.gamma = h->cfg.era_gamma;
   a1.status = h->status;
   const bool pair = h->tile_rows != kTileM;
-  if ((rc = check(pair ? launch_tc_gemm_pair(true, map_x, h->map_wgu, a1, max_tiles, h->num_sms, s)
-                       : launch_tc_gemm(true, map_x, h->map_wgu, a1, max_tiles, h->num_sms, s),
+  if ((rc = check(pair ? launch_tc_gemm_pair(true, map_x, h->map_wgu, a1, max_tiles, sms, s)
+                       : launch_tc_gemm(true, map_x, h->map_wgu, a1, max_tiles, sms, s),
                   "gemm1")) != VMOE_OK)
     return rc;
   mark();
@@ -359,8 +361,8 @@ int run_expert_gemms(vmoe_handle* h, void* xp, int64_t max_rows, const int* tile
   a2.bias_ld = h->Hpad;
   a2.gamma = 0.f;
   a2.status = h->status;
-  return check(pair ? launch_tc_gemm_pair(false, map_h, h->map_wd, a2, max_tiles, h->num_sms, s)
-                    : launch_tc_gemm(false, map_h, h->map_wd, a2, max_tiles, h->num_sms, s),
+  return check(pair ? launch_tc_gemm_pair(false, map_h, h->map_wd, a2, max_tiles, sms, s)
+                    : launch_tc_gemm(false, map_h, h->map_wd, a2, max_tiles, sms, s),
                "gemm2");
 }
 
@@ -971,6 +973,10 @@ int vmoe_ep_p2p_setup(vmoe_handle* h, int64_t max_tokens, int chunks, void* ipc_
   h->p2p_cap_rows = cap;
   h->p2p_max_tokens = max_tokens;
   h->p2p_chunk_tokens = chunk_tokens;
+  // overlapped chunks: keep 16 SMs out of the GEMM grid for the NVLink transfer kernels
+  h->p2p_reserve_sms = chunks > 1 ? 16 : 0;
+  if (const char* r = getenv("VMOE_EP_RESERVE_SMS")) h->p2p_reserve_sms = atoi(r);
+  if (h->p2p_reserve_sms < 0 || h->p2p_reserve_sms > h->num_sms / 2) h->p2p_reserve_sms = 0;
   return VMOE_OK;
 }
 
@@ -1087,7 +1093,12 @@ int p2p_chunk(vmoe_handle* h, int c, const void* x, int64_t T, void* out, float*
   if (c > 0 && (e = cudaStreamWaitEvent(s, h->p2p_sent[c - 1], 0)) != cudaSuccess)
     return cuda_fail(h, e, "dispatch order");
   mark();  // dispatch over NVLink + wait for every rank's rows
-  if ((rc = check(launch_p2p_dispatch(h->dtype, a, x, idx, excl, T, s), "dispatch")) != VMOE_OK)
+  // with reserved SMs the transfer kernels claim 48 KB of shared memory per block, more
+  // than a GEMM CTA leaves free, so they only run on the reserved SMs
+  const size_t xfer_smem = h->p2p_reserve_sms > 0 ? 48 * 1024 : 0;
+  const int gemm_sms = h->num_sms - h->p2p_reserve_sms;
+  if ((rc = check(launch_p2p_dispatch(h->dtype, a, x, idx, excl, T, xfer_smem, s), "dispatch")) !=
+      VMOE_OK)
     return rc;
   if (chained && (e = cudaEventRecord(h->p2p_sent[c], s)) != cudaSuccess)
     return cuda_fail(h, e, "dispatch order");
@@ -1097,14 +1108,15 @@ int p2p_chunk(vmoe_handle* h, int c, const void* x, int64_t T, void* out, float*
   mark();  // gemm1 (inside run_expert_gemms: gemm1, mark, gemm2)
   if ((rc = run_expert_gemms(h, ch.region + h->p2p_recv_off, h->p2p_cap_rows, a.tile_expert,
                              a.num_tiles, ws + p.hbuf, ch.region + h->p2p_y_off, H, s, mark,
-                             check)) != VMOE_OK)
+                             check, gemm_sms)) != VMOE_OK)
     return rc;
   if (chained && (e = cudaEventRecord(h->p2p_gemm_done[c], s)) != cudaSuccess)
     return cuda_fail(h, e, "gemm order");
   mark();  // signal outputs ready, wait for every rank's, combine over NVLink
   if ((rc = check(launch_p2p_signal(a, 2, s), "signal outputs")) != VMOE_OK) return rc;
   if ((rc = check(launch_p2p_wait(a, 2, s), "wait outputs")) != VMOE_OK) return rc;
-  if ((rc = check(launch_p2p_combine(h->dtype, a, idx, tw, T, out, s), "combine")) != VMOE_OK)
+  if ((rc = check(launch_p2p_combine(h->dtype, a, idx, tw, T, out, xfer_smem, s), "combine")) !=
+      VMOE_OK)
     return rc;
   mark();
   return VMOE_OK;
