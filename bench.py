@@ -57,8 +57,9 @@ def parse_args():
     p.add_argument("--cpu-seconds", type=float, default=10.0,
                    help="target CPU time of the cpu_baseline sample")
     p.add_argument("--no-cpu-baseline", action="store_true")
-    p.add_argument("--ep-chunks", type=int, default=4,
-                   help="token chunks of the fused expert-parallel forward (overlap)")
+    p.add_argument("--ep-chunks", type=int, default=0,
+                   help="token chunks of the fused expert-parallel forward (overlap); "
+                        "0 = 1 chunk up to 2 GPUs, 4 beyond (the measured best)")
     return p.parse_args()
 
 
@@ -233,6 +234,8 @@ def run_ours(args, rank, world, local_rank):
     x = torch.randn(T, H, generator=g, device=dev).to(torch.bfloat16).reshape(
         w["batch"], T // w["batch"], H)
 
+    if args.ep_chunks <= 0:
+        args.ep_chunks = 1 if world <= 2 else 4
     if world == 1:
         # the drop-in module (python/vesper/model.py MoELayer interface) on one GPU
         layer = build_layer(w, dev, seed=0)

@@ -973,9 +973,10 @@ int vmoe_ep_p2p_setup(vmoe_handle* h, int64_t max_tokens, int chunks, void* ipc_
   h->p2p_cap_rows = cap;
   h->p2p_max_tokens = max_tokens;
   h->p2p_chunk_tokens = chunk_tokens;
-  // overlapped chunks: keep 16 SMs out of the GEMM grid for the NVLink transfer kernels
-  h->p2p_reserve_sms = chunks > 1 ? 16 : 0;
-  if (const char* r = getenv("VMOE_EP_RESERVE_SMS")) h->p2p_reserve_sms = atoi(r);
+  // VMOE_EP_RESERVE_SMS=n keeps n SMs out of the chunked GEMM grid for the NVLink transfer
+  // kernels (off by default: on 2 GPUs it measured slower)
+  h->p2p_reserve_sms = 0;
+  if (const char* r = getenv("VMOE_EP_RESERVE_SMS")) h->p2p_reserve_sms = chunks > 1 ? atoi(r) : 0;
   if (h->p2p_reserve_sms < 0 || h->p2p_reserve_sms > h->num_sms / 2) h->p2p_reserve_sms = 0;
   return VMOE_OK;
 }
