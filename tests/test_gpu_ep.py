@@ -29,3 +29,18 @@ def test_expert_parallel_matches_single_gpu():
     r = subprocess.run(cmd, capture_output=True, text=True, env=env)
     assert r.returncode == 0, r.stdout[-4000:] + r.stderr[-4000:]
     assert r.stdout.count("EP_OK") == n, r.stdout[-2000:]
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2,
+                    reason="needs 2 GPUs")
+def test_expert_parallel_peer_timeout_is_reported():
+    """A rank that stops launching makes its peer's bounded waits expire: the peer's forward
+    ends with a timeout status and its context stays usable (no GPU fault involved)."""
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    cmd = ["timeout", "-k", "30", "300", sys.executable, "-m", "torch.distributed.run",
+           "--nnodes=1", "--nproc-per-node=2", "--master-addr=127.0.0.1",
+           f"--master-port={_free_port()}", os.path.join(HERE, "ep_fault_worker.py")]
+    r = subprocess.run(cmd, capture_output=True, text=True, env=env)
+    assert r.returncode == 0, r.stdout[-4000:] + r.stderr[-4000:]
+    assert r.stdout.count("FAULT_OK") == 2, r.stdout[-2000:]
+

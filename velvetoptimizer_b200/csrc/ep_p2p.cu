@@ -102,6 +102,7 @@ p2p_dispatch_kernel(P2PArgs a, const T* __restrict__ x, const int32_t* __restric
   for (int i = tid; i < 4 * E; i += 128) masks[i] = 0u;
   __syncthreads();
   const bool ok = ok_s != 0;
+  if (!ok && blk == 0 && tid == 0) *a.num_tiles = 0;  // no GEMM work after a failed wait
   if (ok) {
     const int* all_counts = reinterpret_cast<const int*>(a.peer_base[a.me] + a.counts_off);
     for (int i = tid; i < G * E; i += 128) cnt[i] = all_counts[i];
@@ -128,6 +129,7 @@ p2p_dispatch_kernel(P2PArgs a, const T* __restrict__ x, const int32_t* __restric
     }
     // block 0 writes this rank's tile map (segments of its local experts)
     if (blk == 0 && tid == 0) {
+      *a.num_tiles = 0;
       int64_t t0 = 0;
       for (int el = 0; el < El; ++el) {
         int64_t n = 0;
@@ -160,6 +162,8 @@ p2p_dispatch_kernel(P2PArgs a, const T* __restrict__ x, const int32_t* __restric
         d = e / El;
         row = base_s[e] + excl[blk * E + e] + wbase[warp * E + e] + __popc(masks[warp * E + e] & lt);
       }
+    }
+    if (t < T_tok) {  // -1 also when the wait gave up: the combine then skips the row
       a.dest_rank[t * K + k] = d;
       a.dest_row[t * K + k] = row;
     }
@@ -238,7 +242,7 @@ p2p_combine_kernel(P2PArgs a, const int32_t* __restrict__ topk_idx, const float*
 #pragma unroll
     for (int i = 0; i < V; ++i) acc[i] = 0.f;
     for (int j = 0; j < n; ++j) {
-      if (ord_d[j] < 0) continue;
+      if (ord_d[j] < 0 || ord_d[j] >= a.G || ord_r[j] < 0 || ord_r[j] >= a.cap_rows) continue;
       const T* y = reinterpret_cast<const T*>(a.peer_base[ord_d[j]] + a.y_off) +
                    static_cast<int64_t>(ord_r[j]) * a.H;
       float f[V];
