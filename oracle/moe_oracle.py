@@ -87,6 +87,24 @@ def near_ties(probs, k, rel=1e-4):
     return gap <= rel * s[:, k - 1]
 
 
+def same_expert_sets(a, b):
+    """Row-wise equality of the chosen expert SETS of two [T, K] index arrays.
+
+    The order inside a token's K choices follows the probabilities; where two chosen
+    experts are a near-tie, two correct implementations may order them differently, which
+    changes nothing downstream except the fp add order of the combine.
+    """
+    return np.all(np.sort(a, axis=-1) == np.sort(b, axis=-1), axis=-1)
+
+
+def order_follows_probs(idx, probs):
+    """True per token when idx lists experts by (probability desc, index asc)."""
+    p = np.take_along_axis(probs, idx, axis=-1)
+    dp = p[:, :-1] - p[:, 1:]
+    di = idx[:, :-1] - idx[:, 1:]
+    return np.all((dp > 0) | ((dp == 0) & (di < 0)), axis=-1)
+
+
 def dispatch(topk_idx, experts):
     """Per-expert counts and the stable expert-major permutation (model.py:339-349).
 

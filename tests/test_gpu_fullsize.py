@@ -147,7 +147,9 @@ def test_full_size_parity_and_invariants(name):
     probs = O.softmax(logits)
     _, oidx = O.topk_lowest_index(probs, K)
     tie = O.near_ties(probs, K, rel=1e-4)
-    assert np.array_equal(idx[~tie], oidx[~tie])
+    assert O.same_expert_sets(idx[~tie], oidx[~tie]).all()
+    # the GPU lists each token's experts by its own probabilities, lowest index on ties
+    assert O.order_follows_probs(idx, O.softmax(r1["logits"].cpu().numpy())).all()
     aux = float(O.load_balancing_loss(O.softmax(r1["logits"].cpu().numpy()), idx, E))
     assert abs(float(r1["aux"].item()) - aux) <= 1e-4 * abs(aux)
 

@@ -91,6 +91,16 @@ def test_topk_lowest_index_tie_break():
     assert idx.tolist() == [[0, 1], [1, 2]]
 
 
+def test_expert_set_and_order_helpers():
+    a = np.array([[3, 1], [0, 2]])
+    b = np.array([[1, 3], [0, 1]])
+    assert O.same_expert_sets(a, b).tolist() == [True, False]
+    p = np.array([[0.1, 0.4, 0.1, 0.4]])
+    assert O.order_follows_probs(np.array([[1, 3]]), p).all()      # tie -> lowest index first
+    assert not O.order_follows_probs(np.array([[3, 1]]), p).all()
+    assert not O.order_follows_probs(np.array([[0, 1]]), p).all()
+
+
 def test_dispatch_is_stable_expert_major():
     idx = np.array([[2, 0], [0, 1], [2, 1], [0, 2]])
     counts, tok, slot = O.dispatch(idx, 3)
