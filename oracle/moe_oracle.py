@@ -97,11 +97,17 @@ def same_expert_sets(a, b):
     return np.all(np.sort(a, axis=-1) == np.sort(b, axis=-1), axis=-1)
 
 
-def order_follows_probs(idx, probs):
-    """True per token when idx lists experts by (probability desc, index asc)."""
+def order_follows_probs(idx, probs, rel=0.0):
+    """True per token when idx lists experts by (probability desc, index asc).
+
+    With ``rel`` > 0 (``probs`` recomputed elsewhere, last-ulp differences possible) only
+    clear inversions count: a later choice more than ``rel`` above an earlier one.
+    """
     p = np.take_along_axis(probs, idx, axis=-1)
     dp = p[:, :-1] - p[:, 1:]
     di = idx[:, :-1] - idx[:, 1:]
+    if rel > 0:
+        return np.all(dp >= -rel * p[:, :-1], axis=-1)
     return np.all((dp > 0) | ((dp == 0) & (di < 0)), axis=-1)
 
 

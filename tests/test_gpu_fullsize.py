@@ -149,7 +149,7 @@ def test_full_size_parity_and_invariants(name):
     tie = O.near_ties(probs, K, rel=1e-4)
     assert O.same_expert_sets(idx[~tie], oidx[~tie]).all()
     # the GPU lists each token's experts by its own probabilities, lowest index on ties
-    assert O.order_follows_probs(idx, O.softmax(r1["logits"].cpu().numpy())).all()
+    assert O.order_follows_probs(idx, O.softmax(r1["logits"].cpu().numpy()), rel=1e-5).all()
     aux = float(O.load_balancing_loss(O.softmax(r1["logits"].cpu().numpy()), idx, E))
     assert abs(float(r1["aux"].item()) - aux) <= 1e-4 * abs(aux)
 

@@ -137,7 +137,7 @@ def test_bf16_matches_oracle(name):
     tie = O.near_ties(ora["probs"], case.top_k, rel=1e-4)
     assert O.norm_rel_err(res["logits"], ora["logits"]) < 1e-4
     assert O.same_expert_sets(res["topk_idx"][~tie], ora["topk_idx"][~tie]).all()
-    assert O.order_follows_probs(res["topk_idx"], O.softmax(res["logits"])).all()
+    assert O.order_follows_probs(res["topk_idx"], O.softmax(res["logits"]), rel=1e-5).all()
     check_dispatch(layer, case.tokens, res, res["topk_idx"])
     forced = O.moe_forward(inp, case, force_idx=res["topk_idx"])
     err = O.norm_rel_err(res["out"], forced["out"])
