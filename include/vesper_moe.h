@@ -229,6 +229,17 @@ VMOE_API int vmoe_ep_p2p_forward(vmoe_handle* h, const void* x, int64_t tokens, 
                                  float* router_logits, float* aux_loss, void* workspace,
                                  size_t workspace_bytes, void* stream);
 
+/* ---- Dense FFN -----------------------------------------------------------------------
+ * The non-MoE layers' FeedForward (python/vesper/model.py:249-270):
+ *   out = down(ERA(gate(x)) * up(x)),  gate/up FlyLoRA linears folded as for the experts,
+ * on the same grouped GEMMs as the experts (one expert, no router).  vmoe_ffn_create takes a
+ * vmoe_config whose num_experts / top_k / capacity are ignored; vmoe_set_weights then takes
+ * the gate/up/down tensors with a leading expert dimension of 1 (router_w may be NULL). */
+VMOE_API int vmoe_ffn_create(const vmoe_config* cfg, int device, vmoe_handle** out);
+VMOE_API int vmoe_ffn_workspace_size(const vmoe_handle* h, int64_t tokens, size_t* bytes);
+VMOE_API int vmoe_ffn_forward(vmoe_handle* h, const void* x, int64_t tokens, void* out,
+                              void* workspace, size_t workspace_bytes, void* stream);
+
 /* Read (and clear) the device status word the kernels write when a bounded wait gives
  * up or an index check fails.  Synchronises `stream`.  *code = 0 when all is well. */
 VMOE_API int vmoe_device_status(vmoe_handle* h, int32_t* code, void* stream);

@@ -168,6 +168,13 @@ def expert_ffn(x_e, p, e, gamma, scaling, dtype):
     return _mm(h, p["w_d"][e], dtype) + p["b_d"][e].astype(dtype)
 
 
+def ffn_forward(p, case, dtype=np.float32):
+    """Dense FeedForward: down(ERA(gate(x)) * up(x)) with FlyLoRA (model.py:249-270).
+
+    ``p`` holds one expert's weights at index 0 (``make_inputs`` with experts=1)."""
+    return expert_ffn(p["x"], p, 0, case.era_gamma, case.lora_scaling, dtype)
+
+
 def load_balancing_loss(probs, topk_idx, experts):
     """Switch-Transformer aux loss E * sum_e f_e * P_e  (model.py:366-385)."""
     t, k = topk_idx.shape

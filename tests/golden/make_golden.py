@@ -114,6 +114,47 @@ def run_reference(case: MoECase):
     }
 
 
+# dense FeedForward cases (python/vesper/model.py:249-270): the non-MoE layers' FFN
+FFN_CASES = {
+    "ffn_t64_lora_bias": MoECase(tokens=64, batch=2, hidden=128, inter=256, experts=1, top_k=1,
+                                 lora_on=True, bias_std=0.05, seed=21),
+    "ffn_t3_small": MoECase(tokens=3, batch=1, hidden=32, inter=48, experts=1, top_k=1, seed=22),
+}
+
+
+def run_reference_ffn(case: MoECase):
+    import torch
+    sys.path.insert(0, REFERENCE_PY)
+    from vesper.config import VesperConfig  # noqa: E402
+    from vesper.model import FeedForward  # noqa: E402
+
+    inp = make_inputs(case)
+    cfg = VesperConfig(hidden_size=case.hidden, intermediate_size=case.inter, num_heads=1,
+                       era_gamma=case.era_gamma, flylora_rank=case.lora_rank,
+                       flylora_alpha=case.lora_alpha)
+    torch.manual_seed(case.seed)
+    ffn = FeedForward(cfg)
+    sd = ffn.state_dict()
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a))  # noqa: E731
+    new = {}
+    for p, name in (("g", "gate_proj"), ("u", "up_proj")):
+        new[f"{name}.base.weight"] = t(inp[f"w_{p}"][0])
+        new[f"{name}.base.bias"] = t(inp[f"b_{p}"][0])
+        new[f"{name}.lora_down.weight"] = t(inp[f"a_{p}"][0])
+        new[f"{name}.lora_down.bias"] = t(inp[f"ba_{p}"][0])
+        new[f"{name}.lora_up.weight"] = t(inp[f"l_{p}"][0])
+        new[f"{name}.lora_up.bias"] = t(inp[f"bl_{p}"][0])
+        new[f"{name}.proj_a"] = sd[f"{name}.proj_a"]
+    new["down_proj.weight"] = t(inp["w_d"][0])
+    new["down_proj.bias"] = t(inp["b_d"][0])
+    assert set(new) == set(sd), set(sd) ^ set(new)
+    ffn.load_state_dict(new)
+    x = torch.from_numpy(inp["x"]).reshape(case.batch, case.seq, case.hidden)
+    with torch.no_grad():
+        out = ffn(x)
+    return {"out": out.reshape(case.tokens, case.hidden).numpy()}
+
+
 def dump_state_dict_keys():
     """Record the reference MoELayer's state_dict keys and shapes for a small config."""
     sys.path.insert(0, REFERENCE_PY)
@@ -124,9 +165,11 @@ def dump_state_dict_keys():
     cfg = VesperConfig(hidden_size=64, intermediate_size=96, num_heads=1, flylora_rank=8,
                        flylora_alpha=16.0).with_moe(num_experts=3, top_k=2)
     keys = {k: list(v.shape) for k, v in MoELayer(cfg).state_dict().items()}
+    from vesper.model import FeedForward  # noqa: E402
+    ffn_keys = {k: list(v.shape) for k, v in FeedForward(cfg).state_dict().items()}
     path = os.path.join(HERE, "state_dict_keys.json")
     with open(path, "w") as f:
-        json.dump({"config": conf, "keys": keys}, f, indent=1)
+        json.dump({"config": conf, "keys": keys, "ffn_keys": ffn_keys}, f, indent=1)
     print(f"state_dict keys: {len(keys)} -> {path}")
 
 
@@ -135,6 +178,14 @@ def main(names=None):
     torch.set_num_threads(os.cpu_count() or 1)
     if not names:
         dump_state_dict_keys()
+    for name, case in FFN_CASES.items():
+        if names and name not in names:
+            continue
+        res = run_reference_ffn(case)
+        path = os.path.join(HERE, f"{name}.npz")
+        np.savez_compressed(path, case=np.asarray(json.dumps(case.to_dict())),
+                            torch_version=np.asarray(torch.__version__), **res)
+        print(f"{name}: out {res['out'].shape} -> {path}")
     for name, case in CASES.items():
         if names and name not in names:
             continue

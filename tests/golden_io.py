@@ -11,7 +11,14 @@ GOLDEN_DIR = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
 
 
 def golden_names():
-    return sorted(os.path.basename(p)[:-4] for p in glob.glob(os.path.join(GOLDEN_DIR, "*.npz")))
+    """The MoE-layer goldens (the dense FeedForward ones start with 'ffn_')."""
+    return sorted(n for n in (os.path.basename(p)[:-4]
+                              for p in glob.glob(os.path.join(GOLDEN_DIR, "*.npz")))
+                  if not n.startswith("ffn_"))
+
+
+def ffn_golden_names():
+    return sorted(os.path.basename(p)[:-4] for p in glob.glob(os.path.join(GOLDEN_DIR, "ffn_*.npz")))
 
 
 def load_golden(name):

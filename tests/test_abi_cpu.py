@@ -108,6 +108,13 @@ def test_state_dict_keys_match_reference(golden_dir):
     assert got == ref["keys"]
 
 
+def test_feedforward_state_dict_keys_match_reference(golden_dir):
+    from velvetoptimizer_b200 import FeedForward
+    ref = json.load(open(os.path.join(golden_dir, "state_dict_keys.json")))
+    m = FeedForward(MoEConfig(**ref["config"]))
+    assert {k: list(v.shape) for k, v in m.state_dict().items()} == ref["ffn_keys"]
+
+
 def test_config_validation_mirrors_reference():
     with pytest.raises(AssertionError):
         MoELayer(MoEConfig(moe_num_experts=4, moe_top_k=5))

@@ -14,7 +14,7 @@ import torch
 from oracle import moe_oracle as O
 from oracle.inputs import MoECase, bf16_inputs, make_inputs
 from tests.abi_runner import AbiLayer
-from tests.golden_io import golden_names, load_golden
+from tests.golden_io import ffn_golden_names, golden_names, load_golden
 
 pytestmark = pytest.mark.gpu
 
@@ -259,3 +259,73 @@ def test_module_bf16_lora_matches_oracle():
     forced = O.moe_forward(ib, case, force_idx=idx)
     assert O.norm_rel_err(out.float().reshape(-1, case.hidden).cpu().numpy(), forced["out"]) < BF16_TOL
     m.close()
+
+
+# ----------------------------------------------------------------------------------------
+# the dense FeedForward (non-MoE layers) on the same GEMMs
+# ----------------------------------------------------------------------------------------
+def _ffn_run(case, inp, dtype):
+    import ctypes
+    from tests.abi_runner import abi_config, _WEIGHT_KEYS
+    from velvetoptimizer_b200 import _lib
+    tdt = torch.float32 if dtype == "f32" else torch.bfloat16
+    h = _lib.Handle(abi_config(case, dtype), 0, dense=True)
+    dev = torch.device("cuda", 0)
+    w = {k: torch.from_numpy(np.ascontiguousarray(inp[v])).to(dev, tdt)
+         for k, v in _WEIGHT_KEYS.items() if not k.startswith("router")}
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    h.set_weights(_lib.VmoeWeights(**{k: ctypes.c_void_p(t.data_ptr()) for k, t in w.items()}),
+                  stream)
+    x = torch.from_numpy(inp["x"]).to(dev, tdt)
+    out = torch.empty_like(x)
+    n = ctypes.c_size_t()
+    _lib.check(h.lib.vmoe_ffn_workspace_size(h.ptr, x.shape[0], ctypes.byref(n)), h.ptr)
+    ws = torch.empty(n.value, dtype=torch.uint8, device=dev)
+    _lib.check(h.lib.vmoe_ffn_forward(h.ptr, ctypes.c_void_p(x.data_ptr()), x.shape[0],
+                                      ctypes.c_void_p(out.data_ptr()), ctypes.c_void_p(ws.data_ptr()),
+                                      ws.numel(), ctypes.c_void_p(stream)), h.ptr)
+    torch.cuda.synchronize()
+    assert h.device_status(stream) == 0
+    h.close()
+    return out.float().cpu().numpy()
+
+
+@pytest.mark.parametrize("name", ffn_golden_names())
+def test_ffn_fp32_matches_reference_goldens(name):
+    case, g = load_golden(name)
+    got = _ffn_run(case, make_inputs(case), "f32")
+    assert O.norm_rel_err(got, g["out"]) < FP32_TOL
+
+
+@pytest.mark.parametrize("case", [
+    MoECase(tokens=300, hidden=256, inter=512, experts=1, top_k=1, lora_on=True, bias_std=0.05, seed=41),
+    MoECase(tokens=77, hidden=200, inter=136, experts=1, top_k=1, seed=42),
+])
+def test_ffn_bf16_matches_oracle(case):
+    inp = bf16_inputs(make_inputs(case))
+    got = _ffn_run(case, inp, "bf16")
+    assert O.norm_rel_err(got, O.ffn_forward(inp, case)) < BF16_TOL
+
+
+def test_ffn_module_matches_reference_golden():
+    from velvetoptimizer_b200 import FeedForward, MoEConfig
+    case, g = load_golden("ffn_t64_lora_bias")
+    inp = make_inputs(case)
+    m = FeedForward(MoEConfig(hidden_size=case.hidden, intermediate_size=case.inter,
+                              flylora_rank=case.lora_rank, flylora_alpha=case.lora_alpha,
+                              era_gamma=case.era_gamma))
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a))  # noqa: E731
+    sd = dict(m.state_dict())
+    for p, nm in (("g", "gate_proj"), ("u", "up_proj")):
+        sd[f"{nm}.base.weight"], sd[f"{nm}.base.bias"] = t(inp[f"w_{p}"][0]), t(inp[f"b_{p}"][0])
+        sd[f"{nm}.lora_down.weight"], sd[f"{nm}.lora_down.bias"] = t(inp[f"a_{p}"][0]), t(inp[f"ba_{p}"][0])
+        sd[f"{nm}.lora_up.weight"], sd[f"{nm}.lora_up.bias"] = t(inp[f"l_{p}"][0]), t(inp[f"bl_{p}"][0])
+    sd["down_proj.weight"], sd["down_proj.bias"] = t(inp["w_d"][0]), t(inp["b_d"][0])
+    m.load_state_dict(sd)
+    m = m.cuda()
+    x = torch.from_numpy(inp["x"]).reshape(case.batch, case.seq, case.hidden).cuda()
+    out = m(x)
+    assert out.shape == x.shape
+    assert O.norm_rel_err(out.reshape(-1, case.hidden).cpu().numpy(), g["out"]) < FP32_TOL
+    m.close()
+

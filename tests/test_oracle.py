@@ -10,13 +10,14 @@ import pytest
 
 from oracle import moe_oracle as O
 from oracle.inputs import make_inputs, round_bf16
-from tests.golden_io import golden_names, load_golden
+from tests.golden_io import ffn_golden_names, golden_names, load_golden
 
 NAMES = golden_names()
 
 
 def test_goldens_present():
     assert "c1_fp32" in NAMES and len(NAMES) >= 8
+    assert len(ffn_golden_names()) >= 2
 
 
 @pytest.mark.parametrize("name", NAMES)
@@ -47,6 +48,14 @@ def test_oracle_matches_reference(name):
     assert abs(float(forced["aux"]) - float(g["aux"])) <= 1e-5 * abs(float(g["aux"]))
     if not tie.any():
         assert O.norm_rel_err(res["out"], g["out"]) < 1e-5
+
+
+@pytest.mark.parametrize("name", ffn_golden_names())
+def test_oracle_ffn_matches_reference(name):
+    # the reference's dense FeedForward (python/vesper/model.py:249-270)
+    case, g = load_golden(name)
+    out = O.ffn_forward(make_inputs(case), case)
+    assert O.norm_rel_err(out, g["out"]) < 1e-5
 
 
 def test_tied_router_case_is_all_ties():

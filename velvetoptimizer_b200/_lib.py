@@ -35,7 +35,8 @@ EXPORTED = (
     "vmoe_last_launch_count", "vmoe_last_error", "vmoe_status_string", "vmoe_abi_version",
     "vmoe_create_ep", "vmoe_ep_workspace_size", "vmoe_ep_route", "vmoe_ep_experts",
     "vmoe_ep_combine", "vmoe_ep_p2p_setup", "vmoe_ep_p2p_connect", "vmoe_ep_p2p_workspace_size",
-    "vmoe_ep_p2p_forward", "vmoe_gemm_tile_rows",
+    "vmoe_ep_p2p_forward", "vmoe_gemm_tile_rows", "vmoe_ffn_create", "vmoe_ffn_workspace_size",
+    "vmoe_ffn_forward",
 )
 
 
@@ -134,6 +135,12 @@ def load() -> ctypes.CDLL:
     lib.vmoe_stage_name.restype = c_char_p
     lib.vmoe_last_launch_count.argtypes = [H]
     lib.vmoe_last_launch_count.restype = c_int
+    lib.vmoe_ffn_create.argtypes = [POINTER(VmoeConfig), c_int, POINTER(H)]
+    lib.vmoe_ffn_create.restype = c_int
+    lib.vmoe_ffn_workspace_size.argtypes = [H, c_int64, POINTER(c_size_t)]
+    lib.vmoe_ffn_workspace_size.restype = c_int
+    lib.vmoe_ffn_forward.argtypes = [H, c_void_p, c_int64, c_void_p, c_void_p, c_size_t, c_void_p]
+    lib.vmoe_ffn_forward.restype = c_int
     lib.vmoe_gemm_tile_rows.argtypes = [H]
     lib.vmoe_gemm_tile_rows.restype = c_int
     lib.vmoe_last_error.argtypes = [H]
@@ -161,13 +168,14 @@ def check(rc: int, handle=None, what: str = "vmoe call") -> None:
 class Handle:
     """Owns one ``vmoe_handle`` (one layer configuration on one device)."""
 
-    def __init__(self, cfg: VmoeConfig, device: int):
+    def __init__(self, cfg: VmoeConfig, device: int, dense: bool = False):
         self.lib = load()
         self.cfg = cfg
         self.device = device
         self.ptr = c_void_p()
-        check(self.lib.vmoe_create(ctypes.byref(cfg), device, ctypes.byref(self.ptr)),
-              None, "vmoe_create")
+        create = self.lib.vmoe_ffn_create if dense else self.lib.vmoe_create
+        check(create(ctypes.byref(cfg), device, ctypes.byref(self.ptr)), None,
+              "vmoe_ffn_create" if dense else "vmoe_create")
 
     def close(self) -> None:
         if self.ptr:

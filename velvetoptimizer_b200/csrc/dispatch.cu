@@ -244,7 +244,20 @@ __global__ void aux_merge_kernel(const char* ws, size_t stride, size_t counts_of
   *aux = static_cast<float>(E) * s;
 }
 
+// ---- 6. dense layer: every tile is expert 0 -------------------------------------------
+__global__ void fill_tiles_kernel(int* __restrict__ tile_expert, int n, int* __restrict__ num_tiles) {
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x)
+    tile_expert[i] = 0;
+  if (blockIdx.x == 0 && threadIdx.x == 0) *num_tiles = n;
+}
+
 }  // namespace
+
+cudaError_t launch_fill_tiles(int* tile_expert, int n, int* num_tiles, cudaStream_t s) {
+  fill_tiles_kernel<<<(n + 255) / 256 > 0 ? (n + 255) / 256 : 1, 256, 0, s>>>(tile_expert, n,
+                                                                            num_tiles);
+  return cudaGetLastError();
+}
 
 cudaError_t launch_aux_merge_ws(const void* ws, size_t stride, size_t counts_off, size_t psum_off,
                                 int chunks, int64_t T, int E, int K, float* aux, cudaStream_t s) {

@@ -39,6 +39,9 @@ cudaError_t launch_plan(const int* counts, const float* psum_tot, int64_t T, int
 cudaError_t launch_aux_merge_ws(const void* ws, size_t stride, size_t counts_off, size_t psum_off,
                                 int chunks, int64_t T, int E, int K, float* aux, cudaStream_t s);
 
+// Tile map of a dense layer: n tiles, all expert 0.
+cudaError_t launch_fill_tiles(int* tile_expert, int n, int* num_tiles, cudaStream_t s);
+
 // Stable expert-major slots for every (token, k) and the row gather x -> x_perm.
 cudaError_t launch_dispatch(int dtype, const void* x, const int32_t* topk_idx, const int* excl,
                             const int* offs, int64_t T, int H, int E, int K, int64_t capacity,

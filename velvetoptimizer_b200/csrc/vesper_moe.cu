@@ -100,6 +100,7 @@ struct vmoe_handle {
   int* status = nullptr;
   CUtensorMap map_wgu{}, map_wd{};
   int tile_rows = kTileM;  // GEMM M tile: 256 with CTA-pair GEMMs (bf16), else 128
+  bool dense = false;      // a dense FeedForward handle (one expert, no router)
   CUtensorMap map_wr{};   // router weights for the tensor-core router (bf16, E <= 64)
   int router_bn = 0;      // its N tile; 0 = CUDA-core router
   bool ready = false;
@@ -524,7 +525,7 @@ int vmoe_destroy(vmoe_handle* h) {
 int vmoe_set_weights(vmoe_handle* h, const vmoe_weights* w, void* stream) {
   if (!h) return VMOE_ERR_INVALID_ARG;
   if (!w) return fail(h, VMOE_ERR_INVALID_ARG, "weights is NULL");
-  if (!w->router_w || !w->gate_w || !w->up_w || !w->down_w)
+  if ((!w->router_w && !h->dense) || !w->gate_w || !w->up_w || !w->down_w)
     return fail(h, VMOE_ERR_INVALID_ARG, "router_w, gate_w, up_w and down_w are required");
   DeviceGuard g(h->device);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
@@ -548,8 +549,11 @@ int vmoe_set_weights(vmoe_handle* h, const vmoe_weights* w, void* stream) {
   if ((rc = alloc(h, &h->b_d, El * Hpad * 4, "down bias")) != VMOE_OK) return rc;
 
   cudaError_t e;
-  // router: plain copy of W_r, bias to fp32
-  e = cudaMemcpyAsync(h->w_r, w->router_w, E * H * elt, cudaMemcpyDeviceToDevice, s);
+  // router: plain copy of W_r, bias to fp32 (zeros for a dense handle)
+  if (w->router_w)
+    e = cudaMemcpyAsync(h->w_r, w->router_w, E * H * elt, cudaMemcpyDeviceToDevice, s);
+  else
+    e = cudaMemsetAsync(h->w_r, 0, E * H * elt, s);
   if (e != cudaSuccess) return cuda_fail(h, e, "router weight copy");
   {
     PackBiasArgs b{h->dtype, w->router_b, nullptr, nullptr, nullptr, 0, 0.f,
@@ -1182,6 +1186,98 @@ int vmoe_ep_p2p_forward(vmoe_handle* h, const void* x, int64_t tokens, void* out
     ++h->last_launches;
   }
   if (prof) ++h->prof_count;
+  return VMOE_OK;
+}
+
+int vmoe_ffn_create(const vmoe_config* cfg, int device, vmoe_handle** out) {
+  if (!cfg || !out) return VMOE_ERR_INVALID_ARG;
+  vmoe_config c = *cfg;
+  c.num_experts = 2;  // passes the MoE checks; the handle below holds one expert
+  c.top_k = 1;
+  c.capacity = 0;
+  const int rc = vmoe_create(&c, device, out);
+  if (rc != VMOE_OK) return rc;
+  vmoe_handle* h = *out;
+  h->cfg.num_experts = 1;
+  h->E = h->E_local = 1;
+  h->K = 1;
+  h->dense = true;
+  return VMOE_OK;
+}
+
+namespace {
+struct FfnPlan {
+  int64_t max_rows = 0;
+  size_t xp = 0, h = 0, y = 0, tiles = 0, ntiles = 0, total = 0;
+};
+FfnPlan make_ffn_plan(const vmoe_handle* h, int64_t T) {
+  FfnPlan p;
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    const size_t o = off;
+    off += (bytes + 255) & ~static_cast<size_t>(255);
+    return o;
+  };
+  const size_t elt = dtype_bytes(h->dtype);
+  p.max_rows = round_up(T > 0 ? T : 1, h->tile_rows);
+  p.xp = take(static_cast<size_t>(p.max_rows) * h->H * elt);
+  p.h = take(static_cast<size_t>(p.max_rows) * h->Ipad * elt);
+  p.y = take(static_cast<size_t>(p.max_rows) * h->Hpad * elt);
+  p.tiles = take(p.max_rows / h->tile_rows * 4);
+  p.ntiles = take(4);
+  p.total = off;
+  return p;
+}
+}  // namespace
+
+int vmoe_ffn_workspace_size(const vmoe_handle* h, int64_t tokens, size_t* bytes) {
+  if (!h || !bytes || tokens < 0 || !h->dense) return VMOE_ERR_INVALID_ARG;
+  *bytes = make_ffn_plan(h, tokens).total;
+  return VMOE_OK;
+}
+
+int vmoe_ffn_forward(vmoe_handle* h, const void* x, int64_t tokens, void* out, void* workspace,
+                     size_t workspace_bytes, void* stream) {
+  if (!h) return VMOE_ERR_INVALID_ARG;
+  h->last_launches = 0;
+  if (!h->dense) return fail(h, VMOE_ERR_INVALID_ARG, "not a dense FFN handle (vmoe_ffn_create)");
+  if (!h->ready) return fail(h, VMOE_ERR_NOT_READY, "vmoe_set_weights has not been called");
+  const int64_t T = tokens, H = h->H;
+  if (T < 0 || T >= (static_cast<int64_t>(1) << 31))
+    return fail(h, VMOE_ERR_INVALID_ARG, "bad token count %lld", static_cast<long long>(T));
+  if (T == 0) return VMOE_OK;
+  if (!x || !out) return fail(h, VMOE_ERR_INVALID_ARG, "x and out are required");
+  const FfnPlan p = make_ffn_plan(h, T);
+  if (!workspace || workspace_bytes < p.total)
+    return fail(h, VMOE_ERR_WORKSPACE, "workspace needs %zu bytes (got %zu)", p.total,
+                workspace ? workspace_bytes : static_cast<size_t>(0));
+  if (reinterpret_cast<uintptr_t>(workspace) & 255u)
+    return fail(h, VMOE_ERR_WORKSPACE, "workspace must be 256-byte aligned");
+  DeviceGuard g(h->device);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  char* ws = static_cast<char*>(workspace);
+  const size_t elt = dtype_bytes(h->dtype);
+  int* tiles = reinterpret_cast<int*>(ws + p.tiles);
+  int* ntiles = reinterpret_cast<int*>(ws + p.ntiles);
+  auto mark = []() {};
+  auto check = [&](cudaError_t err, const char* what) -> int {
+    if (err != cudaSuccess) return cuda_fail(h, err, what);
+    ++h->last_launches;
+    return VMOE_OK;
+  };
+  int rc;
+  if ((rc = check(launch_fill_tiles(tiles, static_cast<int>(p.max_rows / h->tile_rows), ntiles, s),
+                  "tile map")) != VMOE_OK)
+    return rc;
+  // x into a buffer padded to whole GEMM tiles (the GEMMs read full tiles)
+  cudaError_t e = cudaMemcpyAsync(ws + p.xp, x, T * H * elt, cudaMemcpyDeviceToDevice, s);
+  if (e != cudaSuccess) return cuda_fail(h, e, "x copy");
+  if ((rc = run_expert_gemms(h, ws + p.xp, p.max_rows, tiles, ntiles, ws + p.h, ws + p.y, h->Hpad,
+                             s, mark, check)) != VMOE_OK)
+    return rc;
+  e = cudaMemcpy2DAsync(out, H * elt, ws + p.y, h->Hpad * elt, H * elt, T,
+                        cudaMemcpyDeviceToDevice, s);
+  if (e != cudaSuccess) return cuda_fail(h, e, "out copy");
   return VMOE_OK;
 }
 

@@ -126,10 +126,124 @@ def _(x, handle_id, want_logits):
             x.new_empty((), dtype=torch.float32))
 
 
+@torch.library.custom_op("vesper_moe::ffn", mutates_args=(), device_types="cuda")
+def ffn_op(x: torch.Tensor, handle_id: int) -> torch.Tensor:
+    """Dense FeedForward out[T,H] for x[T,H] through vmoe_ffn_forward."""
+    packed = _HANDLES[handle_id]
+    h = packed.handle
+    T, _ = x.shape
+    x = x.contiguous()
+    out = torch.empty_like(x)
+    n = ctypes.c_size_t()
+    _lib.check(h.lib.vmoe_ffn_workspace_size(h.ptr, T, ctypes.byref(n)), h.ptr)
+    if packed.ws is None or packed.ws.numel() < n.value:
+        packed.ws = torch.empty(max(n.value, 256), dtype=torch.uint8, device=x.device)
+    stream = torch.cuda.current_stream(x.device).cuda_stream
+    _lib.check(h.lib.vmoe_ffn_forward(h.ptr, ctypes.c_void_p(x.data_ptr()), T,
+                                      ctypes.c_void_p(out.data_ptr()),
+                                      ctypes.c_void_p(packed.ws.data_ptr()), packed.ws.numel(),
+                                      ctypes.c_void_p(stream)), h.ptr, "vmoe_ffn_forward")
+    return out
+
+
+@ffn_op.register_fake
+def _(x, handle_id):
+    return torch.empty_like(x)
+
+
+class _PackedHandleMixin:
+    """Repack-on-change handle management shared by the MoE and dense layers."""
+
+    def _weight_key(self):
+        return tuple((p.data_ptr(), p._version) for p in self.parameters())
+
+    def _abi_config(self, dtype: torch.dtype) -> _lib.VmoeConfig:
+        c = self.config
+        return _lib.VmoeConfig(hidden=c.hidden_size, inter=c.intermediate_size,
+                               num_experts=c.moe_num_experts, top_k=c.moe_top_k,
+                               lora_rank=c.flylora_rank, lora_scaling=c.lora_scaling,
+                               era_gamma=c.era_gamma, dtype=_DTYPES[dtype],
+                               capacity=c.moe_capacity)
+
+    def packed_for(self, device: torch.device, dtype: torch.dtype) -> _Packed:
+        """The handle for (device, dtype), repacking if any parameter changed."""
+        if dtype not in _DTYPES:
+            raise TypeError(f"vesper_moe supports float32 and bfloat16 inputs, not {dtype}")
+        if device.type != "cuda":
+            raise RuntimeError(f"velvetoptimizer_b200.{type(self).__name__} runs on CUDA tensors "
+                               "only (there is no CPU path)")
+        dev = device.index if device.index is not None else torch.cuda.current_device()
+        slot = (dev, dtype)
+        key = self._weight_key()
+        packed = self._packed.get(slot)
+        if packed is not None and packed.key == key:
+            return packed
+        if packed is None:
+            packed = _Packed(self._new_handle(self._abi_config(dtype), dev), key)
+            self._packed[slot] = packed
+        with torch.cuda.device(dev):
+            w = {k: v.to(device) for k, v in self.stacked_weights(dtype).items()}
+            vw = _lib.VmoeWeights(**{k: ctypes.c_void_p(v.data_ptr()) for k, v in w.items()})
+            stream = torch.cuda.current_stream(dev)
+            packed.handle.set_weights(vw, stream.cuda_stream)
+            # the stacked temporaries must outlive the enqueued copies
+            stream.synchronize()
+        packed.key = key
+        return packed
+
+    def close(self) -> None:
+        for p in self._packed.values():
+            p.release()
+        self._packed.clear()
+
+
+class FeedForward(_PackedHandleMixin, nn.Module):
+    """Drop-in for the reference dense FeedForward (python/vesper/model.py:249-270).
+
+    Same submodule names (``gate_proj``/``up_proj`` FlyLoRA linears, ``down_proj``), so the
+    reference's state_dict loads unchanged; ``forward(x[..., H]) -> out[..., H]``.  It runs
+    on the same grouped tensor-core GEMMs as the MoE experts (one expert, no router).
+    """
+
+    def __init__(self, config):
+        super().__init__()
+        cfg = MoEConfig.from_any(config)
+        self.config = cfg
+        args = (cfg.hidden_size, cfg.intermediate_size, cfg.flylora_rank, cfg.flylora_alpha,
+                cfg.flylora_sparsity)
+        self.gate_proj = FlyLoRALinear(*args)
+        self.up_proj = FlyLoRALinear(*args)
+        self.down_proj = nn.Linear(cfg.intermediate_size, cfg.hidden_size)
+        self._packed: dict[tuple, _Packed] = {}
+
+    def _new_handle(self, abi, dev):
+        return _lib.Handle(abi, dev, dense=True)
+
+    def stacked_weights(self, dtype: torch.dtype) -> dict[str, torch.Tensor]:
+        def one(t):
+            return t.detach().to(dtype).unsqueeze(0).contiguous()
+
+        w = {}
+        for name, mod in (("gate", self.gate_proj), ("up", self.up_proj)):
+            w[f"{name}_w"], w[f"{name}_b"] = one(mod.base.weight), one(mod.base.bias)
+            w[f"{name}_lora_down_w"] = one(mod.lora_down.weight)
+            w[f"{name}_lora_down_b"] = one(mod.lora_down.bias)
+            w[f"{name}_lora_up_w"] = one(mod.lora_up.weight)
+            w[f"{name}_lora_up_b"] = one(mod.lora_up.bias)
+        w["down_w"], w["down_b"] = one(self.down_proj.weight), one(self.down_proj.bias)
+        return w
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        shape = x.shape
+        packed = self.packed_for(x.device, x.dtype)
+        out = torch.ops.vesper_moe.ffn(x.reshape(-1, shape[-1]), packed.id)
+        return out.reshape(shape)
+
+
 # ---------------------------------------------------------------------------------------
 # the layer
 # ---------------------------------------------------------------------------------------
-class MoELayer(nn.Module):
+class MoELayer(_PackedHandleMixin, nn.Module):
     """Mixture of Experts with top-K routing and the Switch load-balancing loss.
 
     Same constructor argument (a VesperConfig-like object), parameters, state_dict keys
@@ -149,8 +263,8 @@ class MoELayer(nn.Module):
         self._packed: dict[tuple, _Packed] = {}
 
     # -- weights ---------------------------------------------------------------------
-    def _weight_key(self):
-        return tuple((p.data_ptr(), p._version) for p in self.parameters())
+    def _new_handle(self, abi, dev):
+        return _lib.Handle(abi, dev)
 
     def stacked_weights(self, dtype: torch.dtype) -> dict[str, torch.Tensor]:
         """The per-expert parameters stacked on a leading expert axis, in ``dtype``."""
@@ -172,40 +286,6 @@ class MoELayer(nn.Module):
         w["down_b"] = st(lambda e: e.down_proj.bias)
         return w
 
-    def _abi_config(self, dtype: torch.dtype) -> _lib.VmoeConfig:
-        c = self.config
-        return _lib.VmoeConfig(hidden=c.hidden_size, inter=c.intermediate_size,
-                               num_experts=c.moe_num_experts, top_k=c.moe_top_k,
-                               lora_rank=c.flylora_rank, lora_scaling=c.lora_scaling,
-                               era_gamma=c.era_gamma, dtype=_DTYPES[dtype],
-                               capacity=c.moe_capacity)
-
-    def packed_for(self, device: torch.device, dtype: torch.dtype) -> _Packed:
-        """The handle for (device, dtype), repacking if any parameter changed."""
-        if dtype not in _DTYPES:
-            raise TypeError(f"vesper_moe supports float32 and bfloat16 inputs, not {dtype}")
-        if device.type != "cuda":
-            raise RuntimeError("velvetoptimizer_b200.MoELayer runs on CUDA tensors only "
-                               "(there is no CPU path)")
-        dev = device.index if device.index is not None else torch.cuda.current_device()
-        slot = (dev, dtype)
-        key = self._weight_key()
-        packed = self._packed.get(slot)
-        if packed is not None and packed.key == key:
-            return packed
-        if packed is None:
-            packed = _Packed(_lib.Handle(self._abi_config(dtype), dev), key)
-            self._packed[slot] = packed
-        with torch.cuda.device(dev):
-            w = {k: v.to(device) for k, v in self.stacked_weights(dtype).items()}
-            vw = _lib.VmoeWeights(**{k: ctypes.c_void_p(v.data_ptr()) for k, v in w.items()})
-            stream = torch.cuda.current_stream(dev)
-            packed.handle.set_weights(vw, stream.cuda_stream)
-            # the stacked temporaries must outlive the enqueued copies
-            stream.synchronize()
-        packed.key = key
-        return packed
-
     # -- forward ---------------------------------------------------------------------
     def forward(self, x: torch.Tensor, return_router_logits: bool = False):
         """(out[B,S,H], aux_loss[]) — or (out, aux_loss, router_logits[B,S,E])."""
@@ -217,8 +297,3 @@ class MoELayer(nn.Module):
         if return_router_logits:
             return out, aux, logits.reshape(B, S, self.num_experts)
         return out, aux
-
-    def close(self) -> None:
-        for p in self._packed.values():
-            p.release()
-        self._packed.clear()
