@@ -13,9 +13,10 @@ zero biases, FlyLoRA off.
 * ``value``  tokens/s of the whole job, inputs resident in HBM, CUDA events around
   exactly K steps bracketed by barrier + synchronize, max over ranks.  Inputs (x: 512 MiB,
   weights: 3.2 GiB) are larger than the 126 MB L2, so no flush is needed between steps.
-* ``e2e``    the same metric through ``MoELayer.forward`` with the step's x copied from
-  pinned host memory and the output copied back to pinned host memory inside the timed
-  region.
+* ``e2e``    the same metric through the public API with x in pinned host memory and the
+  output copied back to pinned host memory inside the timed region: on one GPU
+  ``MoELayer.forward_host`` (token chunks whose copies overlap the layer), on N GPUs
+  ``ExpertParallelMoE.forward`` after a host->device copy.
 * ``roofline`` the dominant kernel (the gate/up grouped GEMM) from CUDA events recorded
   around every launch of the timed region; algorithmic FLOPs = 4 * T * K * H * I.
 * ``cpu_baseline`` the CPU restatement of the reference algorithm (the oracle, numpy fp32)
@@ -60,6 +61,9 @@ def parse_args():
     p.add_argument("--ep-chunks", type=int, default=0,
                    help="token chunks of the fused expert-parallel forward (overlap); "
                         "0 = 1 chunk up to 2 GPUs, 4 beyond (the measured best)")
+    p.add_argument("--host-chunks", type=int, default=0,
+                   help="token chunks of the single-GPU host-buffer forward timed as e2e "
+                        "(0 = automatic)")
     return p.parse_args()
 
 
@@ -322,21 +326,26 @@ def run_ours(args, rank, world, local_rank):
     x_host.copy_(x)
     out_host = torch.empty(x.shape, dtype=x.dtype, pin_memory=True)
     aux_host = torch.empty((), dtype=torch.float32, pin_memory=True)
+    if world == 1:
+        # the layer's host-buffer forward: token chunks whose copies overlap the layer
+        def e2e_step():
+            _, a = layer.forward_host(x_host, device=dev, chunks=args.host_chunks, out=out_host)
+            aux_host.copy_(a)
+    else:
+        def e2e_step():
+            xd = x_host.to(dev, non_blocking=True)
+            o, a = fwd(xd)
+            out_host.copy_(o, non_blocking=True)
+            aux_host.copy_(a, non_blocking=True)
     for _ in range(2):
-        xd = x_host.to(dev, non_blocking=True)
-        o, a = fwd(xd)
-        out_host.copy_(o, non_blocking=True)
-        aux_host.copy_(a, non_blocking=True)
+        e2e_step()
     barrier()
     torch.cuda.synchronize()
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
     e0.record(stream)
     for _ in range(args.steps):
-        xd = x_host.to(dev, non_blocking=True)
-        o, a = fwd(xd)
-        out_host.copy_(o, non_blocking=True)
-        aux_host.copy_(a, non_blocking=True)
+        e2e_step()
     e1.record(stream)
     e1.synchronize()
     barrier()
@@ -402,7 +411,9 @@ def run_ours(args, rank, world, local_rank):
         "e2e": {"value": round(e2e_value, 1), "unit": "tokens/s",
                 "h2d_bytes_per_step": int(x.numel() * x.element_size()),
                 "d2h_bytes_per_step": int(x.numel() * x.element_size() + 4),
-                "api": "velvetoptimizer_b200.MoELayer.forward" if world == 1 else
+                "api": "velvetoptimizer_b200.MoELayer.forward_host (vmoe_forward_host: "
+                       "pinned host x/out, copies overlapped with the layer in token chunks)"
+                       if world == 1 else
                        "velvetoptimizer_b200.ep.ExpertParallelMoE.forward"},
         "roofline": {"kernel": roof_kernel,
                      "bound": "tensor", "achieved": round(achieved, 1),

@@ -167,6 +167,23 @@ VMOE_API int vmoe_forward(vmoe_handle* h, const void* x, int64_t tokens, void* o
                  int32_t* expert_counts, float* aux_loss,
                  void* workspace, size_t workspace_bytes, void* stream);
 
+/* The same forward with x and out in HOST memory -- the reference's CPU-tensor call of
+ * MoELayer.forward (python/vesper/model.py:317-364) served by the GPU.  The batch is cut
+ * into `chunks` token chunks (0 = automatic: chunks of >= 8192 tokens, at most 8; at
+ * most 16) whose host->device copy, forward and device->host copy overlap on two internal
+ * copy streams; outputs are bit-identical to vmoe_forward on the same tokens and aux_loss
+ * (host fp32 scalar, optional) is the loss of the whole batch.
+ *   x_host, out_host   [T, H] config dtype; pinned (page-locked) memory for the copies to
+ *                      overlap -- pageable memory works but serialises them
+ *   workspace          device, >= vmoe_forward_host_workspace_size bytes, 256-byte aligned
+ * Enqueued on `stream` (which ends after the last copy): out_host and *aux_loss_host are
+ * valid once `stream` has been synchronised. */
+VMOE_API int vmoe_forward_host_workspace_size(const vmoe_handle* h, int64_t tokens, int chunks,
+                                              size_t* bytes);
+VMOE_API int vmoe_forward_host(vmoe_handle* h, const void* x_host, int64_t tokens,
+                               void* out_host, float* aux_loss_host, int chunks,
+                               void* workspace, size_t workspace_bytes, void* stream);
+
 /* ---- Expert parallelism -------------------------------------------------------------
  * The reference has no distributed code (no collective anywhere in the project); the
  * path's specification partitions this layer expert-parallel: with G ranks, rank r holds

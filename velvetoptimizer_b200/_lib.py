@@ -36,7 +36,7 @@ EXPORTED = (
     "vmoe_create_ep", "vmoe_ep_workspace_size", "vmoe_ep_route", "vmoe_ep_experts",
     "vmoe_ep_combine", "vmoe_ep_p2p_setup", "vmoe_ep_p2p_connect", "vmoe_ep_p2p_workspace_size",
     "vmoe_ep_p2p_forward", "vmoe_gemm_tile_rows", "vmoe_ffn_create", "vmoe_ffn_workspace_size",
-    "vmoe_ffn_forward",
+    "vmoe_ffn_forward", "vmoe_forward_host_workspace_size", "vmoe_forward_host",
 )
 
 
@@ -104,6 +104,11 @@ def load() -> ctypes.CDLL:
     lib.vmoe_forward_no_alloc.argtypes = [H, c_void_p, c_int64, c_void_p, c_void_p, c_void_p,
                                           c_void_p, c_void_p, c_void_p, c_void_p]
     lib.vmoe_forward_no_alloc.restype = c_int
+    lib.vmoe_forward_host_workspace_size.argtypes = [H, c_int64, c_int, POINTER(c_size_t)]
+    lib.vmoe_forward_host_workspace_size.restype = c_int
+    lib.vmoe_forward_host.argtypes = [H, c_void_p, c_int64, c_void_p, c_void_p, c_int, c_void_p,
+                                      c_size_t, c_void_p]
+    lib.vmoe_forward_host.restype = c_int
     lib.vmoe_create_ep.argtypes = [POINTER(VmoeConfig), c_int, c_int, c_int, POINTER(H)]
     lib.vmoe_create_ep.restype = c_int
     lib.vmoe_ep_workspace_size.argtypes = [H, c_int64, c_int64, POINTER(c_size_t)]
@@ -208,6 +213,17 @@ class Handle:
         rc = self.lib.vmoe_forward(self.ptr, x, tokens, out, logits, idx, topw, counts, aux, ws,
                                    ws_bytes, c_void_p(stream))
         check(rc, self.ptr, "vmoe_forward")
+
+    def host_workspace_size(self, tokens: int, chunks: int = 0) -> int:
+        n = c_size_t()
+        check(self.lib.vmoe_forward_host_workspace_size(self.ptr, tokens, chunks, ctypes.byref(n)),
+              self.ptr, "vmoe_forward_host_workspace_size")
+        return n.value
+
+    def forward_host(self, x_host, tokens, out_host, aux_host, chunks, ws, ws_bytes, stream):
+        rc = self.lib.vmoe_forward_host(self.ptr, x_host, tokens, out_host, aux_host, chunks, ws,
+                                        ws_bytes, c_void_p(stream))
+        check(rc, self.ptr, "vmoe_forward_host")
 
     def device_status(self, stream: int) -> int:
         code = c_int32()

@@ -47,6 +47,7 @@ struct DeviceGuard {
 };
 
 constexpr int kMaxChunks = 4;
+constexpr int kMaxHostChunks = 16;
 
 // One token chunk's symmetric region and its bookkeeping.
 struct P2PChannel {
@@ -88,6 +89,11 @@ struct vmoe_handle {
   cudaEvent_t p2p_sent[kMaxChunks] = {};       // and their dispatches
   bool p2p_connected = false;
   int p2p_reserve_sms = 0;  // SMs the chunked GEMMs leave to the transfer kernels
+  // host-buffer forward (vmoe_forward_host): copy streams and per-chunk events, made on
+  // first use
+  cudaStream_t host_in = nullptr, host_out = nullptr;
+  cudaEvent_t host_start = nullptr, host_out_done = nullptr;
+  cudaEvent_t host_in_ev[kMaxHostChunks] = {}, host_comp_ev[kMaxHostChunks] = {};
   // packed weights (library-owned)
   void* w_r = nullptr;
   float* b_r = nullptr;
@@ -406,6 +412,73 @@ int run_router(vmoe_handle* h, const void* x, int64_t T, float* logits, int32_t*
   return VMOE_OK;
 }
 
+// One single-GPU forward of T >= 1 tokens on stream s, workspace laid out by make_plan(h, T).
+// psum_tot_out (nullable) takes the batch's per-expert probability sums instead of the
+// workspace, so that a chunked caller can merge the aux loss of the whole batch.
+int forward_batch(vmoe_handle* h, const void* x, int64_t T, void* out, float* router_logits,
+                  int32_t* topk_idx, float* topk_w, int32_t* expert_counts, float* aux_loss,
+                  char* ws, const Plan& p, cudaStream_t s, bool prof, float* psum_tot_out) {
+  const int64_t E = h->E, K = h->K, H = h->H;
+  int32_t* idx = topk_idx ? topk_idx : reinterpret_cast<int32_t*>(ws + p.idx);
+  float* tw = topk_w ? topk_w : reinterpret_cast<float*>(ws + p.w);
+  int* hist = reinterpret_cast<int*>(ws + p.hist);
+  float* psum = reinterpret_cast<float*>(ws + p.psum);
+  int* excl = reinterpret_cast<int*>(ws + p.excl);
+  int* counts = reinterpret_cast<int*>(ws + p.counts);
+  float* psum_tot = psum_tot_out ? psum_tot_out : reinterpret_cast<float*>(ws + p.psum_tot);
+  int* offs = reinterpret_cast<int*>(ws + p.offs);
+  int* tiles = reinterpret_cast<int*>(ws + p.tiles);
+  int* ntiles = reinterpret_cast<int*>(ws + p.ntiles);
+  float* aux = aux_loss ? aux_loss : reinterpret_cast<float*>(ws + p.aux);
+  int* slot = reinterpret_cast<int*>(ws + p.slot);
+  void* xp = ws + p.xp;
+  void* hb = ws + p.h;
+  void* yb = ws + p.y;
+
+  cudaEvent_t* ev = prof ? &h->prof_ev[static_cast<size_t>(h->prof_count) * (kStages + 1)] : nullptr;
+  int stage = 0;
+  auto mark = [&]() {
+    if (prof) cudaEventRecord(ev[stage], s);
+    ++stage;
+  };
+  auto check = [&](cudaError_t err, const char* what) -> int {
+    if (err != cudaSuccess) return cuda_fail(h, err, what);
+    ++h->last_launches;
+    return VMOE_OK;
+  };
+  int rc;
+  mark();
+  if ((rc = run_router(h, x, T, router_logits, idx, tw, hist, psum, s)) != VMOE_OK) return rc;
+  mark();
+  if ((rc = check(launch_scan_blocks(hist, psum, p.nblk, static_cast<int>(E), excl, counts,
+                                     psum_tot, s),
+                  "scan")) != VMOE_OK)
+    return rc;
+  mark();
+  if ((rc = check(launch_plan(counts, psum_tot, T, static_cast<int>(E), static_cast<int>(K),
+                              h->cfg.capacity, static_cast<int>(h->tile_rows), offs, tiles,
+                              ntiles, aux, expert_counts, s),
+                  "plan")) != VMOE_OK)
+    return rc;
+  mark();
+  if ((rc = check(launch_dispatch(h->dtype, x, idx, excl, offs, T, static_cast<int>(H),
+                                  static_cast<int>(E), static_cast<int>(K), h->cfg.capacity, slot,
+                                  xp, H, h->status, s),
+                  "dispatch")) != VMOE_OK)
+    return rc;
+  mark();
+  if ((rc = run_expert_gemms(h, xp, p.max_rows, tiles, ntiles, hb, yb, h->Hpad, s, mark,
+                             check)) != VMOE_OK)
+    return rc;
+  mark();
+  if ((rc = check(launch_combine(h->dtype, yb, h->Hpad, idx, tw, slot, T, static_cast<int>(H),
+                                 static_cast<int>(K), out, s),
+                  "combine")) != VMOE_OK)
+    return rc;
+  mark();
+  return VMOE_OK;
+}
+
 }  // namespace
 
 namespace vmoe {
@@ -515,6 +588,14 @@ int vmoe_destroy(vmoe_handle* h) {
       if (h->p2p_sent[i]) cudaEventDestroy(h->p2p_sent[i]);
     }
     if (h->p2p_start) cudaEventDestroy(h->p2p_start);
+    for (int i = 0; i < kMaxHostChunks; ++i) {
+      if (h->host_in_ev[i]) cudaEventDestroy(h->host_in_ev[i]);
+      if (h->host_comp_ev[i]) cudaEventDestroy(h->host_comp_ev[i]);
+    }
+    if (h->host_start) cudaEventDestroy(h->host_start);
+    if (h->host_out_done) cudaEventDestroy(h->host_out_done);
+    if (h->host_in) cudaStreamDestroy(h->host_in);
+    if (h->host_out) cudaStreamDestroy(h->host_out);
     if (h->status) cudaFree(h->status);
     for (cudaEvent_t ev : h->prof_ev) cudaEventDestroy(ev);
   }
@@ -705,67 +786,173 @@ int vmoe_forward(vmoe_handle* h, const void* x, int64_t tokens, void* out, float
   if (reinterpret_cast<uintptr_t>(workspace) & 255u)
     return fail(h, VMOE_ERR_WORKSPACE, "workspace must be 256-byte aligned");
 
-  char* ws = static_cast<char*>(workspace);
-  int32_t* idx = topk_idx ? topk_idx : reinterpret_cast<int32_t*>(ws + p.idx);
-  float* tw = topk_w ? topk_w : reinterpret_cast<float*>(ws + p.w);
-  int* hist = reinterpret_cast<int*>(ws + p.hist);
-  float* psum = reinterpret_cast<float*>(ws + p.psum);
-  int* excl = reinterpret_cast<int*>(ws + p.excl);
-  int* counts = reinterpret_cast<int*>(ws + p.counts);
-  float* psum_tot = reinterpret_cast<float*>(ws + p.psum_tot);
-  int* offs = reinterpret_cast<int*>(ws + p.offs);
-  int* tiles = reinterpret_cast<int*>(ws + p.tiles);
-  int* ntiles = reinterpret_cast<int*>(ws + p.ntiles);
-  float* aux = aux_loss ? aux_loss : reinterpret_cast<float*>(ws + p.aux);
-  int* slot = reinterpret_cast<int*>(ws + p.slot);
-  void* xp = ws + p.xp;
-  void* hb = ws + p.h;
-  void* yb = ws + p.y;
-
   const bool prof = h->prof_count < h->prof_slots;
-  cudaEvent_t* ev = prof ? &h->prof_ev[static_cast<size_t>(h->prof_count) * (kStages + 1)] : nullptr;
-  int stage = 0;
-  auto mark = [&]() {
-    if (prof) cudaEventRecord(ev[stage], s);
-    ++stage;
+  const int rc = forward_batch(h, x, T, out, router_logits, topk_idx, topk_w, expert_counts,
+                               aux_loss, static_cast<char*>(workspace), p, s, prof, nullptr);
+  if (rc == VMOE_OK && prof) ++h->prof_count;
+  return rc;
+}
+
+// ---- forward on host buffers: chunked copy-in / compute / copy-out pipeline -------------
+namespace {
+
+struct HostPlan {
+  int chunks = 1;
+  int64_t chunk_tokens = 0;
+  size_t x = 0, out = 0, small = 0, small_stride = 0, psum_off = 0, aux = 0, fwd = 0, total = 0;
+};
+
+// Workspace: x and out of the whole batch on the device, per-chunk expert counts and
+// probability sums (for the aux loss of the whole batch), and one chunk's forward workspace
+// (the chunks' forwards run one after another on the caller's stream and share it).
+HostPlan make_host_plan(const vmoe_handle* h, int64_t T, int chunks) {
+  HostPlan hp;
+  if (chunks <= 0) {  // automatic: chunks of at least 8192 tokens, at most 8 of them
+    const int64_t a = T / 8192;
+    chunks = a < 1 ? 1 : (a > 8 ? 8 : static_cast<int>(a));
+  }
+  if (chunks > kMaxHostChunks) chunks = kMaxHostChunks;
+  int64_t ct = round_up((T + chunks - 1) / chunks, kTileM);
+  if (ct < kTileM) ct = kTileM;
+  hp.chunk_tokens = ct;
+  hp.chunks = T > 0 ? static_cast<int>((T + ct - 1) / ct) : 1;
+  const size_t row = static_cast<size_t>(h->H) * dtype_bytes(h->dtype);
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    const size_t o = off;
+    off += (bytes + 255) & ~static_cast<size_t>(255);
+    return o;
   };
-  auto check = [&](cudaError_t err, const char* what) -> int {
-    if (err != cudaSuccess) return cuda_fail(h, err, what);
-    ++h->last_launches;
-    return VMOE_OK;
-  };
-  int rc;
-  mark();
-  if ((rc = run_router(h, x, T, router_logits, idx, tw, hist, psum, s)) != VMOE_OK) return rc;
-  mark();
-  if ((rc = check(launch_scan_blocks(hist, psum, p.nblk, static_cast<int>(E), excl, counts,
-                                     psum_tot, s),
-                  "scan")) != VMOE_OK)
-    return rc;
-  mark();
-  if ((rc = check(launch_plan(counts, psum_tot, T, static_cast<int>(E), static_cast<int>(K),
-                              h->cfg.capacity, static_cast<int>(h->tile_rows), offs, tiles,
-                              ntiles, aux, expert_counts, s),
-                  "plan")) != VMOE_OK)
-    return rc;
-  mark();
-  if ((rc = check(launch_dispatch(h->dtype, x, idx, excl, offs, T, static_cast<int>(H),
-                                  static_cast<int>(E), static_cast<int>(K), h->cfg.capacity, slot,
-                                  xp, H, h->status, s),
-                  "dispatch")) != VMOE_OK)
-    return rc;
-  mark();
-  if ((rc = run_expert_gemms(h, xp, p.max_rows, tiles, ntiles, hb, yb, h->Hpad, s, mark,
-                             check)) != VMOE_OK)
-    return rc;
-  mark();
-  if ((rc = check(launch_combine(h->dtype, yb, h->Hpad, idx, tw, slot, T, static_cast<int>(H),
-                                 static_cast<int>(K), out, s),
-                  "combine")) != VMOE_OK)
-    return rc;
-  mark();
-  if (prof) ++h->prof_count;
+  hp.x = take(static_cast<size_t>(T) * row);
+  hp.out = take(static_cast<size_t>(T) * row);
+  hp.small_stride = round_up(8 * h->E, 256);
+  hp.psum_off = 4 * h->E;
+  hp.small = take(hp.small_stride * hp.chunks);
+  hp.aux = take(4);
+  hp.fwd = take(make_plan(h, T < ct ? T : ct).total);
+  hp.total = off;
+  return hp;
+}
+
+void CUDART_CB write_nan(void* p) { *static_cast<float*>(p) = __builtin_nanf(""); }
+
+int ensure_host_streams(vmoe_handle* h) {
+  if (h->host_in) return VMOE_OK;
+  cudaError_t e = cudaStreamCreateWithFlags(&h->host_in, cudaStreamNonBlocking);
+  if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&h->host_out, cudaStreamNonBlocking);
+  if (e == cudaSuccess) e = cudaEventCreateWithFlags(&h->host_start, cudaEventDisableTiming);
+  if (e == cudaSuccess) e = cudaEventCreateWithFlags(&h->host_out_done, cudaEventDisableTiming);
+  for (int c = 0; c < kMaxHostChunks && e == cudaSuccess; ++c) {
+    e = cudaEventCreateWithFlags(&h->host_in_ev[c], cudaEventDisableTiming);
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&h->host_comp_ev[c], cudaEventDisableTiming);
+  }
+  if (e != cudaSuccess) {
+    // leave the handle as it was so that a later call retries
+    if (h->host_in) cudaStreamDestroy(h->host_in);
+    if (h->host_out) cudaStreamDestroy(h->host_out);
+    h->host_in = h->host_out = nullptr;
+    return cuda_fail(h, e, "host copy streams");
+  }
   return VMOE_OK;
+}
+
+}  // namespace
+
+int vmoe_forward_host_workspace_size(const vmoe_handle* h, int64_t tokens, int chunks,
+                                     size_t* bytes) {
+  if (!h || !bytes || tokens < 0) return VMOE_ERR_INVALID_ARG;
+  *bytes = make_host_plan(h, tokens, chunks).total;
+  return VMOE_OK;
+}
+
+int vmoe_forward_host(vmoe_handle* h, const void* x_host, int64_t tokens, void* out_host,
+                      float* aux_loss_host, int chunks, void* workspace, size_t workspace_bytes,
+                      void* stream) {
+  if (!h) return VMOE_ERR_INVALID_ARG;
+  h->last_launches = 0;
+  if (!h->ready) return fail(h, VMOE_ERR_NOT_READY, "vmoe_set_weights has not been called");
+  if (h->ep_size > 1 || h->dense)
+    return fail(h, VMOE_ERR_INVALID_ARG, "vmoe_forward_host takes a single-GPU MoE handle");
+  if (tokens < 0) return fail(h, VMOE_ERR_INVALID_ARG, "tokens must be >= 0 (got %lld)",
+                              static_cast<long long>(tokens));
+  const int64_t E = h->E, K = h->K, T = tokens;
+  if (T * K + E * kTileM >= (static_cast<int64_t>(1) << 31))
+    return fail(h, VMOE_ERR_UNSUPPORTED_SHAPE, "tokens * top_k too large (%lld)",
+                static_cast<long long>(T * K));
+  DeviceGuard g(h->device);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  cudaError_t e;
+  if (T == 0) {  // as vmoe_forward: no rows, aux NaN (written in stream order)
+    if (aux_loss_host && (e = cudaLaunchHostFunc(s, write_nan, aux_loss_host)) != cudaSuccess)
+      return cuda_fail(h, e, "aux write");
+    return VMOE_OK;
+  }
+  if (!x_host || !out_host) return fail(h, VMOE_ERR_INVALID_ARG, "x and out are required");
+  if (chunks < 0 || chunks > kMaxHostChunks)
+    return fail(h, VMOE_ERR_INVALID_ARG, "chunks must be in [0, %d] (got %d)", kMaxHostChunks,
+                chunks);
+  const HostPlan hp = make_host_plan(h, T, chunks);
+  if (!workspace || workspace_bytes < hp.total)
+    return fail(h, VMOE_ERR_WORKSPACE, "workspace needs %zu bytes (got %zu)", hp.total,
+                workspace ? workspace_bytes : static_cast<size_t>(0));
+  if (reinterpret_cast<uintptr_t>(workspace) & 255u)
+    return fail(h, VMOE_ERR_WORKSPACE, "workspace must be 256-byte aligned");
+  int rc = ensure_host_streams(h);
+  if (rc != VMOE_OK) return rc;
+
+  char* ws = static_cast<char*>(workspace);
+  const size_t row = static_cast<size_t>(h->H) * dtype_bytes(h->dtype);
+  const int C = hp.chunks;
+  float* aux_dev = reinterpret_cast<float*>(ws + hp.aux);
+  // the copy-in of this call may overwrite x only after the caller's earlier work on s
+  if ((e = cudaEventRecord(h->host_start, s)) != cudaSuccess) return cuda_fail(h, e, "event");
+  if ((e = cudaStreamWaitEvent(h->host_in, h->host_start, 0)) != cudaSuccess)
+    return cuda_fail(h, e, "wait");
+  // every exit after this point joins the copy streams into s
+  auto join = [&](int code) {
+    cudaEventRecord(h->host_out_done, h->host_out);
+    cudaStreamWaitEvent(s, h->host_out_done, 0);
+    cudaEventRecord(h->host_out_done, h->host_in);
+    cudaStreamWaitEvent(s, h->host_out_done, 0);
+    return code;
+  };
+  for (int c = 0; c < C; ++c) {
+    const int64_t t0 = c * hp.chunk_tokens;
+    const int64_t tc = (T - t0) < hp.chunk_tokens ? (T - t0) : hp.chunk_tokens;
+    if ((e = cudaMemcpyAsync(ws + hp.x + t0 * row, static_cast<const char*>(x_host) + t0 * row,
+                             tc * row, cudaMemcpyHostToDevice, h->host_in)) != cudaSuccess ||
+        (e = cudaEventRecord(h->host_in_ev[c], h->host_in)) != cudaSuccess)
+      return join(cuda_fail(h, e, "copy in"));
+  }
+  for (int c = 0; c < C; ++c) {
+    const int64_t t0 = c * hp.chunk_tokens;
+    const int64_t tc = (T - t0) < hp.chunk_tokens ? (T - t0) : hp.chunk_tokens;
+    char* small = ws + hp.small + c * hp.small_stride;
+    if ((e = cudaStreamWaitEvent(s, h->host_in_ev[c], 0)) != cudaSuccess)
+      return join(cuda_fail(h, e, "wait"));
+    rc = forward_batch(h, ws + hp.x + t0 * row, tc, ws + hp.out + t0 * row, nullptr, nullptr,
+                       nullptr, reinterpret_cast<int32_t*>(small), C == 1 ? aux_dev : nullptr,
+                       ws + hp.fwd, make_plan(h, tc), s, false,
+                       C == 1 ? nullptr : reinterpret_cast<float*>(small + hp.psum_off));
+    if (rc != VMOE_OK) return join(rc);
+    if ((e = cudaEventRecord(h->host_comp_ev[c], s)) != cudaSuccess ||
+        (e = cudaStreamWaitEvent(h->host_out, h->host_comp_ev[c], 0)) != cudaSuccess ||
+        (e = cudaMemcpyAsync(static_cast<char*>(out_host) + t0 * row, ws + hp.out + t0 * row,
+                             tc * row, cudaMemcpyDeviceToHost, h->host_out)) != cudaSuccess)
+      return join(cuda_fail(h, e, "copy out"));
+  }
+  if (aux_loss_host) {
+    if (C > 1) {  // the loss of the whole batch from every chunk's counts and sums
+      if ((e = launch_aux_merge_ws(ws + hp.small, hp.small_stride, 0, hp.psum_off, C, T,
+                                   static_cast<int>(E), static_cast<int>(K), aux_dev, s)) !=
+          cudaSuccess)
+        return join(cuda_fail(h, e, "aux merge"));
+      ++h->last_launches;
+    }
+    if ((e = cudaMemcpyAsync(aux_loss_host, aux_dev, 4, cudaMemcpyDeviceToHost, s)) != cudaSuccess)
+      return join(cuda_fail(h, e, "aux copy"));
+  }
+  return join(VMOE_OK);
 }
 
 int vmoe_create_ep(const vmoe_config* cfg, int device, int ep_size, int ep_rank,

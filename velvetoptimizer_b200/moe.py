@@ -85,7 +85,9 @@ class _Packed:
         _HANDLES[self.id] = self
 
     def workspace(self, tokens: int, device) -> torch.Tensor:
-        need = self.handle.workspace_size(tokens)
+        return self.scratch(self.handle.workspace_size(tokens), device)
+
+    def scratch(self, need: int, device) -> torch.Tensor:
         if self.ws is None or self.ws.numel() < need:
             self.ws = torch.empty(max(need, 256), dtype=torch.uint8, device=device)
         return self.ws
@@ -296,4 +298,39 @@ class MoELayer(_PackedHandleMixin, nn.Module):
         out = out.reshape(B, S, H)
         if return_router_logits:
             return out, aux, logits.reshape(B, S, self.num_experts)
+        return out, aux
+
+    def forward_host(self, x: torch.Tensor, device=None, chunks: int = 0,
+                     out: torch.Tensor | None = None):
+        """``forward`` for x[B,S,H] in host memory, computed on a CUDA device.
+
+        The reference runs a CPU tensor through the layer on the CPU; here the batch goes
+        to ``device`` (default: the current CUDA device) in token chunks whose host->device
+        copy, layer forward and device->host copy overlap (``vmoe_forward_host``).  x and
+        ``out`` should be pinned (``pin_memory()``) for the copies to overlap.  Returns
+        (out[B,S,H], aux_loss[]) as host tensors, ready on return; out is bit-identical to
+        ``forward`` of the same tokens.
+        """
+        if x.device.type != "cpu":
+            raise ValueError("forward_host takes a host tensor; use forward for CUDA tensors")
+        B, S, H = x.shape
+        if device is None:
+            device = torch.device("cuda", torch.cuda.current_device())
+        device = torch.device(device)
+        packed = self.packed_for(device, x.dtype)
+        x = x.contiguous()
+        if out is None:
+            out = torch.empty(x.shape, dtype=x.dtype, pin_memory=x.is_pinned())
+        elif out.shape != x.shape or out.dtype != x.dtype or out.device.type != "cpu" \
+                or not out.is_contiguous():
+            raise ValueError("out must be a contiguous host tensor shaped and typed like x")
+        aux = torch.empty((), dtype=torch.float32, pin_memory=True)
+        T = B * S
+        h = packed.handle
+        with torch.cuda.device(device):
+            ws = packed.scratch(h.host_workspace_size(T, chunks), device)
+            stream = torch.cuda.current_stream(device)
+            h.forward_host(x.data_ptr(), T, out.data_ptr(), aux.data_ptr(), int(chunks),
+                           ws.data_ptr(), ws.numel(), stream.cuda_stream)
+            stream.synchronize()
         return out, aux
