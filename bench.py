@@ -61,6 +61,10 @@ def parse_args():
     p.add_argument("--ep-chunks", type=int, default=0,
                    help="token chunks of the fused expert-parallel forward (overlap); "
                         "0 = 1 chunk up to 2 GPUs, 4 beyond (the measured best)")
+    p.add_argument("--prenorm", action="store_true",
+                   help="time the fused pre-norm block x + MoE(LayerNorm(x)) "
+                        "(MoELayer.forward_residual) on one GPU, and beside it the unfused "
+                        "torch LayerNorm -> MoELayer.forward -> torch add")
     p.add_argument("--host-chunks", type=int, default=0,
                    help="token chunks of the single-GPU host-buffer forward timed as e2e "
                         "(0 = automatic)")
@@ -245,8 +249,15 @@ def run_ours(args, rank, world, local_rank):
         layer = build_layer(w, dev, seed=0)
         packed = layer.packed_for(dev, torch.bfloat16)
 
-        def fwd(inp):
-            return layer(inp)
+        if args.prenorm:
+            # the layer's ffn_norm (model.py:399) as _init_weights leaves it: ones, zeros
+            norm = torch.nn.LayerNorm(H, eps=1e-6, device=dev, dtype=torch.bfloat16)
+
+            def fwd(inp):
+                return layer.forward_residual(inp, norm)
+        else:
+            def fwd(inp):
+                return layer(inp)
 
         def start_profile():
             packed.handle.set_profiling(args.steps)
@@ -321,12 +332,37 @@ def run_ours(args, rank, world, local_rank):
     ms_max = float(ms_t.item())
     value = world * T / (ms_max * 1e-3)
 
+    prenorm_report = None
+    if args.prenorm and world == 1:
+        # the same block unfused: torch LayerNorm, the MoE layer, torch residual add
+        def unfused(inp):
+            o, a = layer(norm(inp))
+            return inp + o, a
+        for _ in range(args.warmup):
+            unfused(x)
+        torch.cuda.synchronize()
+        u0 = torch.cuda.Event(enable_timing=True)
+        u1 = torch.cuda.Event(enable_timing=True)
+        u0.record(stream)
+        for _ in range(args.steps):
+            unfused(x)
+        u1.record(stream)
+        u1.synchronize()
+        ms_u = u0.elapsed_time(u1) / args.steps
+        elt = x.element_size()
+        prenorm_report = {
+            "fused_ms": round(ms, 4), "unfused_ms": round(ms_u, 4),
+            "unfused": "torch LayerNorm -> MoELayer.forward -> torch residual add",
+            "bytes_saved_per_step": 4 * T * H * elt,
+            "note": "fused: LayerNorm folded into the router (row statistics from MMAs on the x "
+                    "tile, folded weights) and the dispatch read, residual add in the combine"}
+
     # ---- end-to-end through the public module, host buffers in/out ----
     x_host = torch.empty(x.shape, dtype=x.dtype, pin_memory=True)
     x_host.copy_(x)
     out_host = torch.empty(x.shape, dtype=x.dtype, pin_memory=True)
     aux_host = torch.empty((), dtype=torch.float32, pin_memory=True)
-    if world == 1:
+    if world == 1 and not args.prenorm:
         # the layer's host-buffer forward: token chunks whose copies overlap the layer
         def e2e_step():
             _, a = layer.forward_host(x_host, device=dev, chunks=args.host_chunks, out=out_host)
@@ -413,6 +449,8 @@ def run_ours(args, rank, world, local_rank):
                 "d2h_bytes_per_step": int(x.numel() * x.element_size() + 4),
                 "api": "velvetoptimizer_b200.MoELayer.forward_host (vmoe_forward_host: "
                        "pinned host x/out, copies overlapped with the layer in token chunks)"
+                       if world == 1 and not args.prenorm else
+                       "velvetoptimizer_b200.MoELayer.forward_residual after a host copy"
                        if world == 1 else
                        "velvetoptimizer_b200.ep.ExpertParallelMoE.forward"},
         "roofline": {"kernel": roof_kernel,
@@ -425,6 +463,9 @@ def run_ours(args, rank, world, local_rank):
         "gpu_launches": launches,
         "clocks": clocks,
     }
+    if prenorm_report:
+        line["prenorm"] = prenorm_report
+        line["config"]["workload"] += "; fused pre-norm block x + MoE(LayerNorm(x))"
     if world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(layer, x.reshape(T, H), w, args.cpu_seconds)
     return line

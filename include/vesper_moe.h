@@ -167,6 +167,23 @@ VMOE_API int vmoe_forward(vmoe_handle* h, const void* x, int64_t tokens, void* o
                  int32_t* expert_counts, float* aux_loss,
                  void* workspace, size_t workspace_bytes, void* stream);
 
+/* Fused pre-norm block: the FFN half of TransformerLayer.forward
+ * (python/vesper/model.py:418-425) for a MoE layer,
+ *     normed = ffn_norm(x);  ffn_out, aux = ffn(normed);  return x + ffn_out, aux
+ * in one call.  The LayerNorm is folded into the router's and the dispatch's reads of x
+ * (the normalised rows are never written to HBM) and the residual add into the combine.
+ * vmoe_set_norm takes the nn.LayerNorm parameters (device, config dtype, [H]; NULL weight =
+ * ones, NULL bias = zeros) and its eps (model.py:398-399, config.layer_norm_eps); call it
+ * again when they change.  vmoe_forward_residual has vmoe_forward's arguments with
+ * x = the residual stream (hidden_states) and out = x + ffn_out (out may equal x); the
+ * optional outputs describe the routing of LayerNorm(x).  Workspace: vmoe_workspace_size. */
+VMOE_API int vmoe_set_norm(vmoe_handle* h, const void* ln_weight, const void* ln_bias, float eps,
+                           void* stream);
+VMOE_API int vmoe_forward_residual(vmoe_handle* h, const void* x, int64_t tokens, void* out,
+                                   float* router_logits, int32_t* topk_idx, float* topk_w,
+                                   int32_t* expert_counts, float* aux_loss,
+                                   void* workspace, size_t workspace_bytes, void* stream);
+
 /* The same forward with x and out in HOST memory -- the reference's CPU-tensor call of
  * MoELayer.forward (python/vesper/model.py:317-364) served by the GPU.  The batch is cut
  * into `chunks` token chunks (0 = automatic: chunks of >= 8192 tokens, at most 8; at

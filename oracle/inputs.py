@@ -121,6 +121,25 @@ def make_inputs(case: MoECase) -> dict[str, np.ndarray]:
     return out
 
 
+def make_norm_inputs(case: MoECase, eps: float = 1e-6) -> dict[str, np.ndarray]:
+    """Residual-stream input and LayerNorm parameters for the fused pre-norm block.
+
+    x = 2 * N(0,1) + a per-token offset N(0,1) + a per-channel offset N(0,0.5), so the mean
+    subtraction matters; ln_w = 1 + N(0,0.1), ln_b = N(0,0.1); eps as config.layer_norm_eps
+    (python/vesper/config.py:26).  Seeded from the case (its seed + 1000).
+    """
+    rng = np.random.default_rng(case.seed + 1000)
+    f32 = np.float32
+    T, H = case.tokens, case.hidden
+    base = make_inputs(case)["x"]
+    x = (f32(2.0) * base + rng.standard_normal((T, 1), dtype=f32)
+         + f32(0.5) * rng.standard_normal((1, H), dtype=f32)).astype(f32)
+    return {"x": x,
+            "ln_w": (f32(1.0) + f32(0.1) * rng.standard_normal(H, dtype=f32)).astype(f32),
+            "ln_b": (f32(0.1) * rng.standard_normal(H, dtype=f32)).astype(f32),
+            "eps": np.asarray(eps, dtype=f32)}
+
+
 def round_bf16(a: np.ndarray) -> np.ndarray:
     """Round fp32 values to the nearest bf16 (ties to even), returned as fp32."""
     a = np.ascontiguousarray(a, dtype=np.float32)

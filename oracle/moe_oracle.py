@@ -17,6 +17,7 @@ VelvetOptimizer project root):
 * expert FFN             python/vesper/model.py:295-298
 * combine                python/vesper/model.py:337,354-357 (index_add_ in expert order)
 * load-balancing loss    python/vesper/model.py:366-385
+* pre-norm block         python/vesper/model.py:418-425 (ffn_norm LayerNorm, residual add)
 
 Pinning: ``tests/golden/make_golden.py`` executes the reference ``MoELayer`` itself (in
 the container where the reference is mounted) and commits its outputs as fixtures;
@@ -237,6 +238,32 @@ def moe_forward(p, case, *, dtype=np.float32, force_idx=None, token_subset=None,
         "counts": counts, "perm_tok": perm_tok, "perm_k": perm_k,
         "out": out, "aux": np.asarray(aux, dtype=dtype),
     }
+
+
+def layer_norm(x, w, b, eps):
+    """nn.LayerNorm over the last axis (model.py:398-399): biased variance, affine."""
+    x64 = np.asarray(x, dtype=np.float64)
+    mu = x64.mean(axis=-1, keepdims=True)
+    var = ((x64 - mu) ** 2).mean(axis=-1, keepdims=True)
+    y = (x64 - mu) / np.sqrt(var + float(eps)) * np.asarray(w, np.float64) + np.asarray(b, np.float64)
+    return y.astype(np.float32)
+
+
+def prenorm_moe_forward(p, case, ln_w, ln_b, eps, **kw):
+    """The FFN half of TransformerLayer.forward for a MoE layer (model.py:418-425):
+    normed = ffn_norm(x); ffn_out, aux = ffn(normed); out = x + ffn_out.
+
+    ``p["x"]`` is the residual stream; keyword arguments go to ``moe_forward`` (whose
+    ``token_subset`` also selects the residual rows).
+    """
+    q = dict(p)
+    q["x"] = layer_norm(p["x"], ln_w, ln_b, eps)
+    r = moe_forward(q, case, **kw)
+    sub = kw.get("token_subset")
+    xr = p["x"] if sub is None else p["x"][np.asarray(sub, dtype=np.int64)]
+    r["normed"] = q["x"]
+    r["out"] = (xr.astype(np.float32) + r["out"]).astype(np.float32)
+    return r
 
 
 def norm_rel_err(got, ref):

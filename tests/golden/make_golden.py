@@ -155,6 +155,44 @@ def run_reference_ffn(case: MoECase):
     return {"out": out.reshape(case.tokens, case.hidden).numpy()}
 
 
+# fused pre-norm block cases (python/vesper/model.py:418-425): residual stream x with
+# per-token and per-channel offsets, LayerNorm with random affine parameters
+LN_CASES = {
+    "ln_t96_bias": MoECase(tokens=96, batch=2, hidden=128, inter=192, experts=8, top_k=2,
+                           bias_std=0.05, seed=31),
+    "ln_t40_lora_e16k4": MoECase(tokens=40, batch=1, hidden=64, inter=96, experts=16, top_k=4,
+                                 lora_on=True, seed=32),
+}
+
+
+def run_reference_prenorm(case: MoECase):
+    """ffn_norm + MoELayer + residual exactly as TransformerLayer.forward (model.py:418-425)."""
+    import torch
+    from oracle.inputs import make_norm_inputs
+
+    inp = make_inputs(case)
+    ni = make_norm_inputs(case)
+    moe = reference_layer(case, inp)
+    norm = torch.nn.LayerNorm(case.hidden, eps=float(ni["eps"]))   # model.py:399
+    with torch.no_grad():
+        norm.weight.copy_(torch.from_numpy(ni["ln_w"]))
+        norm.bias.copy_(torch.from_numpy(ni["ln_b"]))
+    captured = {}
+    moe.router.register_forward_hook(lambda m, i, o: captured.__setitem__("logits", o.detach().clone()))
+    hidden = torch.from_numpy(ni["x"]).reshape(case.batch, case.seq, case.hidden)
+    with torch.no_grad():
+        normed = norm(hidden)                 # model.py:418
+        ffn_out, aux = moe(normed)            # model.py:420
+        out = hidden + ffn_out                # model.py:425
+    T = case.tokens
+    probs = torch.softmax(captured["logits"], dim=-1)
+    return {"normed": normed.reshape(T, case.hidden).numpy(),
+            "logits": captured["logits"].reshape(T, case.experts).numpy(),
+            "probs": probs.reshape(T, case.experts).numpy(),
+            "out": out.reshape(T, case.hidden).numpy(),
+            "aux": np.asarray(aux.item(), dtype=np.float32)}
+
+
 def dump_state_dict_keys():
     """Record the reference MoELayer's state_dict keys and shapes for a small config."""
     sys.path.insert(0, REFERENCE_PY)
@@ -186,6 +224,14 @@ def main(names=None):
         np.savez_compressed(path, case=np.asarray(json.dumps(case.to_dict())),
                             torch_version=np.asarray(torch.__version__), **res)
         print(f"{name}: out {res['out'].shape} -> {path}")
+    for name, case in LN_CASES.items():
+        if names and name not in names:
+            continue
+        res = run_reference_prenorm(case)
+        path = os.path.join(HERE, f"{name}.npz")
+        np.savez_compressed(path, case=np.asarray(json.dumps(case.to_dict())),
+                            torch_version=np.asarray(torch.__version__), **res)
+        print(f"{name}: aux={float(res['aux']):.6f} -> {path}")
     for name, case in CASES.items():
         if names and name not in names:
             continue

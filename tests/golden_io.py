@@ -11,14 +11,18 @@ GOLDEN_DIR = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
 
 
 def golden_names():
-    """The MoE-layer goldens (the dense FeedForward ones start with 'ffn_')."""
+    """The MoE-layer goldens (dense FeedForward ones start with 'ffn_', pre-norm blocks 'ln_')."""
     return sorted(n for n in (os.path.basename(p)[:-4]
                               for p in glob.glob(os.path.join(GOLDEN_DIR, "*.npz")))
-                  if not n.startswith("ffn_"))
+                  if not n.startswith(("ffn_", "ln_")))
 
 
 def ffn_golden_names():
     return sorted(os.path.basename(p)[:-4] for p in glob.glob(os.path.join(GOLDEN_DIR, "ffn_*.npz")))
+
+
+def ln_golden_names():
+    return sorted(os.path.basename(p)[:-4] for p in glob.glob(os.path.join(GOLDEN_DIR, "ln_*.npz")))
 
 
 def load_golden(name):

@@ -10,7 +10,7 @@ import pytest
 
 from oracle import moe_oracle as O
 from oracle.inputs import make_inputs, round_bf16
-from tests.golden_io import ffn_golden_names, golden_names, load_golden
+from tests.golden_io import ffn_golden_names, golden_names, ln_golden_names, load_golden
 
 NAMES = golden_names()
 
@@ -18,6 +18,7 @@ NAMES = golden_names()
 def test_goldens_present():
     assert "c1_fp32" in NAMES and len(NAMES) >= 8
     assert len(ffn_golden_names()) >= 2
+    assert len(ln_golden_names()) >= 2
 
 
 @pytest.mark.parametrize("name", NAMES)
@@ -56,6 +57,22 @@ def test_oracle_ffn_matches_reference(name):
     case, g = load_golden(name)
     out = O.ffn_forward(make_inputs(case), case)
     assert O.norm_rel_err(out, g["out"]) < 1e-5
+
+
+@pytest.mark.parametrize("name", ln_golden_names())
+def test_oracle_prenorm_matches_reference(name):
+    # ffn_norm + MoELayer + residual as TransformerLayer.forward (python/vesper/model.py:418-425)
+    from oracle.inputs import make_norm_inputs
+    case, g = load_golden(name)
+    ni = make_norm_inputs(case)
+    p = make_inputs(case)
+    p["x"] = ni["x"]
+    res = O.prenorm_moe_forward(p, case, ni["ln_w"], ni["ln_b"], ni["eps"])
+    assert O.norm_rel_err(res["normed"], g["normed"]) < 1e-5
+    assert O.norm_rel_err(res["logits"], g["logits"]) < 1e-5
+    assert not O.near_ties(g["probs"], case.top_k, rel=1e-5).any()
+    assert O.norm_rel_err(res["out"], g["out"]) < 1e-5
+    assert abs(float(res["aux"]) - float(g["aux"])) <= 1e-5 * abs(float(g["aux"]))
 
 
 def test_tied_router_case_is_all_ties():

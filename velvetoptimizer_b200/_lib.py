@@ -37,6 +37,7 @@ EXPORTED = (
     "vmoe_ep_combine", "vmoe_ep_p2p_setup", "vmoe_ep_p2p_connect", "vmoe_ep_p2p_workspace_size",
     "vmoe_ep_p2p_forward", "vmoe_gemm_tile_rows", "vmoe_ffn_create", "vmoe_ffn_workspace_size",
     "vmoe_ffn_forward", "vmoe_forward_host_workspace_size", "vmoe_forward_host",
+    "vmoe_set_norm", "vmoe_forward_residual",
 )
 
 
@@ -109,6 +110,10 @@ def load() -> ctypes.CDLL:
     lib.vmoe_forward_host.argtypes = [H, c_void_p, c_int64, c_void_p, c_void_p, c_int, c_void_p,
                                       c_size_t, c_void_p]
     lib.vmoe_forward_host.restype = c_int
+    lib.vmoe_set_norm.argtypes = [H, c_void_p, c_void_p, c_float, c_void_p]
+    lib.vmoe_set_norm.restype = c_int
+    lib.vmoe_forward_residual.argtypes = lib.vmoe_forward.argtypes
+    lib.vmoe_forward_residual.restype = c_int
     lib.vmoe_create_ep.argtypes = [POINTER(VmoeConfig), c_int, c_int, c_int, POINTER(H)]
     lib.vmoe_create_ep.restype = c_int
     lib.vmoe_ep_workspace_size.argtypes = [H, c_int64, c_int64, POINTER(c_size_t)]
@@ -213,6 +218,17 @@ class Handle:
         rc = self.lib.vmoe_forward(self.ptr, x, tokens, out, logits, idx, topw, counts, aux, ws,
                                    ws_bytes, c_void_p(stream))
         check(rc, self.ptr, "vmoe_forward")
+
+    def set_norm(self, weight, bias, eps: float, stream: int) -> None:
+        """LayerNorm parameters (device pointers or None) of the fused pre-norm block."""
+        check(self.lib.vmoe_set_norm(self.ptr, weight, bias, float(eps), c_void_p(stream)),
+              self.ptr, "vmoe_set_norm")
+
+    def forward_residual(self, x, tokens, out, logits, idx, topw, counts, aux, ws, ws_bytes,
+                         stream):
+        rc = self.lib.vmoe_forward_residual(self.ptr, x, tokens, out, logits, idx, topw, counts,
+                                            aux, ws, ws_bytes, c_void_p(stream))
+        check(rc, self.ptr, "vmoe_forward_residual")
 
     def host_workspace_size(self, tokens: int, chunks: int = 0) -> int:
         n = c_size_t()

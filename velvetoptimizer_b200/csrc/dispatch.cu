@@ -109,12 +109,13 @@ plan_kernel(const int* __restrict__ counts, const float* __restrict__ psum_tot, 
 
 // ---- 3. slot assignment + gather -----------------------------------------------------
 // grid = nblk, block = 128 (one thread per token of the routing block)
-template <typename T>
+template <typename T, bool LN>
 __global__ void __launch_bounds__(128)
 dispatch_kernel(const T* __restrict__ x, const int32_t* __restrict__ topk_idx,
                 const int* __restrict__ excl, const int* __restrict__ offs, int64_t T_tok, int H,
                 int E, int K, int64_t capacity, int* __restrict__ slot_of, T* __restrict__ x_perm,
-                int64_t xp_ld, int* status) {
+                int64_t xp_ld, int* status, const float2* __restrict__ ln_stats,
+                const float* __restrict__ ln_w, const float* __restrict__ ln_b) {
   extern __shared__ uint32_t dsm[];
   uint32_t* masks = dsm;                            // [4 warps][E] token bitmasks
   int* wbase = reinterpret_cast<int*>(dsm + 4 * E);  // [4][E]
@@ -157,12 +158,32 @@ dispatch_kernel(const T* __restrict__ x, const int32_t* __restrict__ topk_idx,
   const int ntok = static_cast<int>(T_tok - blk * kTileM < kTileM ? T_tok - blk * kTileM : kTileM);
   for (int i = warp; i < ntok; i += 4) {
     const T* src = x + (blk * kTileM + i) * static_cast<int64_t>(H);
+    float2 st = make_float2(0.f, 0.f);
+    if constexpr (LN) st = ln_stats[blk * kTileM + i];
     for (int v0 = 0; v0 < nvec; v0 += 32 * 4) {
       uint4 buf[4];
 #pragma unroll
       for (int u = 0; u < 4; ++u) {
         const int v = v0 + u * 32 + lane;
-        if (v < nvec) buf[u] = reinterpret_cast<const uint4*>(src)[v];
+        if (v < nvec) {
+          buf[u] = reinterpret_cast<const uint4*>(src)[v];
+          if constexpr (LN) {  // (x - mean) * rstd * w + b, rounded to the dtype (model.py:418)
+            float f[V];
+            load16_to_f(reinterpret_cast<const T*>(&buf[u]), f);
+            // w / b as 16-byte vectors (V floats from a 4V-byte aligned offset)
+            const float4* w4 = reinterpret_cast<const float4*>(ln_w + v * V);
+            const float4* b4 = reinterpret_cast<const float4*>(ln_b + v * V);
+#pragma unroll
+            for (int q = 0; q < V / 4; ++q) {
+              const float4 w = w4[q], b = b4[q];
+              f[4 * q + 0] = fmaf((f[4 * q + 0] - st.x) * st.y, w.x, b.x);
+              f[4 * q + 1] = fmaf((f[4 * q + 1] - st.x) * st.y, w.y, b.y);
+              f[4 * q + 2] = fmaf((f[4 * q + 2] - st.x) * st.y, w.z, b.z);
+              f[4 * q + 3] = fmaf((f[4 * q + 3] - st.x) * st.y, w.w, b.w);
+            }
+            store16_from_f(reinterpret_cast<T*>(&buf[u]), f);
+          }
+        }
       }
       for (int k = 0; k < K; ++k) {
         const int s = slots[i * K + k];
@@ -184,7 +205,7 @@ template <typename T>
 __global__ void __launch_bounds__(256)
 combine_kernel(const T* __restrict__ y, int64_t y_ld, const int32_t* __restrict__ topk_idx,
                const float* __restrict__ topk_w, const int* __restrict__ slot_of, int64_t T_tok,
-               int H, int K, T* __restrict__ out) {
+               int H, int K, T* out, const T* resid) {
   const int lane = threadIdx.x & 31;
   const int64_t t = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
   if (t >= T_tok) return;
@@ -217,6 +238,14 @@ combine_kernel(const T* __restrict__ y, int64_t y_ld, const int32_t* __restrict_
       const float w = ord_w[j];
 #pragma unroll
       for (int i = 0; i < V; ++i) acc[i] = __fadd_rn(acc[i], __fmul_rn(f[i], w));  // (y*w) then add
+    }
+    if (resid) {
+      // hidden_states + ffn_out (model.py:425): ffn_out is rounded to the dtype first;
+      // each thread reads its resid vector before it writes the same out vector
+      float r[V];
+      load16_to_f(resid + t * static_cast<int64_t>(H) + v * V, r);
+#pragma unroll
+      for (int i = 0; i < V; ++i) acc[i] = __fadd_rn(r[i], Elt<T>::to_f(Elt<T>::from_f(acc[i])));
     }
     store16_from_f(orow + v * V, acc);
   }
@@ -280,38 +309,48 @@ cudaError_t launch_plan(const int* counts, const float* psum_tot, int64_t T, int
   return cudaGetLastError();
 }
 
+namespace {
+template <typename T, bool LN>
+void dispatch_as(const void* x, const int32_t* topk_idx, const int* excl, const int* offs,
+                 int64_t T_tok, int H, int E, int K, int64_t capacity, int* slot_of, void* x_perm,
+                 int64_t xp_ld, int* status, const LnArgs* ln, cudaStream_t s) {
+  const unsigned nblk = static_cast<unsigned>((T_tok + kTileM - 1) / kTileM);
+  const size_t smem = (8 * static_cast<size_t>(E) + static_cast<size_t>(kTileM) * K) * 4;
+  auto kern = dispatch_kernel<T, LN>;
+  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+  kern<<<nblk, 128, smem, s>>>(static_cast<const T*>(x), topk_idx, excl, offs, T_tok, H, E, K,
+                               capacity, slot_of, static_cast<T*>(x_perm), xp_ld, status,
+                               LN ? ln->stats : nullptr, LN ? ln->weight : nullptr,
+                               LN ? ln->bias : nullptr);
+}
+}  // namespace
+
 cudaError_t launch_dispatch(int dtype, const void* x, const int32_t* topk_idx, const int* excl,
                             const int* offs, int64_t T, int H, int E, int K, int64_t capacity,
                             int* slot_of, void* x_perm, int64_t xp_ld, int* status,
-                            cudaStream_t s) {
-  const unsigned nblk = static_cast<unsigned>((T + kTileM - 1) / kTileM);
-  const size_t smem = (8 * static_cast<size_t>(E) + static_cast<size_t>(kTileM) * K) * 4;
+                            const LnArgs* ln, cudaStream_t s) {
   if (dtype == kF32) {
-    auto kern = dispatch_kernel<float>;
-    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
-    kern<<<nblk, 128, smem, s>>>(static_cast<const float*>(x), topk_idx, excl, offs, T, H, E, K,
-                                 capacity, slot_of, static_cast<float*>(x_perm), xp_ld, status);
+    if (ln) dispatch_as<float, true>(x, topk_idx, excl, offs, T, H, E, K, capacity, slot_of, x_perm, xp_ld, status, ln, s);
+    else dispatch_as<float, false>(x, topk_idx, excl, offs, T, H, E, K, capacity, slot_of, x_perm, xp_ld, status, ln, s);
   } else {
-    auto kern = dispatch_kernel<__nv_bfloat16>;
-    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
-    kern<<<nblk, 128, smem, s>>>(static_cast<const __nv_bfloat16*>(x), topk_idx, excl, offs, T, H,
-                                 E, K, capacity, slot_of, static_cast<__nv_bfloat16*>(x_perm),
-                                 xp_ld, status);
+    if (ln) dispatch_as<__nv_bfloat16, true>(x, topk_idx, excl, offs, T, H, E, K, capacity, slot_of, x_perm, xp_ld, status, ln, s);
+    else dispatch_as<__nv_bfloat16, false>(x, topk_idx, excl, offs, T, H, E, K, capacity, slot_of, x_perm, xp_ld, status, ln, s);
   }
   return cudaGetLastError();
 }
 
 cudaError_t launch_combine(int dtype, const void* y, int64_t y_ld, const int32_t* topk_idx,
                            const float* topk_w, const int* slot_of, int64_t T, int H, int K,
-                           void* out, cudaStream_t s) {
+                           void* out, const void* resid, cudaStream_t s) {
   const unsigned grid = static_cast<unsigned>((T + 7) / 8);
   if (dtype == kF32) {
     combine_kernel<float><<<grid, 256, 0, s>>>(static_cast<const float*>(y), y_ld, topk_idx,
-                                               topk_w, slot_of, T, H, K, static_cast<float*>(out));
+                                               topk_w, slot_of, T, H, K, static_cast<float*>(out),
+                                               static_cast<const float*>(resid));
   } else {
     combine_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>(
         static_cast<const __nv_bfloat16*>(y), y_ld, topk_idx, topk_w, slot_of, T, H, K,
-        static_cast<__nv_bfloat16*>(out));
+        static_cast<__nv_bfloat16*>(out), static_cast<const __nv_bfloat16*>(resid));
   }
   return cudaGetLastError();
 }

@@ -6,6 +6,13 @@
 //   kRouter (router)      : logits = x W_r^T + b_r, softmax, top-K, renormalise :322-329, plus
 //                           the per-128-token expert histogram and probability sums the
 //                           dispatch and the load-balancing loss (:366-385) consume
+//   kRouterLN             : the same router on LayerNorm(x) (the ffn_norm of :418) without
+//                           materialising the normalised rows: the B operand holds
+//                           W' = W_r * ln_w, and two more MMAs per k-step on the x tile that
+//                           is already in shared memory give every token's sum (x against a
+//                           ones row) and sum of squares (the diagonal of x x^T); the epilogue
+//                           forms mean / rstd and logits = rstd (x W'^T - mean c) + b' with
+//                           c = row sums of W' and b' = b_r + W_r ln_b (folded at load time)
 //
 // Design (one CTA per SM, persistent over (M tile, N tile) work items):
 //   warp 0      TMA producer: A tile [128 x 64] and B tile [BN x 64] per k-block into a
@@ -32,7 +39,12 @@
 namespace vmoe {
 namespace {
 
-enum Epi { kPlain = 0, kGated = 1, kRouter = 2 };
+enum Epi { kPlain = 0, kGated = 1, kRouter = 2, kRouterLN = 3 };
+
+// kRouterLN accumulator columns: [0, BN) logits, kSumCol.. the x-sum block (N 16),
+// kSqCol.. x x^T (N 128); one accumulator spans kLnAccCols columns.
+constexpr int kSumCol = 64, kSqCol = 128, kLnAccCols = 256;
+constexpr uint32_t kOnesBytes = 16 * 128;  // 16-row K-major ones tile (row 0 = 1, rest 0)
 
 constexpr int BK = 64;
 constexpr uint32_t A_BYTES = kTileM * BK * 2;  // 16 KB
@@ -64,9 +76,10 @@ struct TcShared {
   float psum[4][64];
 };
 
-template <int BN>
+template <int BN, int EPI = kPlain>
 constexpr size_t tc_smem_bytes() {
-  return 1024 + TcCfg<BN>::STAGES * TcCfg<BN>::STAGE_BYTES + sizeof(TcShared<TcCfg<BN>::STAGES>) + 64;
+  return 1024 + TcCfg<BN>::STAGES * TcCfg<BN>::STAGE_BYTES + (EPI == kRouterLN ? kOnesBytes : 0) +
+         sizeof(TcShared<TcCfg<BN>::STAGES>) + 64;
 }
 
 template <int STAGES>
@@ -99,7 +112,7 @@ __device__ __forceinline__ float warp_sum(float v) {
 }
 
 // Router epilogue for one 128-token tile: each thread owns one token's logits.
-template <int BN, int STAGES>
+template <int BN, int STAGES, bool LN>
 __device__ __forceinline__ void router_epilogue(const TcGemmArgs& args, TcShared<STAGES>* sh,
                                                 uint32_t t_row, int m, int q, int lane) {
   float lg[BN];
@@ -108,8 +121,26 @@ __device__ __forceinline__ void router_epilogue(const TcGemmArgs& args, TcShared
   const int E = args.num_experts, K = args.top_k;
   const int64_t t = static_cast<int64_t>(m) * kTileM + q * 32 + lane;
   const bool valid = t < args.tokens;
+  if constexpr (LN) {
+    // this token's sum (column kSumCol) and sum of squares (its own diagonal entry of x x^T)
+    float sx[16], sq[32];
+    tmem_ld16(t_row + kSumCol, sx);
+    tmem_ld32(t_row + kSqCol + q * 32, sq);
+    float ss = 0.f;
 #pragma unroll
-  for (int e = 0; e < BN; ++e) lg[e] = e < E ? lg[e] + args.bias[e] : -INFINITY;
+    for (int j = 0; j < 32; ++j) ss = j == lane ? sq[j] : ss;
+    const float inv_h = 1.0f / static_cast<float>(args.ln_h);
+    const float mean = sx[0] * inv_h;
+    const float var = fmaxf(fmaf(ss, inv_h, -mean * mean), 0.f);
+    const float rstd = 1.0f / sqrtf(var + args.ln_eps);
+    if (valid) args.ln_stats[t] = make_float2(mean, rstd);
+#pragma unroll
+    for (int e = 0; e < BN; ++e)
+      lg[e] = e < E ? fmaf(rstd, fmaf(-mean, args.ln_c[e], lg[e]), args.bias[e]) : -INFINITY;
+  } else {
+#pragma unroll
+    for (int e = 0; e < BN; ++e) lg[e] = e < E ? lg[e] + args.bias[e] : -INFINITY;
+  }
   if (valid && args.logits) {
     float* dst = args.logits + t * E;
 #pragma unroll
@@ -180,15 +211,30 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_constant_
                const TcGemmArgs args) {
   using Cfg = TcCfg<BN>;
   constexpr int STAGES = Cfg::STAGES;
+  constexpr bool LN = EPI == kRouterLN;
+  constexpr bool ROUTER = EPI == kRouter || EPI == kRouterLN;
+  constexpr uint32_t TCOLS = LN ? 2 * kLnAccCols : Cfg::TMEM_COLS;
+  constexpr uint32_t ACC_COLS = LN ? kLnAccCols : BN;
+  static_assert(!LN || BN <= kSumCol, "the LayerNorm router keeps E <= 64 logit columns");
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
   uint8_t* gbase = smem_raw + (base - raw);
   const uint32_t a_s = base;
   const uint32_t b_s = base + STAGES * A_BYTES;
-  auto* sh = reinterpret_cast<TcShared<STAGES>*>(gbase + STAGES * Cfg::STAGE_BYTES);
+  const uint32_t ones_s = base + STAGES * Cfg::STAGE_BYTES;  // kRouterLN only
+  auto* sh = reinterpret_cast<TcShared<STAGES>*>(gbase + STAGES * Cfg::STAGE_BYTES +
+                                                 (LN ? kOnesBytes : 0));
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if constexpr (LN) {
+    // row 0 of the 16-row tile is 64 bf16 ones (0x3F80), rows 1..15 zero; with one 128-byte
+    // row per K-block the 128B swizzle leaves row 0 in place
+    uint32_t* ones = reinterpret_cast<uint32_t*>(gbase + STAGES * Cfg::STAGE_BYTES);
+    for (int i = threadIdx.x; i < static_cast<int>(kOnesBytes / 4); i += blockDim.x)
+      ones[i] = i < 32 ? 0x3F803F80u : 0u;
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // visible to tcgen05.mma
+  }
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -207,7 +253,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_constant_
     prefetch_tmap(&a_map);
     prefetch_tmap(&b_map);
   }
-  if (warp == 1) tmem_alloc(smem_u32(&sh->tmem_base), Cfg::TMEM_COLS);
+  if (warp == 1) tmem_alloc(smem_u32(&sh->tmem_base), TCOLS);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -261,7 +307,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_constant_
           break;
         }
         tc_fence_after();
-        const uint32_t d_tmem = tmem + acc * BN;
+        const uint32_t d_tmem = tmem + acc * ACC_COLS;
         bool ok = true;
         for (int kb = 0; kb < k_blocks; ++kb, ++it) {
           const int s = it % STAGES;
@@ -275,8 +321,14 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_constant_
           const uint32_t a_addr = a_s + s * A_BYTES, b_addr = b_s + s * Cfg::B_BYTES;
 #pragma unroll
           for (int k = 0; k < BK / 16; ++k) {
-            umma_bf16(d_tmem, umma_desc_sw128(a_addr + k * 32), umma_desc_sw128(b_addr + k * 32),
-                      Cfg::IDESC, (kb | k) != 0 ? 1u : 0u);
+            const uint64_t a_desc = umma_desc_sw128(a_addr + k * 32);
+            const uint32_t accum = (kb | k) != 0 ? 1u : 0u;
+            umma_bf16(d_tmem, a_desc, umma_desc_sw128(b_addr + k * 32), Cfg::IDESC, accum);
+            if constexpr (LN) {
+              umma_bf16(d_tmem + kSumCol, a_desc, umma_desc_sw128(ones_s + k * 32),
+                        umma_idesc_bf16(kTileM, 16), accum);
+              umma_bf16(d_tmem + kSqCol, a_desc, a_desc, umma_idesc_bf16(kTileM, 128), accum);
+            }
           }
           umma_commit(smem_u32(&sh->empty[s]));
           *reinterpret_cast<volatile int*>(&sh->consumed) = it + 1;
@@ -299,7 +351,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_constant_
       const bool got = mbar_wait(smem_u32(&sh->tfull[acc]), aph);
       __syncwarp();
       const bool warp_ok = __all_sync(0xffffffffu, got);
-      if constexpr (EPI == kRouter) {
+      if constexpr (ROUTER) {
         // the router epilogue synchronises the four epilogue warps, so they must agree
         // on whether to go on (each warp's wait above is bounded)
         if (lane == 0) sh->ep_ok[q] = warp_ok ? 1 : 0;
@@ -315,9 +367,9 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_constant_
       }
       tc_fence_after();
       const int m = tile / n_tiles, n = tile - m * n_tiles;
-      const uint32_t t_row = tmem + (static_cast<uint32_t>(q * 32) << 16) + acc * BN;
-      if constexpr (EPI == kRouter) {
-        router_epilogue<BN>(args, sh, t_row, m, q, lane);
+      const uint32_t t_row = tmem + (static_cast<uint32_t>(q * 32) << 16) + acc * ACC_COLS;
+      if constexpr (ROUTER) {
+        router_epilogue<BN, STAGES, LN>(args, sh, t_row, m, q, lane);
       } else {
         const int e = expert_of(args, m);
         const int64_t row = static_cast<int64_t>(m) * kTileM + q * 32 + lane;
@@ -382,14 +434,14 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_constant_
   if (warp == 1) {
     __syncwarp();
     tc_fence_after();
-    tmem_dealloc(tmem, Cfg::TMEM_COLS);
+    tmem_dealloc(tmem, TCOLS);
   }
 }
 
 template <int EPI, int BN>
 cudaError_t launch_cfg(const CUtensorMap& a_map, const CUtensorMap& b_map, const TcGemmArgs& args,
                        int64_t work, int num_sms, cudaStream_t s) {
-  constexpr size_t smem = tc_smem_bytes<BN>();
+  constexpr size_t smem = tc_smem_bytes<BN, EPI>();
   static_assert(smem <= 232448, "shared memory budget");
   const int grid = static_cast<int>(work < num_sms ? (work > 0 ? work : 1) : num_sms);
   auto kern = tc_gemm_kernel<EPI, BN>;
@@ -458,8 +510,17 @@ int tc_router_width(int E) {
 }
 
 cudaError_t launch_tc_router(const CUtensorMap& x_map, const CUtensorMap& w_map,
-                             const TcGemmArgs& args, int num_sms, cudaStream_t s) {
+                             const TcGemmArgs& args, int num_sms, cudaStream_t s, bool ln) {
   const int64_t work = args.m_tiles_host;
+  if (ln) {
+    if (!args.ln_stats || !args.ln_c || args.ln_h <= 0) return cudaErrorInvalidValue;
+    switch (tc_router_width(args.num_experts)) {
+      case 16: return launch_cfg<kRouterLN, 16>(x_map, w_map, args, work, num_sms, s);
+      case 32: return launch_cfg<kRouterLN, 32>(x_map, w_map, args, work, num_sms, s);
+      case 64: return launch_cfg<kRouterLN, 64>(x_map, w_map, args, work, num_sms, s);
+      default: return cudaErrorInvalidValue;
+    }
+  }
   switch (tc_router_width(args.num_experts)) {
     case 16: return launch_cfg<kRouter, 16>(x_map, w_map, args, work, num_sms, s);
     case 32: return launch_cfg<kRouter, 32>(x_map, w_map, args, work, num_sms, s);

@@ -16,12 +16,23 @@ constexpr int kTileM = 128;
 
 inline size_t dtype_bytes(int dt) { return dt == kF32 ? 4 : 2; }
 
+// ---- fused pre-norm ------------------------------------------------------------------
+// LayerNorm over H folded into the router's and the dispatch's read of x (the residual
+// stream): per-token (mean, 1/sqrt(var + eps)) in `stats`, affine weight / bias in fp32.
+struct LnArgs {
+  float2* stats;        // [T]: written by the router (or its statistics pass), read by dispatch
+  const float* weight;  // [H]
+  const float* bias;    // [H]
+  float eps;
+};
+
 // ---- routing ------------------------------------------------------------------------
 // Router GEMM + softmax + top-K (lowest-index tie-break) + renormalise, per 128-token
-// block also the expert histogram hist[blk][E] and probability sums psum[blk][E].
+// block also the expert histogram hist[blk][E] and probability sums psum[blk][E].  With
+// `ln`, the router reads LayerNorm(x) (statistics pass first, rows normalised on load).
 cudaError_t launch_router(int dtype, const void* x, const void* w_r, const float* b_r, int64_t T,
                           int H, int E, int K, float* logits, int32_t* topk_idx, float* topk_w,
-                          int* hist, float* psum, cudaStream_t s);
+                          int* hist, float* psum, const LnArgs* ln, cudaStream_t s);
 
 // Per expert: exclusive prefix of hist over blocks (excl[blk][E]), counts, prob sums.
 cudaError_t launch_scan_blocks(const int* hist, const float* psum, int nblk, int E, int* excl,
@@ -42,16 +53,19 @@ cudaError_t launch_aux_merge_ws(const void* ws, size_t stride, size_t counts_off
 // Tile map of a dense layer: n tiles, all expert 0.
 cudaError_t launch_fill_tiles(int* tile_expert, int n, int* num_tiles, cudaStream_t s);
 
-// Stable expert-major slots for every (token, k) and the row gather x -> x_perm.
+// Stable expert-major slots for every (token, k) and the row gather x -> x_perm (with
+// `ln`: LayerNorm(x) rows, normalised on the way, rounded to the dtype).
 cudaError_t launch_dispatch(int dtype, const void* x, const int32_t* topk_idx, const int* excl,
                             const int* offs, int64_t T, int H, int E, int K, int64_t capacity,
                             int* slot_of, void* x_perm, int64_t xp_ld, int* status,
-                            cudaStream_t s);
+                            const LnArgs* ln, cudaStream_t s);
 
-// out[t] = sum over the token's experts in ascending id of w * y[slot]  (fp32 sum).
+// out[t] = sum over the token's experts in ascending id of w * y[slot]  (fp32 sum); with
+// `resid`, out[t] = resid[t] + that sum rounded to the dtype (the residual add of the
+// pre-norm block; out may alias resid).
 cudaError_t launch_combine(int dtype, const void* y, int64_t y_ld, const int32_t* topk_idx,
                            const float* topk_w, const int* slot_of, int64_t T, int H, int K,
-                           void* out, cudaStream_t s);
+                           void* out, const void* resid, cudaStream_t s);
 
 // ---- fp32 expert GEMMs (CUDA cores; the fp32 correctness path) ------------------------
 // h = ERA(A Wg^T + bg) * (A Wu^T + bu) per M tile's expert.
@@ -89,6 +103,11 @@ struct TcGemmArgs {
   int64_t bias_ld;          // elements per expert
   float gamma;              // ERA gamma (gated epilogue)
   int* status;
+  // LayerNorm router (launch_tc_router with ln): b operand = W_r * ln_w, bias = b_r + W_r ln_b
+  float2* ln_stats;         // [T] (mean, rstd) out
+  const float* ln_c;        // [E] row sums of the folded weights
+  float ln_eps;
+  int ln_h;                 // H (the normalised width)
 };
 // gated = true : B tile = [128 gate rows | 128 up rows], h = ERA(gate) * up (128 cols)
 // gated = false: plain bias epilogue, 256 output columns per tile
@@ -105,9 +124,11 @@ cudaError_t launch_tc_gemm_pair(bool gated, const CUtensorMap& a_map, const CUte
 // Router on the tensor cores: logits = x W_r^T (+ bias in `args.bias`), softmax, top-K,
 // renormalised weights, per-128-token histogram and probability sums.  E <= 64;
 // tc_router_width(E) is the N tile (16, 32 or 64), 0 when E is too wide.
+// With `ln` the router reads the raw residual stream and applies LayerNorm through the
+// folded weights (args.ln_*), writing every token's statistics for the dispatch.
 int tc_router_width(int E);
 cudaError_t launch_tc_router(const CUtensorMap& x_map, const CUtensorMap& w_map,
-                             const TcGemmArgs& args, int num_sms, cudaStream_t s);
+                             const TcGemmArgs& args, int num_sms, cudaStream_t s, bool ln);
 
 // Build a 2-D bf16 tensor map: [rows, cols] row-major with `ld` elements per row, box
 // {64 cols, box_rows rows}, 128-byte swizzle.  Returns false on failure.
@@ -174,6 +195,16 @@ struct PackBiasArgs {
   int which;
 };
 cudaError_t launch_pack_bias(const PackBiasArgs& a, cudaStream_t s);
+
+// LayerNorm fold into the tensor-core router (bf16 W_r [E, H], fp32 b_r [E], ln_w / ln_b
+// fp32 [H]): w_out = bf16(W_r * ln_w), c_out[e] = sum_j w_out[e, j], b_out[e] = b_r[e] +
+// sum_j W_r[e, j] ln_b[j] (fixed summation order).
+cudaError_t launch_fold_router_ln(const void* w_r, const float* b_r, const float* ln_w,
+                                  const float* ln_b, int E, int H, void* w_out, float* b_out,
+                                  float* c_out, cudaStream_t s);
+// fp32 copy of a [n] vector of the given dtype (null src: fill with `fill`).
+cudaError_t launch_to_f32(int dtype, const void* src, int64_t n, float fill, float* dst,
+                          cudaStream_t s);
 
 }  // namespace vmoe
 

@@ -79,7 +79,66 @@ __global__ void pack_bias_kernel(PackBiasArgs a) {
   }
 }
 
+// One block per expert row e: w_out[e, :] = bf16(W_r[e, :] * ln_w), then in a fixed
+// order c[e] = sum_j w_out[e, j] and b_out[e] = b_r[e] + sum_j W_r[e, j] * ln_b[j].
+__global__ void __launch_bounds__(256)
+fold_router_ln_kernel(const __nv_bfloat16* __restrict__ w_r, const float* __restrict__ b_r,
+                      const float* __restrict__ ln_w, const float* __restrict__ ln_b, int H,
+                      __nv_bfloat16* __restrict__ w_out, float* __restrict__ b_out,
+                      float* __restrict__ c_out) {
+  const int e = blockIdx.x, tid = threadIdx.x;
+  float c = 0.f, b = 0.f;
+  for (int j = tid; j < H; j += blockDim.x) {
+    const float w = __bfloat162float(w_r[static_cast<int64_t>(e) * H + j]);
+    const __nv_bfloat16 f = __float2bfloat16_rn(w * ln_w[j]);
+    w_out[static_cast<int64_t>(e) * H + j] = f;
+    c += __bfloat162float(f);
+    b = fmaf(w, ln_b[j], b);
+  }
+  __shared__ float sc[256], sb[256];
+  sc[tid] = c;
+  sb[tid] = b;
+  __syncthreads();
+  for (int o = blockDim.x / 2; o > 0; o >>= 1) {
+    if (tid < o) {
+      sc[tid] += sc[tid + o];
+      sb[tid] += sb[tid + o];
+    }
+    __syncthreads();
+  }
+  if (tid == 0) {
+    c_out[e] = sc[0];
+    b_out[e] = b_r[e] + sb[0];
+  }
+}
+
+template <typename T>
+__global__ void to_f32_kernel(const T* __restrict__ src, int64_t n, float fill, float* __restrict__ dst) {
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+    dst[i] = src ? Elt<T>::to_f(src[i]) : fill;
+}
+
 }  // namespace
+
+cudaError_t launch_fold_router_ln(const void* w_r, const float* b_r, const float* ln_w,
+                                  const float* ln_b, int E, int H, void* w_out, float* b_out,
+                                  float* c_out, cudaStream_t s) {
+  fold_router_ln_kernel<<<E, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(w_r), b_r, ln_w, ln_b,
+                                          H, static_cast<__nv_bfloat16*>(w_out), b_out, c_out);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_to_f32(int dtype, const void* src, int64_t n, float fill, float* dst,
+                          cudaStream_t s) {
+  const unsigned grid = static_cast<unsigned>((n + 255) / 256 > 0 ? (n + 255) / 256 : 1);
+  if (dtype == kF32)
+    to_f32_kernel<float><<<grid, 256, 0, s>>>(static_cast<const float*>(src), n, fill, dst);
+  else
+    to_f32_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(src), n,
+                                                      fill, dst);
+  return cudaGetLastError();
+}
 
 cudaError_t launch_pack_weight(const PackArgs& a, cudaStream_t s) {
   if (a.dtype == kF32)

@@ -4,6 +4,11 @@
 // Reference: python/vesper/model.py:314,322 (router Linear), :323 (softmax), :326
 // (torch.topk), :329 (renormalise), :366-385 (the sums the load-balancing loss needs).
 //
+// With a fused pre-norm (LayerNorm of python/vesper/model.py:418 folded into this read of
+// x), ln_stats_kernel first computes every token's mean and 1/sqrt(var + eps) (two passes
+// over the row, fp32), and the router normalises x while it stages it: the normalised rows
+// never go to HBM.
+//
 // One CTA routes 128 tokens.  The [128 x E] logit tile is computed on CUDA cores from
 // 32-column chunks of x and W_r staged in shared memory (fp32 accumulation, inputs of
 // either dtype); then one thread per token does softmax and selection.  The per-block
@@ -19,12 +24,48 @@ constexpr int kThreads = 256;
 constexpr int kChunk = 32;
 constexpr int kMaxTopK = 32;
 
-template <typename T, int EB>
+// one warp per token: mean, then the centred sum of squares (the row is re-read from L1/L2)
+template <typename T>
+__global__ void __launch_bounds__(256)
+ln_stats_kernel(const T* __restrict__ x, int64_t T_tok, int H, float eps, float2* __restrict__ stats) {
+  const int lane = threadIdx.x & 31;
+  const int64_t t = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
+  if (t >= T_tok) return;
+  constexpr int V = Vec16<T>::N;
+  const T* row = x + t * H;
+  const int nvec = H / V;
+  float s = 0.f;
+  for (int v = lane; v < nvec; v += 32) {
+    float f[V];
+    load16_to_f(row + v * V, f);
+#pragma unroll
+    for (int i = 0; i < V; ++i) s += f[i];
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  const float mean = s / static_cast<float>(H);
+  float q = 0.f;
+  for (int v = lane; v < nvec; v += 32) {
+    float f[V];
+    load16_to_f(row + v * V, f);
+#pragma unroll
+    for (int i = 0; i < V; ++i) {
+      const float d = f[i] - mean;
+      q = fmaf(d, d, q);
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) q += __shfl_xor_sync(0xffffffffu, q, o);
+  if (lane == 0) stats[t] = make_float2(mean, 1.0f / sqrtf(q / static_cast<float>(H) + eps));
+}
+
+template <typename T, int EB, bool LN>
 __global__ void __launch_bounds__(kThreads)
 router_kernel(const T* __restrict__ x, const T* __restrict__ w_r, const float* __restrict__ b_r,
               int64_t T_tok, int H, int E, int K, float* __restrict__ logits_out,
               int32_t* __restrict__ topk_idx, float* __restrict__ topk_w, int* __restrict__ hist,
-              float* __restrict__ psum) {
+              float* __restrict__ psum, const float2* __restrict__ ln_stats,
+              const float* __restrict__ ln_w, const float* __restrict__ ln_b) {
   constexpr int TE = EB / 8;          // experts per thread
   constexpr int PITCH = kChunk + 1;   // padded smem row (floats)
   extern __shared__ float sm[];
@@ -52,6 +93,14 @@ router_kernel(const T* __restrict__ x, const T* __restrict__ w_r, const float* _
       float f[V];
       if (row < valid && h0 + c < H) {
         load16_to_f(x + (tok0 + row) * H + h0 + c, f);
+        if constexpr (LN) {
+          // the reference's normalised row, rounded to the activation dtype (model.py:418)
+          const float2 st = ln_stats[tok0 + row];
+#pragma unroll
+          for (int i = 0; i < V; ++i)
+            f[i] = Elt<T>::to_f(Elt<T>::from_f(
+                fmaf((f[i] - st.x) * st.y, ln_w[h0 + c + i], ln_b[h0 + c + i])));
+        }
       } else {
 #pragma unroll
         for (int i = 0; i < V; ++i) f[i] = 0.f;
@@ -147,44 +196,65 @@ router_kernel(const T* __restrict__ x, const T* __restrict__ w_r, const float* _
   }
 }
 
-template <typename T, int EB>
-cudaError_t launch_eb(const void* x, const void* w_r, const float* b_r, int64_t T_tok, int H,
-                      int E, int K, float* logits, int32_t* idx, float* w, int* hist,
-                      float* psum, cudaStream_t s) {
+struct RouterCall {
+  const void* x;
+  const void* w_r;
+  const float* b_r;
+  int64_t T;
+  int H, E, K;
+  float* logits;
+  int32_t* idx;
+  float* w;
+  int* hist;
+  float* psum;
+  const LnArgs* ln;
+};
+
+template <typename T, int EB, bool LN>
+cudaError_t launch_eb(const RouterCall& c, cudaStream_t s) {
   const size_t stage = static_cast<size_t>(kTileM + EB) * (kChunk + 1);
   const size_t logit = static_cast<size_t>(kTileM) * (EB + 1);
   const size_t bytes = (stage > logit ? stage : logit) * sizeof(float);
-  auto kern = router_kernel<T, EB>;
+  auto kern = router_kernel<T, EB, LN>;
   cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(bytes));
   if (err != cudaSuccess) return err;
-  const unsigned nblk = static_cast<unsigned>((T_tok + kTileM - 1) / kTileM);
-  kern<<<nblk, kThreads, bytes, s>>>(static_cast<const T*>(x), static_cast<const T*>(w_r), b_r,
-                                     T_tok, H, E, K, logits, idx, w, hist, psum);
+  const unsigned nblk = static_cast<unsigned>((c.T + kTileM - 1) / kTileM);
+  kern<<<nblk, kThreads, bytes, s>>>(
+      static_cast<const T*>(c.x), static_cast<const T*>(c.w_r), c.b_r, c.T, c.H, c.E, c.K,
+      c.logits, c.idx, c.w, c.hist, c.psum, LN ? c.ln->stats : nullptr,
+      LN ? c.ln->weight : nullptr, LN ? c.ln->bias : nullptr);
   return cudaGetLastError();
 }
 
+template <typename T, bool LN>
+cudaError_t launch_t(const RouterCall& c, cudaStream_t s) {
+  if (c.E <= 8) return launch_eb<T, 8, LN>(c, s);
+  if (c.E <= 16) return launch_eb<T, 16, LN>(c, s);
+  if (c.E <= 32) return launch_eb<T, 32, LN>(c, s);
+  if (c.E <= 64) return launch_eb<T, 64, LN>(c, s);
+  if (c.E <= 128) return launch_eb<T, 128, LN>(c, s);
+  return launch_eb<T, 256, LN>(c, s);
+}
+
 template <typename T>
-cudaError_t launch_t(const void* x, const void* w_r, const float* b_r, int64_t T_tok, int H,
-                     int E, int K, float* logits, int32_t* idx, float* w, int* hist, float* psum,
-                     cudaStream_t s) {
-  if (E <= 8) return launch_eb<T, 8>(x, w_r, b_r, T_tok, H, E, K, logits, idx, w, hist, psum, s);
-  if (E <= 16) return launch_eb<T, 16>(x, w_r, b_r, T_tok, H, E, K, logits, idx, w, hist, psum, s);
-  if (E <= 32) return launch_eb<T, 32>(x, w_r, b_r, T_tok, H, E, K, logits, idx, w, hist, psum, s);
-  if (E <= 64) return launch_eb<T, 64>(x, w_r, b_r, T_tok, H, E, K, logits, idx, w, hist, psum, s);
-  if (E <= 128)
-    return launch_eb<T, 128>(x, w_r, b_r, T_tok, H, E, K, logits, idx, w, hist, psum, s);
-  return launch_eb<T, 256>(x, w_r, b_r, T_tok, H, E, K, logits, idx, w, hist, psum, s);
+cudaError_t launch_stats_then_router(const RouterCall& c, cudaStream_t s) {
+  if (!c.ln) return launch_t<T, false>(c, s);
+  ln_stats_kernel<T><<<static_cast<unsigned>((c.T + 7) / 8), 256, 0, s>>>(
+      static_cast<const T*>(c.x), c.T, c.H, c.ln->eps, c.ln->stats);
+  cudaError_t err = cudaGetLastError();
+  if (err != cudaSuccess) return err;
+  return launch_t<T, true>(c, s);
 }
 
 }  // namespace
 
 cudaError_t launch_router(int dtype, const void* x, const void* w_r, const float* b_r, int64_t T,
                           int H, int E, int K, float* logits, int32_t* topk_idx, float* topk_w,
-                          int* hist, float* psum, cudaStream_t s) {
-  if (dtype == kF32)
-    return launch_t<float>(x, w_r, b_r, T, H, E, K, logits, topk_idx, topk_w, hist, psum, s);
-  return launch_t<__nv_bfloat16>(x, w_r, b_r, T, H, E, K, logits, topk_idx, topk_w, hist, psum, s);
+                          int* hist, float* psum, const LnArgs* ln, cudaStream_t s) {
+  const RouterCall c{x, w_r, b_r, T, H, E, K, logits, topk_idx, topk_w, hist, psum, ln};
+  if (dtype == kF32) return launch_stats_then_router<float>(c, s);
+  return launch_stats_then_router<__nv_bfloat16>(c, s);
 }
 
 }  // namespace vmoe

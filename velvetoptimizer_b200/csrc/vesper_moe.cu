@@ -62,7 +62,7 @@ struct Plan {
   int nblk = 0;
   int64_t max_tiles = 0, max_rows = 0;
   size_t idx = 0, w = 0, hist = 0, psum = 0, excl = 0, counts = 0, psum_tot = 0, offs = 0,
-         tiles = 0, ntiles = 0, aux = 0, slot = 0, xp = 0, h = 0, y = 0, total = 0;
+         tiles = 0, ntiles = 0, aux = 0, slot = 0, stats = 0, xp = 0, h = 0, y = 0, total = 0;
 };
 
 }  // namespace
@@ -109,6 +109,17 @@ struct vmoe_handle {
   bool dense = false;      // a dense FeedForward handle (one expert, no router)
   CUtensorMap map_wr{};   // router weights for the tensor-core router (bf16, E <= 64)
   int router_bn = 0;      // its N tile; 0 = CUDA-core router
+  // fused pre-norm (vmoe_set_norm / vmoe_forward_residual): LayerNorm weight and bias in
+  // fp32, and for the tensor-core router the folded W_r * ln_w, its row sums and the
+  // folded bias b_r + W_r ln_b (recomputed whenever the weights or the norm change)
+  float* ln_w = nullptr;
+  float* ln_b = nullptr;
+  float ln_eps = 0.f;
+  void* w_r_ln = nullptr;
+  float* b_r_ln = nullptr;
+  float* c_ln = nullptr;
+  CUtensorMap map_wr_ln{};
+  bool ln_ready = false;
   bool ready = false;
   // profiling ring: prof_slots forwards x (kStages + 1) events
   int prof_slots = 0;
@@ -168,6 +179,7 @@ Plan make_plan(const vmoe_handle* h, int64_t T) {
   p.ntiles = take(4);
   p.aux = take(4);
   p.slot = take(T * K * 4);
+  p.stats = take(T * 8);
   p.xp = take(static_cast<size_t>(p.max_rows) * h->H * elt);
   p.h = take(static_cast<size_t>(p.max_rows) * h->Ipad * elt);
   p.y = take(static_cast<size_t>(p.max_rows) * h->Hpad * elt);
@@ -245,12 +257,14 @@ P2PPlan make_p2p_plan(const vmoe_handle* h, int64_t T) {
 }
 
 void free_weights(vmoe_handle* h) {
-  void* bufs[] = {h->w_r, h->b_r, h->w_g, h->w_u, h->b_g, h->b_u, h->w_d, h->b_d};
+  void* bufs[] = {h->w_r, h->b_r, h->w_g, h->w_u, h->b_g, h->b_u, h->w_d, h->b_d,
+                  h->w_r_ln, h->b_r_ln, h->c_ln};
   for (void* b : bufs)
     if (b) cudaFree(b);
-  h->w_r = h->w_g = h->w_u = h->w_d = nullptr;
-  h->b_r = h->b_g = h->b_u = h->b_d = nullptr;
+  h->w_r = h->w_g = h->w_u = h->w_d = h->w_r_ln = nullptr;
+  h->b_r = h->b_g = h->b_u = h->b_d = h->b_r_ln = h->c_ln = nullptr;
   h->ready = false;
+  h->ln_ready = false;
 }
 
 int validate_config(const vmoe_config* c, char* why, size_t n) {
@@ -375,8 +389,11 @@ int run_expert_gemms(vmoe_handle* h, void* xp, int64_t max_rows, const int* tile
 
 // Router + softmax + top-K + per-block histogram / probability sums: on the tensor cores
 // for bf16 with E <= 64, on CUDA cores otherwise (fp32 parity, or wider routers).
+// With `ln` the router reads LayerNorm(x) without materialising it: the tensor-core router
+// through the folded weights (and its own row statistics), the CUDA-core router through a
+// statistics pass and normalisation on load.
 int run_router(vmoe_handle* h, const void* x, int64_t T, float* logits, int32_t* idx, float* tw,
-               int* hist, float* psum, cudaStream_t s) {
+               int* hist, float* psum, const LnArgs* ln, cudaStream_t s) {
   const int64_t H = h->H;
   cudaError_t e;
   if (h->dtype == kBF16 && h->router_bn > 0) {
@@ -402,23 +419,35 @@ int run_router(vmoe_handle* h, const void* x, int64_t T, float* logits, int32_t*
     a.topk_w = tw;
     a.hist = hist;
     a.psum = psum;
-    e = launch_tc_router(map_x, h->map_wr, a, h->num_sms, s);
+    if (ln) {
+      a.bias = h->b_r_ln;
+      a.ln_stats = ln->stats;
+      a.ln_c = h->c_ln;
+      a.ln_eps = ln->eps;
+      a.ln_h = static_cast<int>(H);
+    }
+    e = launch_tc_router(map_x, ln ? h->map_wr_ln : h->map_wr, a, h->num_sms, s, ln != nullptr);
   } else {
     e = launch_router(h->dtype, x, h->w_r, h->b_r, T, static_cast<int>(H), static_cast<int>(h->E),
-                      static_cast<int>(h->K), logits, idx, tw, hist, psum, s);
+                      static_cast<int>(h->K), logits, idx, tw, hist, psum, ln, s);
   }
   if (e != cudaSuccess) return cuda_fail(h, e, "router");
-  ++h->last_launches;
+  h->last_launches += (ln && !(h->dtype == kBF16 && h->router_bn > 0)) ? 2 : 1;
   return VMOE_OK;
 }
 
 // One single-GPU forward of T >= 1 tokens on stream s, workspace laid out by make_plan(h, T).
 // psum_tot_out (nullable) takes the batch's per-expert probability sums instead of the
 // workspace, so that a chunked caller can merge the aux loss of the whole batch.
+// With prenorm, x is the residual stream: the layer runs on LayerNorm(x) (folded into the
+// router's and the dispatch's reads) and out = x + MoE(LayerNorm(x)).
 int forward_batch(vmoe_handle* h, const void* x, int64_t T, void* out, float* router_logits,
                   int32_t* topk_idx, float* topk_w, int32_t* expert_counts, float* aux_loss,
-                  char* ws, const Plan& p, cudaStream_t s, bool prof, float* psum_tot_out) {
+                  char* ws, const Plan& p, cudaStream_t s, bool prof, float* psum_tot_out,
+                  bool prenorm = false) {
   const int64_t E = h->E, K = h->K, H = h->H;
+  LnArgs ln_args{reinterpret_cast<float2*>(ws + p.stats), h->ln_w, h->ln_b, h->ln_eps};
+  const LnArgs* ln = prenorm ? &ln_args : nullptr;
   int32_t* idx = topk_idx ? topk_idx : reinterpret_cast<int32_t*>(ws + p.idx);
   float* tw = topk_w ? topk_w : reinterpret_cast<float*>(ws + p.w);
   int* hist = reinterpret_cast<int*>(ws + p.hist);
@@ -448,7 +477,7 @@ int forward_batch(vmoe_handle* h, const void* x, int64_t T, void* out, float* ro
   };
   int rc;
   mark();
-  if ((rc = run_router(h, x, T, router_logits, idx, tw, hist, psum, s)) != VMOE_OK) return rc;
+  if ((rc = run_router(h, x, T, router_logits, idx, tw, hist, psum, ln, s)) != VMOE_OK) return rc;
   mark();
   if ((rc = check(launch_scan_blocks(hist, psum, p.nblk, static_cast<int>(E), excl, counts,
                                      psum_tot, s),
@@ -463,7 +492,7 @@ int forward_batch(vmoe_handle* h, const void* x, int64_t T, void* out, float* ro
   mark();
   if ((rc = check(launch_dispatch(h->dtype, x, idx, excl, offs, T, static_cast<int>(H),
                                   static_cast<int>(E), static_cast<int>(K), h->cfg.capacity, slot,
-                                  xp, H, h->status, s),
+                                  xp, H, h->status, ln, s),
                   "dispatch")) != VMOE_OK)
     return rc;
   mark();
@@ -472,7 +501,7 @@ int forward_batch(vmoe_handle* h, const void* x, int64_t T, void* out, float* ro
     return rc;
   mark();
   if ((rc = check(launch_combine(h->dtype, yb, h->Hpad, idx, tw, slot, T, static_cast<int>(H),
-                                 static_cast<int>(K), out, s),
+                                 static_cast<int>(K), out, prenorm ? x : nullptr, s),
                   "combine")) != VMOE_OK)
     return rc;
   mark();
@@ -597,11 +626,38 @@ int vmoe_destroy(vmoe_handle* h) {
     if (h->host_in) cudaStreamDestroy(h->host_in);
     if (h->host_out) cudaStreamDestroy(h->host_out);
     if (h->status) cudaFree(h->status);
+    if (h->ln_w) cudaFree(h->ln_w);
+    if (h->ln_b) cudaFree(h->ln_b);
     for (cudaEvent_t ev : h->prof_ev) cudaEventDestroy(ev);
   }
   delete h;
   return VMOE_OK;
 }
+
+namespace {
+// The LayerNorm fold of the tensor-core router (W_r * ln_w, its row sums, b_r + W_r ln_b);
+// the CUDA-core router needs none.  Runs after the weights or the norm change.
+int refold_norm(vmoe_handle* h, cudaStream_t s) {
+  h->ln_ready = false;
+  if (h->dtype == kBF16 && h->router_bn > 0) {
+    const int64_t E = h->E, H = h->H;
+    int rc;
+    if (!h->w_r_ln && (rc = alloc(h, &h->w_r_ln, E * H * 2, "folded router weight")) != VMOE_OK)
+      return rc;
+    if (!h->b_r_ln && (rc = alloc(h, &h->b_r_ln, E * 4, "folded router bias")) != VMOE_OK) return rc;
+    if (!h->c_ln && (rc = alloc(h, &h->c_ln, E * 4, "folded router sums")) != VMOE_OK) return rc;
+    cudaError_t e = launch_fold_router_ln(h->w_r, h->b_r, h->ln_w, h->ln_b, static_cast<int>(E),
+                                          static_cast<int>(H), h->w_r_ln, h->b_r_ln, h->c_ln, s);
+    if (e != cudaSuccess) return cuda_fail(h, e, "router LayerNorm fold");
+    char why[256];
+    if (!make_tmap_bf16(&h->map_wr_ln, h->w_r_ln, E, H, H, static_cast<uint32_t>(h->router_bn),
+                        why, sizeof(why)))
+      return fail(h, VMOE_ERR_CUDA, "folded router tensor map: %s", why);
+  }
+  h->ln_ready = true;
+  return VMOE_OK;
+}
+}  // namespace
 
 int vmoe_set_weights(vmoe_handle* h, const vmoe_weights* w, void* stream) {
   if (!h) return VMOE_ERR_INVALID_ARG;
@@ -721,6 +777,7 @@ int vmoe_set_weights(vmoe_handle* h, const vmoe_weights* w, void* stream) {
       return fail(h, VMOE_ERR_CUDA, "down tensor map: %s", why);
   }
   h->ready = true;
+  if (h->ln_w && (rc = refold_norm(h, s)) != VMOE_OK) return rc;
   h->err.clear();
   return VMOE_OK;
 }
@@ -789,6 +846,70 @@ int vmoe_forward(vmoe_handle* h, const void* x, int64_t tokens, void* out, float
   const bool prof = h->prof_count < h->prof_slots;
   const int rc = forward_batch(h, x, T, out, router_logits, topk_idx, topk_w, expert_counts,
                                aux_loss, static_cast<char*>(workspace), p, s, prof, nullptr);
+  if (rc == VMOE_OK && prof) ++h->prof_count;
+  return rc;
+}
+
+int vmoe_set_norm(vmoe_handle* h, const void* ln_weight, const void* ln_bias, float eps,
+                  void* stream) {
+  if (!h) return VMOE_ERR_INVALID_ARG;
+  if (h->dense || h->ep_size > 1)
+    return fail(h, VMOE_ERR_INVALID_ARG, "the fused pre-norm takes a single-GPU MoE handle");
+  if (!(eps >= 0.f) || eps > 1.f)
+    return fail(h, VMOE_ERR_INVALID_ARG, "eps must be in [0, 1] (got %g)", static_cast<double>(eps));
+  DeviceGuard g(h->device);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int64_t H = h->H;
+  int rc;
+  if (!h->ln_w && (rc = alloc(h, &h->ln_w, H * 4, "LayerNorm weight")) != VMOE_OK) return rc;
+  if (!h->ln_b && (rc = alloc(h, &h->ln_b, H * 4, "LayerNorm bias")) != VMOE_OK) return rc;
+  cudaError_t e = launch_to_f32(h->dtype, ln_weight, H, 1.f, h->ln_w, s);
+  if (e == cudaSuccess) e = launch_to_f32(h->dtype, ln_bias, H, 0.f, h->ln_b, s);
+  if (e != cudaSuccess) return cuda_fail(h, e, "LayerNorm parameters");
+  h->ln_eps = eps;
+  h->ln_ready = false;
+  return h->ready ? refold_norm(h, s) : VMOE_OK;
+}
+
+int vmoe_forward_residual(vmoe_handle* h, const void* x, int64_t tokens, void* out,
+                          float* router_logits, int32_t* topk_idx, float* topk_w,
+                          int32_t* expert_counts, float* aux_loss, void* workspace,
+                          size_t workspace_bytes, void* stream) {
+  if (!h) return VMOE_ERR_INVALID_ARG;
+  h->last_launches = 0;
+  if (!h->ready) return fail(h, VMOE_ERR_NOT_READY, "vmoe_set_weights has not been called");
+  if (!h->ln_ready) return fail(h, VMOE_ERR_NOT_READY, "vmoe_set_norm has not been called");
+  if (tokens < 0) return fail(h, VMOE_ERR_INVALID_ARG, "tokens must be >= 0 (got %lld)",
+                              static_cast<long long>(tokens));
+  const int64_t E = h->E, K = h->K, T = tokens;
+  if (T * K + E * kTileM >= (static_cast<int64_t>(1) << 31))
+    return fail(h, VMOE_ERR_UNSUPPORTED_SHAPE, "tokens * top_k too large (%lld)",
+                static_cast<long long>(T * K));
+  DeviceGuard g(h->device);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  cudaError_t e;
+  if (T == 0) {
+    if (aux_loss) {
+      const float nan = __builtin_nanf("");
+      if ((e = cudaMemcpyAsync(aux_loss, &nan, 4, cudaMemcpyHostToDevice, s)) != cudaSuccess)
+        return cuda_fail(h, e, "aux write");
+    }
+    if (expert_counts && (e = cudaMemsetAsync(expert_counts, 0, E * 4, s)) != cudaSuccess)
+      return cuda_fail(h, e, "counts write");
+    return VMOE_OK;
+  }
+  if (!x || !out) return fail(h, VMOE_ERR_INVALID_ARG, "x and out are required");
+  if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(out)) & 15u)
+    return fail(h, VMOE_ERR_INVALID_ARG, "x and out must be 16-byte aligned");
+  const Plan p = make_plan(h, T);
+  if (!workspace || workspace_bytes < p.total)
+    return fail(h, VMOE_ERR_WORKSPACE, "workspace needs %zu bytes (got %zu)", p.total,
+                workspace ? workspace_bytes : static_cast<size_t>(0));
+  if (reinterpret_cast<uintptr_t>(workspace) & 255u)
+    return fail(h, VMOE_ERR_WORKSPACE, "workspace must be 256-byte aligned");
+  const bool prof = h->prof_count < h->prof_slots;
+  const int rc = forward_batch(h, x, T, out, router_logits, topk_idx, topk_w, expert_counts,
+                               aux_loss, static_cast<char*>(workspace), p, s, prof, nullptr, true);
   if (rc == VMOE_OK && prof) ++h->prof_count;
   return rc;
 }
@@ -1046,7 +1167,8 @@ int vmoe_ep_route(vmoe_handle* h, const void* x, int64_t tokens, void* send_rows
     ++h->last_launches;
     return VMOE_OK;
   };
-  if ((rc = run_router(h, x, T, router_logits, idx, tw, hist, psum, s)) != VMOE_OK) return rc;
+  if ((rc = run_router(h, x, T, router_logits, idx, tw, hist, psum, nullptr, s)) != VMOE_OK)
+    return rc;
   if ((rc = check(launch_scan_blocks(hist, psum, p.nblk, static_cast<int>(E), excl, counts,
                                      psum_tot, s), "scan")) != VMOE_OK)
     return rc;
@@ -1055,7 +1177,7 @@ int vmoe_ep_route(vmoe_handle* h, const void* x, int64_t tokens, void* send_rows
     return rc;
   return check(launch_dispatch(h->dtype, x, idx, excl, offs, T, static_cast<int>(H),
                                static_cast<int>(E), static_cast<int>(K), 0, slot, send_rows, H,
-                               h->status, s), "dispatch");
+                               h->status, nullptr, s), "dispatch");
 }
 
 int vmoe_ep_experts(vmoe_handle* h, const void* recv_rows, int64_t recv_rows_cap,
@@ -1109,7 +1231,8 @@ int vmoe_ep_combine(vmoe_handle* h, const void* back_rows, int64_t tokens, void*
                                        reinterpret_cast<int32_t*>(ws + p.idx),
                                        reinterpret_cast<float*>(ws + p.w),
                                        reinterpret_cast<int*>(ws + p.slot), tokens,
-                                       static_cast<int>(h->H), static_cast<int>(h->K), out, s);
+                                       static_cast<int>(h->H), static_cast<int>(h->K), out,
+                                       nullptr, s);
   if (e != cudaSuccess) return cuda_fail(h, e, "combine");
   h->last_launches = 1;
   return VMOE_OK;
@@ -1267,7 +1390,8 @@ int p2p_chunk(vmoe_handle* h, int c, const void* x, int64_t T, void* out, float*
   };
   int rc;
   mark();  // router
-  if (T > 0 && (rc = run_router(h, x, T, logits, idx, tw, hist, psum, s)) != VMOE_OK) return rc;
+  if (T > 0 && (rc = run_router(h, x, T, logits, idx, tw, hist, psum, nullptr, s)) != VMOE_OK)
+    return rc;
   mark();  // scan
   if ((rc = check(launch_scan_blocks(hist, psum, nblk, static_cast<int>(E), excl, counts,
                                      psum_tot, s), "scan")) != VMOE_OK)

@@ -120,6 +120,33 @@ def moe_forward_op(x: torch.Tensor, handle_id: int, want_logits: bool) -> tuple[
     return out, logits, aux
 
 
+@torch.library.custom_op("vesper_moe::forward_residual", mutates_args=(), device_types="cuda")
+def moe_forward_residual_op(x: torch.Tensor, handle_id: int, want_logits: bool) -> tuple[
+        torch.Tensor, torch.Tensor, torch.Tensor]:
+    """x + MoE(LayerNorm(x)) [T,H], router_logits[T,E] (empty unless want_logits), aux[]."""
+    packed = _HANDLES[handle_id]
+    h = packed.handle
+    T, H = x.shape
+    E = h.cfg.num_experts
+    x = x.contiguous()
+    out = torch.empty_like(x)
+    aux = torch.empty((), dtype=torch.float32, device=x.device)
+    logits = torch.empty((T, E) if want_logits else (0, E), dtype=torch.float32, device=x.device)
+    ws = packed.workspace(T, x.device)
+    stream = torch.cuda.current_stream(x.device).cuda_stream
+    h.forward_residual(x.data_ptr(), T, out.data_ptr(), logits.data_ptr() if want_logits else None,
+                       None, None, None, aux.data_ptr(), ws.data_ptr(), ws.numel(), stream)
+    return out, logits, aux
+
+
+@moe_forward_residual_op.register_fake
+def _(x, handle_id, want_logits):
+    T, _ = x.shape
+    E = _HANDLES[handle_id].handle.cfg.num_experts if handle_id in _HANDLES else 1
+    return (torch.empty_like(x), x.new_empty((T, E) if want_logits else (0, E), dtype=torch.float32),
+            x.new_empty((), dtype=torch.float32))
+
+
 @moe_forward_op.register_fake
 def _(x, handle_id, want_logits):
     T, _ = x.shape
@@ -294,6 +321,36 @@ class MoELayer(_PackedHandleMixin, nn.Module):
         B, S, H = x.shape
         packed = self.packed_for(x.device, x.dtype)
         out, logits, aux = torch.ops.vesper_moe.forward(
+            x.reshape(B * S, H), packed.id, bool(return_router_logits))
+        out = out.reshape(B, S, H)
+        if return_router_logits:
+            return out, aux, logits.reshape(B, S, self.num_experts)
+        return out, aux
+
+    def forward_residual(self, hidden_states: torch.Tensor, norm: nn.LayerNorm,
+                         return_router_logits: bool = False):
+        """The FFN half of the reference's pre-norm TransformerLayer.forward in one call:
+        ``(hidden_states + self(norm(hidden_states))[0], aux_loss)`` (python/vesper/model.py
+        :418-425), with the LayerNorm folded into the router's and the dispatch's reads and
+        the residual add into the combine (``vmoe_forward_residual``).  ``norm`` is the
+        layer's ``ffn_norm`` (an ``nn.LayerNorm`` over hidden_size)."""
+        B, S, H = hidden_states.shape
+        if not isinstance(norm, nn.LayerNorm) or tuple(norm.normalized_shape) != (H,):
+            raise ValueError("norm must be an nn.LayerNorm over the hidden size")
+        x = hidden_states
+        packed = self.packed_for(x.device, x.dtype)
+        key = (tuple((p.data_ptr(), p._version) for p in norm.parameters()), float(norm.eps),
+               packed.key)
+        if getattr(packed, "norm_key", None) != key:
+            dev = x.device
+            with torch.cuda.device(dev):
+                w = norm.weight.detach().to(dev, x.dtype).contiguous() if norm.weight is not None else None
+                b = norm.bias.detach().to(dev, x.dtype).contiguous() if norm.bias is not None else None
+                stream = torch.cuda.current_stream(dev)
+                packed.handle.set_norm(_ptr(w), _ptr(b), norm.eps, stream.cuda_stream)
+                stream.synchronize()  # the converted parameters must outlive the enqueued copy
+            packed.norm_key = key
+        out, logits, aux = torch.ops.vesper_moe.forward_residual(
             x.reshape(B * S, H), packed.id, bool(return_router_logits))
         out = out.reshape(B, S, H)
         if return_router_logits:
