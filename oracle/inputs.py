@@ -140,6 +140,12 @@ def make_norm_inputs(case: MoECase, eps: float = 1e-6) -> dict[str, np.ndarray]:
             "eps": np.asarray(eps, dtype=f32)}
 
 
+def backward_inputs(case: MoECase) -> tuple[np.ndarray, np.float32]:
+    """(dout ~ N(0,1) [T,H], daux) of the backward cases, seeded from the case (seed + 2000)."""
+    rng = np.random.default_rng(case.seed + 2000)
+    return rng.standard_normal((case.tokens, case.hidden), dtype=np.float32), np.float32(0.37)
+
+
 def round_bf16(a: np.ndarray) -> np.ndarray:
     """Round fp32 values to the nearest bf16 (ties to even), returned as fp32."""
     a = np.ascontiguousarray(a, dtype=np.float32)

@@ -18,6 +18,9 @@ VelvetOptimizer project root):
 * combine                python/vesper/model.py:337,354-357 (index_add_ in expert order)
 * load-balancing loss    python/vesper/model.py:366-385
 * pre-norm block         python/vesper/model.py:418-425 (ffn_norm LayerNorm, residual add)
+* backward               autograd of all of the above for loss = <out, dout> + daux * aux
+                         (python/train.py:95-96,465 trains through it; ERA derivative as
+                         python/vesper/kernels/era_triton.py:57-84)
 
 Pinning: ``tests/golden/make_golden.py`` executes the reference ``MoELayer`` itself (in
 the container where the reference is mounted) and commits its outputs as fixtures;
@@ -238,6 +241,106 @@ def moe_forward(p, case, *, dtype=np.float32, force_idx=None, token_subset=None,
         "counts": counts, "perm_tok": perm_tok, "perm_k": perm_k,
         "out": out, "aux": np.asarray(aux, dtype=dtype),
     }
+
+
+def era_grad(g, gamma):
+    """d ERA / dg: GELU-tanh derivative + gamma * softplus derivative (sigmoid; 1 above the
+    threshold 20, as torch's softplus backward)  (model.py:62-76, era_triton.py:57-84)."""
+    g = np.asarray(g, dtype=np.float32)
+    k = GELU_C * (g + GELU_A * g * g * g)
+    t = np.tanh(k)
+    d = np.float32(0.5) * (np.float32(1.0) + t) + np.float32(0.5) * g * (np.float32(1.0) - t * t) \
+        * GELU_C * (np.float32(1.0) + np.float32(3.0) * GELU_A * g * g)
+    if gamma > 0.0:
+        with np.errstate(over="ignore"):
+            sig = np.float32(1.0) / (np.float32(1.0) + np.exp(-np.minimum(g, SOFTPLUS_THRESHOLD)))
+        d = d + np.float32(gamma) * np.where(g > SOFTPLUS_THRESHOLD, np.float32(1.0), sig)
+    return d.astype(np.float32)
+
+
+def moe_backward(p, case, dout, daux, *, force_idx=None):
+    """Gradients of L = sum(out * dout) + daux * aux through ``moe_forward`` (fp32).
+
+    Restates autograd of MoELayer.forward (model.py:317-385) on the forward's routing:
+    the combine (out += y_e * w_e) gives dy = w * dout and dw = <dout, y>; the top-K
+    renormalisation w = p_k / S (S = sum_k p_k, :329) gives dp_k = (dw_k - sum_j w_j dw_j) / S;
+    the aux loss (:366-385) adds daux * E * f_e / T to every p[t, e] (counts carry no
+    gradient); softmax backward dl = p * (dp - sum_e p dp); the expert chain
+    down(ERA(gate) * up) (:295-298) and FlyLoRA's effective weight W + s U D (:123-126).
+
+    Returns dx [T,H]; router dw_r [E,H], db_r [E]; per expert (stacked over E) dw_g / dw_u
+    [E,I,H] and db_g / db_u [E,I] (base weights), dw_d [E,H,I], db_d [E,H]; FlyLoRA factors
+    da_g / da_u (lora_down.weight) [E,r,H], dba_* [E,r], dl_g / dl_u (lora_up.weight) [E,I,r],
+    dbl_* [E,I]; and the forward's routing (topk_idx).
+    """
+    f32 = np.float32
+    x = p["x"].astype(f32)
+    t, h = x.shape
+    E, K, s = case.experts, case.top_k, f32(case.lora_scaling)
+    dout = np.asarray(dout, dtype=f32)
+    logits = router_logits(x, p["w_r"], p["b_r"])
+    probs = softmax(logits)
+    _, idx = topk_lowest_index(probs, K)
+    if force_idx is not None:
+        idx = np.asarray(force_idx, dtype=np.int64).reshape(t, K)
+    vals = np.take_along_axis(probs, idx, axis=-1)
+    ssum = vals.sum(axis=-1, keepdims=True)
+    w = vals / ssum
+    counts = np.bincount(idx.reshape(-1), minlength=E).astype(f32)
+
+    g = {k: np.zeros_like(p[k], dtype=f32) for k in
+         ("w_g", "b_g", "w_u", "b_u", "w_d", "b_d", "a_g", "ba_g", "l_g", "bl_g",
+          "a_u", "ba_u", "l_u", "bl_u")}
+    dx = np.zeros((t, h), dtype=f32)
+    dw = np.zeros((t, K), dtype=f32)
+    for e in range(E):
+        mask = idx == e
+        rows = np.nonzero(mask.any(axis=-1))[0]
+        if rows.size == 0:
+            continue
+        kk = np.argmax(mask[rows], axis=-1)
+        xe = x[rows]
+        pre = {}
+        for q in ("g", "u"):
+            pre[q] = flylora_linear(xe, p[f"w_{q}"][e], p[f"b_{q}"][e], p[f"a_{q}"][e],
+                                    p[f"ba_{q}"][e], p[f"l_{q}"][e], p[f"bl_{q}"][e], s, f32)
+        a = era(pre["g"], case.era_gamma)
+        hid = a * pre["u"]
+        y = _mm(hid, p["w_d"][e], f32) + p["b_d"][e].astype(f32)
+        we = w[rows, kk]
+        dw[rows, kk] = (dout[rows] * y).sum(axis=-1)
+        dy = dout[rows] * we[:, None]
+        g["w_d"][e] = dy.T @ hid
+        g["b_d"][e] = dy.sum(axis=0)
+        dh = dy @ p["w_d"][e].astype(f32)
+        dpre = {"g": dh * pre["u"] * era_grad(pre["g"], case.era_gamma), "u": dh * a}
+        for q in ("g", "u"):
+            dq = dpre[q]
+            dW = dq.T @ xe                       # effective weight gradient
+            db = dq.sum(axis=0)
+            down = p[f"a_{q}"][e].astype(f32)    # D [r, H]
+            up = p[f"l_{q}"][e].astype(f32)      # U [I, r]
+            g[f"w_{q}"][e] = dW
+            g[f"b_{q}"][e] = db
+            g[f"l_{q}"][e] = s * (dW @ down.T + np.outer(db, p[f"ba_{q}"][e]))
+            g[f"bl_{q}"][e] = s * db
+            g[f"a_{q}"][e] = s * (up.T @ dW)
+            g[f"ba_{q}"][e] = s * (up.T @ db)
+            # x through base + s * lora_up(lora_down(x)) = x W_eff^T
+            dx[rows] += dq @ (p[f"w_{q}"][e].astype(f32) + s * (up @ down))
+    # router: top-K renormalisation, aux loss, softmax
+    dvals = (dw - (dw * w).sum(axis=-1, keepdims=True)) / ssum
+    dp = np.zeros_like(probs)
+    np.put_along_axis(dp, idx, dvals, axis=-1)
+    dp += f32(daux) * f32(E) * (counts / f32(t * K))[None, :] / f32(t)
+    dl = probs * (dp - (probs * dp).sum(axis=-1, keepdims=True))
+    out = {f"d{k}": v for k, v in g.items()}
+    out["dw_r"] = dl.T @ x
+    out["db_r"] = dl.sum(axis=0)
+    out["dx"] = dx + dl @ p["w_r"].astype(f32)
+    out["dlogits"] = dl
+    out["topk_idx"] = idx
+    return out
 
 
 def layer_norm(x, w, b, eps):

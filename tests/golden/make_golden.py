@@ -28,7 +28,7 @@ REPO = os.path.dirname(os.path.dirname(HERE))
 REFERENCE_PY = "/root/reference/python"
 sys.path.insert(0, REPO)
 
-from oracle.inputs import MoECase, make_inputs  # noqa: E402
+from oracle.inputs import MoECase, backward_inputs, make_inputs  # noqa: E402
 
 # name -> case.  Small enough to commit; together they cover the reference's own edge
 # cases (K == E, E == 2, a single token, empty experts, K = 1) and the option set
@@ -193,6 +193,48 @@ def run_reference_prenorm(case: MoECase):
             "aux": np.asarray(aux.item(), dtype=np.float32)}
 
 
+# backward cases: autograd through the reference MoELayer for
+# L = sum(out * dout) + daux * aux (python/train.py:95-96: the aux weight scales the loss)
+BW_CASES = {
+    "bw_t64_lora_bias": MoECase(tokens=64, batch=2, hidden=64, inter=96, experts=4, top_k=2,
+                                lora_on=True, bias_std=0.05, seed=51),
+    "bw_t37_k1": MoECase(tokens=37, batch=1, hidden=48, inter=64, experts=8, top_k=1, seed=52),
+    "bw_t20_k_eq_e": MoECase(tokens=20, batch=1, hidden=32, inter=48, experts=2, top_k=2,
+                             bias_std=0.05, seed=53),
+}
+
+
+def run_reference_backward(case: MoECase):
+    import torch
+
+    inp = make_inputs(case)
+    moe = reference_layer(case, inp)
+    dout, daux = backward_inputs(case)
+    x = torch.from_numpy(inp["x"]).reshape(case.batch, case.seq, case.hidden).requires_grad_(True)
+    out, aux = moe(x)
+    loss = (out * torch.from_numpy(dout).reshape(out.shape)).sum() + float(daux) * aux
+    loss.backward()
+    E = case.experts
+    st = lambda f: np.stack([f(e).grad.numpy() for e in moe.experts])  # noqa: E731
+    res = {"dx": x.grad.reshape(case.tokens, case.hidden).numpy(),
+           "dw_r": moe.router.weight.grad.numpy(), "db_r": moe.router.bias.grad.numpy(),
+           "dw_d": st(lambda e: e.down_proj.weight), "db_d": st(lambda e: e.down_proj.bias)}
+    for q, name in (("g", "gate_proj"), ("u", "up_proj")):
+        res[f"dw_{q}"] = st(lambda e: getattr(e, name).base.weight)
+        res[f"db_{q}"] = st(lambda e: getattr(e, name).base.bias)
+        res[f"da_{q}"] = st(lambda e: getattr(e, name).lora_down.weight)
+        res[f"dba_{q}"] = st(lambda e: getattr(e, name).lora_down.bias)
+        res[f"dl_{q}"] = st(lambda e: getattr(e, name).lora_up.weight)
+        res[f"dbl_{q}"] = st(lambda e: getattr(e, name).lora_up.bias)
+    with torch.no_grad():
+        probs = torch.softmax(moe.router(x.reshape(-1, case.hidden)), dim=-1)
+    res["probs"] = probs.numpy()
+    res["out"] = out.detach().reshape(case.tokens, case.hidden).numpy()
+    res["aux"] = np.asarray(aux.item(), dtype=np.float32)
+    assert E == res["dw_g"].shape[0]
+    return res
+
+
 def dump_state_dict_keys():
     """Record the reference MoELayer's state_dict keys and shapes for a small config."""
     sys.path.insert(0, REFERENCE_PY)
@@ -224,6 +266,14 @@ def main(names=None):
         np.savez_compressed(path, case=np.asarray(json.dumps(case.to_dict())),
                             torch_version=np.asarray(torch.__version__), **res)
         print(f"{name}: out {res['out'].shape} -> {path}")
+    for name, case in BW_CASES.items():
+        if names and name not in names:
+            continue
+        res = run_reference_backward(case)
+        path = os.path.join(HERE, f"{name}.npz")
+        np.savez_compressed(path, case=np.asarray(json.dumps(case.to_dict())),
+                            torch_version=np.asarray(torch.__version__), **res)
+        print(f"{name}: |dx|={np.abs(res['dx']).max():.4f} -> {path}")
     for name, case in LN_CASES.items():
         if names and name not in names:
             continue

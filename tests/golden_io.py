@@ -14,11 +14,15 @@ def golden_names():
     """The MoE-layer goldens (dense FeedForward ones start with 'ffn_', pre-norm blocks 'ln_')."""
     return sorted(n for n in (os.path.basename(p)[:-4]
                               for p in glob.glob(os.path.join(GOLDEN_DIR, "*.npz")))
-                  if not n.startswith(("ffn_", "ln_")))
+                  if not n.startswith(("ffn_", "ln_", "bw_")))
 
 
 def ffn_golden_names():
     return sorted(os.path.basename(p)[:-4] for p in glob.glob(os.path.join(GOLDEN_DIR, "ffn_*.npz")))
+
+
+def bw_golden_names():
+    return sorted(os.path.basename(p)[:-4] for p in glob.glob(os.path.join(GOLDEN_DIR, "bw_*.npz")))
 
 
 def ln_golden_names():

@@ -10,7 +10,8 @@ import pytest
 
 from oracle import moe_oracle as O
 from oracle.inputs import make_inputs, round_bf16
-from tests.golden_io import ffn_golden_names, golden_names, ln_golden_names, load_golden
+from tests.golden_io import (bw_golden_names, ffn_golden_names, golden_names, ln_golden_names,
+                              load_golden)
 
 NAMES = golden_names()
 
@@ -19,6 +20,7 @@ def test_goldens_present():
     assert "c1_fp32" in NAMES and len(NAMES) >= 8
     assert len(ffn_golden_names()) >= 2
     assert len(ln_golden_names()) >= 2
+    assert len(bw_golden_names()) >= 3
 
 
 @pytest.mark.parametrize("name", NAMES)
@@ -73,6 +75,23 @@ def test_oracle_prenorm_matches_reference(name):
     assert not O.near_ties(g["probs"], case.top_k, rel=1e-5).any()
     assert O.norm_rel_err(res["out"], g["out"]) < 1e-5
     assert abs(float(res["aux"]) - float(g["aux"])) <= 1e-5 * abs(float(g["aux"]))
+
+
+BW_KEYS = ("dx", "dw_r", "db_r", "dw_g", "db_g", "dw_u", "db_u", "dw_d", "db_d", "da_g", "dba_g",
+           "dl_g", "dbl_g", "da_u", "dba_u", "dl_u", "dbl_u")
+
+
+@pytest.mark.parametrize("name", bw_golden_names())
+def test_oracle_backward_matches_reference_autograd(name):
+    # autograd through the reference MoELayer for L = <out, dout> + daux * aux
+    from oracle.inputs import backward_inputs
+    case, g = load_golden(name)
+    assert not O.near_ties(g["probs"], case.top_k, rel=1e-5).any()
+    dout, daux = backward_inputs(case)
+    res = O.moe_backward(make_inputs(case), case, dout, daux)
+    for k in BW_KEYS:
+        err = O.norm_rel_err(res[k], g[k])
+        assert err < 1e-5, (k, err)
 
 
 def test_tied_router_case_is_all_ties():
