@@ -233,6 +233,8 @@ def run_ours(args, rank, world, local_rank):
     import torch
     import torch.distributed as dist
 
+    torch.set_grad_enabled(False)  # the forward (inference) step; --backward times training
+
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
     w = dict(WORKLOADS[args.workload])

@@ -167,6 +167,46 @@ VMOE_API int vmoe_forward(vmoe_handle* h, const void* x, int64_t tokens, void* o
                  int32_t* expert_counts, float* aux_loss,
                  void* workspace, size_t workspace_bytes, void* stream);
 
+/* ---- training: forward that keeps its intermediates, and the backward -------------------
+ * The reference trains through this layer (python/train.py:95-96,465: loss = CE +
+ * moe_aux_loss_weight * aux, backward by autograd under bf16 autocast).  These entries are
+ * the autograd of MoELayer.forward (python/vesper/model.py:317-385) for bf16 single-GPU
+ * handles:
+ *  - vmoe_set_training(h, 1, stream) derives transposed copies of the packed weights the
+ *    backward GEMMs read (again after every vmoe_set_weights);
+ *  - vmoe_forward_train: vmoe_forward's results (out, optional router_logits [T, E] fp32,
+ *    aux) that also keeps in `saved`
+ *    (vmoe_train_workspace_size) what the backward reads: routing, slots, logits, the
+ *    expert inputs, gate|up pre-activations, hidden and expert outputs;
+ *  - vmoe_backward: given dout = dL/dout [T, H] and daux = dL/daux (device fp32 scalar,
+ *    NULL = 0; the aux-loss weight, 0.01 in the reference), writes dx = dL/dx [T, H] and
+ *    the fp32 parameter gradients
+ *    below (overwritten, not accumulated).  gate_w / up_w / gate_b / up_b are the gradients
+ *    of the effective FlyLoRA weights W + s*U*D and b + s*(U*b_D + b_U) (model.py:123-126),
+ *    which are also the base weights' gradients; the LoRA factors' gradients follow as
+ *    dU = s*(dW D^T + db b_D^T), db_U = s*db, dD = s*U^T dW, db_D = s*U^T db.
+ *  `saved` must be untouched between the two calls; `scratch` is free after the backward. */
+typedef struct vmoe_grads {
+  float* router_w; /* [E, H]    router.weight            */
+  float* router_b; /* [E]                                */
+  float* gate_w;   /* [E, I, H] experts.e.gate_proj.base  */
+  float* gate_b;   /* [E, I]                             */
+  float* up_w;     /* [E, I, H] experts.e.up_proj.base    */
+  float* up_b;     /* [E, I]                             */
+  float* down_w;   /* [E, H, I] experts.e.down_proj       */
+  float* down_b;   /* [E, H]                             */
+} vmoe_grads;
+VMOE_API int vmoe_set_training(vmoe_handle* h, int enable, void* stream);
+VMOE_API int vmoe_train_workspace_size(const vmoe_handle* h, int64_t tokens, size_t* saved_bytes,
+                                       size_t* scratch_bytes);
+VMOE_API int vmoe_forward_train(vmoe_handle* h, const void* x, int64_t tokens, void* out,
+                                float* router_logits, float* aux_loss, void* saved,
+                                size_t saved_bytes, void* stream);
+VMOE_API int vmoe_backward(vmoe_handle* h, const void* x, const void* dout, int64_t tokens,
+                           const float* daux, void* dx, const vmoe_grads* grads, const void* saved,
+                           size_t saved_bytes, void* scratch, size_t scratch_bytes,
+                           void* stream);
+
 /* Fused pre-norm block: the FFN half of TransformerLayer.forward
  * (python/vesper/model.py:418-425) for a MoE layer,
  *     normed = ffn_norm(x);  ffn_out, aux = ffn(normed);  return x + ffn_out, aux

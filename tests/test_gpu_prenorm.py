@@ -123,6 +123,7 @@ def test_bf16_prenorm_against_oracle(name):
     layer.close()
 
 
+@torch.no_grad()
 def test_module_forward_residual_matches_unfused():
     from velvetoptimizer_b200 import MoEConfig, MoELayer
     cfg = MoEConfig(hidden_size=256, intermediate_size=384, moe_num_experts=8, moe_top_k=2)

@@ -37,8 +37,15 @@ EXPORTED = (
     "vmoe_ep_combine", "vmoe_ep_p2p_setup", "vmoe_ep_p2p_connect", "vmoe_ep_p2p_workspace_size",
     "vmoe_ep_p2p_forward", "vmoe_gemm_tile_rows", "vmoe_ffn_create", "vmoe_ffn_workspace_size",
     "vmoe_ffn_forward", "vmoe_forward_host_workspace_size", "vmoe_forward_host",
-    "vmoe_set_norm", "vmoe_forward_residual",
+    "vmoe_set_norm", "vmoe_forward_residual", "vmoe_set_training", "vmoe_train_workspace_size",
+    "vmoe_forward_train", "vmoe_backward",
 )
+
+
+class VmoeGrads(ctypes.Structure):
+    """vmoe_grads: fp32 device pointers of the parameter gradients."""
+    _fields_ = [(n, c_void_p) for n in ("router_w", "router_b", "gate_w", "gate_b", "up_w", "up_b",
+                                         "down_w", "down_b")]
 
 
 class VmoeConfig(ctypes.Structure):
@@ -110,6 +117,17 @@ def load() -> ctypes.CDLL:
     lib.vmoe_forward_host.argtypes = [H, c_void_p, c_int64, c_void_p, c_void_p, c_int, c_void_p,
                                       c_size_t, c_void_p]
     lib.vmoe_forward_host.restype = c_int
+    lib.vmoe_set_training.argtypes = [H, c_int, c_void_p]
+    lib.vmoe_set_training.restype = c_int
+    lib.vmoe_train_workspace_size.argtypes = [H, c_int64, POINTER(c_size_t), POINTER(c_size_t)]
+    lib.vmoe_train_workspace_size.restype = c_int
+    lib.vmoe_forward_train.argtypes = [H, c_void_p, c_int64, c_void_p, c_void_p, c_void_p,
+                                       c_void_p, c_size_t, c_void_p]
+    lib.vmoe_forward_train.restype = c_int
+    lib.vmoe_backward.argtypes = [H, c_void_p, c_void_p, c_int64, c_void_p, c_void_p,
+                                  POINTER(VmoeGrads), c_void_p, c_size_t, c_void_p, c_size_t,
+                                  c_void_p]
+    lib.vmoe_backward.restype = c_int
     lib.vmoe_set_norm.argtypes = [H, c_void_p, c_void_p, c_float, c_void_p]
     lib.vmoe_set_norm.restype = c_int
     lib.vmoe_forward_residual.argtypes = lib.vmoe_forward.argtypes
@@ -218,6 +236,27 @@ class Handle:
         rc = self.lib.vmoe_forward(self.ptr, x, tokens, out, logits, idx, topw, counts, aux, ws,
                                    ws_bytes, c_void_p(stream))
         check(rc, self.ptr, "vmoe_forward")
+
+    def set_training(self, enable: bool, stream: int) -> None:
+        check(self.lib.vmoe_set_training(self.ptr, 1 if enable else 0, c_void_p(stream)), self.ptr,
+              "vmoe_set_training")
+
+    def train_workspace_size(self, tokens: int) -> tuple[int, int]:
+        a, b = c_size_t(), c_size_t()
+        check(self.lib.vmoe_train_workspace_size(self.ptr, tokens, ctypes.byref(a), ctypes.byref(b)),
+              self.ptr, "vmoe_train_workspace_size")
+        return a.value, b.value
+
+    def forward_train(self, x, tokens, out, logits, aux, saved, saved_bytes, stream):
+        check(self.lib.vmoe_forward_train(self.ptr, x, tokens, out, logits, aux, saved,
+                                          saved_bytes, c_void_p(stream)), self.ptr,
+              "vmoe_forward_train")
+
+    def backward(self, x, dout, tokens, daux, dx, grads: "VmoeGrads", saved, saved_bytes, scratch,
+                 scratch_bytes, stream):
+        check(self.lib.vmoe_backward(self.ptr, x, dout, tokens, daux, dx, ctypes.byref(grads),
+                                     saved, saved_bytes, scratch, scratch_bytes, c_void_p(stream)),
+              self.ptr, "vmoe_backward")
 
     def set_norm(self, weight, bias, eps: float, stream: int) -> None:
         """LayerNorm parameters (device pointers or None) of the fused pre-norm block."""

@@ -102,6 +102,18 @@ __device__ __forceinline__ float era_fast(float g, float gamma) {
   return gelu + gamma * sp;
 }
 
+// ERA(g) and its derivative together (the backward of the gated product):
+// d/dg GELU_tanh = 0.5 (1 + t) + 0.5 g (1 - t^2) kC (1 + 3 kA g^2) with t = tanh(kC (g + kA g^3)),
+// d/dg softplus = sigmoid(g), 1 above the threshold 20 (torch's softplus backward).
+__device__ __forceinline__ void era_and_grad_fast(float g, float gamma, float& era, float& d) {
+  const float kC = 0.7978845608028654f, kA = 0.044715f;
+  const float t = tanh_fast(kC * (g + kA * g * g * g));
+  const float e = __expf(g);
+  era = 0.5f * g * (1.0f + t) + gamma * (g > 20.0f ? g : __logf(1.0f + e));
+  d = 0.5f * (1.0f + t) + 0.5f * g * (1.0f - t * t) * kC * (1.0f + 3.0f * kA * g * g) +
+      gamma * (g > 20.0f ? 1.0f : __fdividef(e, 1.0f + e));
+}
+
 // ---------------------------------------------------------------------------------
 // mbarrier + TMA + tcgen05 wrappers (sm_100a)
 // ---------------------------------------------------------------------------------

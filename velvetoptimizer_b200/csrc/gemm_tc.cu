@@ -374,7 +374,8 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_constant_
         const int e = expert_of(args, m);
         const int64_t row = static_cast<int64_t>(m) * kTileM + q * 32 + lane;
         __nv_bfloat16* outp = static_cast<__nv_bfloat16*>(args.out) + row * args.ldo;
-        const float* bias = args.bias + static_cast<int64_t>(e) * args.bias_ld + n * BN;
+        const float* bias =
+            args.bias ? args.bias + static_cast<int64_t>(e) * args.bias_ld + n * BN : nullptr;
         if constexpr (EPI == kGated) {
           outp += n * (BN / 2);
 #pragma unroll 1
@@ -401,10 +402,13 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_constant_
           for (int c = 0; c < BN; c += 32) {
             float v32[32];
             tmem_ld32(t_row + c, v32);
+            if (bias) {
+#pragma unroll
+              for (int j = 0; j < 32; ++j) v32[j] += bias[c + j];
+            }
             uint32_t packed[16];
 #pragma unroll
-            for (int j = 0; j < 32; j += 2)
-              packed[j / 2] = pack_bf16x2(v32[j] + bias[c + j], v32[j + 1] + bias[c + j + 1]);
+            for (int j = 0; j < 32; j += 2) packed[j / 2] = pack_bf16x2(v32[j], v32[j + 1]);
             uint4* dst = reinterpret_cast<uint4*>(outp + c);
 #pragma unroll
             for (int v = 0; v < 4; ++v)

@@ -64,7 +64,9 @@ __device__ __forceinline__ int pair_expert_of(const TcGemmArgs& args, int m) {
   return 0;
 }
 
-template <bool GATED>
+enum PairEpi { kPairPlain = 0, kPairGated = 1, kPairGluBwd = 2 };
+
+template <int EPI>
 __global__ void __launch_bounds__(192, 1)
 tc_gemm_pair_kernel(const __grid_constant__ CUtensorMap a_map,
                     const __grid_constant__ CUtensorMap b_map, const TcGemmArgs args) {
@@ -196,20 +198,43 @@ tc_gemm_pair_kernel(const __grid_constant__ CUtensorMap a_map,
       const int64_t row = static_cast<int64_t>(m) * PAIR_M + rank * kTileM + q * 32 + lane;
       const uint32_t t_row = tmem + (static_cast<uint32_t>(q * 32) << 16) + acc * BN;
       __nv_bfloat16* outp = static_cast<__nv_bfloat16*>(args.out) + row * args.ldo;
-      const float* bias = args.bias + static_cast<int64_t>(e) * args.bias_ld + n * BN;
-      if constexpr (GATED) {
+      if constexpr (EPI == kPairGated) {
+        const float* bias = args.bias + static_cast<int64_t>(e) * args.bias_ld + n * BN;
         outp += n * (BN / 2);
+        // training: also keep the pre-activations for the backward (tile layout: gate | up)
+        __nv_bfloat16* gup = args.gu_out ? static_cast<__nv_bfloat16*>(args.gu_out) +
+                                               row * args.gu_ld + n * BN
+                                         : nullptr;
 #pragma unroll 1
         for (int c = 0; c < BN / 2; c += 32) {
           float g[32], u[32];
           tmem_ld32(t_row + c, g);
           tmem_ld32(t_row + BN / 2 + c, u);
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            g[j] += bias[c + j];
+            u[j] += bias[BN / 2 + c + j];
+          }
+          if (gup) {
+            uint32_t pg[16], pu[16];
+#pragma unroll
+            for (int j = 0; j < 32; j += 2) {
+              pg[j / 2] = pack_bf16x2(g[j], g[j + 1]);
+              pu[j / 2] = pack_bf16x2(u[j], u[j + 1]);
+            }
+            uint4* dg = reinterpret_cast<uint4*>(gup + c);
+            uint4* du = reinterpret_cast<uint4*>(gup + BN / 2 + c);
+#pragma unroll
+            for (int v = 0; v < 4; ++v) {
+              dg[v] = make_uint4(pg[4 * v], pg[4 * v + 1], pg[4 * v + 2], pg[4 * v + 3]);
+              du[v] = make_uint4(pu[4 * v], pu[4 * v + 1], pu[4 * v + 2], pu[4 * v + 3]);
+            }
+          }
           uint32_t packed[16];
 #pragma unroll
           for (int j = 0; j < 32; j += 2) {
-            const float h0 = era_fast(g[j] + bias[c + j], args.gamma) * (u[j] + bias[BN / 2 + c + j]);
-            const float h1 = era_fast(g[j + 1] + bias[c + j + 1], args.gamma) *
-                             (u[j + 1] + bias[BN / 2 + c + j + 1]);
+            const float h0 = era_fast(g[j], args.gamma) * u[j];
+            const float h1 = era_fast(g[j + 1], args.gamma) * u[j + 1];
             packed[j / 2] = pack_bf16x2(h0, h1);
           }
           uint4* dst = reinterpret_cast<uint4*>(outp + c);
@@ -217,16 +242,55 @@ tc_gemm_pair_kernel(const __grid_constant__ CUtensorMap a_map,
           for (int v = 0; v < 4; ++v)
             dst[v] = make_uint4(packed[4 * v], packed[4 * v + 1], packed[4 * v + 2], packed[4 * v + 3]);
         }
+      } else if constexpr (EPI == kPairGluBwd) {
+        // accumulator = dh for I columns [n*BN, n*BN + BN); g, u at their interleaved
+        // positions (128-column blocks: gate then up) of the saved pre-activations
+        const __nv_bfloat16* gurow = static_cast<const __nv_bfloat16*>(args.gu_in) + row * args.gu_ld;
+#pragma unroll 1
+        for (int c = 0; c < BN; c += 32) {
+          const int i0 = n * BN + c;
+          if (i0 >= args.i_valid) break;
+          const int gcol = (i0 / 128) * 256 + (i0 & 127);
+          float dh[32], g[32], u[32];
+          tmem_ld32(t_row + c, dh);
+#pragma unroll
+          for (int v = 0; v < 4; ++v) {
+            load16_to_f(gurow + gcol + 8 * v, g + 8 * v);
+            load16_to_f(gurow + gcol + 128 + 8 * v, u + 8 * v);
+          }
+          uint32_t pg[16], pu[16];
+#pragma unroll
+          for (int j = 0; j < 32; j += 2) {
+            float a0, d0, a1, d1;
+            era_and_grad_fast(g[j], args.gamma, a0, d0);
+            era_and_grad_fast(g[j + 1], args.gamma, a1, d1);
+            pg[j / 2] = pack_bf16x2(dh[j] * u[j] * d0, dh[j + 1] * u[j + 1] * d1);
+            pu[j / 2] = pack_bf16x2(dh[j] * a0, dh[j + 1] * a1);
+          }
+          uint4* dg = reinterpret_cast<uint4*>(outp + gcol);
+          uint4* du = reinterpret_cast<uint4*>(outp + gcol + 128);
+#pragma unroll
+          for (int v = 0; v < 4; ++v) {
+            dg[v] = make_uint4(pg[4 * v], pg[4 * v + 1], pg[4 * v + 2], pg[4 * v + 3]);
+            du[v] = make_uint4(pu[4 * v], pu[4 * v + 1], pu[4 * v + 2], pu[4 * v + 3]);
+          }
+        }
       } else {
+        // plain: + bias (none when args.bias is null)
+        const float* bias = args.bias ? args.bias + static_cast<int64_t>(e) * args.bias_ld + n * BN
+                                      : nullptr;
         outp += n * BN;
 #pragma unroll 1
         for (int c = 0; c < BN; c += 32) {
           float v32[32];
           tmem_ld32(t_row + c, v32);
+          if (bias) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v32[j] += bias[c + j];
+          }
           uint32_t packed[16];
 #pragma unroll
-          for (int j = 0; j < 32; j += 2)
-            packed[j / 2] = pack_bf16x2(v32[j] + bias[c + j], v32[j + 1] + bias[c + j + 1]);
+          for (int j = 0; j < 32; j += 2) packed[j / 2] = pack_bf16x2(v32[j], v32[j + 1]);
           uint4* dst = reinterpret_cast<uint4*>(outp + c);
 #pragma unroll
           for (int v = 0; v < 4; ++v)
@@ -257,11 +321,11 @@ tc_gemm_pair_kernel(const __grid_constant__ CUtensorMap a_map,
 
 }  // namespace
 
-cudaError_t launch_tc_gemm_pair(bool gated, const CUtensorMap& a_map, const CUtensorMap& b_map,
-                                const TcGemmArgs& args, int64_t max_pair_tiles, int num_sms,
-                                cudaStream_t s) {
-  const void* kern = gated ? reinterpret_cast<const void*>(&tc_gemm_pair_kernel<true>)
-                           : reinterpret_cast<const void*>(&tc_gemm_pair_kernel<false>);
+namespace {
+template <int EPI>
+cudaError_t launch_pair(const CUtensorMap& a_map, const CUtensorMap& b_map, const TcGemmArgs& args,
+                        int64_t max_pair_tiles, int num_sms, cudaStream_t s) {
+  auto kern = tc_gemm_pair_kernel<EPI>;
   cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(SMEM_BYTES));
   if (err != cudaSuccess) return err;
@@ -279,7 +343,7 @@ cudaError_t launch_tc_gemm_pair(bool gated, const CUtensorMap& a_map, const CUte
   // as many CTA pairs as can be resident at once (persistent), no more than the work
   cfg.gridDim = dim3(static_cast<unsigned>(num_sms & ~1), 1, 1);
   int max_clusters = 0;
-  err = cudaOccupancyMaxActiveClusters(&max_clusters, kern, &cfg);
+  err = cudaOccupancyMaxActiveClusters(&max_clusters, reinterpret_cast<const void*>(kern), &cfg);
   if (err != cudaSuccess) return err;
   if (max_clusters < 1) return cudaErrorInvalidConfiguration;
   int64_t work = max_pair_tiles * args.n_tiles;
@@ -288,12 +352,24 @@ cudaError_t launch_tc_gemm_pair(bool gated, const CUtensorMap& a_map, const CUte
   if (pairs > num_sms / 2) pairs = num_sms / 2;  // the caller's SM budget
   if (pairs < 1) pairs = 1;
   cfg.gridDim = dim3(static_cast<unsigned>(2 * pairs), 1, 1);
-  if (gated)
-    err = cudaLaunchKernelEx(&cfg, tc_gemm_pair_kernel<true>, a_map, b_map, args);
-  else
-    err = cudaLaunchKernelEx(&cfg, tc_gemm_pair_kernel<false>, a_map, b_map, args);
+  err = cudaLaunchKernelEx(&cfg, kern, a_map, b_map, args);
   if (err != cudaSuccess) return err;
   return cudaGetLastError();
+}
+}  // namespace
+
+cudaError_t launch_tc_gemm_pair(bool gated, const CUtensorMap& a_map, const CUtensorMap& b_map,
+                                const TcGemmArgs& args, int64_t max_pair_tiles, int num_sms,
+                                cudaStream_t s) {
+  if (gated) return launch_pair<kPairGated>(a_map, b_map, args, max_pair_tiles, num_sms, s);
+  return launch_pair<kPairPlain>(a_map, b_map, args, max_pair_tiles, num_sms, s);
+}
+
+cudaError_t launch_tc_gemm_pair_glu_bwd(const CUtensorMap& a_map, const CUtensorMap& b_map,
+                                        const TcGemmArgs& args, int64_t max_pair_tiles,
+                                        int num_sms, cudaStream_t s) {
+  if (!args.gu_in || args.i_valid <= 0) return cudaErrorInvalidValue;
+  return launch_pair<kPairGluBwd>(a_map, b_map, args, max_pair_tiles, num_sms, s);
 }
 
 }  // namespace vmoe

@@ -103,6 +103,13 @@ struct TcGemmArgs {
   int64_t bias_ld;          // elements per expert
   float gamma;              // ERA gamma (gated epilogue)
   int* status;
+  // training: the gated epilogue also stores the pre-activations (gate | up + bias, bf16,
+  // same interleaved column layout as the accumulator tile) when gu_out is set
+  void* gu_out;
+  int64_t gu_ld;
+  // GLU backward epilogue (launch_tc_gemm_pair_glu_bwd): reads gu, writes dgu
+  const void* gu_in;
+  int64_t i_valid;          // columns (of I) that exist: the N tiles may run past Ipad
   // LayerNorm router (launch_tc_router with ln): b operand = W_r * ln_w, bias = b_r + W_r ln_b
   float2* ln_stats;         // [T] (mean, rstd) out
   const float* ln_c;        // [E] row sums of the folded weights
@@ -121,6 +128,14 @@ cudaError_t launch_tc_gemm_pair(bool gated, const CUtensorMap& a_map, const CUte
                                 const TcGemmArgs& args, int64_t max_pair_tiles, int num_sms,
                                 cudaStream_t s);
 
+// Backward of the gated product on CTA pairs: accumulator = dh = dy W_d (the B operand is
+// W_d transposed, [E, Ipad2, Hpad]); the epilogue reads the saved pre-activations
+// (args.gu_in, interleaved gate|up) and writes dgu = [dh * u * ERA'(g) | dh * ERA(g)] in the
+// same interleaved layout (args.out, ldo = 2*Ipad).  No bias.
+cudaError_t launch_tc_gemm_pair_glu_bwd(const CUtensorMap& a_map, const CUtensorMap& b_map,
+                                        const TcGemmArgs& args, int64_t max_pair_tiles,
+                                        int num_sms, cudaStream_t s);
+
 // Router on the tensor cores: logits = x W_r^T (+ bias in `args.bias`), softmax, top-K,
 // renormalised weights, per-128-token histogram and probability sums.  E <= 64;
 // tc_router_width(E) is the N tile (16, 32 or 64), 0 when E is too wide.
@@ -129,6 +144,71 @@ cudaError_t launch_tc_gemm_pair(bool gated, const CUtensorMap& a_map, const CUte
 int tc_router_width(int E);
 cudaError_t launch_tc_router(const CUtensorMap& x_map, const CUtensorMap& w_map,
                              const TcGemmArgs& args, int num_sms, cudaStream_t s, bool ln);
+
+// ---- backward --------------------------------------------------------------------------
+// Grouped weight gradient: for e < num_experts, dW_e = A_e^T B_e over the rows of e's
+// segment [seg_offs[e], seg_offs[e+1]) (multiples of 64; seg_offs null: one segment of
+// seg_rows_host rows).  a_map: A^T [M_total, rows_total] (box 64 x 128), b_map: B^T
+// [N_total, rows_total] (box 64 x 256).  mode 0 writes out[e][m][n] for m < m_valid,
+// n < n_valid; mode 1 de-interleaves the packed gate|up rows m of 2*Ipad into
+// out (gate) / out2 (up) [e][i][n], i < m_valid.
+struct WgradArgs {
+  const int* seg_offs;
+  int seg_rows_host;
+  int rows_total;
+  int num_experts;
+  int m_tiles, n_tiles;
+  int m_valid, n_valid;
+  float* out;
+  float* out2;
+  int64_t ld_out;
+  int64_t out_expert_stride;
+  int mode;
+  bool vec_ok;              // out / out2 16-byte aligned and ld_out % 4 == 0
+  int* status;
+};
+cudaError_t launch_wgrad(const CUtensorMap& a_map, const CUtensorMap& b_map, const WgradArgs& args,
+                         int num_sms, cudaStream_t s);
+
+// Batched 2-D transpose of bf16: dst[b][c][r] = src[b][r][c] for r < rows, c < cols, zero in
+// the padding of dst ([batch][dst_rows][dst_cols], dst_rows >= cols, dst_cols >= rows).  With
+// colsum (fp32 [batch][ceil(rows/64)][cols]) also every 64-row block's column sums.
+cudaError_t launch_transpose_bf16(const void* src, int64_t rows, int64_t cols, int64_t src_ld,
+                                  int64_t src_batch_stride, int batch, void* dst,
+                                  int64_t dst_rows, int64_t dst_cols, int64_t dst_batch_stride,
+                                  float* colsum, cudaStream_t s);
+
+// Zero the padding rows [offs[e] + counts[e], offs[e+1]) of every expert segment of buf.
+cudaError_t launch_zero_pad_rows(void* buf, int64_t ld_bytes, int64_t row_bytes, const int* offs,
+                                 const int* counts, int E, int64_t capacity, cudaStream_t s);
+
+// Combine backward (model.py:337,354-357): for every kept (t, k) with row r = slot_of[t, k],
+// dy[r] = bf16(w[t,k] * dout[t]) and dw[t,k] = <dout[t], y[r]> (fp32); dw = 0 for dropped.
+cudaError_t launch_combine_bwd(const void* dout, const void* y, int64_t y_ld,
+                               const int32_t* topk_idx, const float* topk_w, const int* slot_of,
+                               int64_t T, int H, int K, void* dy, int64_t dy_ld, float* dw,
+                               cudaStream_t s);
+
+// Router backward (model.py:322-329, 366-385): top-K renormalisation, aux loss and softmax
+// gradients from the logits, dw and daux -> dlogits fp32 [T, E] and bf16 [T, e_ld] (zero
+// padded to e_ld columns), per-128-token-block column sums [ceil(T/128), E] for the bias.
+cudaError_t launch_router_bwd(const float* logits, const int32_t* topk_idx, const float* dw,
+                              const int32_t* counts, int64_t T, int E, int K, const float* daux,
+                              float* dlogits, void* dl_bf16, int e_ld, float* dl_blocksum,
+                              cudaStream_t s);
+
+// dx[t] = sum over the token's kept slots in ascending expert id of dxr[slot] + dxr_router[t]
+// (fp32 sum, rounded to bf16).
+cudaError_t launch_gather_dx(const void* dxr, int64_t dxr_ld, const void* dxr_router,
+                             int64_t router_ld, const int32_t* topk_idx, const int* slot_of,
+                             int64_t T, int H, int K, void* dx, cudaStream_t s);
+
+// Sum of fp32 row-block partials per expert: out[e][c] = sum of part[b][c] over the
+// 64-row blocks b of e's segment (offs[e] / 64 .. offs[e+1] / 64); with `interleave`, column
+// c of the packed gate|up layout goes to out (gate) / out2 (up) at its unpacked index.
+cudaError_t launch_segment_sum(const float* part, int64_t part_ld, const int* offs, int E,
+                               int cols, int blk_rows, float* out, float* out2, int valid,
+                               bool interleave, cudaStream_t s);
 
 // Build a 2-D bf16 tensor map: [rows, cols] row-major with `ld` elements per row, box
 // {64 cols, box_rows rows}, 128-byte swizzle.  Returns false on failure.

@@ -120,6 +120,15 @@ struct vmoe_handle {
   float* c_ln = nullptr;
   CUtensorMap map_wr_ln{};
   bool ln_ready = false;
+  // training (vmoe_set_training): transposed copies of the packed weights for the backward
+  // GEMMs (every operand K-major): W_d^T [E, Ipad2, Hpad], (gate|up)^T [E, Hpad, 2*Ipad],
+  // W_r^T [Hpad, Epad64]
+  bool training = false;
+  int64_t Ipad2 = 0, Epad64 = 0;
+  void* w_dT = nullptr;
+  void* w_guT = nullptr;
+  void* w_rT = nullptr;
+  CUtensorMap map_wdT{}, map_guT{}, map_wrT{};
   bool ready = false;
   // profiling ring: prof_slots forwards x (kStages + 1) events
   int prof_slots = 0;
@@ -323,7 +332,7 @@ int alloc(vmoe_handle* h, T** p, size_t bytes, const char* what) {
 template <typename Mark, typename Check>
 int run_expert_gemms(vmoe_handle* h, void* xp, int64_t max_rows, const int* tiles,
                      const int* ntiles, void* hb, void* yb, int64_t y_ld, cudaStream_t s,
-                     Mark&& mark, Check&& check, int gemm_sms = 0) {
+                     Mark&& mark, Check&& check, int gemm_sms = 0, void* gu_out = nullptr) {
   const int sms = gemm_sms > 0 ? gemm_sms : h->num_sms;  // persistent GEMM grid bound
   const int64_t H = h->H, max_tiles = max_rows / h->tile_rows;
   int rc;
@@ -362,6 +371,8 @@ int run_expert_gemms(vmoe_handle* h, void* xp, int64_t max_rows, const int* tile
   a1.bias_ld = 2 * h->Ipad;
   a1.gamma = h->cfg.era_gamma;
   a1.status = h->status;
+  a1.gu_out = gu_out;  // training: keep the pre-activations for the backward
+  a1.gu_ld = 2 * h->Ipad;
   const bool pair = h->tile_rows != kTileM;
   if ((rc = check(pair ? launch_tc_gemm_pair(true, map_x, h->map_wgu, a1, max_tiles, sms, s)
                        : launch_tc_gemm(true, map_x, h->map_wgu, a1, max_tiles, sms, s),
@@ -628,6 +639,9 @@ int vmoe_destroy(vmoe_handle* h) {
     if (h->status) cudaFree(h->status);
     if (h->ln_w) cudaFree(h->ln_w);
     if (h->ln_b) cudaFree(h->ln_b);
+    if (h->w_dT) cudaFree(h->w_dT);
+    if (h->w_guT) cudaFree(h->w_guT);
+    if (h->w_rT) cudaFree(h->w_rT);
     for (cudaEvent_t ev : h->prof_ev) cudaEventDestroy(ev);
   }
   delete h;
@@ -635,6 +649,32 @@ int vmoe_destroy(vmoe_handle* h) {
 }
 
 namespace {
+// Transposed copies of the packed (FlyLoRA-folded) weights for the backward GEMMs.
+int make_training_copies(vmoe_handle* h, cudaStream_t s) {
+  const int64_t E = h->E, H = h->H, Hpad = h->Hpad, Ipad = h->Ipad;
+  h->Ipad2 = round_up(Ipad, 256);
+  h->Epad64 = round_up(E, 64);
+  int rc;
+  if (!h->w_dT && (rc = alloc(h, &h->w_dT, E * h->Ipad2 * Hpad * 2, "W_d^T")) != VMOE_OK) return rc;
+  if (!h->w_guT && (rc = alloc(h, &h->w_guT, E * Hpad * 2 * Ipad * 2, "gate|up^T")) != VMOE_OK)
+    return rc;
+  if (!h->w_rT && (rc = alloc(h, &h->w_rT, Hpad * h->Epad64 * 2, "W_r^T")) != VMOE_OK) return rc;
+  cudaError_t e = launch_transpose_bf16(h->w_d, Hpad, Ipad, Ipad, Hpad * Ipad, static_cast<int>(E),
+                                        h->w_dT, h->Ipad2, Hpad, h->Ipad2 * Hpad, nullptr, s);
+  if (e == cudaSuccess)
+    e = launch_transpose_bf16(h->w_g, 2 * Ipad, H, H, 2 * Ipad * H, static_cast<int>(E), h->w_guT,
+                              Hpad, 2 * Ipad, Hpad * 2 * Ipad, nullptr, s);
+  if (e == cudaSuccess)
+    e = launch_transpose_bf16(h->w_r, E, H, H, 0, 1, h->w_rT, Hpad, h->Epad64, 0, nullptr, s);
+  if (e != cudaSuccess) return cuda_fail(h, e, "weight transposes");
+  char why[256];
+  if (!make_tmap_bf16(&h->map_wdT, h->w_dT, E * h->Ipad2, Hpad, Hpad, 128, why, sizeof(why)) ||
+      !make_tmap_bf16(&h->map_guT, h->w_guT, E * Hpad, 2 * Ipad, 2 * Ipad, 128, why, sizeof(why)) ||
+      !make_tmap_bf16(&h->map_wrT, h->w_rT, Hpad, h->Epad64, h->Epad64, 256, why, sizeof(why)))
+    return fail(h, VMOE_ERR_CUDA, "backward weight tensor maps: %s", why);
+  return VMOE_OK;
+}
+
 // The LayerNorm fold of the tensor-core router (W_r * ln_w, its row sums, b_r + W_r ln_b);
 // the CUDA-core router needs none.  Runs after the weights or the norm change.
 int refold_norm(vmoe_handle* h, cudaStream_t s) {
@@ -778,6 +818,7 @@ int vmoe_set_weights(vmoe_handle* h, const vmoe_weights* w, void* stream) {
   }
   h->ready = true;
   if (h->ln_w && (rc = refold_norm(h, s)) != VMOE_OK) return rc;
+  if (h->training && (rc = make_training_copies(h, s)) != VMOE_OK) return rc;
   h->err.clear();
   return VMOE_OK;
 }
@@ -1589,6 +1630,379 @@ int vmoe_ffn_forward(vmoe_handle* h, const void* x, int64_t tokens, void* out, v
   e = cudaMemcpy2DAsync(out, H * elt, ws + p.y, h->Hpad * elt, H * elt, T,
                         cudaMemcpyDeviceToDevice, s);
   if (e != cudaSuccess) return cuda_fail(h, e, "out copy");
+  return VMOE_OK;
+}
+
+// ---- training: forward that keeps what the backward needs, and the backward -------------
+namespace {
+
+// The saved workspace of vmoe_forward_train: the forward's own plan (routing, slots, x_perm,
+// h, y) plus the gate|up pre-activations and the router logits.
+struct TrainPlan {
+  Plan p;
+  size_t gu = 0, logits = 0, total = 0;
+};
+
+TrainPlan make_train_plan(const vmoe_handle* h, int64_t T) {
+  TrainPlan tp;
+  tp.p = make_plan(h, T);
+  size_t off = tp.p.total;
+  auto take = [&](size_t bytes) {
+    const size_t o = off;
+    off += (bytes + 255) & ~static_cast<size_t>(255);
+    return o;
+  };
+  tp.gu = take(static_cast<size_t>(tp.p.max_rows) * 2 * h->Ipad * 2);
+  tp.logits = take(static_cast<size_t>(T) * h->E * 4);
+  tp.total = off;
+  return tp;
+}
+
+// Scratch of vmoe_backward.
+struct BwdPlan {
+  int64_t Tpad = 0, Mr = 0;  // tokens padded to 128; rows of the dW_r M dimension
+  size_t dy, dyT, hT, dgu, dguT, xpT, dxr, dw, dl, dl_bf, dlT, xT, dxrt, dl_bs, dy_cs, dgu_cs,
+      total;
+};
+
+BwdPlan make_bwd_plan(const vmoe_handle* h, int64_t T, const Plan& p) {
+  BwdPlan b{};
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    const size_t o = off;
+    off += (bytes + 255) & ~static_cast<size_t>(255);
+    return o;
+  };
+  const size_t R = static_cast<size_t>(p.max_rows);
+  const size_t Hp = h->Hpad, Ip = h->Ipad;
+  b.Tpad = round_up(T > 0 ? T : 1, kTileM);
+  b.Mr = round_up(h->E, kTileM);
+  b.dy = take(R * Hp * 2);
+  b.dyT = take(Hp * R * 2);
+  b.hT = take(Ip * R * 2);
+  b.dgu = take(R * 2 * Ip * 2);
+  b.dguT = take(2 * Ip * R * 2);
+  b.xpT = take(Hp * R * 2);
+  b.dxr = take(R * Hp * 2);
+  b.dw = take(static_cast<size_t>(T) * h->K * 4);
+  b.dl = take(static_cast<size_t>(T) * h->E * 4);
+  b.dl_bf = take(static_cast<size_t>(b.Tpad) * h->Epad64 * 2);
+  b.dlT = take(static_cast<size_t>(b.Mr) * b.Tpad * 2);
+  b.xT = take(Hp * b.Tpad * 2);
+  b.dxrt = take(static_cast<size_t>(b.Tpad) * Hp * 2);
+  b.dl_bs = take(static_cast<size_t>((T + 127) / 128) * h->E * 4);
+  b.dy_cs = take((R / 64) * Hp * 4);
+  b.dgu_cs = take((R / 64) * 2 * Ip * 4);
+  b.total = off;
+  return b;
+}
+
+int check_trainable(vmoe_handle* h) {
+  if (!h->ready) return fail(h, VMOE_ERR_NOT_READY, "vmoe_set_weights has not been called");
+  if (!h->training) return fail(h, VMOE_ERR_NOT_READY, "vmoe_set_training has not been called");
+  return VMOE_OK;
+}
+
+}  // namespace
+
+int vmoe_set_training(vmoe_handle* h, int enable, void* stream) {
+  if (!h) return VMOE_ERR_INVALID_ARG;
+  if (!enable) {
+    h->training = false;
+    return VMOE_OK;
+  }
+  if (h->dtype != kBF16 || h->dense || h->ep_size > 1 || h->tile_rows != 2 * kTileM)
+    return fail(h, VMOE_ERR_UNSUPPORTED_SHAPE,
+                "the backward runs on single-GPU bf16 MoE handles with the CTA-pair GEMMs");
+  if (h->K > 32 || h->H % 8)
+    return fail(h, VMOE_ERR_UNSUPPORTED_SHAPE, "the backward needs top_k <= 32 and hidden %% 8 == 0");
+  DeviceGuard g(h->device);
+  h->training = true;
+  return h->ready ? make_training_copies(h, static_cast<cudaStream_t>(stream)) : VMOE_OK;
+}
+
+int vmoe_train_workspace_size(const vmoe_handle* h, int64_t tokens, size_t* saved_bytes,
+                              size_t* scratch_bytes) {
+  if (!h || tokens < 0 || !saved_bytes || !scratch_bytes) return VMOE_ERR_INVALID_ARG;
+  const TrainPlan tp = make_train_plan(h, tokens);
+  *saved_bytes = tp.total;
+  *scratch_bytes = make_bwd_plan(h, tokens, tp.p).total;
+  return VMOE_OK;
+}
+
+int vmoe_forward_train(vmoe_handle* h, const void* x, int64_t tokens, void* out,
+                       float* router_logits, float* aux_loss, void* saved, size_t saved_bytes,
+                       void* stream) {
+  if (!h) return VMOE_ERR_INVALID_ARG;
+  h->last_launches = 0;
+  int rc = check_trainable(h);
+  if (rc != VMOE_OK) return rc;
+  const int64_t E = h->E, K = h->K, H = h->H, T = tokens;
+  if (T < 1 || T * K + E * kTileM >= (static_cast<int64_t>(1) << 31))
+    return fail(h, VMOE_ERR_INVALID_ARG, "tokens must be in [1, 2^31 / top_k) (got %lld)",
+                static_cast<long long>(T));
+  if (!x || !out) return fail(h, VMOE_ERR_INVALID_ARG, "x and out are required");
+  if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(out)) & 15u)
+    return fail(h, VMOE_ERR_INVALID_ARG, "x and out must be 16-byte aligned");
+  const TrainPlan tp = make_train_plan(h, T);
+  if (!saved || saved_bytes < tp.total || (reinterpret_cast<uintptr_t>(saved) & 255u))
+    return fail(h, VMOE_ERR_WORKSPACE, "saved workspace needs %zu bytes, 256-byte aligned",
+                tp.total);
+  DeviceGuard g(h->device);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  char* ws = static_cast<char*>(saved);
+  const Plan& p = tp.p;
+  auto check = [&](cudaError_t err, const char* what) -> int {
+    if (err != cudaSuccess) return cuda_fail(h, err, what);
+    ++h->last_launches;
+    return VMOE_OK;
+  };
+  auto mark = []() {};
+  int32_t* idx = reinterpret_cast<int32_t*>(ws + p.idx);
+  float* tw = reinterpret_cast<float*>(ws + p.w);
+  int* hist = reinterpret_cast<int*>(ws + p.hist);
+  float* psum = reinterpret_cast<float*>(ws + p.psum);
+  int* excl = reinterpret_cast<int*>(ws + p.excl);
+  int* counts = reinterpret_cast<int*>(ws + p.counts);
+  float* psum_tot = reinterpret_cast<float*>(ws + p.psum_tot);
+  int* offs = reinterpret_cast<int*>(ws + p.offs);
+  int* tiles = reinterpret_cast<int*>(ws + p.tiles);
+  int* ntiles = reinterpret_cast<int*>(ws + p.ntiles);
+  float* aux = aux_loss ? aux_loss : reinterpret_cast<float*>(ws + p.aux);
+  int* slot = reinterpret_cast<int*>(ws + p.slot);
+  float* logits = reinterpret_cast<float*>(ws + tp.logits);
+  if ((rc = run_router(h, x, T, logits, idx, tw, hist, psum, nullptr, s)) != VMOE_OK) return rc;
+  if ((rc = check(launch_scan_blocks(hist, psum, p.nblk, static_cast<int>(E), excl, counts,
+                                     psum_tot, s), "scan")) != VMOE_OK)
+    return rc;
+  if ((rc = check(launch_plan(counts, psum_tot, T, static_cast<int>(E), static_cast<int>(K),
+                              h->cfg.capacity, static_cast<int>(h->tile_rows), offs, tiles, ntiles,
+                              aux, nullptr, s), "plan")) != VMOE_OK)
+    return rc;
+  if ((rc = check(launch_dispatch(h->dtype, x, idx, excl, offs, T, static_cast<int>(H),
+                                  static_cast<int>(E), static_cast<int>(K), h->cfg.capacity, slot,
+                                  ws + p.xp, H, h->status, nullptr, s), "dispatch")) != VMOE_OK)
+    return rc;
+  // zero the padding rows of every segment: the weight gradients reduce over whole segments
+  if ((rc = check(launch_zero_pad_rows(ws + p.xp, H * 2, H * 2, offs, counts, static_cast<int>(E),
+                                       h->cfg.capacity, s), "pad rows")) != VMOE_OK)
+    return rc;
+  if ((rc = run_expert_gemms(h, ws + p.xp, p.max_rows, tiles, ntiles, ws + p.h, ws + p.y, h->Hpad,
+                             s, mark, check, 0, ws + tp.gu)) != VMOE_OK)
+    return rc;
+  if ((rc = check(launch_combine(h->dtype, ws + p.y, h->Hpad, idx, tw, slot, T, static_cast<int>(H),
+                                 static_cast<int>(K), out, nullptr, s), "combine")) != VMOE_OK)
+    return rc;
+  if (router_logits) {
+    cudaError_t e = cudaMemcpyAsync(router_logits, logits, T * E * 4, cudaMemcpyDeviceToDevice, s);
+    if (e != cudaSuccess) return cuda_fail(h, e, "logits copy");
+  }
+  return VMOE_OK;
+}
+
+int vmoe_backward(vmoe_handle* h, const void* x, const void* dout, int64_t tokens, const float* daux,
+                  void* dx, const vmoe_grads* grads, const void* saved, size_t saved_bytes,
+                  void* scratch, size_t scratch_bytes, void* stream) {
+  if (!h) return VMOE_ERR_INVALID_ARG;
+  h->last_launches = 0;
+  int rc = check_trainable(h);
+  if (rc != VMOE_OK) return rc;
+  const int64_t E = h->E, K = h->K, H = h->H, I = h->I, T = tokens;
+  const int64_t Hp = h->Hpad, Ip = h->Ipad;
+  if (T < 1) return fail(h, VMOE_ERR_INVALID_ARG, "tokens must be >= 1");
+  if (!x || !dout || !dx || !grads || !grads->router_w || !grads->router_b || !grads->gate_w ||
+      !grads->gate_b || !grads->up_w || !grads->up_b || !grads->down_w || !grads->down_b)
+    return fail(h, VMOE_ERR_INVALID_ARG, "x, dout, dx and every gradient pointer are required");
+  if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(dout) |
+       reinterpret_cast<uintptr_t>(dx)) & 15u)
+    return fail(h, VMOE_ERR_INVALID_ARG, "x, dout and dx must be 16-byte aligned");
+  const TrainPlan tp = make_train_plan(h, T);
+  const Plan& p = tp.p;
+  const BwdPlan b = make_bwd_plan(h, T, p);
+  if (!saved || saved_bytes < tp.total || (reinterpret_cast<uintptr_t>(saved) & 255u))
+    return fail(h, VMOE_ERR_WORKSPACE, "saved workspace needs %zu bytes", tp.total);
+  if (!scratch || scratch_bytes < b.total || (reinterpret_cast<uintptr_t>(scratch) & 255u))
+    return fail(h, VMOE_ERR_WORKSPACE, "backward scratch needs %zu bytes, 256-byte aligned",
+                b.total);
+  DeviceGuard g(h->device);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const char* ws = static_cast<const char*>(saved);
+  char* sc = static_cast<char*>(scratch);
+  auto check = [&](cudaError_t err, const char* what) -> int {
+    if (err != cudaSuccess) return cuda_fail(h, err, what);
+    ++h->last_launches;
+    return VMOE_OK;
+  };
+  const int32_t* idx = reinterpret_cast<const int32_t*>(ws + p.idx);
+  const float* tw = reinterpret_cast<const float*>(ws + p.w);
+  const int* counts = reinterpret_cast<const int*>(ws + p.counts);
+  const int* offs = reinterpret_cast<const int*>(ws + p.offs);
+  const int* tiles = reinterpret_cast<const int*>(ws + p.tiles);
+  const int* ntiles = reinterpret_cast<const int*>(ws + p.ntiles);
+  const int* slot = reinterpret_cast<const int*>(ws + p.slot);
+  const float* logits = reinterpret_cast<const float*>(ws + tp.logits);
+  const int64_t R = p.max_rows, max_tiles = R / h->tile_rows;
+  cudaError_t e;
+
+  // 1. combine backward: dy (expert-major rows) and dw; padding rows / columns zeroed
+  if (Hp != H && (e = cudaMemsetAsync(sc + b.dy, 0, R * Hp * 2, s)) != cudaSuccess)
+    return cuda_fail(h, e, "dy clear");
+  if ((rc = check(launch_combine_bwd(dout, ws + p.y, Hp, idx, tw, slot, T, static_cast<int>(H),
+                                     static_cast<int>(K), sc + b.dy, Hp,
+                                     reinterpret_cast<float*>(sc + b.dw), s), "combine bwd")) != VMOE_OK)
+    return rc;
+  if ((rc = check(launch_zero_pad_rows(sc + b.dy, Hp * 2, Hp * 2, offs, counts, static_cast<int>(E),
+                                       h->cfg.capacity, s), "dy pad rows")) != VMOE_OK)
+    return rc;
+  // 2. router backward
+  if ((rc = check(launch_router_bwd(logits, idx, reinterpret_cast<const float*>(sc + b.dw), counts,
+                                    T, static_cast<int>(E), static_cast<int>(K), daux,
+                                    reinterpret_cast<float*>(sc + b.dl), sc + b.dl_bf,
+                                    static_cast<int>(h->Epad64),
+                                    reinterpret_cast<float*>(sc + b.dl_bs), s), "router bwd")) != VMOE_OK)
+    return rc;
+  // 3. dh = dy W_d with the GLU / ERA backward epilogue -> dgu
+  char why[256];
+  CUtensorMap m_dy, m_dgu, m_dl;
+  if (!make_tmap_bf16(&m_dy, sc + b.dy, R, Hp, Hp, kTileM, why, sizeof(why)) ||
+      !make_tmap_bf16(&m_dgu, sc + b.dgu, R, 2 * Ip, 2 * Ip, kTileM, why, sizeof(why)) ||
+      !make_tmap_bf16(&m_dl, sc + b.dl_bf, b.Tpad, h->Epad64, h->Epad64, kTileM, why, sizeof(why)))
+    return fail(h, VMOE_ERR_CUDA, "backward tensor maps: %s", why);
+  TcGemmArgs a1{};
+  a1.num_m_tiles = ntiles;
+  a1.tile_expert = tiles;
+  a1.max_m_tiles = static_cast<int>(max_tiles);
+  a1.num_experts = static_cast<int>(E);
+  a1.n_tiles = static_cast<int>(h->Ipad2 / 256);
+  a1.k_blocks = static_cast<int>(Hp / 64);
+  a1.b_rows_per_expert = static_cast<int>(h->Ipad2);
+  a1.out = sc + b.dgu;
+  a1.ldo = 2 * Ip;
+  a1.gamma = h->cfg.era_gamma;
+  a1.status = h->status;
+  a1.gu_in = ws + tp.gu;
+  a1.gu_ld = 2 * Ip;
+  a1.i_valid = Ip;
+  if ((rc = check(launch_tc_gemm_pair_glu_bwd(m_dy, h->map_wdT, a1, max_tiles, h->num_sms, s),
+                  "dh gemm")) != VMOE_OK)
+    return rc;
+  // 4. dx rows = dgu (gate|up)^T-major weights
+  TcGemmArgs a2{};
+  a2.num_m_tiles = ntiles;
+  a2.tile_expert = tiles;
+  a2.max_m_tiles = static_cast<int>(max_tiles);
+  a2.num_experts = static_cast<int>(E);
+  a2.n_tiles = static_cast<int>(Hp / 256);
+  a2.k_blocks = static_cast<int>(2 * Ip / 64);
+  a2.b_rows_per_expert = static_cast<int>(Hp);
+  a2.out = sc + b.dxr;
+  a2.ldo = Hp;
+  a2.bias = nullptr;
+  a2.status = h->status;
+  if ((rc = check(launch_tc_gemm_pair(false, m_dgu, h->map_guT, a2, max_tiles, h->num_sms, s),
+                  "dx gemm")) != VMOE_OK)
+    return rc;
+  // 5. the router's share of dx: dlogits W_r
+  TcGemmArgs a3{};
+  a3.num_m_tiles = nullptr;
+  a3.m_tiles_host = static_cast<int>(b.Tpad / kTileM);
+  a3.tile_expert = nullptr;
+  a3.max_m_tiles = a3.m_tiles_host;
+  a3.num_experts = 1;
+  a3.n_tiles = static_cast<int>(Hp / 256);
+  a3.k_blocks = static_cast<int>(h->Epad64 / 64);
+  a3.b_rows_per_expert = 0;
+  a3.out = sc + b.dxrt;
+  a3.ldo = Hp;
+  a3.bias = nullptr;
+  a3.status = h->status;
+  if ((rc = check(launch_tc_gemm(false, m_dl, h->map_wrT, a3, a3.m_tiles_host, h->num_sms, s),
+                  "router dx gemm")) != VMOE_OK)
+    return rc;
+  // 6. dx = sum over each token's rows (ascending expert) + router share
+  if ((rc = check(launch_gather_dx(sc + b.dxr, Hp, sc + b.dxrt, Hp, idx, slot, T,
+                                   static_cast<int>(H), static_cast<int>(K), dx, s), "dx gather")) != VMOE_OK)
+    return rc;
+  // 7. K-contiguous operands of the weight gradients (+ bias column sums)
+  if ((rc = check(launch_transpose_bf16(sc + b.dy, R, Hp, Hp, 0, 1, sc + b.dyT, Hp, R, 0,
+                                        reinterpret_cast<float*>(sc + b.dy_cs), s), "dy^T")) != VMOE_OK ||
+      (rc = check(launch_transpose_bf16(ws + p.h, R, Ip, Ip, 0, 1, sc + b.hT, Ip, R, 0, nullptr, s),
+                  "h^T")) != VMOE_OK ||
+      (rc = check(launch_transpose_bf16(sc + b.dgu, R, 2 * Ip, 2 * Ip, 0, 1, sc + b.dguT, 2 * Ip, R, 0,
+                                        reinterpret_cast<float*>(sc + b.dgu_cs), s), "dgu^T")) != VMOE_OK ||
+      (rc = check(launch_transpose_bf16(ws + p.xp, R, H, H, 0, 1, sc + b.xpT, Hp, R, 0, nullptr, s),
+                  "x_perm^T")) != VMOE_OK ||
+      (rc = check(launch_transpose_bf16(x, T, H, H, 0, 1, sc + b.xT, Hp, b.Tpad, 0, nullptr, s),
+                  "x^T")) != VMOE_OK ||
+      (rc = check(launch_transpose_bf16(sc + b.dl_bf, T, h->Epad64, h->Epad64, 0, 1, sc + b.dlT,
+                                        b.Mr, b.Tpad, 0, nullptr, s), "dlogits^T")) != VMOE_OK)
+    return rc;
+  // 8. weight gradients (fp32, straight into the caller's layout)
+  CUtensorMap m_dyT, m_hT, m_dguT, m_xpT, m_xT, m_dlT;
+  if (!make_tmap_bf16(&m_dyT, sc + b.dyT, Hp, R, R, kTileM, why, sizeof(why)) ||
+      !make_tmap_bf16(&m_hT, sc + b.hT, Ip, R, R, 256, why, sizeof(why)) ||
+      !make_tmap_bf16(&m_dguT, sc + b.dguT, 2 * Ip, R, R, kTileM, why, sizeof(why)) ||
+      !make_tmap_bf16(&m_xpT, sc + b.xpT, Hp, R, R, 256, why, sizeof(why)) ||
+      !make_tmap_bf16(&m_xT, sc + b.xT, Hp, b.Tpad, b.Tpad, 256, why, sizeof(why)) ||
+      !make_tmap_bf16(&m_dlT, sc + b.dlT, b.Mr, b.Tpad, b.Tpad, kTileM, why, sizeof(why)))
+    return fail(h, VMOE_ERR_CUDA, "weight-gradient tensor maps: %s", why);
+  auto aligned = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15u) == 0; };
+  WgradArgs wd{};
+  wd.seg_offs = offs;
+  wd.rows_total = static_cast<int>(R);
+  wd.num_experts = static_cast<int>(E);
+  wd.m_tiles = static_cast<int>(Hp / kTileM);
+  wd.n_tiles = static_cast<int>((Ip + 255) / 256);
+  wd.m_valid = static_cast<int>(H);
+  wd.n_valid = static_cast<int>(I);
+  wd.out = grads->down_w;
+  wd.ld_out = I;
+  wd.out_expert_stride = H * I;
+  wd.mode = 0;
+  wd.vec_ok = (I % 4 == 0) && aligned(grads->down_w);
+  wd.status = h->status;
+  if ((rc = check(launch_wgrad(m_dyT, m_hT, wd, h->num_sms, s), "dW_down")) != VMOE_OK) return rc;
+  WgradArgs wg = wd;
+  wg.m_tiles = static_cast<int>(2 * Ip / kTileM);
+  wg.n_tiles = static_cast<int>(Hp / 256);
+  wg.m_valid = static_cast<int>(I);
+  wg.n_valid = static_cast<int>(H);
+  wg.out = grads->gate_w;
+  wg.out2 = grads->up_w;
+  wg.ld_out = H;
+  wg.out_expert_stride = I * H;
+  wg.mode = 1;
+  wg.vec_ok = (H % 4 == 0) && aligned(grads->gate_w) && aligned(grads->up_w);
+  if ((rc = check(launch_wgrad(m_dguT, m_xpT, wg, h->num_sms, s), "dW_gate_up")) != VMOE_OK) return rc;
+  WgradArgs wr{};
+  wr.seg_offs = nullptr;
+  wr.seg_rows_host = static_cast<int>(b.Tpad);
+  wr.rows_total = static_cast<int>(b.Tpad);
+  wr.num_experts = 1;
+  wr.m_tiles = static_cast<int>(b.Mr / kTileM);
+  wr.n_tiles = static_cast<int>(Hp / 256);
+  wr.m_valid = static_cast<int>(E);
+  wr.n_valid = static_cast<int>(H);
+  wr.out = grads->router_w;
+  wr.ld_out = H;
+  wr.out_expert_stride = 0;
+  wr.mode = 0;
+  wr.vec_ok = (H % 4 == 0) && aligned(grads->router_w);
+  wr.status = h->status;
+  if ((rc = check(launch_wgrad(m_dlT, m_xT, wr, h->num_sms, s), "dW_router")) != VMOE_OK) return rc;
+  // 9. bias gradients: per-expert sums of the 64-row block column sums
+  if ((rc = check(launch_segment_sum(reinterpret_cast<const float*>(sc + b.dy_cs), Hp, offs,
+                                     static_cast<int>(E), static_cast<int>(Hp), 64, grads->down_b,
+                                     nullptr, static_cast<int>(H), false, s), "db_down")) != VMOE_OK ||
+      (rc = check(launch_segment_sum(reinterpret_cast<const float*>(sc + b.dgu_cs), 2 * Ip, offs,
+                                     static_cast<int>(E), static_cast<int>(2 * Ip), 64,
+                                     grads->gate_b, grads->up_b, static_cast<int>(I), true, s),
+                  "db_gate_up")) != VMOE_OK ||
+      (rc = check(launch_segment_sum(reinterpret_cast<const float*>(sc + b.dl_bs), E, nullptr,
+                                     static_cast<int>((T + 127) / 128), static_cast<int>(E), 128,
+                                     grads->router_b, nullptr, static_cast<int>(E), false, s),
+                  "db_router")) != VMOE_OK)
+    return rc;
   return VMOE_OK;
 }
 

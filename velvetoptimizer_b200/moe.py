@@ -10,12 +10,20 @@ reference's return signature so ``TransformerLayer`` (model.py:419-420) does not
 The forward runs through ``torch.ops.vesper_moe.forward``, a custom op whose body calls
 the C ABI (include/vesper_moe.h) on torch's current stream.  There is no CPU or eager
 fallback: CPU tensors, a missing library or an unsupported dtype raise.
+
+Training (the reference trains through this layer, python/train.py:465): with gradients
+wanted on a bf16 input, the forward runs ``vmoe_forward_train`` inside an autograd
+Function whose backward is ``vmoe_backward`` (dx, the router's and every expert's weight
+and bias gradients); the FlyLoRA factors' gradients follow from the effective-weight
+gradients by the chain rule of W + s U D (model.py:123-126).  fp32 inputs have no
+backward here: they run the forward only (with a warning when gradients were wanted).
 """
 from __future__ import annotations
 
 import ctypes
 import itertools
 import math
+import warnings
 
 import torch
 import torch.nn as nn
@@ -180,6 +188,83 @@ def _(x, handle_id):
     return torch.empty_like(x)
 
 
+def _param_grad(g: torch.Tensor, p: torch.Tensor) -> torch.Tensor:
+    return g.to(p.dtype) if g.dtype != p.dtype else g
+
+
+class _MoETrainFn(torch.autograd.Function):
+    """Autograd of the MoE layer through vmoe_forward_train / vmoe_backward (bf16)."""
+
+    @staticmethod
+    def forward(ctx, x2d, handle_id, layer, want_logits, *params):
+        packed = _HANDLES[handle_id]
+        h = packed.handle
+        T, _ = x2d.shape
+        dev = x2d.device
+        saved_b, scratch_b = h.train_workspace_size(T)
+        saved = torch.empty(max(saved_b, 256), dtype=torch.uint8, device=dev)
+        out = torch.empty_like(x2d)
+        aux = torch.empty((), dtype=torch.float32, device=dev)
+        E = layer.config.moe_num_experts
+        logits = torch.empty((T, E) if want_logits else (0, E), dtype=torch.float32, device=dev)
+        stream = torch.cuda.current_stream(dev).cuda_stream
+        h.forward_train(x2d.data_ptr(), T, out.data_ptr(), logits.data_ptr() if want_logits else None,
+                        aux.data_ptr(), saved.data_ptr(), saved.numel(), stream)
+        ctx.save_for_backward(x2d, saved)
+        ctx.handle_id, ctx.layer, ctx.scratch_b = handle_id, layer, scratch_b
+        ctx.mark_non_differentiable(logits)
+        return out, aux, logits
+
+    @staticmethod
+    def backward(ctx, dout, daux, dlogits):
+        x2d, saved = ctx.saved_tensors
+        layer = ctx.layer
+        h = _HANDLES[ctx.handle_id].handle
+        dev = x2d.device
+        T, H = x2d.shape
+        c = layer.config
+        E, I = c.moe_num_experts, c.intermediate_size
+        if dout is None:
+            dout = torch.zeros_like(x2d)
+        dout = dout.to(x2d.dtype).contiguous()
+        daux_t = (daux if daux is not None else torch.zeros((), device=dev)).float().reshape(1).contiguous()
+        f = dict(device=dev, dtype=torch.float32)
+        g = {"router_w": torch.empty(E, H, **f), "router_b": torch.empty(E, **f),
+             "gate_w": torch.empty(E, I, H, **f), "gate_b": torch.empty(E, I, **f),
+             "up_w": torch.empty(E, I, H, **f), "up_b": torch.empty(E, I, **f),
+             "down_w": torch.empty(E, H, I, **f), "down_b": torch.empty(E, H, **f)}
+        dx = torch.empty_like(x2d)
+        scratch = torch.empty(max(ctx.scratch_b, 256), dtype=torch.uint8, device=dev)
+        vg = _lib.VmoeGrads(**{k: ctypes.c_void_p(v.data_ptr()) for k, v in g.items()})
+        stream = torch.cuda.current_stream(dev).cuda_stream
+        h.backward(x2d.data_ptr(), dout.data_ptr(), T, daux_t.data_ptr(), dx.data_ptr(), vg,
+                   saved.data_ptr(), saved.numel(), scratch.data_ptr(), scratch.numel(), stream)
+        # FlyLoRA factors from the effective-weight gradients (W_eff = W + s U D,
+        # b_eff = b + s (U b_D + b_U)): dU = s (dW D^T + db b_D^T), db_U = s db,
+        # dD = s U^T dW, db_D = s U^T db
+        s = c.lora_scaling
+        lora = {}
+        for name, attr in (("gate", "gate_proj"), ("up", "up_proj")):
+            dW, db = g[f"{name}_w"], g[f"{name}_b"]
+            U = torch.stack([getattr(e, attr).lora_up.weight.detach() for e in layer.experts]).float()
+            D = torch.stack([getattr(e, attr).lora_down.weight.detach() for e in layer.experts]).float()
+            bD = torch.stack([getattr(e, attr).lora_down.bias.detach() for e in layer.experts]).float()
+            lora[name] = {
+                "up_w": s * (torch.bmm(dW, D.transpose(1, 2)) + db[:, :, None] * bD[:, None, :]),
+                "up_b": s * db,
+                "down_w": s * torch.bmm(U.transpose(1, 2), dW),
+                "down_b": s * torch.bmm(U.transpose(1, 2), db[:, :, None])[..., 0],
+            }
+        grads = [g["router_w"], g["router_b"]]
+        for e in range(E):
+            for name in ("gate", "up"):
+                grads += [g[f"{name}_w"][e], g[f"{name}_b"][e], lora[name]["down_w"][e],
+                          lora[name]["down_b"][e], lora[name]["up_w"][e], lora[name]["up_b"][e]]
+            grads += [g["down_w"][e], g["down_b"][e]]
+        params = layer._train_params()
+        return (dx, None, None, None, *[_param_grad(gr, p) for gr, p in zip(grads, params)])
+
+
 class _PackedHandleMixin:
     """Repack-on-change handle management shared by the MoE and dense layers."""
 
@@ -315,11 +400,41 @@ class MoELayer(_PackedHandleMixin, nn.Module):
         w["down_b"] = st(lambda e: e.down_proj.bias)
         return w
 
+    def _train_params(self) -> list:
+        """The parameters in the order the training autograd Function takes them."""
+        ps = [self.router.weight, self.router.bias]
+        for e in self.experts:
+            for proj in (e.gate_proj, e.up_proj):
+                ps += [proj.base.weight, proj.base.bias, proj.lora_down.weight,
+                       proj.lora_down.bias, proj.lora_up.weight, proj.lora_up.bias]
+            ps += [e.down_proj.weight, e.down_proj.bias]
+        return ps
+
+    def _wants_grad(self, x: torch.Tensor) -> bool:
+        return torch.is_grad_enabled() and (
+            x.requires_grad or any(p.requires_grad for p in self.parameters()))
+
     # -- forward ---------------------------------------------------------------------
     def forward(self, x: torch.Tensor, return_router_logits: bool = False):
         """(out[B,S,H], aux_loss[]) — or (out, aux_loss, router_logits[B,S,E])."""
         B, S, H = x.shape
         packed = self.packed_for(x.device, x.dtype)
+        if self._wants_grad(x):
+            if x.dtype == torch.bfloat16:
+                if not getattr(packed, "training", False):
+                    packed.handle.set_training(True, torch.cuda.current_stream(x.device).cuda_stream)
+                    packed.training = True
+                out, aux, logits = _MoETrainFn.apply(
+                    x.reshape(B * S, H).contiguous(), packed.id, self, bool(return_router_logits),
+                    *self._train_params())
+                out = out.reshape(B, S, H)
+                if return_router_logits:
+                    return out, aux, logits.reshape(B, S, self.num_experts)
+                return out, aux
+            if not getattr(self, "_warned_fp32_grad", False):
+                warnings.warn("velvetoptimizer_b200.MoELayer: the backward runs on bfloat16 "
+                              "inputs; this float32 forward carries no gradient")
+                self._warned_fp32_grad = True
         out, logits, aux = torch.ops.vesper_moe.forward(
             x.reshape(B * S, H), packed.id, bool(return_router_logits))
         out = out.reshape(B, S, H)
