@@ -65,6 +65,9 @@ def parse_args():
                    help="time the fused pre-norm block x + MoE(LayerNorm(x)) "
                         "(MoELayer.forward_residual) on one GPU, and beside it the unfused "
                         "torch LayerNorm -> MoELayer.forward -> torch add")
+    p.add_argument("--backward", action="store_true",
+                   help="time the training step instead: vmoe_forward_train + vmoe_backward "
+                        "(dx, router / expert weight and bias gradients) on one GPU")
     p.add_argument("--host-chunks", type=int, default=0,
                    help="token chunks of the single-GPU host-buffer forward timed as e2e "
                         "(0 = automatic)")
@@ -474,6 +477,124 @@ def run_ours(args, rank, world, local_rank):
 
 
 # --------------------------------------------------------------------------------------
+# training step: forward that keeps its intermediates + backward
+# --------------------------------------------------------------------------------------
+def run_backward(args, rank, world, local_rank):
+    import ctypes
+
+    import torch
+
+    from velvetoptimizer_b200 import _lib
+
+    torch.set_grad_enabled(False)
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    w = dict(WORKLOADS[args.workload])
+    T, H, I, E, K = w["tokens"], w["hidden"], w["inter"], w["experts"], w["top_k"]
+    layer = build_layer(w, dev, seed=0)
+    h = layer.packed_for(dev, torch.bfloat16).handle
+    stream = torch.cuda.current_stream(dev)
+    h.set_training(True, stream.cuda_stream)
+    g = torch.Generator(device=dev)
+    g.manual_seed(2000 + rank)
+    x = torch.randn(T, H, generator=g, device=dev).to(torch.bfloat16)
+    dout = (torch.randn(T, H, generator=g, device=dev) * 1e-2).to(torch.bfloat16)
+    daux = torch.full((1,), 0.01, device=dev)  # the reference's moe_aux_loss_weight
+    saved_b, scratch_b = h.train_workspace_size(T)
+    saved = torch.empty(saved_b, dtype=torch.uint8, device=dev)
+    scratch = torch.empty(scratch_b, dtype=torch.uint8, device=dev)
+    out = torch.empty_like(x)
+    aux = torch.empty(1, device=dev)
+    dx = torch.empty_like(x)
+    f = dict(device=dev, dtype=torch.float32)
+    grads = {"router_w": torch.empty(E, H, **f), "router_b": torch.empty(E, **f),
+             "gate_w": torch.empty(E, I, H, **f), "gate_b": torch.empty(E, I, **f),
+             "up_w": torch.empty(E, I, H, **f), "up_b": torch.empty(E, I, **f),
+             "down_w": torch.empty(E, H, I, **f), "down_b": torch.empty(E, H, **f)}
+    vg = _lib.VmoeGrads(**{k: ctypes.c_void_p(v.data_ptr()) for k, v in grads.items()})
+    ev_mid = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
+    launches = [0]
+
+    def step(i=None, e0=None):
+        h.forward_train(x.data_ptr(), T, out.data_ptr(), None, aux.data_ptr(), saved.data_ptr(),
+                        saved_b, stream.cuda_stream)
+        n = h.last_launch_count()
+        if i is not None:
+            ev_mid[i].record(stream)
+        h.backward(x.data_ptr(), dout.data_ptr(), T, daux.data_ptr(), dx.data_ptr(), vg,
+                   saved.data_ptr(), saved_b, scratch.data_ptr(), scratch_b, stream.cuda_stream)
+        launches[0] += n + h.last_launch_count()
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    assert h.device_status(stream.cuda_stream) == 0
+    props = torch.cuda.get_device_properties(dev)
+    gpu_id = str(getattr(props, "uuid", "") or local_rank)
+    if gpu_id and not gpu_id.startswith("GPU-") and len(gpu_id) > 8:
+        gpu_id = "GPU-" + gpu_id
+    h.set_profiling(args.steps)
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
+    torch.cuda.synchronize()
+    sampler = ClockSampler(gpu_id)
+    time.sleep(0.3)
+    launches[0] = 0
+    for i in range(args.steps):
+        starts[i].record(stream)
+        step(i)
+    starts[args.steps].record(stream)
+    starts[args.steps].synchronize()
+    clocks = sampler.stop()
+    ms = starts[0].elapsed_time(starts[args.steps]) / args.steps
+    fwd_ms = statistics.mean(starts[i].elapsed_time(ev_mid[i]) for i in range(args.steps))
+    bwd_ms = statistics.mean(ev_mid[i].elapsed_time(starts[i + 1]) for i in range(args.steps))
+    stages, nprof = h.backward_stage_times()
+    assert h.device_status(stream.cuda_stream) == 0
+    pk = peaks()
+    flop = {"dh_glu_bwd_gemm": 2.0 * T * K * H * I, "dx_gemm": 4.0 * T * K * H * I,
+            "wgrad_down": 2.0 * T * K * H * I, "wgrad_gate_up": 4.0 * T * K * H * I,
+            "router_dx_gemm": 2.0 * T * E * H}
+    e = 2
+    byts = {"combine_bwd": T * H * e + 2 * T * K * H * e + T * K * 4,
+            "dx_gather": T * K * H * e + 2 * T * H * e,
+            "transposes": 2 * e * (T * K * (2 * H + 3 * I) + T * H + T * E)}
+    rep = {}
+    for name, t_ms in stages.items():
+        rec = {"ms": round(t_ms, 4), "share": round(t_ms / max(sum(stages.values()), 1e-9), 4)}
+        if name in flop:
+            a = flop[name] / (t_ms * 1e-3) / 1e12
+            rec.update(achieved=round(a, 1), unit="TFLOP/s", frac=round(a / pk["bf16_tflops"], 4))
+        elif name in byts:
+            a = byts[name] / (t_ms * 1e-3) / 1e9
+            rec.update(achieved=round(a, 1), unit="GB/s", frac=round(a / pk["hbm_gbs"], 4))
+        rep[name] = rec
+    top = max(flop, key=lambda k: stages.get(k, 0.0))  # the backward kernel that takes longest
+    top_ms = stages[top]
+    achieved = flop[top] / (top_ms * 1e-3) / 1e12
+    return {
+        "metric": "MoE-layer training step (fwd + bwd) tokens/s",
+        "value": round(T / (ms * 1e-3), 1), "unit": "tokens/s", "n_gpus": 1,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
+        "fwd_ms": round(fwd_ms, 4), "bwd_ms": round(bwd_ms, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic: x~N(0,1), dout~N(0,1e-4), weights~N(0,0.02), zero bias, FlyLoRA off",
+        "config": {"workload": f"{args.workload}: MoE FFN layer training step, {T} tokens, "
+                               f"d_model {H}, expert d_ff {I}, {E} experts, top-{K}; outputs dx and "
+                               f"fp32 router / expert weight and bias gradients",
+                   "l2": "inputs larger than L2; no flush"},
+        "e2e": None,
+        "roofline": {"kernel": top, "bound": "tensor", "achieved": round(achieved, 1),
+                     "peak": pk["bf16_tflops"], "peak_source": pk["source"] + " bf16 burst",
+                     "unit": "TFLOP/s", "frac": round(achieved / pk["bf16_tflops"], 4),
+                     "traffic": None, "flop_per_launch": flop[top], "avg_launch_ms": round(top_ms, 4),
+                     "launches_timed": nprof},
+        "stages": rep,
+        "gpu_launches": launches[0],
+        "clocks": clocks,
+    }
+
+
+# --------------------------------------------------------------------------------------
 # reference arm: the CPU implementation of the path (the oracle port) on host cores
 # --------------------------------------------------------------------------------------
 def run_reference(args):
@@ -549,6 +670,11 @@ def main():
         torch.cuda.set_device(local_rank)
         dist.init_process_group("nccl", timeout=timedelta(seconds=120),
                                 device_id=torch.device("cuda", local_rank))
+    if args.backward:
+        if world > 1:
+            raise SystemExit("--backward runs on one GPU")
+        print(json.dumps(run_backward(args, rank, world, local_rank)), flush=True)
+        return 0
     try:
         line = run_ours(args, rank, world, local_rank)
         if line is not None:

@@ -328,6 +328,10 @@ VMOE_API int vmoe_device_status(vmoe_handle* h, int32_t* code, void* stream);
 VMOE_API int vmoe_set_profiling(vmoe_handle* h, int n);
 VMOE_API int vmoe_stage_times(vmoe_handle* h, float* ms, int n, int* n_out, int* forwards);
 VMOE_API const char* vmoe_stage_name(int stage);
+/* The same for the stages of vmoe_backward (recorded for the next n backwards after
+ * vmoe_set_profiling(h, n)). */
+VMOE_API int vmoe_backward_stage_times(vmoe_handle* h, float* ms, int n, int* n_out, int* calls);
+VMOE_API const char* vmoe_backward_stage_name(int stage);
 
 /* Number of kernel launches the last vmoe_forward enqueued. */
 VMOE_API int vmoe_last_launch_count(const vmoe_handle* h);

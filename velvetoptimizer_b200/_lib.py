@@ -38,7 +38,8 @@ EXPORTED = (
     "vmoe_ep_p2p_forward", "vmoe_gemm_tile_rows", "vmoe_ffn_create", "vmoe_ffn_workspace_size",
     "vmoe_ffn_forward", "vmoe_forward_host_workspace_size", "vmoe_forward_host",
     "vmoe_set_norm", "vmoe_forward_residual", "vmoe_set_training", "vmoe_train_workspace_size",
-    "vmoe_forward_train", "vmoe_backward",
+    "vmoe_forward_train", "vmoe_backward", "vmoe_backward_stage_times",
+    "vmoe_backward_stage_name",
 )
 
 
@@ -117,6 +118,11 @@ def load() -> ctypes.CDLL:
     lib.vmoe_forward_host.argtypes = [H, c_void_p, c_int64, c_void_p, c_void_p, c_int, c_void_p,
                                       c_size_t, c_void_p]
     lib.vmoe_forward_host.restype = c_int
+    lib.vmoe_backward_stage_times.argtypes = [H, POINTER(c_float), c_int, POINTER(c_int),
+                                              POINTER(c_int)]
+    lib.vmoe_backward_stage_times.restype = c_int
+    lib.vmoe_backward_stage_name.argtypes = [c_int]
+    lib.vmoe_backward_stage_name.restype = c_char_p
     lib.vmoe_set_training.argtypes = [H, c_int, c_void_p]
     lib.vmoe_set_training.restype = c_int
     lib.vmoe_train_workspace_size.argtypes = [H, c_int64, POINTER(c_size_t), POINTER(c_size_t)]
@@ -297,6 +303,15 @@ class Handle:
         check(self.lib.vmoe_stage_times(self.ptr, buf, 16, ctypes.byref(n), ctypes.byref(f)),
               self.ptr, "vmoe_stage_times")
         return {self.lib.vmoe_stage_name(i).decode(): float(buf[i]) for i in range(n.value)}, f.value
+
+    def backward_stage_times(self) -> tuple[dict[str, float], int]:
+        """(average ms per backward stage, number of backwards averaged); restarts recording."""
+        buf = (c_float * 16)()
+        n, f = c_int(), c_int()
+        check(self.lib.vmoe_backward_stage_times(self.ptr, buf, 16, ctypes.byref(n), ctypes.byref(f)),
+              self.ptr, "vmoe_backward_stage_times")
+        return ({self.lib.vmoe_backward_stage_name(i).decode(): float(buf[i]) for i in range(n.value)},
+                f.value)
 
     def last_launch_count(self) -> int:
         return int(self.lib.vmoe_last_launch_count(self.ptr))

@@ -29,6 +29,10 @@ namespace {
 constexpr int kStages = 7;
 const char* const kStageNames[kStages] = {"router", "scan", "plan", "dispatch",
                                           "gemm1_gate_up_era", "gemm2_down", "combine"};
+constexpr int kBwdStages = 10;
+const char* const kBwdStageNames[kBwdStages] = {
+    "combine_bwd", "router_bwd", "dh_glu_bwd_gemm", "dx_gemm", "router_dx_gemm", "dx_gather",
+    "transposes", "wgrad_down", "wgrad_gate_up", "wgrad_router_and_biases"};
 constexpr int kGateUpInterleave = 128;  // rows of gate (then up) per 256-row B tile
 constexpr int kDownTileN = 256;         // N tile of the down projection
 
@@ -134,6 +138,9 @@ struct vmoe_handle {
   int prof_slots = 0;
   int prof_count = 0;
   std::vector<cudaEvent_t> prof_ev;
+  // the same for backward stages
+  int bprof_count = 0;
+  std::vector<cudaEvent_t> bprof_ev;
   int last_launches = 0;
   std::string err;
 };
@@ -643,6 +650,7 @@ int vmoe_destroy(vmoe_handle* h) {
     if (h->w_guT) cudaFree(h->w_guT);
     if (h->w_rT) cudaFree(h->w_rT);
     for (cudaEvent_t ev : h->prof_ev) cudaEventDestroy(ev);
+    for (cudaEvent_t ev : h->bprof_ev) cudaEventDestroy(ev);
   }
   delete h;
   return VMOE_OK;
@@ -1843,8 +1851,17 @@ int vmoe_backward(vmoe_handle* h, const void* x, const void* dout, int64_t token
   const float* logits = reinterpret_cast<const float*>(ws + tp.logits);
   const int64_t R = p.max_rows, max_tiles = R / h->tile_rows;
   cudaError_t e;
+  const bool prof = h->bprof_count < h->prof_slots;
+  cudaEvent_t* pev =
+      prof ? &h->bprof_ev[static_cast<size_t>(h->bprof_count) * (kBwdStages + 1)] : nullptr;
+  int stage = 0;
+  auto mark = [&]() {
+    if (prof) cudaEventRecord(pev[stage], s);
+    ++stage;
+  };
 
   // 1. combine backward: dy (expert-major rows) and dw; padding rows / columns zeroed
+  mark();
   if (Hp != H && (e = cudaMemsetAsync(sc + b.dy, 0, R * Hp * 2, s)) != cudaSuccess)
     return cuda_fail(h, e, "dy clear");
   if ((rc = check(launch_combine_bwd(dout, ws + p.y, Hp, idx, tw, slot, T, static_cast<int>(H),
@@ -1855,6 +1872,7 @@ int vmoe_backward(vmoe_handle* h, const void* x, const void* dout, int64_t token
                                        h->cfg.capacity, s), "dy pad rows")) != VMOE_OK)
     return rc;
   // 2. router backward
+  mark();
   if ((rc = check(launch_router_bwd(logits, idx, reinterpret_cast<const float*>(sc + b.dw), counts,
                                     T, static_cast<int>(E), static_cast<int>(K), daux,
                                     reinterpret_cast<float*>(sc + b.dl), sc + b.dl_bf,
@@ -1862,6 +1880,7 @@ int vmoe_backward(vmoe_handle* h, const void* x, const void* dout, int64_t token
                                     reinterpret_cast<float*>(sc + b.dl_bs), s), "router bwd")) != VMOE_OK)
     return rc;
   // 3. dh = dy W_d with the GLU / ERA backward epilogue -> dgu
+  mark();
   char why[256];
   CUtensorMap m_dy, m_dgu, m_dl;
   if (!make_tmap_bf16(&m_dy, sc + b.dy, R, Hp, Hp, kTileM, why, sizeof(why)) ||
@@ -1887,6 +1906,7 @@ int vmoe_backward(vmoe_handle* h, const void* x, const void* dout, int64_t token
                   "dh gemm")) != VMOE_OK)
     return rc;
   // 4. dx rows = dgu (gate|up)^T-major weights
+  mark();
   TcGemmArgs a2{};
   a2.num_m_tiles = ntiles;
   a2.tile_expert = tiles;
@@ -1903,6 +1923,7 @@ int vmoe_backward(vmoe_handle* h, const void* x, const void* dout, int64_t token
                   "dx gemm")) != VMOE_OK)
     return rc;
   // 5. the router's share of dx: dlogits W_r
+  mark();
   TcGemmArgs a3{};
   a3.num_m_tiles = nullptr;
   a3.m_tiles_host = static_cast<int>(b.Tpad / kTileM);
@@ -1920,10 +1941,12 @@ int vmoe_backward(vmoe_handle* h, const void* x, const void* dout, int64_t token
                   "router dx gemm")) != VMOE_OK)
     return rc;
   // 6. dx = sum over each token's rows (ascending expert) + router share
+  mark();
   if ((rc = check(launch_gather_dx(sc + b.dxr, Hp, sc + b.dxrt, Hp, idx, slot, T,
                                    static_cast<int>(H), static_cast<int>(K), dx, s), "dx gather")) != VMOE_OK)
     return rc;
   // 7. K-contiguous operands of the weight gradients (+ bias column sums)
+  mark();
   if ((rc = check(launch_transpose_bf16(sc + b.dy, R, Hp, Hp, 0, 1, sc + b.dyT, Hp, R, 0,
                                         reinterpret_cast<float*>(sc + b.dy_cs), s), "dy^T")) != VMOE_OK ||
       (rc = check(launch_transpose_bf16(ws + p.h, R, Ip, Ip, 0, 1, sc + b.hT, Ip, R, 0, nullptr, s),
@@ -1961,7 +1984,9 @@ int vmoe_backward(vmoe_handle* h, const void* x, const void* dout, int64_t token
   wd.mode = 0;
   wd.vec_ok = (I % 4 == 0) && aligned(grads->down_w);
   wd.status = h->status;
+  mark();
   if ((rc = check(launch_wgrad(m_dyT, m_hT, wd, h->num_sms, s), "dW_down")) != VMOE_OK) return rc;
+  mark();
   WgradArgs wg = wd;
   wg.m_tiles = static_cast<int>(2 * Ip / kTileM);
   wg.n_tiles = static_cast<int>(Hp / 256);
@@ -1974,6 +1999,7 @@ int vmoe_backward(vmoe_handle* h, const void* x, const void* dout, int64_t token
   wg.mode = 1;
   wg.vec_ok = (H % 4 == 0) && aligned(grads->gate_w) && aligned(grads->up_w);
   if ((rc = check(launch_wgrad(m_dguT, m_xpT, wg, h->num_sms, s), "dW_gate_up")) != VMOE_OK) return rc;
+  mark();
   WgradArgs wr{};
   wr.seg_offs = nullptr;
   wr.seg_rows_host = static_cast<int>(b.Tpad);
@@ -2003,6 +2029,8 @@ int vmoe_backward(vmoe_handle* h, const void* x, const void* dout, int64_t token
                                      grads->router_b, nullptr, static_cast<int>(E), false, s),
                   "db_router")) != VMOE_OK)
     return rc;
+  mark();
+  if (prof) ++h->bprof_count;
   return VMOE_OK;
 }
 
@@ -2026,20 +2054,54 @@ int vmoe_set_profiling(vmoe_handle* h, int n) {
   if (!h || n < 0) return VMOE_ERR_INVALID_ARG;
   DeviceGuard g(h->device);
   for (cudaEvent_t ev : h->prof_ev) cudaEventDestroy(ev);
+  for (cudaEvent_t ev : h->bprof_ev) cudaEventDestroy(ev);
   h->prof_ev.clear();
+  h->bprof_ev.clear();
   h->prof_slots = 0;
   h->prof_count = 0;
+  h->bprof_count = 0;
   if (n == 0) return VMOE_OK;
   h->prof_ev.resize(static_cast<size_t>(n) * (kStages + 1));
-  for (auto& ev : h->prof_ev) {
-    cudaError_t e = cudaEventCreate(&ev);
-    if (e != cudaSuccess) {
-      ev = nullptr;
-      return cuda_fail(h, e, "profiling events");
+  h->bprof_ev.resize(static_cast<size_t>(n) * (kBwdStages + 1));
+  for (auto* ring : {&h->prof_ev, &h->bprof_ev}) {
+    for (auto& ev : *ring) {
+      cudaError_t e = cudaEventCreate(&ev);
+      if (e != cudaSuccess) {
+        ev = nullptr;
+        return cuda_fail(h, e, "profiling events");
+      }
     }
   }
   h->prof_slots = n;
   return VMOE_OK;
+}
+
+int vmoe_backward_stage_times(vmoe_handle* h, float* ms, int n, int* n_out, int* calls) {
+  if (!h || !ms || n < 0) return VMOE_ERR_INVALID_ARG;
+  if (h->bprof_count == 0) return fail(h, VMOE_ERR_NOT_READY, "no profiled backward recorded");
+  DeviceGuard g(h->device);
+  const int m = n < kBwdStages ? n : kBwdStages;
+  for (int i = 0; i < m; ++i) ms[i] = 0.f;
+  for (int f = 0; f < h->bprof_count; ++f) {
+    cudaEvent_t* ev = &h->bprof_ev[static_cast<size_t>(f) * (kBwdStages + 1)];
+    cudaError_t e = cudaEventSynchronize(ev[kBwdStages]);
+    if (e != cudaSuccess) return cuda_fail(h, e, "stage timing");
+    for (int i = 0; i < m; ++i) {
+      float t = 0.f;
+      e = cudaEventElapsedTime(&t, ev[i], ev[i + 1]);
+      if (e != cudaSuccess) return cuda_fail(h, e, "stage timing");
+      ms[i] += t;
+    }
+  }
+  for (int i = 0; i < m; ++i) ms[i] /= static_cast<float>(h->bprof_count);
+  if (n_out) *n_out = m;
+  if (calls) *calls = h->bprof_count;
+  h->bprof_count = 0;
+  return VMOE_OK;
+}
+
+const char* vmoe_backward_stage_name(int stage) {
+  return stage >= 0 && stage < kBwdStages ? kBwdStageNames[stage] : "";
 }
 
 int vmoe_stage_times(vmoe_handle* h, float* ms, int n, int* n_out, int* forwards) {
