@@ -15,60 +15,73 @@ namespace vmoe {
 namespace {
 
 // ---- transpose -------------------------------------------------------------------------
-// 64 x 64 tiles through shared memory; block (32, 8); grid (dst_cols / 64, dst_rows / 64, batch)
+// 64 x 64 tiles through shared memory with 16-byte loads and stores; block 256; grid
+// (dst_cols / 64, dst_rows / 64, batch).  Tile rows are stored with their 8-column chunks
+// rotated by (row / 8) so that the column reads of the store phase hit 16 distinct banks.
+constexpr int kTP = 72;  // shared row pitch (elements): 144 bytes, 16-byte aligned rows
+
+__device__ __forceinline__ int tpos(int r, int c) { return 8 * (((c >> 3) + (r >> 3)) & 7) + (c & 7); }
+
 __global__ void __launch_bounds__(256)
 transpose_bf16_kernel(const __nv_bfloat16* __restrict__ src, int64_t rows, int64_t cols,
                       int64_t src_ld, int64_t src_bs, __nv_bfloat16* __restrict__ dst,
                       int64_t dst_rows, int64_t dst_cols, int64_t dst_bs,
                       float* __restrict__ colsum) {
-  __shared__ float tile[64][65];
-  const int tx = threadIdx.x, ty = threadIdx.y;
+  __shared__ __align__(16) __nv_bfloat16 tile[64 * kTP];
+  const int tid = threadIdx.x;
   const int64_t r0 = static_cast<int64_t>(blockIdx.x) * 64;  // source rows = dst columns
   const int64_t c0 = static_cast<int64_t>(blockIdx.y) * 64;  // source cols = dst rows
   const int b = blockIdx.z;
   const __nv_bfloat16* sb = src + b * src_bs;
+  const bool vec_src = (src_ld & 7) == 0 && (reinterpret_cast<uintptr_t>(sb) & 15) == 0;
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const int rr = ty + 8 * i;
-    const int64_t r = r0 + rr;
-    const int64_t c = c0 + 2 * tx;
-    float v0 = 0.f, v1 = 0.f;
+  for (int it = 0; it < 2; ++it) {
+    const int i = tid + 256 * it;
+    const int rr = i >> 3, ch = i & 7;
+    const int64_t r = r0 + rr, c = c0 + 8 * ch;
+    uint4 v = make_uint4(0u, 0u, 0u, 0u);
     if (r < rows) {
-      if (c + 1 < cols && ((src_ld | c) & 1) == 0) {
-        const __nv_bfloat162 p = *reinterpret_cast<const __nv_bfloat162*>(sb + r * src_ld + c);
-        v0 = __bfloat162float(p.x);
-        v1 = __bfloat162float(p.y);
+      if (vec_src && c + 8 <= cols) {
+        v = *reinterpret_cast<const uint4*>(sb + r * src_ld + c);
       } else {
-        if (c < cols) v0 = __bfloat162float(sb[r * src_ld + c]);
-        if (c + 1 < cols) v1 = __bfloat162float(sb[r * src_ld + c + 1]);
+        __align__(16) __nv_bfloat16 e[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) e[j] = c + j < cols ? sb[r * src_ld + c + j] : __float2bfloat16_rn(0.f);
+        v = *reinterpret_cast<const uint4*>(e);
       }
     }
-    tile[rr][2 * tx] = v0;
-    tile[rr][2 * tx + 1] = v1;
+    *reinterpret_cast<uint4*>(tile + rr * kTP + tpos(rr, 8 * ch)) = v;
   }
   __syncthreads();
-  if (colsum && ty == 0) {  // this 64-row block's column sums, rows in ascending order
-    for (int cc = tx; cc < 64; cc += 32) {
-      if (c0 + cc >= cols) continue;
+  if (colsum && tid < 64) {  // this 64-row block's column sums, rows in ascending order
+    const int cc = tid;
+    const int64_t nrb = (rows + 63) / 64;
+    if (c0 + cc < cols && blockIdx.x < nrb) {
       float s = 0.f;
-      for (int rr = 0; rr < 64; ++rr) s += tile[rr][cc];
-      const int64_t nrb = (rows + 63) / 64;
-      if (blockIdx.x < nrb) colsum[(static_cast<int64_t>(b) * nrb + blockIdx.x) * cols + c0 + cc] = s;
+      for (int rr = 0; rr < 64; ++rr) s += __bfloat162float(tile[rr * kTP + tpos(rr, cc)]);
+      colsum[(static_cast<int64_t>(b) * nrb + blockIdx.x) * cols + c0 + cc] = s;
     }
   }
   __nv_bfloat16* db = dst + b * dst_bs;
+  const bool vec_dst = (dst_cols & 7) == 0 && (reinterpret_cast<uintptr_t>(db) & 15) == 0;
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const int cc = ty + 8 * i;
-    const int64_t drow = c0 + cc;
-    const int64_t dcol = r0 + 2 * tx;
+  for (int it = 0; it < 2; ++it) {
+    const int i = tid + 256 * it;
+    const int cc = i >> 3, ch = i & 7;  // dst row c0 + cc, dst columns r0 + 8 ch .. + 8
+    const int64_t drow = c0 + cc, dcol = r0 + 8 * ch;
     if (drow >= dst_rows) continue;
-    if (dcol + 1 < dst_cols && ((dst_cols | dcol) & 1) == 0) {
-      *reinterpret_cast<__nv_bfloat162*>(db + drow * dst_cols + dcol) =
-          __floats2bfloat162_rn(tile[2 * tx][cc], tile[2 * tx + 1][cc]);
+    __align__(16) __nv_bfloat16 e[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int rr = 8 * ch + j;
+      e[j] = tile[rr * kTP + tpos(rr, cc)];
+    }
+    if (vec_dst && dcol + 8 <= dst_cols) {
+      *reinterpret_cast<uint4*>(db + drow * dst_cols + dcol) = *reinterpret_cast<const uint4*>(e);
     } else {
-      if (dcol < dst_cols) db[drow * dst_cols + dcol] = __float2bfloat16_rn(tile[2 * tx][cc]);
-      if (dcol + 1 < dst_cols) db[drow * dst_cols + dcol + 1] = __float2bfloat16_rn(tile[2 * tx + 1][cc]);
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        if (dcol + j < dst_cols) db[drow * dst_cols + dcol + j] = e[j];
     }
   }
 }
@@ -91,6 +104,9 @@ __global__ void zero_pad_rows_kernel(char* __restrict__ buf, int64_t ld_bytes, i
 }
 
 // ---- combine backward: one warp per token -----------------------------------------------
+// KMAX bounds top_k at compile time so the per-slot state stays in registers and the K row
+// loads of each 16-byte column chunk are issued together.
+template <int KMAX>
 __global__ void __launch_bounds__(256)
 combine_bwd_kernel(const __nv_bfloat16* __restrict__ dout, const __nv_bfloat16* __restrict__ y,
                    int64_t y_ld, const int32_t* __restrict__ topk_idx,
@@ -100,10 +116,10 @@ combine_bwd_kernel(const __nv_bfloat16* __restrict__ dout, const __nv_bfloat16* 
   const int lane = threadIdx.x & 31;
   const int64_t t = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
   if (t >= T) return;
-  int slot[32];
-  float wk[32], dot[32];
+  int slot[KMAX];
+  float wk[KMAX], dot[KMAX];
 #pragma unroll
-  for (int k = 0; k < 32; ++k) {
+  for (int k = 0; k < KMAX; ++k) {
     slot[k] = k < K ? slot_of[t * K + k] : -1;
     wk[k] = k < K ? topk_w[t * K + k] : 0.f;
     dot[k] = 0.f;
@@ -111,23 +127,28 @@ combine_bwd_kernel(const __nv_bfloat16* __restrict__ dout, const __nv_bfloat16* 
   const int nvec = H / 8;
   const __nv_bfloat16* drow = dout + t * static_cast<int64_t>(H);
   for (int v = lane; v < nvec; v += 32) {
-    float d[8];
-    load16_to_f(drow + v * 8, d);
+    const uint4 dv = reinterpret_cast<const uint4*>(drow)[v];
+    uint4 yv[KMAX];
 #pragma unroll
-    for (int k = 0; k < 32; ++k) {
-      if (k >= K || slot[k] < 0) continue;
-      float yv[8], o[8];
-      load16_to_f(y + static_cast<int64_t>(slot[k]) * y_ld + v * 8, yv);
+    for (int k = 0; k < KMAX; ++k)
+      if (slot[k] >= 0) yv[k] = reinterpret_cast<const uint4*>(y + static_cast<int64_t>(slot[k]) * y_ld)[v];
+    float d[8];
+    load16_to_f(reinterpret_cast<const __nv_bfloat16*>(&dv), d);
+#pragma unroll
+    for (int k = 0; k < KMAX; ++k) {
+      if (slot[k] < 0) continue;
+      float f[8], o[8];
+      load16_to_f(reinterpret_cast<const __nv_bfloat16*>(&yv[k]), f);
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
-        dot[k] = fmaf(d[i], yv[i], dot[k]);
+        dot[k] = fmaf(d[i], f[i], dot[k]);
         o[i] = d[i] * wk[k];
       }
       store16_from_f(dy + static_cast<int64_t>(slot[k]) * dy_ld + v * 8, o);
     }
   }
 #pragma unroll
-  for (int k = 0; k < 32; ++k) {
+  for (int k = 0; k < KMAX; ++k) {
     if (k >= K) break;
     float s = dot[k];
 #pragma unroll
@@ -271,7 +292,7 @@ cudaError_t launch_transpose_bf16(const void* src, int64_t rows, int64_t cols, i
   if (dst_rows < cols || dst_cols < rows) return cudaErrorInvalidValue;
   const dim3 grid(static_cast<unsigned>((dst_cols + 63) / 64), static_cast<unsigned>((dst_rows + 63) / 64),
                   static_cast<unsigned>(batch));
-  transpose_bf16_kernel<<<grid, dim3(32, 8), 0, s>>>(
+  transpose_bf16_kernel<<<grid, 256, 0, s>>>(
       static_cast<const __nv_bfloat16*>(src), rows, cols, src_ld, src_batch_stride,
       static_cast<__nv_bfloat16*>(dst), dst_rows, dst_cols, dst_batch_stride, colsum);
   return cudaGetLastError();
@@ -290,9 +311,18 @@ cudaError_t launch_combine_bwd(const void* dout, const void* y, int64_t y_ld,
                                int64_t T, int H, int K, void* dy, int64_t dy_ld, float* dw,
                                cudaStream_t s) {
   if (K > 32 || H % 8) return cudaErrorInvalidValue;
-  combine_bwd_kernel<<<static_cast<unsigned>((T + 7) / 8), 256, 0, s>>>(
-      static_cast<const __nv_bfloat16*>(dout), static_cast<const __nv_bfloat16*>(y), y_ld, topk_idx,
-      topk_w, slot_of, T, H, K, static_cast<__nv_bfloat16*>(dy), dy_ld, dw);
+  const unsigned grid = static_cast<unsigned>((T + 7) / 8);
+  const auto* d = static_cast<const __nv_bfloat16*>(dout);
+  const auto* yy = static_cast<const __nv_bfloat16*>(y);
+  auto* o = static_cast<__nv_bfloat16*>(dy);
+  if (K <= 2)
+    combine_bwd_kernel<2><<<grid, 256, 0, s>>>(d, yy, y_ld, topk_idx, topk_w, slot_of, T, H, K, o, dy_ld, dw);
+  else if (K <= 4)
+    combine_bwd_kernel<4><<<grid, 256, 0, s>>>(d, yy, y_ld, topk_idx, topk_w, slot_of, T, H, K, o, dy_ld, dw);
+  else if (K <= 8)
+    combine_bwd_kernel<8><<<grid, 256, 0, s>>>(d, yy, y_ld, topk_idx, topk_w, slot_of, T, H, K, o, dy_ld, dw);
+  else
+    combine_bwd_kernel<32><<<grid, 256, 0, s>>>(d, yy, y_ld, topk_idx, topk_w, slot_of, T, H, K, o, dy_ld, dw);
   return cudaGetLastError();
 }
 

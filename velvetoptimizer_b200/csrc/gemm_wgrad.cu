@@ -3,11 +3,18 @@
 // For every expert e:  dW_e[M, N] = sum over the rows r of e's segment of  A[r, :]^T B[r, :]
 // -- the nn.Linear weight gradient dW = dY^T X that autograd forms for every expert's
 // Linear in MoELayer.forward (python/vesper/model.py:295-298, 322) -- with the token rows as
-// the reduction (K) dimension.  Both operands are stored transposed (A^T [M_total, R],
-// B^T [N_total, R], rows contiguous along R) so every operand tile is K-major like the
-// forward GEMMs'; the K range of a tile is its expert's segment [offs[e], offs[e+1]) (a
-// multiple of 64 rows), so experts with more tokens simply run longer K loops and empty
-// experts write zeros.
+// the reduction (K) dimension, and the bias gradient db_e = sum over the same rows of A.
+//
+// Both operands stay in their row-major activation layout ([rows, M] and [rows, N]): the
+// tiles are loaded "MN-major" (TMA boxes of 64 columns x 64 rows, 128-byte swizzle: every
+// 128-byte shared row holds 64 consecutive M (or N) elements of one token row) and the MMA
+// reads them transposed (instruction-descriptor A/B major bits; descriptor leading byte
+// offset = 8 KB between 64-wide column chunks, stride byte offset = 1 KB between 8-row
+// groups), so no transposed copy of any activation is ever written.  The K range of a tile
+// is its expert's segment [offs[e], offs[e+1]) (a multiple of 64 rows): experts with more
+// tokens run longer K loops, empty experts write zeros.  With bias outputs, every (expert,
+// M tile) gets one more work item whose B operand is a constant K-major ones row (N = 16):
+// its column 0 is the segment's column sums of A.
 //
 // One CTA per SM, persistent over (expert, M tile, N tile) work items; warp 0 is the TMA
 // producer (A 128 x 64 + B 256 x 64 per stage, 4 stages), warp 1 allocates TMEM (two
@@ -25,12 +32,28 @@ namespace {
 
 constexpr int BK = 64;
 constexpr int BN = 256;
-constexpr uint32_t A_BYTES = kTileM * BK * 2;  // 16 KB
-constexpr uint32_t B_BYTES = BN * BK * 2;      // 32 KB
+constexpr uint32_t CHUNK_BYTES = 64 * BK * 2;   // one 64-column x 64-row box: 8 KB
+constexpr uint32_t A_BYTES = 2 * CHUNK_BYTES;   // 128 M columns
+constexpr uint32_t B_BYTES = 4 * CHUNK_BYTES;   // 256 N columns
 constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
 constexpr int STAGES = 4;
+constexpr uint32_t ONES_BYTES = 16 * 128;       // 16-row K-major ones tile (row 0 = 1)
 constexpr uint32_t TMEM_COLS = 2 * BN;
-constexpr uint32_t IDESC = umma_idesc_bf16(kTileM, BN);
+constexpr uint32_t kMajorA = 1u << 15, kMajorB = 1u << 16;  // operand read MN-major
+constexpr uint32_t IDESC = umma_idesc_bf16(kTileM, BN) | kMajorA | kMajorB;
+constexpr uint32_t IDESC_BIAS = umma_idesc_bf16(kTileM, 16) | kMajorA;  // B: K-major ones
+
+// Descriptor of an MN-major operand chunk sequence: 128-byte swizzle, 64-element MN chunks
+// CHUNK_BYTES apart (leading byte offset), 8-row K groups 1024 bytes apart (stride).
+__device__ __forceinline__ uint64_t desc_mn_sw128(uint32_t smem_addr) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((smem_addr & 0x3FFFFu) >> 4);
+  d |= static_cast<uint64_t>(CHUNK_BYTES >> 4) << 16;
+  d |= static_cast<uint64_t>(1024 >> 4) << 32;
+  d |= static_cast<uint64_t>(1) << 46;
+  d |= static_cast<uint64_t>(2) << 61;
+  return d;
+}
 
 struct WgShared {
   uint64_t full[STAGES];
@@ -44,7 +67,7 @@ struct WgShared {
   int consumed;
 };
 
-constexpr size_t SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + sizeof(WgShared) + 64;
+constexpr size_t SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + ONES_BYTES + sizeof(WgShared) + 64;
 
 __device__ __forceinline__ bool aborted(const WgShared* sh) {
   return *reinterpret_cast<const volatile int*>(&sh->abort) != 0;
@@ -71,6 +94,23 @@ __device__ __forceinline__ void seg_blocks(const WgradArgs& a, int e, int& kb0, 
   nk = (r1 - r0) / BK;
 }
 
+struct Work {
+  int e, m, n;
+  bool bias;
+};
+
+__device__ __forceinline__ Work work_of(const WgradArgs& a, int tile) {
+  const int nt = a.n_tiles + (a.bias_out ? 1 : 0);
+  const int per_expert = a.m_tiles * nt;
+  Work w;
+  w.e = tile / per_expert;
+  const int mn = tile - w.e * per_expert;
+  w.m = mn / nt;
+  w.n = mn - w.m * nt;
+  w.bias = w.n == a.n_tiles;
+  return w;
+}
+
 __global__ void __launch_bounds__(192, 1)
 wgrad_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_constant__ CUtensorMap b_map,
              const WgradArgs args) {
@@ -80,9 +120,16 @@ wgrad_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_constant__ 
   uint8_t* gbase = smem_raw + (base - raw);
   const uint32_t a_s = base;
   const uint32_t b_s = base + STAGES * A_BYTES;
-  auto* sh = reinterpret_cast<WgShared*>(gbase + STAGES * STAGE_BYTES);
+  const uint32_t ones_s = base + STAGES * STAGE_BYTES;
+  auto* sh = reinterpret_cast<WgShared*>(gbase + STAGES * STAGE_BYTES + ONES_BYTES);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
+  {  // the bias tiles' B operand: row 0 = 64 bf16 ones, rows 1..15 zero
+    uint32_t* ones = reinterpret_cast<uint32_t*>(gbase + STAGES * STAGE_BYTES);
+    for (int i = threadIdx.x; i < static_cast<int>(ONES_BYTES / 4); i += blockDim.x)
+      ones[i] = i < 32 ? 0x3F803F80u : 0u;
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  }
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(smem_u32(&sh->full[s]), 1);
@@ -105,17 +152,15 @@ wgrad_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_constant__ 
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = sh->tmem_base;
-  const int per_expert = args.m_tiles * args.n_tiles;
-  const int total = args.num_experts * per_expert;
+  const int total = args.num_experts * args.m_tiles * (args.n_tiles + (args.bias_out ? 1 : 0));
 
   if (warp == 0) {
     if (lane == 0) {
       int it = 0;
       for (int tile = blockIdx.x; tile < total; tile += gridDim.x) {
-        const int e = tile / per_expert, mn = tile - e * per_expert;
-        const int m = mn / args.n_tiles, n = mn - m * args.n_tiles;
+        const Work w = work_of(args, tile);
         int kb0, nk;
-        seg_blocks(args, e, kb0, nk);
+        seg_blocks(args, w.e, kb0, nk);
         bool ok = true;
         for (int kb = 0; kb < nk; ++kb, ++it) {
           const int s = it % STAGES;
@@ -127,9 +172,16 @@ wgrad_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_constant__ 
           }
           if (aborted(sh)) { ok = false; break; }
           const uint32_t fb = smem_u32(&sh->full[s]);
-          mbar_arrive_expect_tx(fb, STAGE_BYTES);
-          tma_load_2d(a_s + s * A_BYTES, &a_map, fb, (kb0 + kb) * BK, m * kTileM);
-          tma_load_2d(b_s + s * B_BYTES, &b_map, fb, (kb0 + kb) * BK, n * BN);
+          const int row = (kb0 + kb) * BK;
+          mbar_arrive_expect_tx(fb, w.bias ? A_BYTES : STAGE_BYTES);
+#pragma unroll
+          for (int j = 0; j < 2; ++j)
+            tma_load_2d(a_s + s * A_BYTES + j * CHUNK_BYTES, &a_map, fb, w.m * kTileM + 64 * j, row);
+          if (!w.bias) {
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+              tma_load_2d(b_s + s * B_BYTES + j * CHUNK_BYTES, &b_map, fb, w.n * BN + 64 * j, row);
+          }
           *reinterpret_cast<volatile int*>(&sh->issued) = it + 1;
         }
         if (!ok) break;
@@ -139,9 +191,9 @@ wgrad_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_constant__ 
     if (lane == 0) {
       int it = 0, local = 0;
       for (int tile = blockIdx.x; tile < total; tile += gridDim.x, ++local) {
-        const int e = tile / per_expert;
+        const Work w = work_of(args, tile);
         int kb0, nk;
-        seg_blocks(args, e, kb0, nk);
+        seg_blocks(args, w.e, kb0, nk);
         const int acc = local & 1;
         const uint32_t aph = (local >> 1) & 1;
         if (!mbar_wait(smem_u32(&sh->tempty[acc]), aph ^ 1)) {
@@ -162,9 +214,15 @@ wgrad_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_constant__ 
           tc_fence_after();
           const uint32_t a_addr = a_s + s * A_BYTES, b_addr = b_s + s * B_BYTES;
 #pragma unroll
-          for (int k = 0; k < BK / 16; ++k)
-            umma_bf16(d_tmem, umma_desc_sw128(a_addr + k * 32), umma_desc_sw128(b_addr + k * 32),
-                      IDESC, (kb | k) != 0 ? 1u : 0u);
+          for (int k = 0; k < BK / 16; ++k) {
+            const uint32_t accum = (kb | k) != 0 ? 1u : 0u;
+            // 16 K rows = two 8-row groups further on
+            const uint64_t a_desc = desc_mn_sw128(a_addr + k * 2048);
+            if (w.bias)
+              umma_bf16(d_tmem, a_desc, umma_desc_sw128(ones_s + k * 32), IDESC_BIAS, accum);
+            else
+              umma_bf16(d_tmem, a_desc, desc_mn_sw128(b_addr + k * 2048), IDESC, accum);
+          }
           umma_commit(smem_u32(&sh->empty[s]));
           *reinterpret_cast<volatile int*>(&sh->consumed) = it + 1;
         }
@@ -179,8 +237,7 @@ wgrad_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_constant__ 
     const int q = warp & 3;
     int local = 0;
     for (int tile = blockIdx.x; tile < total; tile += gridDim.x, ++local) {
-      const int e = tile / per_expert, mn = tile - e * per_expert;
-      const int m = mn / args.n_tiles, n = mn - m * args.n_tiles;
+      const Work w = work_of(args, tile);
       const int acc = local & 1;
       const uint32_t aph = (local >> 1) & 1;
       const bool got = mbar_wait(smem_u32(&sh->tfull[acc]), aph);
@@ -191,41 +248,52 @@ wgrad_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_constant__ 
       }
       tc_fence_after();
       int kb0, nk;
-      seg_blocks(args, e, kb0, nk);
-      const int mrow = m * kTileM + q * 32 + lane;  // row of this expert's M dimension
+      seg_blocks(args, w.e, kb0, nk);
+      const int mrow = w.m * kTileM + q * 32 + lane;  // row of this expert's M dimension
       // destination row: plain, or the gate|up de-interleave of the packed 2*Ipad rows
-      float* dst = nullptr;
-      if (args.mode == 0) {
-        if (mrow < args.m_valid)
-          dst = args.out + static_cast<int64_t>(e) * args.out_expert_stride +
-                static_cast<int64_t>(mrow) * args.ld_out;
-      } else {
-        const int which = (mrow / 128) & 1, i = (mrow / 256) * 128 + (mrow & 127);
-        if (i < args.m_valid)
-          dst = (which ? args.out2 : args.out) + static_cast<int64_t>(e) * args.out_expert_stride +
-                static_cast<int64_t>(i) * args.ld_out;
+      int which = 0, i = mrow;
+      if (args.mode == 1) {
+        which = (mrow / 128) & 1;
+        i = (mrow / 256) * 128 + (mrow & 127);
       }
+      const bool row_ok = i < args.m_valid;
       const uint32_t t_row = tmem + (static_cast<uint32_t>(q * 32) << 16) + acc * BN;
-#pragma unroll 1
-      for (int c = 0; c < BN; c += 32) {
-        float v[32];
+      if (w.bias) {
+        float v[16];
         if (nk > 0) {
-          tmem_ld32(t_row + c, v);
+          tmem_ld16(t_row, v);
         } else {
-#pragma unroll
-          for (int j = 0; j < 32; ++j) v[j] = 0.f;
+          v[0] = 0.f;
         }
-        const int col = n * BN + c;
-        if (dst) {
-          if (col + 32 <= args.n_valid && args.vec_ok) {
-            float4* d4 = reinterpret_cast<float4*>(dst + col);
-#pragma unroll
-            for (int j = 0; j < 8; ++j)
-              d4[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+        if (row_ok)
+          ((which && args.bias_out2) ? args.bias_out2 : args.bias_out)
+              [static_cast<int64_t>(w.e) * args.m_valid + i] = v[0];
+      } else {
+        float* dst = nullptr;
+        if (row_ok)
+          dst = (which ? args.out2 : args.out) + static_cast<int64_t>(w.e) * args.out_expert_stride +
+                static_cast<int64_t>(i) * args.ld_out;
+#pragma unroll 1
+        for (int c = 0; c < BN; c += 32) {
+          float v[32];
+          if (nk > 0) {
+            tmem_ld32(t_row + c, v);
           } else {
 #pragma unroll
-            for (int j = 0; j < 32; ++j)
-              if (col + j < args.n_valid) dst[col + j] = v[j];
+            for (int j = 0; j < 32; ++j) v[j] = 0.f;
+          }
+          const int col = w.n * BN + c;
+          if (dst) {
+            if (col + 32 <= args.n_valid && args.vec_ok) {
+              float4* d4 = reinterpret_cast<float4*>(dst + col);
+#pragma unroll
+              for (int j = 0; j < 8; ++j)
+                d4[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+            } else {
+#pragma unroll
+              for (int j = 0; j < 32; ++j)
+                if (col + j < args.n_valid) dst[col + j] = v[j];
+            }
           }
         }
       }
@@ -259,10 +327,12 @@ wgrad_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_constant__ 
 cudaError_t launch_wgrad(const CUtensorMap& a_map, const CUtensorMap& b_map, const WgradArgs& args,
                          int num_sms, cudaStream_t s) {
   if (args.mode == 1 && !args.out2) return cudaErrorInvalidValue;
+  if (args.mode == 1 && args.bias_out && !args.bias_out2) return cudaErrorInvalidValue;
   cudaError_t err = cudaFuncSetAttribute(wgrad_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(SMEM_BYTES));
   if (err != cudaSuccess) return err;
-  const int64_t work = static_cast<int64_t>(args.num_experts) * args.m_tiles * args.n_tiles;
+  const int64_t work = static_cast<int64_t>(args.num_experts) * args.m_tiles *
+                       (args.n_tiles + (args.bias_out ? 1 : 0));
   const int grid = static_cast<int>(work < num_sms ? (work > 0 ? work : 1) : num_sms);
   wgrad_kernel<<<grid, 192, SMEM_BYTES, s>>>(a_map, b_map, args);
   return cudaGetLastError();

@@ -148,10 +148,12 @@ cudaError_t launch_tc_router(const CUtensorMap& x_map, const CUtensorMap& w_map,
 // ---- backward --------------------------------------------------------------------------
 // Grouped weight gradient: for e < num_experts, dW_e = A_e^T B_e over the rows of e's
 // segment [seg_offs[e], seg_offs[e+1]) (multiples of 64; seg_offs null: one segment of
-// seg_rows_host rows).  a_map: A^T [M_total, rows_total] (box 64 x 128), b_map: B^T
-// [N_total, rows_total] (box 64 x 256).  mode 0 writes out[e][m][n] for m < m_valid,
-// n < n_valid; mode 1 de-interleaves the packed gate|up rows m of 2*Ipad into
-// out (gate) / out2 (up) [e][i][n], i < m_valid.
+// seg_rows_host rows), rows_total bounding both.  A [rows, M_total] and B [rows, N_total]
+// stay row-major: a_map / b_map are their bf16 tensor maps with 64 x 64 boxes, read
+// MN-major by the MMA.  mode 0 writes out[e][m][n] for m < m_valid, n < n_valid; mode 1
+// de-interleaves the packed gate|up rows m of 2*Ipad into out (gate) / out2 (up) [e][i][n],
+// i < m_valid.  With bias_out, also the column sums of A over the segment (the bias
+// gradient) into bias_out (/ bias_out2 in mode 1) [e][i].
 struct WgradArgs {
   const int* seg_offs;
   int seg_rows_host;
@@ -165,6 +167,8 @@ struct WgradArgs {
   int64_t out_expert_stride;
   int mode;
   bool vec_ok;              // out / out2 16-byte aligned and ld_out % 4 == 0
+  float* bias_out;
+  float* bias_out2;
   int* status;
 };
 cudaError_t launch_wgrad(const CUtensorMap& a_map, const CUtensorMap& b_map, const WgradArgs& args,

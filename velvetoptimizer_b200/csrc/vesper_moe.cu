@@ -29,10 +29,10 @@ namespace {
 constexpr int kStages = 7;
 const char* const kStageNames[kStages] = {"router", "scan", "plan", "dispatch",
                                           "gemm1_gate_up_era", "gemm2_down", "combine"};
-constexpr int kBwdStages = 10;
+constexpr int kBwdStages = 9;
 const char* const kBwdStageNames[kBwdStages] = {
     "combine_bwd", "router_bwd", "dh_glu_bwd_gemm", "dx_gemm", "router_dx_gemm", "dx_gather",
-    "transposes", "wgrad_down", "wgrad_gate_up", "wgrad_router_and_biases"};
+    "wgrad_down", "wgrad_gate_up", "wgrad_router"};
 constexpr int kGateUpInterleave = 128;  // rows of gate (then up) per 256-row B tile
 constexpr int kDownTileN = 256;         // N tile of the down projection
 
@@ -1668,9 +1668,8 @@ TrainPlan make_train_plan(const vmoe_handle* h, int64_t T) {
 
 // Scratch of vmoe_backward.
 struct BwdPlan {
-  int64_t Tpad = 0, Mr = 0;  // tokens padded to 128; rows of the dW_r M dimension
-  size_t dy, dyT, hT, dgu, dguT, xpT, dxr, dw, dl, dl_bf, dlT, xT, dxrt, dl_bs, dy_cs, dgu_cs,
-      total;
+  int64_t Tpad = 0;  // tokens padded to 128
+  size_t dy, dgu, dxr, dw, dl, dl_bf, dxrt, dl_bs, total;
 };
 
 BwdPlan make_bwd_plan(const vmoe_handle* h, int64_t T, const Plan& p) {
@@ -1684,23 +1683,14 @@ BwdPlan make_bwd_plan(const vmoe_handle* h, int64_t T, const Plan& p) {
   const size_t R = static_cast<size_t>(p.max_rows);
   const size_t Hp = h->Hpad, Ip = h->Ipad;
   b.Tpad = round_up(T > 0 ? T : 1, kTileM);
-  b.Mr = round_up(h->E, kTileM);
   b.dy = take(R * Hp * 2);
-  b.dyT = take(Hp * R * 2);
-  b.hT = take(Ip * R * 2);
   b.dgu = take(R * 2 * Ip * 2);
-  b.dguT = take(2 * Ip * R * 2);
-  b.xpT = take(Hp * R * 2);
   b.dxr = take(R * Hp * 2);
   b.dw = take(static_cast<size_t>(T) * h->K * 4);
   b.dl = take(static_cast<size_t>(T) * h->E * 4);
   b.dl_bf = take(static_cast<size_t>(b.Tpad) * h->Epad64 * 2);
-  b.dlT = take(static_cast<size_t>(b.Mr) * b.Tpad * 2);
-  b.xT = take(Hp * b.Tpad * 2);
   b.dxrt = take(static_cast<size_t>(b.Tpad) * Hp * 2);
   b.dl_bs = take(static_cast<size_t>((T + 127) / 128) * h->E * 4);
-  b.dy_cs = take((R / 64) * Hp * 4);
-  b.dgu_cs = take((R / 64) * 2 * Ip * 4);
   b.total = off;
   return b;
 }
@@ -1945,29 +1935,16 @@ int vmoe_backward(vmoe_handle* h, const void* x, const void* dout, int64_t token
   if ((rc = check(launch_gather_dx(sc + b.dxr, Hp, sc + b.dxrt, Hp, idx, slot, T,
                                    static_cast<int>(H), static_cast<int>(K), dx, s), "dx gather")) != VMOE_OK)
     return rc;
-  // 7. K-contiguous operands of the weight gradients (+ bias column sums)
+  // 7. weight and bias gradients (fp32, straight into the caller's layout), operands read
+  //    MN-major from their row-major activation buffers
   mark();
-  if ((rc = check(launch_transpose_bf16(sc + b.dy, R, Hp, Hp, 0, 1, sc + b.dyT, Hp, R, 0,
-                                        reinterpret_cast<float*>(sc + b.dy_cs), s), "dy^T")) != VMOE_OK ||
-      (rc = check(launch_transpose_bf16(ws + p.h, R, Ip, Ip, 0, 1, sc + b.hT, Ip, R, 0, nullptr, s),
-                  "h^T")) != VMOE_OK ||
-      (rc = check(launch_transpose_bf16(sc + b.dgu, R, 2 * Ip, 2 * Ip, 0, 1, sc + b.dguT, 2 * Ip, R, 0,
-                                        reinterpret_cast<float*>(sc + b.dgu_cs), s), "dgu^T")) != VMOE_OK ||
-      (rc = check(launch_transpose_bf16(ws + p.xp, R, H, H, 0, 1, sc + b.xpT, Hp, R, 0, nullptr, s),
-                  "x_perm^T")) != VMOE_OK ||
-      (rc = check(launch_transpose_bf16(x, T, H, H, 0, 1, sc + b.xT, Hp, b.Tpad, 0, nullptr, s),
-                  "x^T")) != VMOE_OK ||
-      (rc = check(launch_transpose_bf16(sc + b.dl_bf, T, h->Epad64, h->Epad64, 0, 1, sc + b.dlT,
-                                        b.Mr, b.Tpad, 0, nullptr, s), "dlogits^T")) != VMOE_OK)
-    return rc;
-  // 8. weight gradients (fp32, straight into the caller's layout)
-  CUtensorMap m_dyT, m_hT, m_dguT, m_xpT, m_xT, m_dlT;
-  if (!make_tmap_bf16(&m_dyT, sc + b.dyT, Hp, R, R, kTileM, why, sizeof(why)) ||
-      !make_tmap_bf16(&m_hT, sc + b.hT, Ip, R, R, 256, why, sizeof(why)) ||
-      !make_tmap_bf16(&m_dguT, sc + b.dguT, 2 * Ip, R, R, kTileM, why, sizeof(why)) ||
-      !make_tmap_bf16(&m_xpT, sc + b.xpT, Hp, R, R, 256, why, sizeof(why)) ||
-      !make_tmap_bf16(&m_xT, sc + b.xT, Hp, b.Tpad, b.Tpad, 256, why, sizeof(why)) ||
-      !make_tmap_bf16(&m_dlT, sc + b.dlT, b.Mr, b.Tpad, b.Tpad, kTileM, why, sizeof(why)))
+  CUtensorMap m_dyr, m_hr, m_dgur, m_xpr, m_xr, m_dlr;
+  if (!make_tmap_bf16(&m_dyr, sc + b.dy, R, Hp, Hp, 64, why, sizeof(why)) ||
+      !make_tmap_bf16(&m_hr, ws + p.h, R, Ip, Ip, 64, why, sizeof(why)) ||
+      !make_tmap_bf16(&m_dgur, sc + b.dgu, R, 2 * Ip, 2 * Ip, 64, why, sizeof(why)) ||
+      !make_tmap_bf16(&m_xpr, ws + p.xp, R, H, H, 64, why, sizeof(why)) ||
+      !make_tmap_bf16(&m_xr, x, T, H, H, 64, why, sizeof(why)) ||
+      !make_tmap_bf16(&m_dlr, sc + b.dl_bf, T, h->Epad64, h->Epad64, 64, why, sizeof(why)))
     return fail(h, VMOE_ERR_CUDA, "weight-gradient tensor maps: %s", why);
   auto aligned = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15u) == 0; };
   WgradArgs wd{};
@@ -1983,9 +1960,9 @@ int vmoe_backward(vmoe_handle* h, const void* x, const void* dout, int64_t token
   wd.out_expert_stride = H * I;
   wd.mode = 0;
   wd.vec_ok = (I % 4 == 0) && aligned(grads->down_w);
+  wd.bias_out = grads->down_b;
   wd.status = h->status;
-  mark();
-  if ((rc = check(launch_wgrad(m_dyT, m_hT, wd, h->num_sms, s), "dW_down")) != VMOE_OK) return rc;
+  if ((rc = check(launch_wgrad(m_dyr, m_hr, wd, h->num_sms, s), "dW_down")) != VMOE_OK) return rc;
   mark();
   WgradArgs wg = wd;
   wg.m_tiles = static_cast<int>(2 * Ip / kTileM);
@@ -1998,14 +1975,16 @@ int vmoe_backward(vmoe_handle* h, const void* x, const void* dout, int64_t token
   wg.out_expert_stride = I * H;
   wg.mode = 1;
   wg.vec_ok = (H % 4 == 0) && aligned(grads->gate_w) && aligned(grads->up_w);
-  if ((rc = check(launch_wgrad(m_dguT, m_xpT, wg, h->num_sms, s), "dW_gate_up")) != VMOE_OK) return rc;
+  wg.bias_out = grads->gate_b;
+  wg.bias_out2 = grads->up_b;
+  if ((rc = check(launch_wgrad(m_dgur, m_xpr, wg, h->num_sms, s), "dW_gate_up")) != VMOE_OK) return rc;
   mark();
   WgradArgs wr{};
   wr.seg_offs = nullptr;
   wr.seg_rows_host = static_cast<int>(b.Tpad);
   wr.rows_total = static_cast<int>(b.Tpad);
   wr.num_experts = 1;
-  wr.m_tiles = static_cast<int>(b.Mr / kTileM);
+  wr.m_tiles = static_cast<int>((h->Epad64 + kTileM - 1) / kTileM);
   wr.n_tiles = static_cast<int>(Hp / 256);
   wr.m_valid = static_cast<int>(E);
   wr.n_valid = static_cast<int>(H);
@@ -2015,16 +1994,9 @@ int vmoe_backward(vmoe_handle* h, const void* x, const void* dout, int64_t token
   wr.mode = 0;
   wr.vec_ok = (H % 4 == 0) && aligned(grads->router_w);
   wr.status = h->status;
-  if ((rc = check(launch_wgrad(m_dlT, m_xT, wr, h->num_sms, s), "dW_router")) != VMOE_OK) return rc;
-  // 9. bias gradients: per-expert sums of the 64-row block column sums
-  if ((rc = check(launch_segment_sum(reinterpret_cast<const float*>(sc + b.dy_cs), Hp, offs,
-                                     static_cast<int>(E), static_cast<int>(Hp), 64, grads->down_b,
-                                     nullptr, static_cast<int>(H), false, s), "db_down")) != VMOE_OK ||
-      (rc = check(launch_segment_sum(reinterpret_cast<const float*>(sc + b.dgu_cs), 2 * Ip, offs,
-                                     static_cast<int>(E), static_cast<int>(2 * Ip), 64,
-                                     grads->gate_b, grads->up_b, static_cast<int>(I), true, s),
-                  "db_gate_up")) != VMOE_OK ||
-      (rc = check(launch_segment_sum(reinterpret_cast<const float*>(sc + b.dl_bs), E, nullptr,
+  if ((rc = check(launch_wgrad(m_dlr, m_xr, wr, h->num_sms, s), "dW_router")) != VMOE_OK) return rc;
+  // the router bias: per-block sums of dlogits, added in block order
+  if ((rc = check(launch_segment_sum(reinterpret_cast<const float*>(sc + b.dl_bs), E, nullptr,
                                      static_cast<int>((T + 127) / 128), static_cast<int>(E), 128,
                                      grads->router_b, nullptr, static_cast<int>(E), false, s),
                   "db_router")) != VMOE_OK)
