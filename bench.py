@@ -44,6 +44,9 @@ WORKLOADS = {
     "c4_skewed": dict(tokens=32768, batch=8, hidden=2048, inter=1024, experts=64, top_k=8,
                       lora_on=True, zipf_alpha=1.2),
     "c2_decode": dict(tokens=64, batch=64, hidden=2048, inter=8192, experts=8, top_k=2),
+    # the per-expert shape of c5_ep (4,096 rows per expert, d_model 4096, d_ff 2048) on 8
+    # experts: small enough (a few GB on the device) for full profiler captures
+    "c5_profile_e8": dict(tokens=16384, batch=4, hidden=4096, inter=2048, experts=8, top_k=2),
 }
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
 

@@ -178,3 +178,20 @@ def test_module_autograd_against_oracle():
     assert not bad, (bad, errs)
     assert m.experts[0].gate_proj.proj_a.grad is None  # a buffer
     m.close()
+
+
+def test_pair_and_single_cta_weight_gradients_agree(monkeypatch):
+    """The CTA-pair weight-gradient GEMM (default) against the single-CTA one."""
+    case = CASES["e8k2_lora_bias"]
+    p = bf16_inputs(make_inputs(case))
+    dout, daux = backward_inputs(case)
+    dout = round_bf16(dout)
+    layer = AbiLayer(case, p, "bf16")
+    monkeypatch.setenv("VMOE_PAIR_WGRAD", "0")
+    single = train_step(layer, p["x"], dout, daux)
+    monkeypatch.setenv("VMOE_PAIR_WGRAD", "1")
+    pair = train_step(layer, p["x"], dout, daux)
+    for k in GRAD_KEYS:
+        assert O.norm_rel_err(pair[k], single[k]) < 1e-6, k
+    assert np.array_equal(pair["dx"], single["dx"])
+    layer.close()

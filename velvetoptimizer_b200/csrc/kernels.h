@@ -173,6 +173,9 @@ struct WgradArgs {
 };
 cudaError_t launch_wgrad(const CUtensorMap& a_map, const CUtensorMap& b_map, const WgradArgs& args,
                          int num_sms, cudaStream_t s);
+// The same on CTA pairs: m_tiles counts 256-row M tiles (M_total padded to 256).
+cudaError_t launch_wgrad_pair(const CUtensorMap& a_map, const CUtensorMap& b_map,
+                              const WgradArgs& args, int num_sms, cudaStream_t s);
 
 // Batched 2-D transpose of bf16: dst[b][c][r] = src[b][r][c] for r < rows, c < cols, zero in
 // the padding of dst ([batch][dst_rows][dst_cols], dst_rows >= cols, dst_cols >= rows).  With

@@ -1962,7 +1962,19 @@ int vmoe_backward(vmoe_handle* h, const void* x, const void* dout, int64_t token
   wd.vec_ok = (I % 4 == 0) && aligned(grads->down_w);
   wd.bias_out = grads->down_b;
   wd.status = h->status;
-  if ((rc = check(launch_wgrad(m_dyr, m_hr, wd, h->num_sms, s), "dW_down")) != VMOE_OK) return rc;
+  // single-CTA weight gradients; VMOE_PAIR_WGRAD=1 selects the CTA-pair kernel (M tiles of
+  // 256), which measured slower here: with both operands read MN-major the tensor pipe,
+  // not the operand traffic the pair halves, is the limit
+  const char* pw = getenv("VMOE_PAIR_WGRAD");
+  const bool pair_wgrad = pw && pw[0] == '1';
+  auto wgrad = [&](const CUtensorMap& a, const CUtensorMap& bm, WgradArgs wa) {
+    if (pair_wgrad) {
+      wa.m_tiles = (wa.m_tiles + 1) / 2;  // 128-row tiles -> 256-row pair tiles
+      return launch_wgrad_pair(a, bm, wa, h->num_sms, s);
+    }
+    return launch_wgrad(a, bm, wa, h->num_sms, s);
+  };
+  if ((rc = check(wgrad(m_dyr, m_hr, wd), "dW_down")) != VMOE_OK) return rc;
   mark();
   WgradArgs wg = wd;
   wg.m_tiles = static_cast<int>(2 * Ip / kTileM);
@@ -1977,7 +1989,7 @@ int vmoe_backward(vmoe_handle* h, const void* x, const void* dout, int64_t token
   wg.vec_ok = (H % 4 == 0) && aligned(grads->gate_w) && aligned(grads->up_w);
   wg.bias_out = grads->gate_b;
   wg.bias_out2 = grads->up_b;
-  if ((rc = check(launch_wgrad(m_dgur, m_xpr, wg, h->num_sms, s), "dW_gate_up")) != VMOE_OK) return rc;
+  if ((rc = check(wgrad(m_dgur, m_xpr, wg), "dW_gate_up")) != VMOE_OK) return rc;
   mark();
   WgradArgs wr{};
   wr.seg_offs = nullptr;
@@ -1994,7 +2006,7 @@ int vmoe_backward(vmoe_handle* h, const void* x, const void* dout, int64_t token
   wr.mode = 0;
   wr.vec_ok = (H % 4 == 0) && aligned(grads->router_w);
   wr.status = h->status;
-  if ((rc = check(launch_wgrad(m_dlr, m_xr, wr, h->num_sms, s), "dW_router")) != VMOE_OK) return rc;
+  if ((rc = check(wgrad(m_dlr, m_xr, wr), "dW_router")) != VMOE_OK) return rc;
   // the router bias: per-block sums of dlogits, added in block order
   if ((rc = check(launch_segment_sum(reinterpret_cast<const float*>(sc + b.dl_bs), E, nullptr,
                                      static_cast<int>((T + 127) / 128), static_cast<int>(E), 128,
