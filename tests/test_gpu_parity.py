@@ -227,6 +227,7 @@ def _load_module(case, inp, dtype):
     return m.cuda()
 
 
+@torch.no_grad()
 def test_module_fp32_matches_reference_c1():
     case, g = load_golden("c1_fp32")
     inp = make_inputs(case)
@@ -247,6 +248,7 @@ def test_module_fp32_matches_reference_c1():
     m.close()
 
 
+@torch.no_grad()
 def test_module_bf16_lora_matches_oracle():
     case = BF16_CASES["lora_zipf_e32k8"]
     inp = make_inputs(case)
