@@ -50,6 +50,13 @@ WORKLOADS = {
 }
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
 
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one launch of the gate|up
+# GEMM, measured with ncu on the 8-expert slice of the c5_ep layer (c5_profile_e8: the same
+# 4,096 rows per expert, d_model 4096, d_ff 2048) and scaled to the 64-expert launch by 8
+GEMM1_TRAFFIC = {"c5_ep": {"bytes": 8 * 806_619_392,
+                           "source": "ncu dram bytes of the 8-expert slice (c5_profile_e8) x 8"},
+                 "c5_profile_e8": {"bytes": 806_619_392, "source": "ncu dram bytes"}}
+
 
 def parse_args():
     p = argparse.ArgumentParser()
@@ -465,7 +472,11 @@ def run_ours(args, rank, world, local_rank):
                      "bound": "tensor", "achieved": round(achieved, 1),
                      "peak": pk["bf16_tflops"], "peak_source": pk["source"] + " bf16 burst",
                      "unit": "TFLOP/s", "frac": round(achieved / pk["bf16_tflops"], 4),
-                     "traffic": None, "flop_per_launch": roof_flop,
+                     "traffic": (GEMM1_TRAFFIC[args.workload]["bytes"]
+                                 if world == 1 and args.workload in GEMM1_TRAFFIC else None),
+                     "traffic_source": (GEMM1_TRAFFIC[args.workload]["source"]
+                                        if world == 1 and args.workload in GEMM1_TRAFFIC else None),
+                     "flop_per_launch": roof_flop,
                      "avg_launch_ms": round(g1, 4), "launches_timed": nprof},
         "stages": stage_report,
         "gpu_launches": launches,
