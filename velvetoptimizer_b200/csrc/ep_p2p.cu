@@ -21,6 +21,11 @@
 //   combine  : each token reads its K expert rows from the owners' y (NVLink loads) and
 //              sums them in ascending expert order in fp32 -- the single-GPU arithmetic,
 //              so outputs are bit-identical to the one-GPU forward.
+// Push mode (bf16 with the CTA-pair GEMMs): the dispatch also writes every row's return
+// address (epoch, source rank, t*K + k) into the owner's `ret`; the down GEMM's epilogue
+// stores each output row straight into its source rank's return buffer `back` over NVLink,
+// tile by tile while the GEMM runs (the GEMM -> exchange step is one kernel), and the
+// combine reads the token's rows from local memory in the same order.
 // Flags hold the forward's epoch (monotonic), so nothing is reset between forwards; the
 // stream order of the stages on every rank rules out reuse races (a rank republishes its
 // counts only after its combine, which waited for every peer's experts, which waited for
@@ -166,6 +171,12 @@ p2p_dispatch_kernel(P2PArgs a, const T* __restrict__ x, const int32_t* __restric
     if (t < T_tok) {  // -1 also when the wait gave up: the combine then skips the row
       a.dest_rank[t * K + k] = d;
       a.dest_row[t * K + k] = row;
+      if (a.push && d >= 0) {
+        // the row's return address in the owner's memory: where its expert output goes
+        const int64_t j = t * K + k;
+        reinterpret_cast<int64_t*>(a.peer_base[d] + a.ret_off)[row] =
+            (static_cast<int64_t>(a.epoch) << 32) | (static_cast<int64_t>(a.me) << 24) | j;
+      }
     }
     slot_rank[tid * K + k] = d;
     slot_row[tid * K + k] = row;
@@ -255,7 +266,69 @@ p2p_combine_kernel(P2PArgs a, const int32_t* __restrict__ topk_idx, const float*
   }
 }
 
+// push mode: the K rows of every token are already in this rank's return buffer
+template <typename T>
+__global__ void __launch_bounds__(256)
+p2p_combine_local_kernel(P2PArgs a, const int32_t* __restrict__ topk_idx,
+                         const float* __restrict__ topk_w, int64_t T_tok, T* __restrict__ out) {
+  const int lane = threadIdx.x & 31;
+  const int64_t t = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
+  if (t >= T_tok) return;
+  const int K = a.K;
+  int ord_e[32], ord_j[32];
+  float ord_w[32];
+  int n = 0;
+  for (int k = 0; k < K; ++k) {
+    const int e = topk_idx[t * K + k];
+    const int d = a.dest_rank[t * K + k];
+    const int jrow = (d >= 0 && d < a.G && t * K + k < a.back_rows) ? static_cast<int>(t * K + k) : -1;
+    const float w = topk_w[t * K + k];
+    int j = n++;
+    while (j > 0 && ord_e[j - 1] > e) {
+      ord_e[j] = ord_e[j - 1]; ord_j[j] = ord_j[j - 1]; ord_w[j] = ord_w[j - 1];
+      --j;
+    }
+    ord_e[j] = e; ord_j[j] = jrow; ord_w[j] = w;
+  }
+  constexpr int V = Vec16<T>::N;
+  const int nvec = static_cast<int>(a.H / V);
+  const T* back = reinterpret_cast<const T*>(a.peer_base[a.me] + a.back_off);
+  T* orow = out + t * a.H;
+  for (int v = lane; v < nvec; v += 32) {
+    float acc[V];
+#pragma unroll
+    for (int i = 0; i < V; ++i) acc[i] = 0.f;
+    for (int j = 0; j < n; ++j) {
+      if (ord_j[j] < 0) continue;
+      float f[V];
+      load16_to_f(back + static_cast<int64_t>(ord_j[j]) * a.H + v * V, f);
+      const float w = ord_w[j];
+#pragma unroll
+      for (int i = 0; i < V; ++i) acc[i] = __fadd_rn(acc[i], __fmul_rn(f[i], w));
+    }
+    store16_from_f(orow + v * V, acc);
+  }
+}
+
 }  // namespace
+
+cudaError_t launch_p2p_combine_local(int dtype, const P2PArgs& a, const int32_t* topk_idx,
+                                     const float* topk_w, int64_t T, void* out, size_t min_smem,
+                                     cudaStream_t s) {
+  if (T == 0) return cudaSuccess;
+  if (!a.push) return cudaErrorInvalidValue;
+  const unsigned grid = static_cast<unsigned>((T + 7) / 8);
+  if (dtype == kF32) {
+    auto kern = p2p_combine_local_kernel<float>;
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(min_smem));
+    kern<<<grid, 256, min_smem, s>>>(a, topk_idx, topk_w, T, static_cast<float*>(out));
+  } else {
+    auto kern = p2p_combine_local_kernel<__nv_bfloat16>;
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(min_smem));
+    kern<<<grid, 256, min_smem, s>>>(a, topk_idx, topk_w, T, static_cast<__nv_bfloat16*>(out));
+  }
+  return cudaGetLastError();
+}
 
 cudaError_t launch_p2p_publish(const P2PArgs& a, const int* counts, cudaStream_t s) {
   p2p_publish_kernel<<<1, 256, 0, s>>>(a, counts);

@@ -64,7 +64,15 @@ __device__ __forceinline__ int pair_expert_of(const TcGemmArgs& args, int m) {
   return 0;
 }
 
-enum PairEpi { kPairPlain = 0, kPairGated = 1, kPairGluBwd = 2 };
+enum PairEpi { kPairPlain = 0, kPairGated = 1, kPairGluBwd = 2, kPairPush = 3 };
+
+// push epilogue staging: per epilogue warp 32 rows x 64 bf16 columns, 144-byte row pitch
+constexpr int PUSH_PITCH = 72;  // elements
+constexpr uint32_t PUSH_STG_BYTES = 4 * 32 * PUSH_PITCH * 2;
+
+__device__ __forceinline__ void st_peer_v4(char* p, uint4 v) {
+  *reinterpret_cast<uint4*>(p) = v;
+}
 
 template <int EPI>
 __global__ void __launch_bounds__(192, 1)
@@ -77,6 +85,9 @@ tc_gemm_pair_kernel(const __grid_constant__ CUtensorMap a_map,
   const uint32_t a_s = base;
   const uint32_t b_s = base + STAGES * A_BYTES;
   PairShared* sh = reinterpret_cast<PairShared*>(gbase + STAGES * STAGE_BYTES);
+  // push staging (kPairPush only) sits after the shared state
+  __nv_bfloat16* push_stg = reinterpret_cast<__nv_bfloat16*>(
+      gbase + ((STAGES * STAGE_BYTES + sizeof(PairShared) + 127) & ~static_cast<size_t>(127)));
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t rank = cluster_ctarank();
@@ -275,6 +286,47 @@ tc_gemm_pair_kernel(const __grid_constant__ CUtensorMap a_map,
             du[v] = make_uint4(pu[4 * v], pu[4 * v + 1], pu[4 * v + 2], pu[4 * v + 3]);
           }
         }
+      } else if constexpr (EPI == kPairPush) {
+        // this thread's row goes back to the rank that sent it (epoch-tagged address)
+        const float* bias = args.bias + static_cast<int64_t>(e) * args.bias_ld + n * BN;
+        const int64_t ret = args.push_ret[row];
+        char* dst = nullptr;
+        if (static_cast<unsigned>(ret >> 32) == args.push_epoch) {
+          const int src = static_cast<int>((ret >> 24) & 0xFF);
+          const int64_t j = ret & 0xFFFFFF;
+          if (src < args.push_G && j < args.push_back_rows)
+            dst = args.push_peers[src] + args.push_back_off +
+                  (j * args.ldo + static_cast<int64_t>(n) * BN) * 2;
+        }
+        __nv_bfloat16* stg = push_stg + q * 32 * PUSH_PITCH;
+#pragma unroll 1
+        for (int c = 0; c < BN; c += 64) {
+          float v[64];
+          tmem_ld32(t_row + c, v);
+          tmem_ld32(t_row + c + 32, v + 32);
+          uint32_t packed[32];
+#pragma unroll
+          for (int j = 0; j < 64; j += 2)
+            packed[j / 2] = pack_bf16x2(v[j] + bias[c + j], v[j + 1] + bias[c + j + 1]);
+          __syncwarp();
+          uint4* srow = reinterpret_cast<uint4*>(stg + lane * PUSH_PITCH);
+#pragma unroll
+          for (int u = 0; u < 8; ++u)
+            srow[u] = make_uint4(packed[4 * u], packed[4 * u + 1], packed[4 * u + 2], packed[4 * u + 3]);
+          __syncwarp();
+          // eight lanes per row: 128 contiguous bytes of one row per group of eight lanes,
+          // four rows per pass, eight passes for the warp's 32 rows
+#pragma unroll
+          for (int rr = 0; rr < 8; ++rr) {
+            const int r = rr * 4 + (lane >> 3), seg = lane & 7;
+            const unsigned long long d =
+                __shfl_sync(0xffffffffu, reinterpret_cast<unsigned long long>(dst), r);
+            if (d) {
+              const uint4 val = reinterpret_cast<const uint4*>(stg + r * PUSH_PITCH)[seg];
+              st_peer_v4(reinterpret_cast<char*>(d) + c * 2 + seg * 16, val);
+            }
+          }
+        }
       } else {
         // plain: + bias (none when args.bias is null)
         const float* bias = args.bias ? args.bias + static_cast<int64_t>(e) * args.bias_ld + n * BN
@@ -303,6 +355,8 @@ tc_gemm_pair_kernel(const __grid_constant__ CUtensorMap a_map,
     }
   }
 
+  // pushed rows must be visible to the peers before the signal that follows this kernel
+  if constexpr (EPI == kPairPush) __threadfence_system();
   __syncthreads();
   if (threadIdx.x == 0 && aborted(sh)) {
     // copies issued by this CTA land on the leader's barriers; give any still in flight a
@@ -326,8 +380,10 @@ template <int EPI>
 cudaError_t launch_pair(const CUtensorMap& a_map, const CUtensorMap& b_map, const TcGemmArgs& args,
                         int64_t max_pair_tiles, int num_sms, cudaStream_t s) {
   auto kern = tc_gemm_pair_kernel<EPI>;
+  constexpr size_t smem_bytes = SMEM_BYTES + (EPI == kPairPush ? PUSH_STG_BYTES + 128 : 0);
+  static_assert(smem_bytes <= 232448, "shared memory budget");
   cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(SMEM_BYTES));
+                                         static_cast<int>(smem_bytes));
   if (err != cudaSuccess) return err;
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attr[1];
@@ -336,7 +392,7 @@ cudaError_t launch_pair(const CUtensorMap& a_map, const CUtensorMap& b_map, cons
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
   cfg.blockDim = dim3(192, 1, 1);
-  cfg.dynamicSmemBytes = SMEM_BYTES;
+  cfg.dynamicSmemBytes = smem_bytes;
   cfg.stream = s;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
@@ -363,6 +419,14 @@ cudaError_t launch_tc_gemm_pair(bool gated, const CUtensorMap& a_map, const CUte
                                 cudaStream_t s) {
   if (gated) return launch_pair<kPairGated>(a_map, b_map, args, max_pair_tiles, num_sms, s);
   return launch_pair<kPairPlain>(a_map, b_map, args, max_pair_tiles, num_sms, s);
+}
+
+cudaError_t launch_tc_gemm_pair_push(const CUtensorMap& a_map, const CUtensorMap& b_map,
+                                     const TcGemmArgs& args, int64_t max_pair_tiles, int num_sms,
+                                     cudaStream_t s) {
+  if (!args.push_ret || !args.push_peers || !args.bias || args.push_G < 1 || args.push_G > 256)
+    return cudaErrorInvalidValue;
+  return launch_pair<kPairPush>(a_map, b_map, args, max_pair_tiles, num_sms, s);
 }
 
 cudaError_t launch_tc_gemm_pair_glu_bwd(const CUtensorMap& a_map, const CUtensorMap& b_map,

@@ -110,6 +110,14 @@ struct TcGemmArgs {
   // GLU backward epilogue (launch_tc_gemm_pair_glu_bwd): reads gu, writes dgu
   const void* gu_in;
   int64_t i_valid;          // columns (of I) that exist: the N tiles may run past Ipad
+  // expert-parallel push epilogue (launch_tc_gemm_pair_push): output row r goes to the
+  // source rank's return buffer named by push_ret[r] (see P2PArgs), not to `out`
+  const int64_t* push_ret;
+  char* const* push_peers;
+  size_t push_back_off;
+  int64_t push_back_rows;
+  int push_G;
+  unsigned push_epoch;
   // LayerNorm router (launch_tc_router with ln): b operand = W_r * ln_w, bias = b_r + W_r ln_b
   float2* ln_stats;         // [T] (mean, rstd) out
   const float* ln_c;        // [E] row sums of the folded weights
@@ -135,6 +143,14 @@ cudaError_t launch_tc_gemm_pair(bool gated, const CUtensorMap& a_map, const CUte
 cudaError_t launch_tc_gemm_pair_glu_bwd(const CUtensorMap& a_map, const CUtensorMap& b_map,
                                         const TcGemmArgs& args, int64_t max_pair_tiles,
                                         int num_sms, cudaStream_t s);
+
+// Plain (bias) epilogue that stores each bf16 output row over NVLink into the source rank's
+// return buffer (args.push_*), staged through shared memory so that eight lanes write each
+// row's 128 contiguous bytes; rows whose return address carries another epoch (segment
+// padding) are skipped.  Every thread fences at system scope before the kernel ends.
+cudaError_t launch_tc_gemm_pair_push(const CUtensorMap& a_map, const CUtensorMap& b_map,
+                                     const TcGemmArgs& args, int64_t max_pair_tiles, int num_sms,
+                                     cudaStream_t s);
 
 // Router on the tensor cores: logits = x W_r^T (+ bias in `args.bias`), softmax, top-K,
 // renormalised weights, per-128-token histogram and probability sums.  E <= 64;
@@ -226,6 +242,14 @@ bool make_tmap_bf16(CUtensorMap* map, const void* base, uint64_t rows, uint64_t 
 struct P2PArgs {
   char* const* peer_base;   // device array [G]: every rank's symmetric region (own included)
   size_t sig_off, counts_off, recv_off, y_off;
+  // push mode (bf16 CTA-pair GEMMs): the down GEMM stores every output row straight into
+  // its source rank's return buffer `back` [back_rows, H] (row t*K + k of that rank's chunk);
+  // the dispatch writes, for every row it sends, an epoch-tagged return address into the
+  // owner's `ret` [cap_rows] int64: epoch << 32 | source rank << 24 | t*K + k
+  bool push;
+  size_t ret_off, back_off;
+  int64_t back_rows;
+  char* peer_base_local;    // host-side copy of this rank's own region base (push setup)
   int me, G, E, El, K;
   int64_t H;
   int64_t cap_rows;         // rows of recv / y
@@ -244,6 +268,10 @@ cudaError_t launch_p2p_signal(const P2PArgs& a, int which, cudaStream_t s);
 cudaError_t launch_p2p_dispatch(int dtype, const P2PArgs& a, const void* x,
                                 const int32_t* topk_idx, const int* excl, int64_t T,
                                 size_t min_smem, cudaStream_t s);
+// Push mode: the combine reads every token's K rows from this rank's own return buffer.
+cudaError_t launch_p2p_combine_local(int dtype, const P2PArgs& a, const int32_t* topk_idx,
+                                     const float* topk_w, int64_t T, void* out, size_t min_smem,
+                                     cudaStream_t s);
 cudaError_t launch_p2p_combine(int dtype, const P2PArgs& a, const int32_t* topk_idx,
                                const float* topk_w, int64_t T, void* out, size_t min_smem,
                                cudaStream_t s);

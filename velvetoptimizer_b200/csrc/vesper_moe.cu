@@ -85,6 +85,10 @@ struct vmoe_handle {
   // chunk; every channel has the same region layout
   std::vector<P2PChannel> p2p;
   size_t p2p_sig_off = 0, p2p_counts_off = 0, p2p_recv_off = 0, p2p_y_off = 0;
+  // push mode: the down GEMM stores outputs into the source ranks' return buffers
+  bool p2p_push = false;
+  size_t p2p_ret_off = 0, p2p_back_off = 0;
+  int64_t p2p_back_rows = 0;
   int64_t p2p_cap_rows = 0, p2p_max_tokens = 0, p2p_chunk_tokens = 0;
   cudaStream_t p2p_streams[kMaxChunks] = {};
   cudaEvent_t p2p_start = nullptr;
@@ -339,7 +343,8 @@ int alloc(vmoe_handle* h, T** p, size_t bytes, const char* what) {
 template <typename Mark, typename Check>
 int run_expert_gemms(vmoe_handle* h, void* xp, int64_t max_rows, const int* tiles,
                      const int* ntiles, void* hb, void* yb, int64_t y_ld, cudaStream_t s,
-                     Mark&& mark, Check&& check, int gemm_sms = 0, void* gu_out = nullptr) {
+                     Mark&& mark, Check&& check, int gemm_sms = 0, void* gu_out = nullptr,
+                     const P2PArgs* push = nullptr) {
   const int sms = gemm_sms > 0 ? gemm_sms : h->num_sms;  // persistent GEMM grid bound
   const int64_t H = h->H, max_tiles = max_rows / h->tile_rows;
   int rc;
@@ -400,6 +405,16 @@ int run_expert_gemms(vmoe_handle* h, void* xp, int64_t max_rows, const int* tile
   a2.bias_ld = h->Hpad;
   a2.gamma = 0.f;
   a2.status = h->status;
+  if (push) {  // outputs straight into the source ranks' return buffers over NVLink
+    a2.push_ret = reinterpret_cast<const int64_t*>(push->peer_base_local + push->ret_off);
+    a2.push_peers = push->peer_base;
+    a2.push_back_off = push->back_off;
+    a2.push_back_rows = push->back_rows;
+    a2.push_G = push->G;
+    a2.push_epoch = push->epoch;
+    a2.ldo = h->H;
+    return check(launch_tc_gemm_pair_push(map_h, h->map_wd, a2, max_tiles, sms, s), "gemm2 push");
+  }
   return check(pair ? launch_tc_gemm_pair(false, map_h, h->map_wd, a2, max_tiles, sms, s)
                     : launch_tc_gemm(false, map_h, h->map_wd, a2, max_tiles, sms, s),
                "gemm2");
@@ -1307,10 +1322,20 @@ int vmoe_ep_p2p_setup(vmoe_handle* h, int64_t max_tokens, int chunks, void* ipc_
     off += (bytes + 255) & ~static_cast<size_t>(255);
     return o;
   };
+  // the bf16 CTA-pair GEMMs push their outputs to the source ranks (VMOE_EP_PUSH=0: pull)
+  const char* pe = getenv("VMOE_EP_PUSH");
+  // (the return address holds a 24-bit row of the source's chunk and an 8-bit rank)
+  h->p2p_push = h->dtype == kBF16 && h->tile_rows == 2 * kTileM && !(pe && pe[0] == '0') &&
+                chunk_tokens * K < (static_cast<int64_t>(1) << 24) && G <= 256;
   h->p2p_sig_off = take(3 * G * 4);
   h->p2p_counts_off = take(G * E * 4);
+  h->p2p_ret_off = h->p2p_push ? take(static_cast<size_t>(cap) * 8) : 0;
   h->p2p_recv_off = take(static_cast<size_t>(cap) * H * dtype_bytes(h->dtype));
-  h->p2p_y_off = take(static_cast<size_t>(cap) * H * dtype_bytes(h->dtype));
+  h->p2p_back_rows = chunk_tokens * K;
+  if (h->p2p_push)
+    h->p2p_back_off = take(static_cast<size_t>(h->p2p_back_rows) * H * dtype_bytes(h->dtype));
+  else
+    h->p2p_y_off = take(static_cast<size_t>(cap) * H * dtype_bytes(h->dtype));
   DeviceGuard g(h->device);
   h->p2p.resize(chunks);
   cudaError_t e = cudaSuccess;
@@ -1425,6 +1450,11 @@ int p2p_chunk(vmoe_handle* h, int c, const void* x, int64_t T, void* out, float*
   a.dest_row = reinterpret_cast<int32_t*>(ws + p.drow);
   a.tile_expert = reinterpret_cast<int*>(ws + p.tiles);
   a.num_tiles = reinterpret_cast<int*>(ws + p.ntiles);
+  a.push = h->p2p_push;
+  a.ret_off = h->p2p_ret_off;
+  a.back_off = h->p2p_back_off;
+  a.back_rows = h->p2p_back_rows;
+  a.peer_base_local = ch.region;
 
   cudaEvent_t* ev = prof ? &h->prof_ev[static_cast<size_t>(h->prof_count) * (kStages + 1)] : nullptr;
   int stage = 0;
@@ -1472,16 +1502,18 @@ int p2p_chunk(vmoe_handle* h, int c, const void* x, int64_t T, void* out, float*
     return cuda_fail(h, e, "gemm order");
   mark();  // gemm1 (inside run_expert_gemms: gemm1, mark, gemm2)
   if ((rc = run_expert_gemms(h, ch.region + h->p2p_recv_off, h->p2p_cap_rows, a.tile_expert,
-                             a.num_tiles, ws + p.hbuf, ch.region + h->p2p_y_off, H, s, mark,
-                             check, gemm_sms)) != VMOE_OK)
+                             a.num_tiles, ws + p.hbuf,
+                             a.push ? nullptr : ch.region + h->p2p_y_off, H, s, mark, check,
+                             gemm_sms, nullptr, a.push ? &a : nullptr)) != VMOE_OK)
     return rc;
   if (chained && (e = cudaEventRecord(h->p2p_gemm_done[c], s)) != cudaSuccess)
     return cuda_fail(h, e, "gemm order");
   mark();  // signal outputs ready, wait for every rank's, combine over NVLink
   if ((rc = check(launch_p2p_signal(a, 2, s), "signal outputs")) != VMOE_OK) return rc;
   if ((rc = check(launch_p2p_wait(a, 2, s), "wait outputs")) != VMOE_OK) return rc;
-  if ((rc = check(launch_p2p_combine(h->dtype, a, idx, tw, T, out, xfer_smem, s), "combine")) !=
-      VMOE_OK)
+  if ((rc = check(a.push ? launch_p2p_combine_local(h->dtype, a, idx, tw, T, out, xfer_smem, s)
+                         : launch_p2p_combine(h->dtype, a, idx, tw, T, out, xfer_smem, s),
+                  "combine")) != VMOE_OK)
     return rc;
   mark();
   return VMOE_OK;
