@@ -78,6 +78,9 @@ def parse_args():
     p.add_argument("--backward", action="store_true",
                    help="time the training step instead: vmoe_forward_train + vmoe_backward "
                         "(dx, router / expert weight and bias gradients) on one GPU")
+    p.add_argument("--ffn", action="store_true",
+                   help="time the dense FeedForward (non-MoE layers) on the same GEMMs at the "
+                        "workload's tokens / d_model / d_ff instead of the MoE layer")
     p.add_argument("--host-chunks", type=int, default=0,
                    help="token chunks of the single-GPU host-buffer forward timed as e2e "
                         "(0 = automatic)")
@@ -609,6 +612,73 @@ def run_backward(args, rank, world, local_rank):
 
 
 # --------------------------------------------------------------------------------------
+# dense FeedForward (python/vesper/model.py:249-270) on the same grouped GEMMs
+# --------------------------------------------------------------------------------------
+def run_ffn(args, rank, world, local_rank):
+    import torch
+
+    from velvetoptimizer_b200 import FeedForward, MoEConfig
+
+    torch.set_grad_enabled(False)
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    w = dict(WORKLOADS[args.workload])
+    T, H, I = w["tokens"], w["hidden"], w["inter"]
+    cfg = MoEConfig(hidden_size=H, intermediate_size=I, flylora_rank=16, flylora_alpha=32.0,
+                    era_gamma=0.1)
+    with torch.device(dev):
+        ffn = FeedForward(cfg)
+    g = torch.Generator(device=dev)
+    g.manual_seed(0)
+    for m in ffn.modules():
+        if isinstance(m, torch.nn.Linear):
+            m.weight.normal_(0.0, 0.02, generator=g)
+            m.bias.zero_()
+    for proj in (ffn.gate_proj, ffn.up_proj):
+        proj.lora_up.weight.zero_()
+    x = torch.randn(T, H, generator=g, device=dev).to(torch.bfloat16).reshape(w["batch"], -1, H)
+    stream = torch.cuda.current_stream(dev)
+    for _ in range(args.warmup):
+        ffn(x)
+    torch.cuda.synchronize()
+    props = torch.cuda.get_device_properties(dev)
+    gpu_id = str(getattr(props, "uuid", "") or local_rank)
+    if gpu_id and not gpu_id.startswith("GPU-") and len(gpu_id) > 8:
+        gpu_id = "GPU-" + gpu_id
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    sampler = ClockSampler(gpu_id)
+    time.sleep(0.3)
+    e0.record(stream)
+    for _ in range(args.steps):
+        ffn(x)
+    e1.record(stream)
+    e1.synchronize()
+    clocks = sampler.stop()
+    ms = e0.elapsed_time(e1) / args.steps
+    pk = peaks()
+    flop = 6.0 * T * H * I
+    achieved = flop / (ms * 1e-3) / 1e12
+    return {
+        "metric": "dense FeedForward fwd tokens/s", "value": round(T / (ms * 1e-3), 1),
+        "unit": "tokens/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic: x~N(0,1), weights~N(0,0.02), zero bias, FlyLoRA off",
+        "config": {"workload": f"{args.workload} shape, dense FeedForward (non-MoE layer): "
+                               f"{T} tokens, d_model {H}, d_ff {I}",
+                   "l2": "inputs larger than L2; no flush"},
+        "e2e": None,
+        "roofline": {"kernel": "gate|up GEMM + down GEMM (whole layer)", "bound": "tensor",
+                     "achieved": round(achieved, 1), "peak": pk["bf16_tflops"],
+                     "peak_source": pk["source"] + " bf16 burst", "unit": "TFLOP/s",
+                     "frac": round(achieved / pk["bf16_tflops"], 4), "traffic": None,
+                     "flop_per_launch": flop},
+        "gpu_launches": 3 * args.steps,
+        "clocks": clocks,
+    }
+
+
+# --------------------------------------------------------------------------------------
 # reference arm: the CPU implementation of the path (the oracle port) on host cores
 # --------------------------------------------------------------------------------------
 def run_reference(args):
@@ -684,10 +754,11 @@ def main():
         torch.cuda.set_device(local_rank)
         dist.init_process_group("nccl", timeout=timedelta(seconds=120),
                                 device_id=torch.device("cuda", local_rank))
-    if args.backward:
+    if args.backward or args.ffn:
         if world > 1:
-            raise SystemExit("--backward runs on one GPU")
-        print(json.dumps(run_backward(args, rank, world, local_rank)), flush=True)
+            raise SystemExit("--backward / --ffn run on one GPU")
+        run = run_backward if args.backward else run_ffn
+        print(json.dumps(run(args, rank, world, local_rank)), flush=True)
         return 0
     try:
         line = run_ours(args, rank, world, local_rank)

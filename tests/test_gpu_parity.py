@@ -331,3 +331,36 @@ def test_ffn_module_matches_reference_golden():
     assert O.norm_rel_err(out.reshape(-1, case.hidden).cpu().numpy(), g["out"]) < FP32_TOL
     m.close()
 
+
+
+def test_ffn_bf16_writes_only_its_rows():
+    """The dense FFN reads x and writes out in place (no padded copies): rows past T of the
+    caller's buffer are untouched and the result matches the oracle."""
+    import ctypes
+    from tests.abi_runner import abi_config, _WEIGHT_KEYS
+    from velvetoptimizer_b200 import _lib
+    case = MoECase(tokens=1000, hidden=512, inter=1024, experts=1, top_k=1, lora_on=True,
+                   bias_std=0.05, seed=43)
+    inp = bf16_inputs(make_inputs(case))
+    dev = torch.device("cuda", 0)
+    h = _lib.Handle(abi_config(case, "bf16"), 0, dense=True)
+    w = {k: torch.from_numpy(np.ascontiguousarray(inp[v])).to(dev, torch.bfloat16)
+         for k, v in _WEIGHT_KEYS.items() if not k.startswith("router")}
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    h.set_weights(_lib.VmoeWeights(**{k: ctypes.c_void_p(t.data_ptr()) for k, t in w.items()}),
+                  stream)
+    T = case.tokens
+    x = torch.from_numpy(inp["x"]).to(dev, torch.bfloat16)
+    out = torch.full((T + 24, case.hidden), 7.0, dtype=torch.bfloat16, device=dev)
+    n = ctypes.c_size_t()
+    _lib.check(h.lib.vmoe_ffn_workspace_size(h.ptr, T, ctypes.byref(n)), h.ptr)
+    ws = torch.empty(n.value, dtype=torch.uint8, device=dev)
+    _lib.check(h.lib.vmoe_ffn_forward(h.ptr, ctypes.c_void_p(x.data_ptr()), T,
+                                      ctypes.c_void_p(out.data_ptr()), ctypes.c_void_p(ws.data_ptr()),
+                                      ws.numel(), ctypes.c_void_p(stream)), h.ptr)
+    torch.cuda.synchronize()
+    assert h.device_status(stream) == 0
+    assert bool((out[T:] == 7.0).all())
+    got = out[:T].float().cpu().numpy()
+    assert O.norm_rel_err(got, O.ffn_forward(inp, case)) < BF16_TOL
+    h.close()

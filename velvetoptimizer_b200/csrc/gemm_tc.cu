@@ -398,10 +398,12 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_constant_
           }
         } else {
           outp += n * BN;
+          const bool store = args.row_limit <= 0 || row < args.row_limit;
 #pragma unroll 1
           for (int c = 0; c < BN; c += 32) {
             float v32[32];
             tmem_ld32(t_row + c, v32);
+            if (!store) continue;
             if (bias) {
 #pragma unroll
               for (int j = 0; j < 32; ++j) v32[j] += bias[c + j];

@@ -110,6 +110,9 @@ struct TcGemmArgs {
   // GLU backward epilogue (launch_tc_gemm_pair_glu_bwd): reads gu, writes dgu
   const void* gu_in;
   int64_t i_valid;          // columns (of I) that exist: the N tiles may run past Ipad
+  // plain epilogue: rows >= row_limit are not stored (0 = no limit), so a GEMM over
+  // tile-padded rows can write straight into a caller's [row_limit, N] output
+  int64_t row_limit;
   // expert-parallel push epilogue (launch_tc_gemm_pair_push): output row r goes to the
   // source rank's return buffer named by push_ret[r] (see P2PArgs), not to `out`
   const int64_t* push_ret;

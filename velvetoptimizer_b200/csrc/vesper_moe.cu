@@ -344,7 +344,7 @@ template <typename Mark, typename Check>
 int run_expert_gemms(vmoe_handle* h, void* xp, int64_t max_rows, const int* tiles,
                      const int* ntiles, void* hb, void* yb, int64_t y_ld, cudaStream_t s,
                      Mark&& mark, Check&& check, int gemm_sms = 0, void* gu_out = nullptr,
-                     const P2PArgs* push = nullptr) {
+                     const P2PArgs* push = nullptr, int64_t a_rows = 0, int64_t out_rows = 0) {
   const int sms = gemm_sms > 0 ? gemm_sms : h->num_sms;  // persistent GEMM grid bound
   const int64_t H = h->H, max_tiles = max_rows / h->tile_rows;
   int rc;
@@ -365,7 +365,8 @@ int run_expert_gemms(vmoe_handle* h, void* xp, int64_t max_rows, const int* tile
   }
   char why[256];
   CUtensorMap map_x, map_h;
-  if (!make_tmap_bf16(&map_x, xp, max_rows, H, H, kTileM, why, sizeof(why)))
+  // a_rows < max_rows: A holds only that many rows (the TMA zero-fills the rest of a tile)
+  if (!make_tmap_bf16(&map_x, xp, a_rows > 0 ? a_rows : max_rows, H, H, kTileM, why, sizeof(why)))
     return fail(h, VMOE_ERR_CUDA, "x_perm tensor map: %s", why);
   if (!make_tmap_bf16(&map_h, hb, max_rows, h->Ipad, h->Ipad, kTileM, why, sizeof(why)))
     return fail(h, VMOE_ERR_CUDA, "h tensor map: %s", why);
@@ -405,6 +406,7 @@ int run_expert_gemms(vmoe_handle* h, void* xp, int64_t max_rows, const int* tile
   a2.bias_ld = h->Hpad;
   a2.gamma = 0.f;
   a2.status = h->status;
+  a2.row_limit = out_rows;  // rows past the caller's output are computed but not stored
   if (push) {  // outputs straight into the source ranks' return buffers over NVLink
     a2.push_ret = reinterpret_cast<const int64_t*>(push->peer_base_local + push->ret_off);
     a2.push_peers = push->peer_base;
@@ -1661,6 +1663,14 @@ int vmoe_ffn_forward(vmoe_handle* h, const void* x, int64_t tokens, void* out, v
   if ((rc = check(launch_fill_tiles(tiles, static_cast<int>(p.max_rows / h->tile_rows), ntiles, s),
                   "tile map")) != VMOE_OK)
     return rc;
+  if (h->dtype == kBF16 && h->Hpad == H &&
+      ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(out)) & 15u) == 0) {
+    // the tensor-core GEMMs read x and write out in place: the gate|up GEMM's A tensor map
+    // holds T rows (the TMA zero-fills the rest of the last tile) and the down GEMM stores
+    // only rows < T
+    return run_expert_gemms(h, const_cast<void*>(x), p.max_rows, tiles, ntiles, ws + p.h, out, H,
+                            s, mark, check, 0, nullptr, nullptr, T, T);
+  }
   // x into a buffer padded to whole GEMM tiles (the GEMMs read full tiles)
   cudaError_t e = cudaMemcpyAsync(ws + p.xp, x, T * H * elt, cudaMemcpyDeviceToDevice, s);
   if (e != cudaSuccess) return cuda_fail(h, e, "x copy");
