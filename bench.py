@@ -81,6 +81,9 @@ def parse_args():
     p.add_argument("--ffn", action="store_true",
                    help="time the dense FeedForward (non-MoE layers) on the same GEMMs at the "
                         "workload's tokens / d_model / d_ff instead of the MoE layer")
+    p.add_argument("--no-numa-bind", action="store_true",
+                   help="leave the e2e host buffers wherever the process runs (default: bind "
+                        "to the GPU's NUMA node before allocating them)")
     p.add_argument("--host-chunks", type=int, default=0,
                    help="token chunks of the single-GPU host-buffer forward timed as e2e "
                         "(0 = automatic)")
@@ -376,6 +379,12 @@ def run_ours(args, rank, world, local_rank):
                     "tile, folded weights) and the dispatch read, residual add in the combine"}
 
     # ---- end-to-end through the public module, host buffers in/out ----
+    numa = None
+    if not args.no_numa_bind:
+        # pinned buffers next to the GPU's PCIe root (first touch on its NUMA node)
+        from velvetoptimizer_b200.host import bind_to_device_node, device_numa_node
+        numa = device_numa_node(local_rank)
+        bind_to_device_node(local_rank)
     x_host = torch.empty(x.shape, dtype=x.dtype, pin_memory=True)
     x_host.copy_(x)
     out_host = torch.empty(x.shape, dtype=x.dtype, pin_memory=True)
@@ -463,6 +472,7 @@ def run_ours(args, rank, world, local_rank):
                    f"over NVLink peer memory, {args.ep_chunks} overlapped token chunks",
                    "l2": "inputs larger than L2 (x 512 MiB, weights 3.2 GiB); no flush"},
         "e2e": {"value": round(e2e_value, 1), "unit": "tokens/s",
+                "host_numa_node": numa,
                 "h2d_bytes_per_step": int(x.numel() * x.element_size()),
                 "d2h_bytes_per_step": int(x.numel() * x.element_size() + 4),
                 "api": "velvetoptimizer_b200.MoELayer.forward_host (vmoe_forward_host: "
