@@ -84,6 +84,8 @@ def parse_args():
     p.add_argument("--no-numa-bind", action="store_true",
                    help="leave the e2e host buffers wherever the process runs (default: bind "
                         "to the GPU's NUMA node before allocating them)")
+    p.add_argument("--graph", action="store_true",
+                   help="replay the single-GPU layer forward as a captured CUDA graph")
     p.add_argument("--host-chunks", type=int, default=0,
                    help="token chunks of the single-GPU host-buffer forward timed as e2e "
                         "(0 = automatic)")
@@ -321,13 +323,37 @@ def run_ours(args, rank, world, local_rank):
     for _ in range(args.warmup):
         out, aux = fwd(x)
     torch.cuda.synchronize()
+    graph_stages = None
+    if args.graph and world == 1:
+        # per-stage times from eager forwards first (a replayed graph records no new stage
+        # events), then the whole layer forward captured once as a CUDA graph and replayed
+        # every step (it allocates nothing and never synchronises the host, so it captures
+        # as is)
+        start_profile()
+        for _ in range(args.steps):
+            fwd(x)
+        graph_stages = read_profile()
+        packed.handle.set_profiling(0)  # no stage events inside the captured graph
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            out, aux = fwd(x)
+        graph_launches = launches_of_last()
+        torch.cuda.synchronize()
+
+        def fwd(inp):  # noqa: F811 - replays the captured forward on the same input buffer
+            graph.replay()
+            return out, aux
+
+        def launches_of_last():  # noqa: F811
+            return graph_launches
 
     # ---- device-resident timed region ----
     props = torch.cuda.get_device_properties(dev)
     gpu_id = str(getattr(props, "uuid", "") or local_rank)
     if gpu_id and not gpu_id.startswith("GPU-") and len(gpu_id) > 8:
         gpu_id = "GPU-" + gpu_id
-    start_profile()
+    if graph_stages is None:
+        start_profile()
     stream = torch.cuda.current_stream(dev)
     t_start = torch.cuda.Event(enable_timing=True)
     t_end = torch.cuda.Event(enable_timing=True)
@@ -346,7 +372,7 @@ def run_ours(args, rank, world, local_rank):
     torch.cuda.synchronize()
     clocks = sampler.stop()
     ms = t_start.elapsed_time(t_end) / args.steps
-    stages, nprof = read_profile()
+    stages, nprof = read_profile() if graph_stages is None else graph_stages
     ms_t = torch.tensor([ms], device=dev)
     if world > 1:
         dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
@@ -470,7 +496,8 @@ def run_ours(args, rank, world, local_rank):
                    "parallelism": "single GPU" if world == 1 else
                    f"expert parallel ep{world}: {E // world} experts/GPU, dispatch/combine "
                    f"over NVLink peer memory, {args.ep_chunks} overlapped token chunks",
-                   "l2": "inputs larger than L2 (x 512 MiB, weights 3.2 GiB); no flush"},
+                   "l2": "inputs larger than L2 (x 512 MiB, weights 3.2 GiB); no flush",
+                   "cuda_graph": bool(args.graph and world == 1)},
         "e2e": {"value": round(e2e_value, 1), "unit": "tokens/s",
                 "host_numa_node": numa,
                 "h2d_bytes_per_step": int(x.numel() * x.element_size()),
