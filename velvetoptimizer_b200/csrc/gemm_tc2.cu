@@ -74,8 +74,16 @@ __device__ __forceinline__ void st_peer_v4(char* p, uint4 v) {
   *reinterpret_cast<uint4*>(p) = v;
 }
 
+// Epilogue warps per CTA: four (one per TMEM lane quarter), eight for the GLU backward,
+// whose epilogue (ERA and its derivative, two loads and two stores per element) outlasts a
+// tile's main loop with four: two warps share each lane quarter, each taking half the columns.
 template <int EPI>
-__global__ void __launch_bounds__(192, 1)
+constexpr int pair_epi_warps() { return EPI == kPairGluBwd ? 8 : 4; }
+template <int EPI>
+constexpr int pair_threads() { return 64 + 32 * pair_epi_warps<EPI>(); }
+
+template <int EPI>
+__global__ void __launch_bounds__(pair_threads<EPI>(), 1)
 tc_gemm_pair_kernel(const __grid_constant__ CUtensorMap a_map,
                     const __grid_constant__ CUtensorMap b_map, const TcGemmArgs args) {
   extern __shared__ uint8_t smem_raw[];
@@ -100,7 +108,7 @@ tc_gemm_pair_kernel(const __grid_constant__ CUtensorMap a_map,
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(smem_u32(&sh->tfull[a]), 1);
-      mbar_init(smem_u32(&sh->tempty[a]), 8);
+      mbar_init(smem_u32(&sh->tempty[a]), 2 * pair_epi_warps<EPI>());
     }
     mbar_init(smem_u32(&sh->done), 1);
     sh->abort = 0;
@@ -192,7 +200,8 @@ tc_gemm_pair_kernel(const __grid_constant__ CUtensorMap a_map,
     }
   } else {
     // ---------------- epilogue (warps 2..5, both CTAs) ----------------
-    const int q = warp & 3;
+    const int q = warp & 3;                     // TMEM lane quarter this warp may access
+    const int part = (warp - 2) >> 2;           // which share of the columns (GLU backward)
     int local = 0;
     for (int tile = pair; tile < total; tile += num_pairs, ++local) {
       const int acc = local & 1;
@@ -257,8 +266,9 @@ tc_gemm_pair_kernel(const __grid_constant__ CUtensorMap a_map,
         // accumulator = dh for I columns [n*BN, n*BN + BN); g, u at their interleaved
         // positions (128-column blocks: gate then up) of the saved pre-activations
         const __nv_bfloat16* gurow = static_cast<const __nv_bfloat16*>(args.gu_in) + row * args.gu_ld;
+        constexpr int kCols = BN / (pair_epi_warps<EPI>() / 4);
 #pragma unroll 1
-        for (int c = 0; c < BN; c += 32) {
+        for (int c = part * kCols; c < (part + 1) * kCols; c += 32) {
           const int i0 = n * BN + c;
           if (i0 >= args.i_valid) break;
           const int gcol = (i0 / 128) * 256 + (i0 & 127);
@@ -393,7 +403,7 @@ cudaError_t launch_pair(const CUtensorMap& a_map, const CUtensorMap& b_map, cons
   attr[0].val.clusterDim.x = 2;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
-  cfg.blockDim = dim3(192, 1, 1);
+  cfg.blockDim = dim3(pair_threads<EPI>(), 1, 1);
   cfg.dynamicSmemBytes = smem_bytes;
   cfg.stream = s;
   cfg.attrs = attr;
