@@ -72,16 +72,18 @@ def main():
             (torch.float32, MoEConfig(hidden_size=128, intermediate_size=192, moe_num_experts=8,
                                       moe_top_k=3), 300),
         ]
-        # p2p: bf16 outputs pushed by the down GEMM's epilogue; "pull": VMOE_EP_PUSH=0, the
-        # combine reads them from the owners instead (fp32 always pulls)
-        for transport, chunks in (("nccl", 1), ("p2p", 1), ("p2p", 2), ("p2p", 3), ("pull", 2)):
+        # p2p: the default exchange (bf16 outputs pushed by the down GEMM's epilogue up to 2
+        # ranks, pulled by the combine beyond); "push" / "pull" force either (VMOE_EP_PUSH),
+        # so both run at any rank count (fp32 always pulls)
+        for transport, chunks in (("nccl", 1), ("p2p", 1), ("p2p", 2), ("p2p", 3), ("pull", 2),
+                                  ("push", 2)):
             for dtype, cfg, T0 in cases:
                 T = T0 - 37 * rank  # ranks route different token counts
                 if chunks == 3 and rank == world - 1:
                     T = 5  # this rank's later chunks are empty but still take part
                 w = global_weights(cfg, dev, dtype, seed=7)
-                if transport == "pull":
-                    os.environ["VMOE_EP_PUSH"] = "0"
+                if transport in ("pull", "push"):
+                    os.environ["VMOE_EP_PUSH"] = "0" if transport == "pull" else "1"
                 layer = ExpertParallelMoE(cfg, w, dev, dtype,
                                           transport="nccl" if transport == "nccl" else "p2p",
                                           max_tokens=T0, chunks=chunks)

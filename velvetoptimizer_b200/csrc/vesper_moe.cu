@@ -1324,10 +1324,14 @@ int vmoe_ep_p2p_setup(vmoe_handle* h, int64_t max_tokens, int chunks, void* ipc_
     off += (bytes + 255) & ~static_cast<size_t>(255);
     return o;
   };
-  // the bf16 CTA-pair GEMMs push their outputs to the source ranks (VMOE_EP_PUSH=0: pull)
+  // the bf16 CTA-pair GEMMs push their outputs to the source ranks up to 2 ranks; beyond,
+  // the sources pull them in the combine (measured: with 4 ranks the down GEMM's epilogue
+  // cannot keep enough remote stores in flight, and the pulling combine overlaps the next
+  // chunk's GEMMs).  VMOE_EP_PUSH=1 / 0 forces either.  (The return address holds a 24-bit
+  // row of the source's chunk and an 8-bit rank.)
   const char* pe = getenv("VMOE_EP_PUSH");
-  // (the return address holds a 24-bit row of the source's chunk and an 8-bit rank)
-  h->p2p_push = h->dtype == kBF16 && h->tile_rows == 2 * kTileM && !(pe && pe[0] == '0') &&
+  const bool want_push = pe ? pe[0] == '1' : G <= 2;
+  h->p2p_push = h->dtype == kBF16 && h->tile_rows == 2 * kTileM && want_push &&
                 chunk_tokens * K < (static_cast<int64_t>(1) << 24) && G <= 256;
   h->p2p_sig_off = take(3 * G * 4);
   h->p2p_counts_off = take(G * E * 4);
