@@ -200,8 +200,10 @@ dispatch_kernel(const T* __restrict__ x, const int32_t* __restrict__ topk_idx,
 }
 
 // ---- 4. combine --------------------------------------------------------------------
-// one warp per token; fp32 accumulation in ascending expert order (model.py:339-357)
-template <typename T>
+// one warp per token; fp32 accumulation in ascending expert order (model.py:339-357).  KMAX
+// bounds top_k at compile time: the K rows of each 16-byte column chunk are loaded before
+// any is summed, so their loads are in flight together.
+template <typename T, int KMAX>
 __global__ void __launch_bounds__(256)
 combine_kernel(const T* __restrict__ y, int64_t y_ld, const int32_t* __restrict__ topk_idx,
                const float* __restrict__ topk_w, const int* __restrict__ slot_of, int64_t T_tok,
@@ -209,9 +211,9 @@ combine_kernel(const T* __restrict__ y, int64_t y_ld, const int32_t* __restrict_
   const int lane = threadIdx.x & 31;
   const int64_t t = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
   if (t >= T_tok) return;
-  // the token's K (expert, slot, weight) triples sorted by expert id (K <= 32)
-  int ord_e[32], ord_s[32];
-  float ord_w[32];
+  // the token's K (expert, slot, weight) triples sorted by expert id
+  int ord_e[KMAX], ord_s[KMAX];
+  float ord_w[KMAX];
   int n = 0;
   for (int k = 0; k < K; ++k) {
     const int e = topk_idx[t * K + k];
@@ -228,13 +230,19 @@ combine_kernel(const T* __restrict__ y, int64_t y_ld, const int32_t* __restrict_
   const int nvec = H / V;
   T* orow = out + t * static_cast<int64_t>(H);
   for (int v = lane; v < nvec; v += 32) {
+    uint4 raw[KMAX];
+#pragma unroll
+    for (int j = 0; j < KMAX; ++j)
+      if (j < n && ord_s[j] >= 0)
+        raw[j] = reinterpret_cast<const uint4*>(y + static_cast<int64_t>(ord_s[j]) * y_ld)[v];
     float acc[V];
 #pragma unroll
     for (int i = 0; i < V; ++i) acc[i] = 0.f;
-    for (int j = 0; j < n; ++j) {
-      if (ord_s[j] < 0) continue;  // dropped by capacity
+#pragma unroll
+    for (int j = 0; j < KMAX; ++j) {
+      if (j >= n || ord_s[j] < 0) continue;  // dropped by capacity
       float f[V];
-      load16_to_f(y + static_cast<int64_t>(ord_s[j]) * y_ld + v * V, f);
+      load16_to_f(reinterpret_cast<const T*>(&raw[j]), f);
       const float w = ord_w[j];
 #pragma unroll
       for (int i = 0; i < V; ++i) acc[i] = __fadd_rn(acc[i], __fmul_rn(f[i], w));  // (y*w) then add
@@ -342,15 +350,27 @@ cudaError_t launch_dispatch(int dtype, const void* x, const int32_t* topk_idx, c
 cudaError_t launch_combine(int dtype, const void* y, int64_t y_ld, const int32_t* topk_idx,
                            const float* topk_w, const int* slot_of, int64_t T, int H, int K,
                            void* out, const void* resid, cudaStream_t s) {
+  if (K > 32) return cudaErrorInvalidValue;
   const unsigned grid = static_cast<unsigned>((T + 7) / 8);
+  auto go = [&](auto kern, auto* yy, auto* o, auto* r) {
+    kern<<<grid, 256, 0, s>>>(yy, y_ld, topk_idx, topk_w, slot_of, T, H, K, o, r);
+  };
   if (dtype == kF32) {
-    combine_kernel<float><<<grid, 256, 0, s>>>(static_cast<const float*>(y), y_ld, topk_idx,
-                                               topk_w, slot_of, T, H, K, static_cast<float*>(out),
-                                               static_cast<const float*>(resid));
+    const float* yy = static_cast<const float*>(y);
+    float* o = static_cast<float*>(out);
+    const float* r = static_cast<const float*>(resid);
+    if (K <= 2) go(combine_kernel<float, 2>, yy, o, r);
+    else if (K <= 4) go(combine_kernel<float, 4>, yy, o, r);
+    else if (K <= 8) go(combine_kernel<float, 8>, yy, o, r);
+    else go(combine_kernel<float, 32>, yy, o, r);
   } else {
-    combine_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>(
-        static_cast<const __nv_bfloat16*>(y), y_ld, topk_idx, topk_w, slot_of, T, H, K,
-        static_cast<__nv_bfloat16*>(out), static_cast<const __nv_bfloat16*>(resid));
+    const __nv_bfloat16* yy = static_cast<const __nv_bfloat16*>(y);
+    __nv_bfloat16* o = static_cast<__nv_bfloat16*>(out);
+    const __nv_bfloat16* r = static_cast<const __nv_bfloat16*>(resid);
+    if (K <= 2) go(combine_kernel<__nv_bfloat16, 2>, yy, o, r);
+    else if (K <= 4) go(combine_kernel<__nv_bfloat16, 4>, yy, o, r);
+    else if (K <= 8) go(combine_kernel<__nv_bfloat16, 8>, yy, o, r);
+    else go(combine_kernel<__nv_bfloat16, 32>, yy, o, r);
   }
   return cudaGetLastError();
 }

@@ -222,8 +222,11 @@ p2p_dispatch_kernel(P2PArgs a, const T* __restrict__ x, const int32_t* __restric
   }
 }
 
-// one warp per token; the same fixed-order fp32 arithmetic as the single-GPU combine
-template <typename T>
+// one warp per token; the same fixed-order fp32 arithmetic as the single-GPU combine.  KMAX
+// bounds top_k at compile time: the K rows of each 16-byte column chunk are loaded (over
+// NVLink) before any is summed, so the remote loads are in flight together instead of one
+// after another.
+template <typename T, int KMAX>
 __global__ void __launch_bounds__(256)
 p2p_combine_kernel(P2PArgs a, const int32_t* __restrict__ topk_idx, const float* __restrict__ topk_w,
                    int64_t T_tok, T* __restrict__ out) {
@@ -231,33 +234,40 @@ p2p_combine_kernel(P2PArgs a, const int32_t* __restrict__ topk_idx, const float*
   const int64_t t = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
   if (t >= T_tok) return;
   const int K = a.K;
-  int ord_e[32], ord_d[32], ord_r[32];
-  float ord_w[32];
+  int ord_e[KMAX];
+  const T* ord_y[KMAX];
+  float ord_w[KMAX];
   int n = 0;
-  for (int k = 0; k < K; ++k) {
+  for (int k = 0; k < K; ++k) {  // the token's rows sorted by expert id
     const int e = topk_idx[t * K + k];
     const int d = a.dest_rank[t * K + k], r = a.dest_row[t * K + k];
     const float w = topk_w[t * K + k];
+    const T* y = (d < 0 || d >= a.G || r < 0 || r >= a.cap_rows)
+                     ? nullptr
+                     : reinterpret_cast<const T*>(a.peer_base[d] + a.y_off) + static_cast<int64_t>(r) * a.H;
     int j = n++;
     while (j > 0 && ord_e[j - 1] > e) {
-      ord_e[j] = ord_e[j - 1]; ord_d[j] = ord_d[j - 1]; ord_r[j] = ord_r[j - 1]; ord_w[j] = ord_w[j - 1];
+      ord_e[j] = ord_e[j - 1]; ord_y[j] = ord_y[j - 1]; ord_w[j] = ord_w[j - 1];
       --j;
     }
-    ord_e[j] = e; ord_d[j] = d; ord_r[j] = r; ord_w[j] = w;
+    ord_e[j] = e; ord_y[j] = y; ord_w[j] = w;
   }
   constexpr int V = Vec16<T>::N;
   const int nvec = static_cast<int>(a.H / V);
   T* orow = out + t * a.H;
   for (int v = lane; v < nvec; v += 32) {
+    uint4 raw[KMAX];
+#pragma unroll
+    for (int j = 0; j < KMAX; ++j)
+      if (j < n && ord_y[j]) raw[j] = reinterpret_cast<const uint4*>(ord_y[j])[v];
     float acc[V];
 #pragma unroll
     for (int i = 0; i < V; ++i) acc[i] = 0.f;
-    for (int j = 0; j < n; ++j) {
-      if (ord_d[j] < 0 || ord_d[j] >= a.G || ord_r[j] < 0 || ord_r[j] >= a.cap_rows) continue;
-      const T* y = reinterpret_cast<const T*>(a.peer_base[ord_d[j]] + a.y_off) +
-                   static_cast<int64_t>(ord_r[j]) * a.H;
+#pragma unroll
+    for (int j = 0; j < KMAX; ++j) {
+      if (j >= n || !ord_y[j]) continue;
       float f[V];
-      load16_to_f(y + v * V, f);
+      load16_to_f(reinterpret_cast<const T*>(&raw[j]), f);
       const float w = ord_w[j];
 #pragma unroll
       for (int i = 0; i < V; ++i) acc[i] = __fadd_rn(acc[i], __fmul_rn(f[i], w));
@@ -376,15 +386,24 @@ cudaError_t launch_p2p_combine(int dtype, const P2PArgs& a, const int32_t* topk_
                                const float* topk_w, int64_t T, void* out, size_t min_smem,
                                cudaStream_t s) {
   if (T == 0) return cudaSuccess;
+  if (a.K > 32) return cudaErrorInvalidValue;
   const unsigned grid = static_cast<unsigned>((T + 7) / 8);
+  auto go = [&](auto kern, auto* o) {
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(min_smem));
+    kern<<<grid, 256, min_smem, s>>>(a, topk_idx, topk_w, T, o);
+  };
   if (dtype == kF32) {
-    auto kern = p2p_combine_kernel<float>;
-    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(min_smem));
-    kern<<<grid, 256, min_smem, s>>>(a, topk_idx, topk_w, T, static_cast<float*>(out));
+    float* o = static_cast<float*>(out);
+    if (a.K <= 2) go(p2p_combine_kernel<float, 2>, o);
+    else if (a.K <= 4) go(p2p_combine_kernel<float, 4>, o);
+    else if (a.K <= 8) go(p2p_combine_kernel<float, 8>, o);
+    else go(p2p_combine_kernel<float, 32>, o);
   } else {
-    auto kern = p2p_combine_kernel<__nv_bfloat16>;
-    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(min_smem));
-    kern<<<grid, 256, min_smem, s>>>(a, topk_idx, topk_w, T, static_cast<__nv_bfloat16*>(out));
+    __nv_bfloat16* o = static_cast<__nv_bfloat16*>(out);
+    if (a.K <= 2) go(p2p_combine_kernel<__nv_bfloat16, 2>, o);
+    else if (a.K <= 4) go(p2p_combine_kernel<__nv_bfloat16, 4>, o);
+    else if (a.K <= 8) go(p2p_combine_kernel<__nv_bfloat16, 8>, o);
+    else go(p2p_combine_kernel<__nv_bfloat16, 32>, o);
   }
   return cudaGetLastError();
 }
