@@ -70,10 +70,12 @@ struct TcShared {
   int abort;
   int issued;
   int consumed;
-  // router epilogue scratch (E <= 64)
-  int ep_ok[4];
-  int hist[64];
-  float psum[4][64];
+  // router epilogue scratch (E <= 64), one set per epilogue group
+  int ep_ok[2][4];
+  int hist[2][64];
+  float psum[2][4][64];
+  float bias[64];  // router bias (and the LayerNorm router's folded-weight row sums), staged
+  float ln_c[64];  // once per CTA so that the epilogue makes no global loads
 };
 
 template <int BN, int EPI = kPlain>
@@ -101,45 +103,73 @@ __device__ __forceinline__ int expert_of(const TcGemmArgs& args, int m) {
   return 0;
 }
 
-__device__ __forceinline__ void epilogue_bar() {  // the 4 epilogue warps only
-  asm volatile("bar.sync 1, 128;" ::: "memory");
+// The router runs two epilogue groups of four warps (one per TMEM accumulator, so they take
+// alternate tiles and one group's routing math overlaps the other's); the GEMM epilogues run
+// one.  Group g synchronises on named barrier 1 + g.
+template <int EPI>
+constexpr int tc_epi_groups() { return EPI == kRouter || EPI == kRouterLN ? 2 : 1; }
+template <int EPI>
+constexpr int tc_threads() { return 64 + 128 * tc_epi_groups<EPI>(); }
+
+__device__ __forceinline__ void epilogue_bar(int grp) {  // the 4 warps of one epilogue group
+  asm volatile("bar.sync %0, 128;" ::"r"(1 + grp) : "memory");
 }
 
-__device__ __forceinline__ float warp_sum(float v) {
+// Column sums over the warp's 32 lanes of v[0..31] (a reduce-scatter: lane l returns column
+// l).  Each level adds the same pairs, in the same order, as the xor butterfly
+// v += shfl_xor(v, o) for o = 16..1, so the sums are bit-identical to that butterfly's, with
+// 31 shuffles instead of 160.
+__device__ __forceinline__ float warp_column_sums(float (&v)[32], int lane) {
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-  return v;
+  for (int o = 16; o >= 1; o >>= 1) {
+    const bool up = (lane & o) != 0;
+#pragma unroll
+    for (int i = 0; i < o; ++i) {
+      const float send = up ? v[i] : v[i + o];
+      const float keep = up ? v[i + o] : v[i];
+      v[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+    }
+  }
+  return v[0];
 }
 
-// Router epilogue for one 128-token tile: each thread owns one token's logits.
+// Router epilogue for one 128-token tile by epilogue group `grp`: each thread owns one
+// token's logits.  The accumulator is released (tempty_bar) as soon as it has been read.
 template <int BN, int STAGES, bool LN>
 __device__ __forceinline__ void router_epilogue(const TcGemmArgs& args, TcShared<STAGES>* sh,
-                                                uint32_t t_row, int m, int q, int lane) {
+                                                uint32_t t_row, uint32_t tempty_bar, int grp,
+                                                int m, int q, int lane) {
   float lg[BN];
 #pragma unroll
   for (int c = 0; c < BN; c += 16) tmem_ld16(t_row + c, lg + c);
-  const int E = args.num_experts, K = args.top_k;
-  const int64_t t = static_cast<int64_t>(m) * kTileM + q * 32 + lane;
-  const bool valid = t < args.tokens;
+  float sum_x = 0.f, ss = 0.f;
   if constexpr (LN) {
     // this token's sum (column kSumCol) and sum of squares (its own diagonal entry of x x^T)
     float sx[16], sq[32];
     tmem_ld16(t_row + kSumCol, sx);
     tmem_ld32(t_row + kSqCol + q * 32, sq);
-    float ss = 0.f;
 #pragma unroll
     for (int j = 0; j < 32; ++j) ss = j == lane ? sq[j] : ss;
+    sum_x = sx[0];
+  }
+  tc_fence_before();
+  __syncwarp();
+  if (lane == 0) mbar_arrive(tempty_bar);
+  const int E = args.num_experts, K = args.top_k;
+  const int64_t t = static_cast<int64_t>(m) * kTileM + q * 32 + lane;
+  const bool valid = t < args.tokens;
+  if constexpr (LN) {
     const float inv_h = 1.0f / static_cast<float>(args.ln_h);
-    const float mean = sx[0] * inv_h;
+    const float mean = sum_x * inv_h;
     const float var = fmaxf(fmaf(ss, inv_h, -mean * mean), 0.f);
     const float rstd = 1.0f / sqrtf(var + args.ln_eps);
     if (valid) args.ln_stats[t] = make_float2(mean, rstd);
 #pragma unroll
     for (int e = 0; e < BN; ++e)
-      lg[e] = e < E ? fmaf(rstd, fmaf(-mean, args.ln_c[e], lg[e]), args.bias[e]) : -INFINITY;
+      lg[e] = e < E ? fmaf(rstd, fmaf(-mean, sh->ln_c[e], lg[e]), sh->bias[e]) : -INFINITY;
   } else {
 #pragma unroll
-    for (int e = 0; e < BN; ++e) lg[e] = e < E ? lg[e] + args.bias[e] : -INFINITY;
+    for (int e = 0; e < BN; ++e) lg[e] = e < E ? lg[e] + sh->bias[e] : -INFINITY;
   }
   if (valid && args.logits) {
     float* dst = args.logits + t * E;
@@ -148,9 +178,16 @@ __device__ __forceinline__ void router_epilogue(const TcGemmArgs& args, TcShared
       if (e < E) dst[e] = lg[e];
   }
   // softmax (model.py:323): exp(l - max) / sum, summed in ascending expert order
-  float mx = -INFINITY;
+  // (the maximum as a tree: fmaxf is exact, so the order does not matter, and the tree has
+  // depth log2(N) instead of a chain of N dependent instructions)
+  float mt[BN / 2];
 #pragma unroll
-  for (int e = 0; e < BN; ++e) mx = fmaxf(mx, lg[e]);
+  for (int i = 0; i < BN / 2; ++i) mt[i] = fmaxf(lg[i], lg[i + BN / 2]);
+#pragma unroll
+  for (int w = BN / 4; w >= 1; w >>= 1)
+#pragma unroll
+    for (int i = 0; i < w; ++i) mt[i] = fmaxf(mt[i], mt[i + w]);
+  const float mx = mt[0];
   float s = 0.f;
 #pragma unroll
   for (int e = 0; e < BN; ++e) {
@@ -160,53 +197,68 @@ __device__ __forceinline__ void router_epilogue(const TcGemmArgs& args, TcShared
   }
 #pragma unroll
   for (int e = 0; e < BN; ++e) lg[e] = lg[e] / s;
-  // top-K by (p desc, index asc) (model.py:326): strict '>' keeps the lowest index
-  int sel[32];
-  float vsum = 0.f;
-  uint64_t taken = 0;
-  for (int k = 0; k < K; ++k) {
-    int best = -1;
-    float bv = -INFINITY;
+  // top-K by (p desc, index asc) (model.py:326): strict '>' keeps the lowest index.  The
+  // selection runs twice (the first pass sums the selected probabilities, the second writes
+  // them renormalised and counts them) instead of keeping the chosen indices in a
+  // dynamically indexed array, which would live in local memory: under the router's HBM
+  // stream every local-memory miss is an L2 round trip of about a microsecond.
+  auto select = [&](uint64_t& taken, int& best, float& bv) {
+    best = -1;
+    bv = -INFINITY;
 #pragma unroll
     for (int e = 0; e < BN; ++e) {
       const bool free_e = e < E && !((taken >> e) & 1ull);
       if (free_e && (best < 0 || lg[e] > bv)) { best = e; bv = lg[e]; }
     }
     taken |= 1ull << best;
-    sel[k] = best;
+  };
+  const int et = q * 32 + lane;  // 0..127 over the group's four warps
+  epilogue_bar(grp);             // the group's previous readers of hist / psum are done
+  if (et < E) sh->hist[grp][et] = 0;
+  epilogue_bar(grp);
+  float vsum = 0.f;
+  uint64_t taken = 0;
+  for (int k = 0; k < K; ++k) {
+    int best;
+    float bv;
+    select(taken, best, bv);
     vsum += bv;
   }
   if (valid) {
+    uint64_t again = 0;
     for (int k = 0; k < K; ++k) {
-      float v = 0.f;
-#pragma unroll
-      for (int e = 0; e < BN; ++e) v = e == sel[k] ? lg[e] : v;
-      args.topk_idx[t * K + k] = sel[k];
-      args.topk_w[t * K + k] = v / vsum;  // model.py:329
+      int best;
+      float bv;
+      select(again, best, bv);
+      args.topk_idx[t * K + k] = best;
+      args.topk_w[t * K + k] = bv / vsum;  // model.py:329
+      atomicAdd(&sh->hist[grp][best], 1);
     }
   }
-  // per-tile histogram and probability column sums, fixed reduction order
-  const int et = q * 32 + lane;  // 0..127 over the four epilogue warps
-  epilogue_bar();                // the previous tile's readers of sh->hist / sh->psum are done
-  if (et < E) sh->hist[et] = 0;
-  epilogue_bar();
-  if (valid)
-    for (int k = 0; k < K; ++k) atomicAdd(&sh->hist[sel[k]], 1);
+  // per-tile probability column sums, fixed reduction order: over each warp's 32 tokens,
+  // then over the four warps
 #pragma unroll
-  for (int e = 0; e < BN; ++e) {
-    const float v = warp_sum(valid && e < E ? lg[e] : 0.f);
-    if (lane == 0 && e < E) sh->psum[q][e] = v;
+  for (int c0 = 0; c0 < BN; c0 += 32) {
+    float v[32];
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      const int j = c0 + i < BN ? c0 + i : BN - 1;  // (N 16: lanes 16..31 sum zeros)
+      v[i] = c0 + i < BN && j < E && valid ? lg[j] : 0.f;
+    }
+    const float col = warp_column_sums(v, lane);
+    if (c0 + lane < E) sh->psum[grp][q][c0 + lane] = col;
   }
-  epilogue_bar();
+  epilogue_bar(grp);
   if (et < E) {
     args.psum[static_cast<int64_t>(m) * E + et] =
-        ((sh->psum[0][et] + sh->psum[1][et]) + sh->psum[2][et]) + sh->psum[3][et];
-    args.hist[static_cast<int64_t>(m) * E + et] = sh->hist[et];
+        ((sh->psum[grp][0][et] + sh->psum[grp][1][et]) + sh->psum[grp][2][et]) +
+        sh->psum[grp][3][et];
+    args.hist[static_cast<int64_t>(m) * E + et] = sh->hist[grp][et];
   }
 }
 
 template <int EPI, int BN>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(tc_threads<EPI>(), 1)
 tc_gemm_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_constant__ CUtensorMap b_map,
                const TcGemmArgs args) {
   using Cfg = TcCfg<BN>;
@@ -252,6 +304,12 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_constant_
     fence_mbar_init();
     prefetch_tmap(&a_map);
     prefetch_tmap(&b_map);
+  }
+  if constexpr (ROUTER) {
+    for (int i = threadIdx.x; i < args.num_experts && i < 64; i += blockDim.x) {
+      sh->bias[i] = args.bias[i];
+      if constexpr (LN) sh->ln_c[i] = args.ln_c[i];
+    }
   }
   if (warp == 1) tmem_alloc(smem_u32(&sh->tmem_base), TCOLS);
   tc_fence_before();
@@ -342,21 +400,28 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_constant_
       if (!mbar_wait(smem_u32(&sh->done), 0)) report(args.status, kStatusTimeoutDrain);
     }
   } else {
-    // ---------------- epilogue (warps 2..5) ----------------
+    // ---------------- epilogue (warps 2..5, and 6..9 for the router) ----------------
+    // group g takes this CTA's tiles g, g + G, g + 2G, ... (G groups); with two groups each
+    // one owns one of the two TMEM accumulators
+    constexpr int G = tc_epi_groups<EPI>();
     const int q = warp & 3;  // TMEM lane quarter this warp may access
-    int local = 0;
-    for (int tile = blockIdx.x; tile < total; tile += gridDim.x, ++local) {
+    const int grp = (warp - 2) >> 2;
+    int k_local = 0;
+    for (int tile = blockIdx.x + grp * gridDim.x; tile < total;
+         tile += G * gridDim.x, ++k_local) {
+      const int local = k_local * G + grp;  // this CTA's tiles before this one
       const int acc = local & 1;
       const uint32_t aph = (local >> 1) & 1;
       const bool got = mbar_wait(smem_u32(&sh->tfull[acc]), aph);
       __syncwarp();
       const bool warp_ok = __all_sync(0xffffffffu, got);
       if constexpr (ROUTER) {
-        // the router epilogue synchronises the four epilogue warps, so they must agree
-        // on whether to go on (each warp's wait above is bounded)
-        if (lane == 0) sh->ep_ok[q] = warp_ok ? 1 : 0;
-        epilogue_bar();
-        const bool all_ok = sh->ep_ok[0] && sh->ep_ok[1] && sh->ep_ok[2] && sh->ep_ok[3];
+        // the router epilogue synchronises the group's four warps, so they must agree on
+        // whether to go on (each warp's wait above is bounded)
+        if (lane == 0) sh->ep_ok[grp][q] = warp_ok ? 1 : 0;
+        epilogue_bar(grp);
+        const bool all_ok =
+            sh->ep_ok[grp][0] && sh->ep_ok[grp][1] && sh->ep_ok[grp][2] && sh->ep_ok[grp][3];
         if (!all_ok) {
           if (lane == 0 && !warp_ok) set_abort(sh, args.status, kStatusTimeoutEpilogue);
           break;
@@ -369,7 +434,9 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_constant_
       const int m = tile / n_tiles, n = tile - m * n_tiles;
       const uint32_t t_row = tmem + (static_cast<uint32_t>(q * 32) << 16) + acc * ACC_COLS;
       if constexpr (ROUTER) {
-        router_epilogue<BN, STAGES, LN>(args, sh, t_row, m, q, lane);
+        router_epilogue<BN, STAGES, LN>(args, sh, t_row, smem_u32(&sh->tempty[acc]), grp, m, q,
+                                        lane);
+        continue;  // the router epilogue released the accumulator after reading it
       } else {
         const int e = expert_of(args, m);
         const int64_t row = static_cast<int64_t>(m) * kTileM + q * 32 + lane;
@@ -454,7 +521,7 @@ cudaError_t launch_cfg(const CUtensorMap& a_map, const CUtensorMap& b_map, const
   cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(smem));
   if (err != cudaSuccess) return err;
-  kern<<<grid, 192, smem, s>>>(a_map, b_map, args);
+  kern<<<grid, tc_threads<EPI>(), smem, s>>>(a_map, b_map, args);
   return cudaGetLastError();
 }
 
