@@ -109,9 +109,9 @@ def algorithmic(w, elt=2):
     return {
         "gemm1_flop": 4.0 * T * K * H * I,
         "gemm2_flop": 2.0 * T * K * H * I,
-        # x and W_r read, top-K indices and weights written (the timed forward does not ask
-        # for the router logits, so none are written)
-        "router_bytes": T * H * elt + E * H * elt + T * K * 8,
+        # the survey's routing bytes: x and W_r read, logits, top-K indices and weights
+        # written (the timed forward asks for no logits: T*E*4 of these are not moved)
+        "router_bytes": T * H * elt + E * H * elt + T * E * 4 + T * K * 8,
         "dispatch_bytes": T * H * elt + T * K * H * elt + T * K * 4,
         "combine_bytes": T * K * H * elt + T * K * 4 + T * H * elt,
     }
