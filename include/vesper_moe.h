@@ -229,7 +229,11 @@ VMOE_API int vmoe_forward_residual(vmoe_handle* h, const void* x, int64_t tokens
  * into `chunks` token chunks (0 = automatic: chunks of >= 8192 tokens, at most 8; at
  * most 16) whose host->device copy, forward and device->host copy overlap on two internal
  * copy streams; outputs are bit-identical to vmoe_forward on the same tokens and aux_loss
- * (host fp32 scalar, optional) is the loss of the whole batch.
+ * (host fp32 scalar, optional) is the loss of the whole batch.  Each chunk computes only
+ * whole GEMM tiles of its expert segments and carries the remainder rows into the next
+ * chunk (the last two chunks pad instead), so the chunks do not each pay the tile padding.
+ * With a token capacity (vmoe_config.capacity > 0) the batch is one chunk: the capacity
+ * applies to the batch as a whole.
  *   x_host, out_host   [T, H] config dtype; pinned (page-locked) memory for the copies to
  *                      overlap -- pageable memory works but serialises them
  *   workspace          device, >= vmoe_forward_host_workspace_size bytes, 256-byte aligned

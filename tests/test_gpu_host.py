@@ -89,3 +89,35 @@ def test_module_forward_host_matches_forward():
     assert out_h.device.type == "cpu"
     assert torch.equal(out_h, out_d.cpu())
     assert abs(float(aux_h) - float(aux_d)) <= 1e-6 * abs(float(aux_d))
+
+
+@pytest.mark.parametrize("chunks", [2, 5])
+def test_host_forward_carry_skewed_many_experts(chunks):
+    # 64 experts, Zipf-skewed: small experts' segments are carried from chunk to chunk
+    # (and the last chunk pads them), large ones split into whole tiles plus a remainder
+    case = MoECase(tokens=6000, hidden=256, inter=256, experts=64, top_k=4, zipf_alpha=1.2,
+                   bias_std=0.02, seed=11)
+    p = bf16_inputs(make_inputs(case))
+    layer = AbiLayer(case, p, "bf16")
+    dev = torch.device("cuda", 0)
+    x_dev = torch.from_numpy(p["x"]).to(dev, torch.bfloat16)
+    ref = layer.run_device(x_dev)
+    torch.cuda.synchronize()
+    out, aux = host_run(layer, x_dev.cpu().pin_memory(), chunks)
+    assert torch.equal(out, ref["out"].cpu())
+    ref_aux = float(ref["aux"].item())
+    assert abs(aux - ref_aux) <= 1e-6 * abs(ref_aux)
+
+
+def test_host_forward_capacity_is_one_batch():
+    # a token capacity applies to the whole batch, so the host forward must not cut it into
+    # chunks that would each drop their own late tokens
+    case = MoECase(tokens=1500, hidden=128, inter=256, experts=4, top_k=2, seed=3)
+    p = bf16_inputs(make_inputs(case))
+    layer = AbiLayer(case, p, "bf16", capacity=500)
+    dev = torch.device("cuda", 0)
+    x_dev = torch.from_numpy(p["x"]).to(dev, torch.bfloat16)
+    ref = layer.run_device(x_dev)
+    torch.cuda.synchronize()
+    out, _ = host_run(layer, x_dev.cpu().pin_memory(), 4)
+    assert torch.equal(out, ref["out"].cpu())

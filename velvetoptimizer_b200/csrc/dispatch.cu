@@ -107,15 +107,65 @@ plan_kernel(const int* __restrict__ counts, const float* __restrict__ psum_tot, 
   }
 }
 
+// ---- 2b. segments of one token chunk with carried rows ---------------------------------
+// Expert e's segment in a chunk's buffer holds the rows carried in from the previous chunk
+// (carry_in[e], placed first) and then this chunk's new rows (counts[e]).  Only whole
+// row_align-row tiles are computed; the rows past the last whole tile are carried out to the
+// next chunk, except that every carried-in row is computed now (a row waits at most one
+// chunk) and a chunk flagged `last` computes everything (its last tiles padded).
+// one block of 1024 threads (E <= 1024)
+__global__ void __launch_bounds__(1024)
+plan_carry_kernel(const int* __restrict__ counts, const int* __restrict__ carry_in, int E,
+                  int last, int row_align, int* __restrict__ offs, int* __restrict__ computed,
+                  int* __restrict__ carry_out, int* __restrict__ tile_expert,
+                  int* __restrict__ num_tiles) {
+  __shared__ int pad_s[1024];
+  __shared__ int off_s[1025];
+  const int tid = threadIdx.x;
+  if (tid < E) {
+    const int cin = carry_in[tid], n = cin + counts[tid];
+    const int whole = n / row_align * row_align;
+    const int comp = (!last && whole >= cin) ? whole : (n + row_align - 1) / row_align * row_align;
+    pad_s[tid] = comp;
+    computed[tid] = comp;
+    carry_out[tid] = n > comp ? n - comp : 0;
+  }
+  __syncthreads();
+  if (tid == 0) {
+    int run = 0;
+    for (int e = 0; e < E; ++e) { off_s[e] = run; run += pad_s[e]; }
+    off_s[E] = run;
+    *num_tiles = run / row_align;
+  }
+  __syncthreads();
+  for (int e = tid; e <= E; e += blockDim.x) offs[e] = off_s[e];
+  if (tid < E) {
+    const int t0 = off_s[tid] / row_align, nt = pad_s[tid] / row_align;
+    for (int j = 0; j < nt; ++j) tile_expert[t0 + j] = tid;
+  }
+}
+
 // ---- 3. slot assignment + gather -----------------------------------------------------
-// grid = nblk, block = 128 (one thread per token of the routing block)
+// grid = nblk, block = 128 (one thread per token of the routing block).  With a carry
+// (DispatchCarry::computed set) the token chunk's new rows follow the carried-in rows of
+// each segment, rows past the computed part go to the carry-out list instead of the buffer,
+// and slots are numbered from slot_base (the buffer's first row in a ring of buffers).
+struct DispatchCarry {
+  const int* carry_in;  // [E]
+  const int* computed;  // [E] rows of each segment computed in this chunk (null: no carry)
+  int* list_out;        // [E][kCarryCap] global (token, k) indices carried out
+  int64_t t0;           // global index of the chunk's first token
+  int64_t slot_base;
+};
+
 template <typename T, bool LN>
 __global__ void __launch_bounds__(128)
 dispatch_kernel(const T* __restrict__ x, const int32_t* __restrict__ topk_idx,
                 const int* __restrict__ excl, const int* __restrict__ offs, int64_t T_tok, int H,
                 int E, int K, int64_t capacity, int* __restrict__ slot_of, T* __restrict__ x_perm,
                 int64_t xp_ld, int* status, const float2* __restrict__ ln_stats,
-                const float* __restrict__ ln_w, const float* __restrict__ ln_b) {
+                const float* __restrict__ ln_w, const float* __restrict__ ln_b,
+                const DispatchCarry carry) {
   extern __shared__ uint32_t dsm[];
   uint32_t* masks = dsm;                            // [4 warps][E] token bitmasks
   int* wbase = reinterpret_cast<int*>(dsm + 4 * E);  // [4][E]
@@ -141,13 +191,26 @@ dispatch_kernel(const T* __restrict__ x, const int32_t* __restrict__ topk_idx,
   __syncthreads();
   const uint32_t lt = (1u << lane) - 1u;
   for (int k = 0; k < K; ++k) {
-    int slot = -1;
+    int slot = -1;  // row of x_perm (relative to x_perm)
     if (valid) {
       const int e = topk_idx[t * K + k];
       const int rank = excl[blk * E + e] + wbase[warp * E + e] + __popc(masks[warp * E + e] & lt);
-      if (capacity <= 0 || rank < capacity) slot = offs[e] + rank;
+      if (carry.computed) {
+        const int pos = carry.carry_in[e] + rank;  // position in the segment
+        const int over = pos - carry.computed[e];
+        if (over < 0) {
+          slot = offs[e] + pos;
+        } else if (over < kCarryCap) {
+          carry.list_out[e * kCarryCap + over] = static_cast<int>((carry.t0 + t) * K + k);
+        } else {
+          report(status, kStatusBadSlot);
+        }
+      } else if (capacity <= 0 || rank < capacity) {
+        slot = offs[e] + rank;
+      }
       if (slot >= offs[e + 1]) { report(status, kStatusBadSlot); slot = -1; }
-      slot_of[t * K + k] = slot;
+      // a carried-out row gets its slot from the next chunk (carry_rows_kernel)
+      slot_of[t * K + k] = slot >= 0 ? static_cast<int>(carry.slot_base + slot) : -1;
     }
     slots[tid * K + k] = slot;
   }
@@ -196,6 +259,34 @@ dispatch_kernel(const T* __restrict__ x, const int32_t* __restrict__ topk_idx,
         }
       }
     }
+  }
+}
+
+// ---- 3b. carried-in rows ---------------------------------------------------------------
+// grid = E, block = 256: expert e's carried-in (token, k) rows go to the first carry_in[e]
+// rows of its segment, one warp per row (x holds every token of the batch).
+template <typename T>
+__global__ void __launch_bounds__(256)
+carry_rows_kernel(const T* __restrict__ x, int H, int K, const int* __restrict__ list_in,
+                  const int* __restrict__ carry_in, const int* __restrict__ offs,
+                  T* __restrict__ x_perm, int64_t xp_ld, int64_t slot_base,
+                  int* __restrict__ slot_of, int* status) {
+  const int e = blockIdx.x, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int n = carry_in[e];
+  if (n > kCarryCap) {
+    if (threadIdx.x == 0) report(status, kStatusBadSlot);
+    return;
+  }
+  constexpr int V = Vec16<T>::N;
+  const int nvec = H / V;
+  for (int j = warp; j < n; j += 8) {
+    const int idx = list_in[e * kCarryCap + j];
+    const int64_t t = idx / K;
+    const int row = offs[e] + j;
+    const uint4* src = reinterpret_cast<const uint4*>(x + t * H);
+    uint4* dst = reinterpret_cast<uint4*>(x_perm + static_cast<int64_t>(row) * xp_ld);
+    for (int v = lane; v < nvec; v += 32) dst[v] = src[v];
+    if (lane == 0) slot_of[idx] = static_cast<int>(slot_base + row);
   }
 }
 
@@ -317,11 +408,20 @@ cudaError_t launch_plan(const int* counts, const float* psum_tot, int64_t T, int
   return cudaGetLastError();
 }
 
+cudaError_t launch_plan_carry(const int* counts, const int* carry_in, int E, bool last,
+                              int row_align, int* offs, int* computed, int* carry_out,
+                              int* tile_expert, int* num_tiles, cudaStream_t s) {
+  plan_carry_kernel<<<1, 1024, 0, s>>>(counts, carry_in, E, last ? 1 : 0, row_align, offs,
+                                       computed, carry_out, tile_expert, num_tiles);
+  return cudaGetLastError();
+}
+
 namespace {
 template <typename T, bool LN>
 void dispatch_as(const void* x, const int32_t* topk_idx, const int* excl, const int* offs,
                  int64_t T_tok, int H, int E, int K, int64_t capacity, int* slot_of, void* x_perm,
-                 int64_t xp_ld, int* status, const LnArgs* ln, cudaStream_t s) {
+                 int64_t xp_ld, int* status, const LnArgs* ln, cudaStream_t s,
+                 const DispatchCarry& carry) {
   const unsigned nblk = static_cast<unsigned>((T_tok + kTileM - 1) / kTileM);
   const size_t smem = (8 * static_cast<size_t>(E) + static_cast<size_t>(kTileM) * K) * 4;
   auto kern = dispatch_kernel<T, LN>;
@@ -329,7 +429,7 @@ void dispatch_as(const void* x, const int32_t* topk_idx, const int* excl, const 
   kern<<<nblk, 128, smem, s>>>(static_cast<const T*>(x), topk_idx, excl, offs, T_tok, H, E, K,
                                capacity, slot_of, static_cast<T*>(x_perm), xp_ld, status,
                                LN ? ln->stats : nullptr, LN ? ln->weight : nullptr,
-                               LN ? ln->bias : nullptr);
+                               LN ? ln->bias : nullptr, carry);
 }
 }  // namespace
 
@@ -337,13 +437,41 @@ cudaError_t launch_dispatch(int dtype, const void* x, const int32_t* topk_idx, c
                             const int* offs, int64_t T, int H, int E, int K, int64_t capacity,
                             int* slot_of, void* x_perm, int64_t xp_ld, int* status,
                             const LnArgs* ln, cudaStream_t s) {
+  const DispatchCarry none{nullptr, nullptr, nullptr, 0, 0};
   if (dtype == kF32) {
-    if (ln) dispatch_as<float, true>(x, topk_idx, excl, offs, T, H, E, K, capacity, slot_of, x_perm, xp_ld, status, ln, s);
-    else dispatch_as<float, false>(x, topk_idx, excl, offs, T, H, E, K, capacity, slot_of, x_perm, xp_ld, status, ln, s);
+    if (ln) dispatch_as<float, true>(x, topk_idx, excl, offs, T, H, E, K, capacity, slot_of, x_perm, xp_ld, status, ln, s, none);
+    else dispatch_as<float, false>(x, topk_idx, excl, offs, T, H, E, K, capacity, slot_of, x_perm, xp_ld, status, ln, s, none);
   } else {
-    if (ln) dispatch_as<__nv_bfloat16, true>(x, topk_idx, excl, offs, T, H, E, K, capacity, slot_of, x_perm, xp_ld, status, ln, s);
-    else dispatch_as<__nv_bfloat16, false>(x, topk_idx, excl, offs, T, H, E, K, capacity, slot_of, x_perm, xp_ld, status, ln, s);
+    if (ln) dispatch_as<__nv_bfloat16, true>(x, topk_idx, excl, offs, T, H, E, K, capacity, slot_of, x_perm, xp_ld, status, ln, s, none);
+    else dispatch_as<__nv_bfloat16, false>(x, topk_idx, excl, offs, T, H, E, K, capacity, slot_of, x_perm, xp_ld, status, ln, s, none);
   }
+  return cudaGetLastError();
+}
+
+cudaError_t launch_dispatch_carry(int dtype, const void* x, const int32_t* topk_idx,
+                                  const int* excl, const int* offs, int64_t T, int H, int E,
+                                  int K, int* slot_of, void* x_perm, int64_t xp_ld,
+                                  const int* carry_in, const int* computed, int* list_out,
+                                  int64_t t0, int64_t slot_base, int* status, cudaStream_t s) {
+  const DispatchCarry carry{carry_in, computed, list_out, t0, slot_base};
+  if (dtype == kF32)
+    dispatch_as<float, false>(x, topk_idx, excl, offs, T, H, E, K, 0, slot_of, x_perm, xp_ld, status, nullptr, s, carry);
+  else
+    dispatch_as<__nv_bfloat16, false>(x, topk_idx, excl, offs, T, H, E, K, 0, slot_of, x_perm, xp_ld, status, nullptr, s, carry);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_carry_rows(int dtype, const void* x, int H, int E, int K, const int* list_in,
+                              const int* carry_in, const int* offs, void* x_perm, int64_t xp_ld,
+                              int64_t slot_base, int* slot_of, int* status, cudaStream_t s) {
+  if (dtype == kF32)
+    carry_rows_kernel<float><<<E, 256, 0, s>>>(static_cast<const float*>(x), H, K, list_in, carry_in,
+                                               offs, static_cast<float*>(x_perm), xp_ld, slot_base,
+                                               slot_of, status);
+  else
+    carry_rows_kernel<__nv_bfloat16><<<E, 256, 0, s>>>(
+        static_cast<const __nv_bfloat16*>(x), H, K, list_in, carry_in, offs,
+        static_cast<__nv_bfloat16*>(x_perm), xp_ld, slot_base, slot_of, status);
   return cudaGetLastError();
 }
 

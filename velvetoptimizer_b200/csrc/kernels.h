@@ -45,6 +45,30 @@ cudaError_t launch_plan(const int* counts, const float* psum_tot, int64_t T, int
                         int64_t capacity, int row_align, int* offs, int* tile_expert,
                         int* num_tiles, float* aux, int32_t* counts_out, cudaStream_t s);
 
+// Token chunks with carried rows (the host-buffer forward): expert e's segment holds the
+// carry_in[e] rows carried in from the previous chunk, then this chunk's counts[e] new rows;
+// computed[e] of them (whole row_align-row tiles, at least the carried-in rows; everything
+// when `last`, i.e. nothing is carried out) are computed now and the rest, at most
+// kCarryCap, are carried out.
+constexpr int kCarryCap = 256;
+cudaError_t launch_plan_carry(const int* counts, const int* carry_in, int E, bool last,
+                              int row_align, int* offs, int* computed, int* carry_out,
+                              int* tile_expert, int* num_tiles, cudaStream_t s);
+// The chunk's dispatch: new rows at positions carry_in[e] + rank of their segment, copied
+// when the position is below computed[e], else listed in list_out[e][pos - computed[e]] as
+// global (token, k) indices (t0 + t) * K + k with slot -1 for now.  Slots count from
+// slot_base.
+cudaError_t launch_dispatch_carry(int dtype, const void* x, const int32_t* topk_idx,
+                                  const int* excl, const int* offs, int64_t T, int H, int E,
+                                  int K, int* slot_of, void* x_perm, int64_t xp_ld,
+                                  const int* carry_in, const int* computed, int* list_out,
+                                  int64_t t0, int64_t slot_base, int* status, cudaStream_t s);
+// The previous chunk's carried-out rows: row x[t] of every listed (t, k) to the first
+// carry_in[e] rows of segment e, and its slot (slot_base + row) into the global slot_of.
+cudaError_t launch_carry_rows(int dtype, const void* x, int H, int E, int K, const int* list_in,
+                              const int* carry_in, const int* offs, void* x_perm, int64_t xp_ld,
+                              int64_t slot_base, int* slot_of, int* status, cudaStream_t s);
+
 // Aux loss of a batch routed in chunks: chunk c's per-expert counts (int [E]) and
 // probability sums (float [E]) sit at ws + c*stride + counts_off / psum_off.
 cudaError_t launch_aux_merge_ws(const void* ws, size_t stride, size_t counts_off, size_t psum_off,
