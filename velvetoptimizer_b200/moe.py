@@ -33,6 +33,24 @@ from .config import MoEConfig
 
 _DTYPES = {torch.float32: _lib.VMOE_F32, torch.bfloat16: _lib.VMOE_BF16}
 
+# Every forward checks that the packed weights are current.  Walking the module tree for
+# its parameters costs about a millisecond with 64 experts (900 parameters), more than a
+# decode-sized forward on the GPU, so the layers keep their parameter list and rebuild it
+# only after a parameter or submodule has been (re)assigned on any module: torch's global
+# registration hooks bump this generation.  In-place updates (optimizer steps,
+# load_state_dict) change a parameter's version and `.data` assignment its data pointer,
+# and both are part of the weight key itself.
+_STRUCTURE_GEN = [0]
+
+
+def _structure_changed(*_args):
+    _STRUCTURE_GEN[0] += 1
+    return None  # keep the registered object
+
+
+nn.modules.module.register_module_parameter_registration_hook(_structure_changed)
+nn.modules.module.register_module_module_registration_hook(_structure_changed)
+
 
 class FlyLoRALinear(nn.Module):
     """Parameter container with the reference FlyLoRALinear's names (model.py:83-121).
@@ -268,8 +286,16 @@ class _MoETrainFn(torch.autograd.Function):
 class _PackedHandleMixin:
     """Repack-on-change handle management shared by the MoE and dense layers."""
 
+    def _param_list(self) -> list:
+        """self.parameters() as a list, rebuilt only after a structural change."""
+        cache = self.__dict__.get("_plist_cache")
+        if cache is None or cache[0] != _STRUCTURE_GEN[0]:
+            cache = (_STRUCTURE_GEN[0], list(self.parameters()))
+            self.__dict__["_plist_cache"] = cache
+        return cache[1]
+
     def _weight_key(self):
-        return tuple((p.data_ptr(), p._version) for p in self.parameters())
+        return tuple((p.data_ptr(), p._version) for p in self._param_list())
 
     def _abi_config(self, dtype: torch.dtype) -> _lib.VmoeConfig:
         c = self.config
@@ -412,7 +438,7 @@ class MoELayer(_PackedHandleMixin, nn.Module):
 
     def _wants_grad(self, x: torch.Tensor) -> bool:
         return torch.is_grad_enabled() and (
-            x.requires_grad or any(p.requires_grad for p in self.parameters()))
+            x.requires_grad or any(p.requires_grad for p in self._param_list()))
 
     # -- forward ---------------------------------------------------------------------
     def forward(self, x: torch.Tensor, return_router_logits: bool = False):
