@@ -146,6 +146,23 @@ def test_bf16_matches_oracle(name):
     layer.close()
 
 
+@pytest.mark.parametrize("name", ["ragged_bias", "odd_dims"])
+def test_bf16_single_cta_gemms_match_oracle(name, monkeypatch):
+    # VMOE_PAIR_GEMM=0 selects the single-CTA tcgen05 GEMMs (128-row tiles) at handle creation
+    monkeypatch.setenv("VMOE_PAIR_GEMM", "0")
+    case = BF16_CASES[name]
+    inp = bf16_inputs(make_inputs(case))
+    layer = AbiLayer(case, inp, "bf16")
+    assert layer.handle.lib.vmoe_gemm_tile_rows(layer.handle.ptr) == 128
+    res = layer.run(inp["x"])
+    check_dispatch(layer, case.tokens, res, res["topk_idx"])
+    forced = O.moe_forward(inp, case, force_idx=res["topk_idx"])
+    err = O.norm_rel_err(res["out"], forced["out"])
+    assert err < BF16_TOL, err
+    assert abs(float(res["aux"]) - float(forced["aux"])) <= 1e-4 * abs(float(forced["aux"]))
+    layer.close()
+
+
 def test_bf16_deterministic():
     case = BF16_CASES["ragged_bias"]
     inp = bf16_inputs(make_inputs(case))
