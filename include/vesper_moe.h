@@ -106,7 +106,9 @@ VMOE_API int vmoe_destroy(vmoe_handle* h);
  * any FlyLoRA branch into the base projection (the branch is linear, so
  * W + s*U*D and b + s*(U*bd + bu) reproduce base(x) + s*lora_up(lora_down(x)) of
  * python/vesper/model.py:123-126).  Enqueued on `stream`; returns after the copy is
- * enqueued.  Replaces MoELayer's parameter set (load_state_dict). */
+ * enqueued.  Replaces MoELayer's parameter set (load_state_dict).  A second call (after
+ * an optimizer step) overwrites the same library buffers in place: it is ordered after
+ * forwards enqueued earlier on `stream`, so call it on the stream the forwards use. */
 VMOE_API int vmoe_set_weights(vmoe_handle* h, const vmoe_weights* w, void* stream);
 
 /* Bytes of device workspace vmoe_forward needs for `tokens` tokens (256-byte aligned). */

@@ -1,9 +1,11 @@
 """Generate golden vectors by executing the reference MoELayer on CPU.
 
-Run in a container where the VelvetOptimizer sources are mounted (read-only) at
-``/root/reference``::
+Run where a VelvetOptimizer checkout is available (read-only is enough)::
 
-    python tests/golden/make_golden.py            # writes tests/golden/*.npz
+    python tests/golden/make_golden.py [--reference DIR] [names...]   # writes tests/golden/*.npz
+
+``DIR`` is the checkout's ``python/`` directory; without ``--reference`` it is
+``$VESPER_REFERENCE_PYTHON``, else ``reference/python`` beside this repository.
 
 The reference's Python package is imported in place (``sys.path``), never copied.
 Inputs come from ``oracle.inputs.make_inputs`` (seeded numpy), are loaded into the
@@ -25,10 +27,12 @@ import numpy as np
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 REPO = os.path.dirname(os.path.dirname(HERE))
-REFERENCE_PY = "/root/reference/python"
 sys.path.insert(0, REPO)
 
 from oracle.inputs import MoECase, backward_inputs, make_inputs  # noqa: E402
+from tests.golden_io import reference_python_dir  # noqa: E402
+
+REFERENCE_PY = ""  # set by main()
 
 # name -> case.  Small enough to commit; together they cover the reference's own edge
 # cases (K == E, E == 2, a single token, empty experts, K = 1) and the option set
@@ -253,7 +257,12 @@ def dump_state_dict_keys():
     print(f"state_dict keys: {len(keys)} -> {path}")
 
 
-def main(names=None):
+def main(names=None, reference=None):
+    global REFERENCE_PY
+    REFERENCE_PY = reference or reference_python_dir() or ""
+    if not os.path.isfile(os.path.join(REFERENCE_PY, "vesper", "model.py")):
+        raise SystemExit("no reference checkout found: pass --reference DIR (the checkout's "
+                         "python/ directory) or set VESPER_REFERENCE_PYTHON")
     import torch
     torch.set_num_threads(os.cpu_count() or 1)
     if not names:
@@ -293,4 +302,10 @@ def main(names=None):
 
 
 if __name__ == "__main__":
-    main(sys.argv[1:] or None)
+    argv = sys.argv[1:]
+    ref = None
+    if "--reference" in argv:
+        i = argv.index("--reference")
+        ref = argv[i + 1]
+        del argv[i:i + 2]
+    main(argv or None, ref)

@@ -8,6 +8,17 @@ import numpy as np
 from oracle.inputs import MoECase
 
 GOLDEN_DIR = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def reference_python_dir() -> str | None:
+    """The reference checkout's ``python/`` directory (the one holding the ``vesper``
+    package), or None when it is not available: ``$VESPER_REFERENCE_PYTHON`` if set, else
+    ``reference/python`` in the directory that holds this repository.  Only fixture
+    generation and CPU tests that execute the reference use it; GPU tests never do."""
+    d = os.environ.get("VESPER_REFERENCE_PYTHON") or os.path.join(
+        os.path.dirname(REPO), "reference", "python")
+    return d if os.path.isfile(os.path.join(d, "vesper", "model.py")) else None
 
 
 def golden_names():

@@ -7,6 +7,8 @@ Tolerances (from the path's specification):
     (max|got - ref| / max|ref|) of the reference;
   * bf16: out within 2e-2 norm-relative of the fp32 oracle on the same bf16-rounded inputs.
 """
+import dataclasses
+
 import numpy as np
 import pytest
 import torch
@@ -219,14 +221,8 @@ def test_workspace_too_small_is_reported():
 # ----------------------------------------------------------------------------------------
 # the drop-in module
 # ----------------------------------------------------------------------------------------
-def _load_module(case, inp, dtype):
-    from velvetoptimizer_b200 import MoEConfig, MoELayer
-    cfg = MoEConfig(hidden_size=case.hidden, intermediate_size=case.inter,
-                    moe_num_experts=case.experts, moe_top_k=case.top_k,
-                    flylora_rank=case.lora_rank, flylora_alpha=case.lora_alpha,
-                    era_gamma=case.era_gamma)
-    m = MoELayer(cfg)
-    sd = m.state_dict()
+def _module_state(case, inp, sd):
+    """The reference state_dict keys of ``sd`` filled with the case's weights."""
     t = lambda a: torch.from_numpy(np.ascontiguousarray(a))  # noqa: E731
     new = dict(sd)
     new["router.weight"], new["router.bias"] = t(inp["w_r"]), t(inp["b_r"])
@@ -240,7 +236,17 @@ def _load_module(case, inp, dtype):
             new[f"{pre}.lora_up.bias"] = t(inp[f"bl_{p}"][e])
         new[f"experts.{e}.down_proj.weight"] = t(inp["w_d"][e])
         new[f"experts.{e}.down_proj.bias"] = t(inp["b_d"][e])
-    m.load_state_dict(new)
+    return new
+
+
+def _load_module(case, inp, dtype):
+    from velvetoptimizer_b200 import MoEConfig, MoELayer
+    cfg = MoEConfig(hidden_size=case.hidden, intermediate_size=case.inter,
+                    moe_num_experts=case.experts, moe_top_k=case.top_k,
+                    flylora_rank=case.lora_rank, flylora_alpha=case.lora_alpha,
+                    era_gamma=case.era_gamma)
+    m = MoELayer(cfg)
+    m.load_state_dict(_module_state(case, inp, m.state_dict()))
     return m.cuda()
 
 
@@ -277,6 +283,51 @@ def test_module_bf16_lora_matches_oracle():
     _, idx = O.topk_lowest_index(probs, case.top_k)
     forced = O.moe_forward(ib, case, force_idx=idx)
     assert O.norm_rel_err(out.float().reshape(-1, case.hidden).cpu().numpy(), forced["out"]) < BF16_TOL
+    m.close()
+
+
+class _DataWriteOptimizer(torch.optim.Optimizer):
+    """Writes new parameter values through ``p.data`` inside ``step``, as VelvetOptimizer
+    does (python/vesper/optimizer.py:176,212): no parameter version changes."""
+
+    def __init__(self, named_params, new_state):
+        self.names = {id(p): n for n, p in named_params}
+        self.new_state = new_state
+        super().__init__([p for _, p in named_params], {})
+
+    @torch.no_grad()
+    def step(self, closure=None):
+        for group in self.param_groups:
+            for p in group["params"]:
+                p.data.copy_(self.new_state[self.names[id(p)]].to(p.device, p.dtype))
+
+
+@torch.no_grad()
+def test_module_repacks_after_optimizer_writes_through_data():
+    """A training loop's optimizer step between two forwards: the second forward runs on the
+    new weights (checked against the oracle on them), not on the first packing."""
+    case = BF16_CASES["lora_zipf_e32k8"]
+    inp = make_inputs(case)
+    inp2 = make_inputs(dataclasses.replace(case, seed=case.seed + 101))
+    inp2["x"] = inp["x"]
+    m = _load_module(case, inp, torch.bfloat16)
+    x = torch.from_numpy(inp["x"]).reshape(1, case.tokens, case.hidden).cuda().to(torch.bfloat16)
+    out1, _ = m(x)
+    opt = _DataWriteOptimizer(list(m.named_parameters()), _module_state(case, inp2, m.state_dict()))
+    opt.step()
+    out2, aux2, logits = m(x, return_router_logits=True)
+    assert not torch.equal(out1, out2)
+    probs = O.softmax(logits.reshape(-1, case.experts).cpu().numpy())
+    _, idx = O.topk_lowest_index(probs, case.top_k)
+    forced = O.moe_forward(bf16_inputs(inp2), case, force_idx=idx)
+    assert O.norm_rel_err(out2.float().reshape(-1, case.hidden).cpu().numpy(), forced["out"]) < BF16_TOL
+    # a raw write outside any optimizer step needs mark_weights_dirty()
+    m.router.weight.data.copy_(torch.from_numpy(inp["w_r"]))
+    m.mark_weights_dirty()
+    _, _, logits3 = m(x, return_router_logits=True)
+    mixed = dict(inp2, w_r=inp["w_r"])  # only the router weight was written back
+    ref3 = O.moe_forward(bf16_inputs(mixed), case)["logits"]
+    assert O.norm_rel_err(logits3.reshape(-1, case.experts).cpu().numpy(), ref3) < 1e-4
     m.close()
 
 

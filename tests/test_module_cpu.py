@@ -69,3 +69,91 @@ def test_feedforward_uses_the_same_check():
         ffn.up_proj.base.weight.mul_(2.0)
     assert ffn._weight_key() != k0
     assert ffn._param_list() == list(ffn.parameters())
+
+
+class _DataWriteOptimizer(torch.optim.Optimizer):
+    """Writes its update through ``p.data`` as VelvetOptimizer does
+    (python/vesper/optimizer.py:176,212): the parameter's version does not change."""
+
+    def __init__(self, params, lr=0.1):
+        super().__init__(params, dict(lr=lr))
+
+    @torch.no_grad()
+    def step(self, closure=None):
+        for group in self.param_groups:
+            for p in group["params"]:
+                if p.grad is not None:
+                    p.data.copy_(p.data.float() - group["lr"] * p.grad.float())
+
+
+def test_optimizer_step_through_data_changes_key():
+    layer = small_layer()
+    k0 = layer._weight_key()
+    opt = _DataWriteOptimizer(layer.parameters())
+    for p in layer.parameters():
+        p.grad = torch.ones_like(p)
+    versions = [p._version for p in layer.parameters()]
+    opt.step()
+    assert [p._version for p in layer.parameters()] == versions  # invisible to versions
+    assert layer._weight_key() != k0
+
+
+def test_reference_velvet_optimizer_step_changes_key():
+    """The reference's own optimizer (its PyTorch update path on CPU) through the layer."""
+    import sys
+
+    import pytest
+
+    from tests.golden_io import reference_python_dir
+    ref = reference_python_dir()
+    if ref is None:
+        pytest.skip("no reference checkout beside this repository")
+    if ref not in sys.path:
+        sys.path.insert(0, ref)
+    from vesper.optimizer import VelvetOptimizer
+    layer = small_layer()
+    opt = VelvetOptimizer(layer.parameters(), lr=1e-2)
+    assert opt._kernel_backend == "pytorch"  # CPU: the p.data.copy_ update
+    k0 = layer._weight_key()
+    for p in layer.parameters():
+        p.grad = torch.full_like(p, 0.5)
+    before = layer.router.weight.detach().clone()
+    opt.step()
+    assert not torch.equal(before, layer.router.weight.detach())
+    assert layer._weight_key() != k0
+
+
+def test_mark_weights_dirty_changes_key():
+    layer = small_layer()
+    k0 = layer._weight_key()
+    layer.router.weight.data.add_(1.0)  # neither version nor pointer moves
+    assert layer._weight_key() == k0
+    layer.mark_weights_dirty()
+    assert layer._weight_key() != k0
+
+
+def test_registration_hooks_ignore_other_modules():
+    from velvetoptimizer_b200 import moe
+    layer = small_layer()
+    layer._param_list()
+    g0 = moe._STRUCTURE_GEN[0]
+    other = nn.Sequential(nn.Linear(4, 4), nn.ReLU())  # registers modules and parameters
+    other[0].weight = nn.Parameter(torch.zeros(4, 4))
+    assert moe._STRUCTURE_GEN[0] == g0
+    layer.router.weight = nn.Parameter(torch.zeros_like(layer.router.weight))
+    assert moe._STRUCTURE_GEN[0] > g0
+
+
+def test_hooks_installed_by_the_first_layer_not_at_import():
+    import subprocess
+    import sys
+    code = ("import torch\n"
+            "from velvetoptimizer_b200 import moe, MoEConfig, MoELayer\n"
+            "assert not moe._HOOKS\n"
+            "MoELayer(MoEConfig(hidden_size=16, intermediate_size=16, moe_num_experts=2, "
+            "moe_top_k=1))\n"
+            "assert len(moe._HOOKS) == 3\n")
+    import os
+    repo = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    r = subprocess.run([sys.executable, "-c", code], cwd=repo, capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr

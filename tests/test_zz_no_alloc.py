@@ -5,8 +5,10 @@ the layer (a serving thread under a fixed memory budget, a real-time loop, an en
 no caching allocator): it takes its scratch from a static 64 MiB device array instead of
 a caller workspace.  These tests call both entry points through the C ABI on the same
 inputs, twice in a row for the static one (the array keeps the previous call's contents),
-and compare within the parity tolerances used elsewhere (bf16 2e-2, fp32 1e-5).  The file
-is named to be collected last.
+after first filling the array with an unrelated, larger layer's scratch, and require the
+results to be bit-identical: both entry points run the same kernels on the same inputs,
+and no scratch is read before the call has written it.  The file is named to be collected
+last.
 """
 import ctypes
 
@@ -50,6 +52,21 @@ def _no_alloc_call(layer, x):
             "counts": counts.cpu().numpy(), "aux": float(aux.item())}
 
 
+def _dirty_the_array(dtype):
+    """Fill the static array with another layer's scratch: more tokens, more experts, a
+    larger top-K and other widths, so stale slots, offsets and rows sit everywhere."""
+    other = MoECase(tokens=200, hidden=768, inter=1536, experts=16, top_k=4, bias_std=0.05,
+                    seed=33)
+    oinp = make_inputs(other)
+    if dtype == "bf16":
+        oinp = bf16_inputs(oinp)
+    olayer = AbiLayer(other, oinp, dtype)
+    assert olayer.handle.workspace_size(other.tokens) <= _lib.VMOE_NO_ALLOC_WORKSPACE_BYTES
+    x = torch.from_numpy(oinp["x"]).cuda().to(olayer.tdtype)
+    _no_alloc_call(olayer, x)
+    olayer.close()
+
+
 @pytest.mark.parametrize("dtype,tol", [("bf16", 2e-2), ("f32", 1e-5)])
 def test_no_alloc_matches_forward_twice(dtype, tol):
     # a decode-shaped batch: few tokens, so the scratch fits the static array
@@ -61,12 +78,32 @@ def test_no_alloc_matches_forward_twice(dtype, tol):
     assert layer.handle.workspace_size(case.tokens) <= _lib.VMOE_NO_ALLOC_WORKSPACE_BYTES
     ref = layer.run(inp["x"])                      # vmoe_forward, caller workspace
     x = torch.from_numpy(inp["x"]).cuda().to(layer.tdtype)
+    _dirty_the_array(dtype)
     for _ in range(2):                             # two calls in a row share the array
         got = _no_alloc_call(layer, x)
-        assert O.norm_rel_err(got["out"], ref["out"]) < tol
+        # the same kernels on the same inputs: bit-identical (tol bounds the oracle gap)
+        assert np.array_equal(got["out"], ref["out"])
         assert np.array_equal(got["topk_idx"], ref["topk_idx"])
         assert np.array_equal(got["counts"], ref["counts"])
-        assert abs(got["aux"] - float(ref["aux"])) <= 1e-5 * abs(float(ref["aux"]))
+        assert got["aux"] == float(ref["aux"])
+    oracle = O.moe_forward(inp, case, force_idx=got["topk_idx"])
+    assert O.norm_rel_err(got["out"], oracle["out"]) < tol
+    # a smaller batch after the larger one: the array still holds the 64-token call's rows
+    ref9 = layer.run(inp["x"][:9])
+    got9 = _no_alloc_call(layer, x[:9].contiguous())
+    assert np.array_equal(got9["out"], ref9["out"])
+    layer.close()
+
+
+def test_no_alloc_reports_negative_token_counts():
+    case = MoECase(tokens=8, hidden=128, inter=256, experts=4, top_k=2, seed=34)
+    layer = AbiLayer(case, bf16_inputs(make_inputs(case)), "bf16")
+    x = torch.zeros((8, case.hidden), dtype=torch.bfloat16, device="cuda")  # never read
+    rc = _lib.load().vmoe_forward_no_alloc(layer.handle.ptr, ctypes.c_void_p(x.data_ptr()), -3,
+                                           ctypes.c_void_p(x.data_ptr()), None, None, None,
+                                           None, None, ctypes.c_void_p(layer.stream.cuda_stream))
+    assert rc == _lib.VMOE_ERR_INVALID_ARG
+    assert "tokens must be >= 0" in _lib.load().vmoe_last_error(layer.handle.ptr).decode()
     layer.close()
 
 

@@ -164,6 +164,12 @@ int alloc(vmoe_handle* h, T** p, size_t bytes, const char* what) {
   return VMOE_OK;
 }
 
+// alloc() unless *p already holds a buffer (whose size the handle's config fixes)
+template <typename T>
+int alloc_once(vmoe_handle* h, T** p, size_t bytes, const char* what) {
+  return *p ? VMOE_OK : alloc(h, p, bytes, what);
+}
+
 
 // gate|up GEMM (+ ERA * up) then down GEMM over an expert-major buffer of `max_rows`
 // rows (a multiple of 128) whose M tiles map to experts through tiles / ntiles.

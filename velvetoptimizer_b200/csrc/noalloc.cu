@@ -12,9 +12,12 @@
 // Every GPU that loads this library reserves it until the process exits, whether or not
 // this entry point is used.  Host code cannot use the array's name as a device address
 // (in host code it names a host-side stand-in), so the device address is looked up once
-// per device with cudaGetSymbolAddress, with that device current, and cached.  That
-// lookup happens inside the FIRST call on each device; make that first call before any
-// CUDA stream capture begins.
+// per device with cudaGetSymbolAddress, with that device current, and cached together
+// with the unique id of the CUDA context it belongs to.  That lookup happens inside the
+// FIRST call on each device; make that first call before any CUDA stream capture begins.
+// If the device's context is later destroyed and recreated (cudaDeviceReset), the next
+// call sees a new context id and looks the address up again -- but a reset also frees
+// every handle's weights, so handles must be recreated after one anyway.
 //
 // All calls share the one array: two calls whose GPU work overlaps (different streams,
 // different handles on the same device, or another thread) race on it and corrupt each
@@ -22,6 +25,7 @@
 // previous call left; nothing in the forward reads scratch it has not first written in the
 // same call (routing tables, slots, offsets and all rows that reach the output are rewritten
 // every time), so no clearing is needed between calls.
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <stdio.h>
 
@@ -39,24 +43,62 @@ __device__ __align__(256) unsigned char g_no_alloc_workspace[kNoAllocWorkspaceBy
 
 constexpr int kMaxDevices = 64;
 std::mutex g_mu;
-void* g_workspace_on_device[kMaxDevices] = {};
+struct CachedAddress {
+  unsigned long long ctx_id = 0;  // unique id of the context the address belongs to
+  void* ptr = nullptr;
+};
+CachedAddress g_workspace_on_device[kMaxDevices];
 
-// Device address of the static workspace on `device` (looked up once, then cached).
+typedef CUresult (*CtxGetCurrentFn)(CUcontext*);
+typedef CUresult (*CtxGetIdFn)(CUcontext, unsigned long long*);
+
+// Unique id of the calling thread's current context (0 when it cannot be read).
+unsigned long long current_context_id() {
+  static CtxGetCurrentFn get_current = nullptr;
+  static CtxGetIdFn get_id = nullptr;
+  static bool looked_up = false;
+  if (!looked_up) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_current = reinterpret_cast<CtxGetCurrentFn>(p);
+    if (cudaGetDriverEntryPoint("cuCtxGetId", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_id = reinterpret_cast<CtxGetIdFn>(p);
+    looked_up = true;
+  }
+  CUcontext ctx = nullptr;
+  unsigned long long id = 0;
+  if (get_current && get_id && get_current(&ctx) == CUDA_SUCCESS && ctx &&
+      get_id(ctx, &id) == CUDA_SUCCESS)
+    return id;
+  return 0;
+}
+
+// Device address of the static workspace on `device`: looked up with that device current
+// on the first call (and again if the device's context was recreated), then cached.
 cudaError_t workspace_address(int device, void** out) {
   std::lock_guard<std::mutex> lock(g_mu);
-  if (!g_workspace_on_device[device]) {
-    int prev = -1;
-    if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
-    cudaError_t e = cudaSuccess;
-    if (prev != device) e = cudaSetDevice(device);
-    void* p = nullptr;
-    if (e == cudaSuccess) e = cudaGetSymbolAddress(&p, g_no_alloc_workspace);
-    if (prev >= 0 && prev != device) cudaSetDevice(prev);
-    if (e != cudaSuccess) return e;
-    g_workspace_on_device[device] = p;
+  int prev = -1;
+  if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+  cudaError_t e = cudaSuccess;
+  if (prev != device) e = cudaSetDevice(device);
+  if (e == cudaSuccess) {
+    CachedAddress& c = g_workspace_on_device[device];
+    const unsigned long long id = current_context_id();
+    if (!c.ptr || id != c.ctx_id) {
+      void* p = nullptr;
+      e = cudaGetSymbolAddress(&p, g_no_alloc_workspace);
+      if (e == cudaSuccess) {
+        c.ptr = p;
+        c.ctx_id = id;
+      }
+    }
+    if (e == cudaSuccess) *out = c.ptr;
   }
-  *out = g_workspace_on_device[device];
-  return cudaSuccess;
+  if (prev >= 0 && prev != device) cudaSetDevice(prev);
+  return e;
 }
 
 }  // namespace
@@ -65,9 +107,15 @@ extern "C" int vmoe_forward_no_alloc(vmoe_handle* h, const void* x, int64_t toke
                                      float* router_logits, int32_t* topk_idx, float* topk_w,
                                      int32_t* expert_counts, float* aux_loss, void* stream) {
   if (!h) return VMOE_ERR_INVALID_ARG;
+  if (tokens < 0) {
+    char msg[128];
+    snprintf(msg, sizeof(msg), "vmoe_forward_no_alloc: tokens must be >= 0 (got %lld)",
+             static_cast<long long>(tokens));
+    return vmoe::set_handle_error(h, VMOE_ERR_INVALID_ARG, msg);
+  }
   size_t need = 0;
   int rc = vmoe_workspace_size(h, tokens, &need);
-  if (rc != VMOE_OK) return rc;
+  if (rc != VMOE_OK) return vmoe::set_handle_error(h, rc, "vmoe_forward_no_alloc: workspace size");
   if (need > kNoAllocWorkspaceBytes) {
     char msg[256];
     snprintf(msg, sizeof(msg),

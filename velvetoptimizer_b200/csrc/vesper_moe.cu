@@ -433,24 +433,28 @@ int vmoe_set_weights(vmoe_handle* h, const vmoe_weights* w, void* stream) {
     return fail(h, VMOE_ERR_INVALID_ARG, "router_w, gate_w, up_w and down_w are required");
   DeviceGuard g(h->device);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  free_weights(h);
+  // The packed buffers are sized by the handle's config alone, so a repack (after every
+  // optimizer step of a training loop) reuses them: the pack kernels are ordered after any
+  // forward already enqueued on `s`, and no cudaFree synchronises the device.
+  h->ready = false;
+  h->ln_ready = false;
   const int64_t E = h->E, H = h->H, I = h->I, Ipad = h->Ipad, Hpad = h->Hpad;
   const int64_t El = h->E_local;  // experts held by this handle (E without expert parallelism)
   const size_t elt = dtype_bytes(h->dtype);
   const bool bf16 = h->dtype == kBF16;
   const int R = h->cfg.lora_rank;
   int rc;
-  if ((rc = alloc(h, &h->w_r, E * H * elt, "router weight")) != VMOE_OK) return rc;
-  if ((rc = alloc(h, &h->b_r, E * 4, "router bias")) != VMOE_OK) return rc;
+  if ((rc = alloc_once(h, &h->w_r, E * H * elt, "router weight")) != VMOE_OK) return rc;
+  if ((rc = alloc_once(h, &h->b_r, E * 4, "router bias")) != VMOE_OK) return rc;
   const int64_t gu_rows = bf16 ? 2 * Ipad : I;
-  if ((rc = alloc(h, &h->w_g, El * gu_rows * H * elt, "gate weight")) != VMOE_OK) return rc;
-  if ((rc = alloc(h, &h->b_g, El * gu_rows * 4, "gate bias")) != VMOE_OK) return rc;
+  if ((rc = alloc_once(h, &h->w_g, El * gu_rows * H * elt, "gate weight")) != VMOE_OK) return rc;
+  if ((rc = alloc_once(h, &h->b_g, El * gu_rows * 4, "gate bias")) != VMOE_OK) return rc;
   if (!bf16) {
-    if ((rc = alloc(h, &h->w_u, El * I * H * elt, "up weight")) != VMOE_OK) return rc;
-    if ((rc = alloc(h, &h->b_u, El * I * 4, "up bias")) != VMOE_OK) return rc;
+    if ((rc = alloc_once(h, &h->w_u, El * I * H * elt, "up weight")) != VMOE_OK) return rc;
+    if ((rc = alloc_once(h, &h->b_u, El * I * 4, "up bias")) != VMOE_OK) return rc;
   }
-  if ((rc = alloc(h, &h->w_d, El * Hpad * Ipad * elt, "down weight")) != VMOE_OK) return rc;
-  if ((rc = alloc(h, &h->b_d, El * Hpad * 4, "down bias")) != VMOE_OK) return rc;
+  if ((rc = alloc_once(h, &h->w_d, El * Hpad * Ipad * elt, "down weight")) != VMOE_OK) return rc;
+  if ((rc = alloc_once(h, &h->b_d, El * Hpad * 4, "down bias")) != VMOE_OK) return rc;
 
   cudaError_t e;
   // router: plain copy of W_r, bias to fp32 (zeros for a dense handle)

@@ -24,9 +24,11 @@ import ctypes
 import itertools
 import math
 import warnings
+import weakref
 
 import torch
 import torch.nn as nn
+from torch.optim.optimizer import register_optimizer_step_post_hook
 
 from . import _lib
 from .config import MoEConfig
@@ -36,20 +38,38 @@ _DTYPES = {torch.float32: _lib.VMOE_F32, torch.bfloat16: _lib.VMOE_BF16}
 # Every forward checks that the packed weights are current.  Walking the module tree for
 # its parameters costs about a millisecond with 64 experts (900 parameters), more than a
 # decode-sized forward on the GPU, so the layers keep their parameter list and rebuild it
-# only after a parameter or submodule has been (re)assigned on any module: torch's global
-# registration hooks bump this generation.  In-place updates (optimizer steps,
-# load_state_dict) change a parameter's version and `.data` assignment its data pointer,
-# and both are part of the weight key itself.
+# only after a parameter or submodule has been (re)assigned on one of their own modules
+# (_STRUCTURE_GEN, bumped by torch's registration hooks for the modules in _OWNED).
+# The weight key holds each parameter's data pointer and version (load_state_dict and
+# in-place updates through the parameter bump the version, `.data` assignment moves the
+# pointer) plus two generations for writes that change neither:
+#   * _WRITE_GEN, bumped after every torch optimizer step: optimizers commonly write
+#     through `p.data` (VelvetOptimizer does, python/vesper/optimizer.py:176,212), which
+#     leaves the parameter's version untouched;
+#   * the layer's own counter, bumped by ``mark_weights_dirty()`` for any other such write.
+# The hooks are installed when the first layer is built, not at import.
 _STRUCTURE_GEN = [0]
+_WRITE_GEN = [0]
+_OWNED: "weakref.WeakSet[nn.Module]" = weakref.WeakSet()
+_HOOKS: list = []
 
 
-def _structure_changed(*_args):
-    _STRUCTURE_GEN[0] += 1
+def _structure_changed(module, _name, _obj):
+    if module in _OWNED:
+        _STRUCTURE_GEN[0] += 1
     return None  # keep the registered object
 
 
-nn.modules.module.register_module_parameter_registration_hook(_structure_changed)
-nn.modules.module.register_module_module_registration_hook(_structure_changed)
+def _optimizer_stepped(_optimizer, _args, _kwargs):
+    _WRITE_GEN[0] += 1
+
+
+def _install_hooks() -> None:
+    if _HOOKS:
+        return
+    _HOOKS.append(nn.modules.module.register_module_parameter_registration_hook(_structure_changed))
+    _HOOKS.append(nn.modules.module.register_module_module_registration_hook(_structure_changed))
+    _HOOKS.append(register_optimizer_step_post_hook(_optimizer_stepped))
 
 
 class FlyLoRALinear(nn.Module):
@@ -290,12 +310,25 @@ class _PackedHandleMixin:
         """self.parameters() as a list, rebuilt only after a structural change."""
         cache = self.__dict__.get("_plist_cache")
         if cache is None or cache[0] != _STRUCTURE_GEN[0]:
+            for m in self.modules():  # reassignments on these now invalidate the list
+                _OWNED.add(m)
             cache = (_STRUCTURE_GEN[0], list(self.parameters()))
             self.__dict__["_plist_cache"] = cache
         return cache[1]
 
     def _weight_key(self):
-        return tuple((p.data_ptr(), p._version) for p in self._param_list())
+        return (_WRITE_GEN[0], self.__dict__.get("_dirty", 0),
+                tuple((p.data_ptr(), p._version) for p in self._param_list()))
+
+    def mark_weights_dirty(self) -> None:
+        """Repack the weights before the next forward.
+
+        Needed only after writing parameters in a way the layer cannot see: through
+        ``p.data`` (or a raw device pointer) outside a torch optimizer's ``step``.  Writes
+        through the parameter itself (``with torch.no_grad(): p.copy_(...)``,
+        ``load_state_dict``) and every ``torch.optim.Optimizer.step`` are detected.
+        """
+        self.__dict__["_dirty"] = self.__dict__.get("_dirty", 0) + 1
 
     def _abi_config(self, dtype: torch.dtype) -> _lib.VmoeConfig:
         c = self.config
@@ -346,6 +379,7 @@ class FeedForward(_PackedHandleMixin, nn.Module):
     """
 
     def __init__(self, config):
+        _install_hooks()
         super().__init__()
         cfg = MoEConfig.from_any(config)
         self.config = cfg
@@ -391,6 +425,7 @@ class MoELayer(_PackedHandleMixin, nn.Module):
     """
 
     def __init__(self, config):
+        _install_hooks()
         super().__init__()
         cfg = MoEConfig.from_any(config)
         cfg.validate()
