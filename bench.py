@@ -44,6 +44,10 @@ WORKLOADS = {
     "c4_skewed": dict(tokens=32768, batch=8, hidden=2048, inter=1024, experts=64, top_k=8,
                       lora_on=True, zipf_alpha=1.2),
     "c2_decode": dict(tokens=64, batch=64, hidden=2048, inter=8192, experts=8, top_k=2),
+    # the fp32 correctness configuration (the reference's own CPU-runnable case): CUDA-core
+    # GEMMs, fp32 end to end
+    "c1_fp32": dict(tokens=512, batch=2, hidden=768, inter=3072, experts=8, top_k=2,
+                    dtype="f32"),
     # the per-expert shape of c5_ep (4,096 rows per expert, d_model 4096, d_ff 2048) on 8
     # experts: small enough (a few GB on the device) for full profiler captures
     "c5_profile_e8": dict(tokens=16384, batch=4, hidden=4096, inter=2048, experts=8, top_k=2),
@@ -68,6 +72,11 @@ def parse_args():
     p.add_argument("--cpu-seconds", type=float, default=10.0,
                    help="target CPU time of the cpu_baseline sample")
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--no-workloads", action="store_true",
+                   help="on one GPU, skip timing the other configurations after the headline one")
+    p.add_argument("--no-ep-parity", action="store_true",
+                   help="on N GPUs, skip the bit-identity check of the expert-parallel output "
+                        "against a single-GPU forward (run after the timed regions)")
     p.add_argument("--ep-chunks", type=int, default=0,
                    help="token chunks of the fused expert-parallel forward (overlap); "
                         "0 = 1 chunk up to 2 GPUs, 4 beyond (the measured best)")
@@ -103,18 +112,38 @@ def peaks():
         return dict(FALLBACK_PEAKS, source="fallback")
 
 
-def algorithmic(w, elt=2):
-    """Algorithmic work per forward: FLOPs of the expert GEMMs, bytes of the data stages."""
+def algorithmic(w, elt=2, logits=False):
+    """Algorithmic work per forward: FLOPs of the expert GEMMs, bytes of the data stages.
+
+    Router bytes are the ones the timed forward moves: x and W_r read, top-K indices and
+    weights written, the per-128-token expert histograms and probability sums written;
+    the T*E*4 bytes of router logits only when the forward returns them (``logits``).
+    Expert weight bytes (read once per forward, every expert assumed to receive tokens)
+    bound the decode-sized layer."""
     T, H, I, E, K = w["tokens"], w["hidden"], w["inter"], w["experts"], w["top_k"]
+    nblk = -(-T // 128)
     return {
         "gemm1_flop": 4.0 * T * K * H * I,
         "gemm2_flop": 2.0 * T * K * H * I,
-        # the survey's routing bytes: x and W_r read, logits, top-K indices and weights
-        # written (the timed forward asks for no logits: T*E*4 of these are not moved)
-        "router_bytes": T * H * elt + E * H * elt + T * E * 4 + T * K * 8,
+        "router_bytes": T * H * elt + E * H * elt + T * K * 8 + nblk * E * 8
+                        + (T * E * 4 if logits else 0),
         "dispatch_bytes": T * H * elt + T * K * H * elt + T * K * 4,
         "combine_bytes": T * K * H * elt + T * K * 4 + T * H * elt,
+        "gemm1_weight_bytes": E * 2 * I * H * elt,
+        "gemm2_weight_bytes": E * H * I * elt,
     }
+
+
+def cpu_model() -> str | None:
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    import platform
+    return platform.processor() or None
 
 
 # --------------------------------------------------------------------------------------
@@ -248,8 +277,159 @@ def cpu_baseline(layer, x_dev, w, seconds):
     if n2 > n:
         n, t = n2, run(n2)
     return {"value": n / t, "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port",
+            "cpu_model": cpu_model(),
             "sample": f"{n} of {xs.shape[0]} tokens, numpy fp32 oracle (CPU restatement of "
                       f"python/vesper/model.py:317-385), {t:.1f} s"}
+
+
+# what the expert-parallel forward's profiled stages hold (rank 0, its first token chunk)
+EP_STAGE_NAMES = {"plan": "plan_publish_counts", "dispatch": "dispatch_nvlink_wait_rows",
+                  "gemm2_down": "gemm2_down_push_rows", "combine": "signal_wait_combine"}
+
+
+def stage_table(stages, alg, pk, scale=1.0, weight_bound=False, fp32=False, ep=False):
+    """Per-stage ms, share, achieved rate and fraction of the measured peak.
+
+    GEMM stages are FLOP-rated against the bf16 peak, except in a weight-bound
+    (decode-sized) layer, where their weight bytes are rated against HBM; fp32 CUDA-core
+    GEMMs have no measured peak.  ``scale`` is the share of the workload's tokens the
+    profiled stages processed (the first token chunk of an expert-parallel forward)."""
+    total = max(sum(stages.values()), 1e-9)
+    rep = {}
+    for name, t_ms in stages.items():
+        rec = {"ms": round(t_ms, 4), "share": round(t_ms / total, 4)}
+        sec = max(t_ms, 1e-9) * 1e-3
+        if name.startswith(("gemm1", "gemm2")):
+            key = name[:5]
+            tf = alg[f"{key}_flop"] * scale / sec / 1e12
+            if fp32:
+                rec.update(achieved=round(tf, 2), unit="TFLOP/s", frac=None,
+                           bound="fp32 CUDA cores (no measured peak)")
+            elif weight_bound:
+                gbs = alg[f"{key}_weight_bytes"] / sec / 1e9
+                rec.update(achieved=round(gbs, 1), unit="GB/s", frac=round(gbs / pk["hbm_gbs"], 4),
+                           bound="hbm (expert weights read once)", tflops=round(tf, 2))
+            else:
+                rec.update(achieved=round(tf, 1), unit="TFLOP/s",
+                           frac=round(tf / pk["bf16_tflops"], 4))
+        elif name in ("router", "dispatch", "combine"):
+            gbs = alg[f"{name}_bytes"] * scale / sec / 1e9
+            rec.update(achieved=round(gbs, 1), unit="GB/s", frac=round(gbs / pk["hbm_gbs"], 4))
+        rep[EP_STAGE_NAMES.get(name, name) if ep else name] = rec
+    return rep
+
+
+def time_workload(name, steps, warmup, dev, cpu_seconds, graph=False):
+    """Tokens/s, stage table and roofline of one single-GPU workload (after the headline
+    timed region, in the same process), with the CPU restatement timed beside it."""
+    import torch
+    w = dict(WORKLOADS[name])
+    T, H, E, K = w["tokens"], w["hidden"], w["experts"], w["top_k"]
+    f32 = w.get("dtype") == "f32"
+    tdt = torch.float32 if f32 else torch.bfloat16
+    layer = build_layer(w, dev, seed=0)
+    packed = layer.packed_for(dev, tdt)
+    g = torch.Generator(device=dev)
+    g.manual_seed(1000)
+    x = torch.randn(T, H, generator=g, device=dev).to(tdt).reshape(w["batch"], T // w["batch"], H)
+    for _ in range(warmup):
+        layer(x)
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream(dev)
+    packed.handle.set_profiling(steps)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    launches = 0
+    e0.record(stream)
+    for _ in range(steps):
+        layer(x)
+        launches += packed.handle.last_launch_count()
+    e1.record(stream)
+    e1.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    stages, nprof = packed.handle.stage_times()
+    packed.handle.set_profiling(0)
+    pk = peaks()
+    elt = 4 if f32 else 2
+    alg = algorithmic(w, elt)
+    weight_bound = name == "c2_decode"
+    table = stage_table(stages, alg, pk, weight_bound=weight_bound, fp32=f32)
+    top = max((k for k in table if k.startswith("gemm")), key=lambda k: table[k]["ms"])
+    rec = {"ms_per_step": round(ms, 4), "tokens_per_s": round(T / (ms * 1e-3), 1),
+           "dtype": "f32" if f32 else "bf16", "steps": steps, "warmup": warmup,
+           "gpu_launches": launches,
+           "config": f"{T} tokens, d_model {H}, expert d_ff {w['inter']}, {E} experts, top-{K}"
+                     + (", FlyLoRA r16 on, Zipf(1.2) router bias" if w.get("lora_on") else ""),
+           "stages": table,
+           "roofline": dict(table[top], kernel=top, avg_launch_ms=table[top]["ms"],
+                            launches_timed=nprof,
+                            peak=None if f32 else (pk["hbm_gbs"] if weight_bound else pk["bf16_tflops"]),
+                            peak_source=None if f32 else pk["source"] + (" HBM copy" if weight_bound
+                                                                         else " bf16 burst"))}
+    if graph:
+        # the same forward replayed as one CUDA graph (it allocates nothing and never
+        # synchronises the host, so it captures as is)
+        cg = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(cg):
+            layer(x)
+        for _ in range(warmup):
+            cg.replay()
+        torch.cuda.synchronize()
+        e0.record(stream)
+        for _ in range(steps):
+            cg.replay()
+        e1.record(stream)
+        e1.synchronize()
+        rec["graph_ms_per_step"] = round(e0.elapsed_time(e1) / steps, 4)
+        del cg
+    rec["cpu_baseline"] = cpu_baseline(layer, x.reshape(T, H), w, cpu_seconds)
+    layer.close()
+    del layer, packed, x
+    torch.cuda.empty_cache()
+    return rec
+
+
+def check_ep_parity(layer, x2d, w, dev, world):
+    """Outside the timed regions: this rank's tokens through the expert-parallel layer and
+    through a single-GPU handle holding all E experts; the outputs must be bit-identical
+    (the same kernels compute every row and the combine order is fixed)."""
+    import ctypes
+
+    import torch
+    import torch.distributed as dist
+
+    from velvetoptimizer_b200 import _lib
+    out_ep, aux_ep = layer(x2d)  # every rank takes part
+    torch.cuda.synchronize()
+    status = layer.device_status()
+    gw = global_weights(w, dev, seed=0)
+    c = layer.cfg
+    abi = _lib.VmoeConfig(hidden=c.hidden_size, inter=c.intermediate_size,
+                          num_experts=c.moe_num_experts, top_k=c.moe_top_k,
+                          lora_rank=c.flylora_rank, lora_scaling=c.lora_scaling,
+                          era_gamma=c.era_gamma, dtype=_lib.VMOE_BF16, capacity=0)
+    h = _lib.Handle(abi, dev.index)
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    h.set_weights(_lib.VmoeWeights(**{k: ctypes.c_void_p(v.data_ptr()) for k, v in gw.items()}),
+                  stream)
+    T = x2d.shape[0]
+    ws = torch.empty(h.workspace_size(T), dtype=torch.uint8, device=dev)
+    out = torch.empty_like(x2d)
+    aux = torch.empty((), dtype=torch.float32, device=dev)
+    h.forward(x2d.data_ptr(), T, out.data_ptr(), None, None, None, None, aux.data_ptr(),
+              ws.data_ptr(), ws.numel(), stream)
+    torch.cuda.synchronize()
+    same = bool(torch.equal(out, out_ep))
+    aux_err = abs(aux.item() - aux_ep.item()) / max(abs(aux.item()), 1e-30)
+    h.close()
+    del gw, ws, out, out_ep
+    torch.cuda.empty_cache()
+    flags = torch.tensor([0.0 if same else 1.0, 1.0 if status else 0.0, aux_err], device=dev)
+    dist.all_reduce(flags, op=dist.ReduceOp.MAX)
+    return {"bit_identical": bool(flags[0].item() == 0.0), "tokens_checked": T * world,
+            "device_status_clean": bool(flags[1].item() == 0.0),
+            "aux_max_rel_err": float(flags[2].item()),
+            "reference": "each rank's tokens through a single-GPU handle with all "
+                         f"{c.moe_num_experts} experts (torch.equal of the outputs)"}
 
 
 def run_ours(args, rank, world, local_rank):
@@ -264,7 +444,8 @@ def run_ours(args, rank, world, local_rank):
     T, H, E, K = w["tokens"], w["hidden"], w["experts"], w["top_k"]
     g = torch.Generator(device=dev)
     g.manual_seed(1000 + rank)
-    x = torch.randn(T, H, generator=g, device=dev).to(torch.bfloat16).reshape(
+    f32 = w.get("dtype") == "f32"
+    x = torch.randn(T, H, generator=g, device=dev).to(torch.float32 if f32 else torch.bfloat16).reshape(
         w["batch"], T // w["batch"], H)
 
     if args.ep_chunks <= 0:
@@ -272,7 +453,7 @@ def run_ours(args, rank, world, local_rank):
     if world == 1:
         # the drop-in module (python/vesper/model.py MoELayer interface) on one GPU
         layer = build_layer(w, dev, seed=0)
-        packed = layer.packed_for(dev, torch.bfloat16)
+        packed = layer.packed_for(dev, x.dtype)
 
         if args.prenorm:
             # the layer's ffn_norm (model.py:399) as _init_weights leaves it: ones, zeros
@@ -445,38 +626,29 @@ def run_ours(args, rank, world, local_rank):
         dist.all_reduce(e2e_ms, op=dist.ReduceOp.MAX)
     e2e_value = world * T / (float(e2e_ms.item()) * 1e-3)
 
+    ep_parity = None
+    if world > 1 and not args.no_ep_parity:
+        ep_parity = check_ep_parity(layer, x.reshape(-1, H), w, dev, world)
+
     if rank != 0:
         return None
 
     pk = peaks()
-    alg = algorithmic(w)
+    alg = algorithmic(w, x.element_size())
+    g1 = stages.get("gemm1_gate_up_era", float("nan"))
     if world == 1:
-        g1 = stages.get("gemm1_gate_up_era", float("nan"))
-        achieved = alg["gemm1_flop"] / (g1 * 1e-3) / 1e12
+        scale = 1.0
         roof_kernel = "gemm1_gate_up_era (tcgen05 grouped GEMM, fused ERA*up)"
-        roof_flop = alg["gemm1_flop"]
     else:
-        # rank 0's gate|up GEMM of its first token chunk over the rows its local experts
-        # received (T0*K on average for T0 chunk tokens)
-        g1 = stages.get("gemm1_gate_up_era", float("nan"))
+        # rank 0's stages of its first token chunk; its local experts received the mean
+        # t0*K rows for the t0 chunk tokens
         t0 = min(T, -(-(-(-T // args.ep_chunks)) // 128) * 128)
-        roof_flop = alg["gemm1_flop"] * t0 / T
-        achieved = roof_flop / (g1 * 1e-3) / 1e12
+        scale = t0 / T
         roof_kernel = (f"gemm1_gate_up_era on rank 0's local experts, first of {args.ep_chunks} "
                        f"token chunks ({t0} tokens; FLOPs of the mean {t0}*K received rows)")
-    stage_report = {}
-    for name, t_ms in stages.items():
-        rec = {"ms": round(t_ms, 4), "share": round(t_ms / max(sum(stages.values()), 1e-9), 4)}
-        if name.startswith("gemm1"):
-            rec.update(achieved=round(achieved, 1), unit="TFLOP/s",
-                       frac=round(achieved / pk["bf16_tflops"], 4))
-        elif name.startswith("gemm2"):
-            a2 = alg["gemm2_flop"] / (t_ms * 1e-3) / 1e12
-            rec.update(achieved=round(a2, 1), unit="TFLOP/s", frac=round(a2 / pk["bf16_tflops"], 4))
-        elif name in ("router", "dispatch", "combine"):
-            gbs = alg[f"{name}_bytes"] / (t_ms * 1e-3) / 1e9
-            rec.update(achieved=round(gbs, 1), unit="GB/s", frac=round(gbs / pk["hbm_gbs"], 4))
-        stage_report[name] = rec
+    roof_flop = alg["gemm1_flop"] * scale
+    achieved = roof_flop / (g1 * 1e-3) / 1e12
+    stage_report = stage_table(stages, alg, pk, scale=scale, fp32=f32, ep=world > 1)
 
     line = {
         "metric": "MoE-layer fwd tokens/s",
@@ -489,7 +661,7 @@ def run_ours(args, rank, world, local_rank):
         "higher_is_better": True,
         "scaling": "weak",
         "vs_baseline": None,
-        "dtype": "bf16",
+        "dtype": "f32" if f32 else "bf16",
         "data": "synthetic: x~N(0,1), weights~N(0,0.02), zero bias, FlyLoRA off, seed 0",
         "config": {"workload": f"{args.workload}: MoE FFN layer fwd, {T} tokens/GPU, d_model {H}, "
                                f"expert d_ff {w['inter']}, {E} experts, top-{K}",
@@ -524,11 +696,31 @@ def run_ours(args, rank, world, local_rank):
         "gpu_launches": launches,
         "clocks": clocks,
     }
+    if world > 1:
+        line["stages_note"] = ("rank 0's first token chunk: plan includes publishing the counts "
+                               "to every rank, dispatch the wait for every rank's rows, gemm2 the "
+                               "NVLink push of the outputs when pushing, combine the signal and "
+                               "wait for every rank's outputs")
+    if ep_parity is not None:
+        line["ep_parity"] = ep_parity
     if prenorm_report:
         line["prenorm"] = prenorm_report
         line["config"]["workload"] += "; fused pre-norm block x + MoE(LayerNorm(x))"
     if world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(layer, x.reshape(T, H), w, args.cpu_seconds)
+    if world == 1 and not args.no_workloads and not args.prenorm and not args.graph:
+        # the other configurations, each timed after the headline region in this process
+        layer.close()
+        del layer, packed, x, x_host, out_host
+        torch.cuda.empty_cache()
+        extra = {}
+        for name in ("c2_decode", "c3_prefill", "c4_skewed", "c1_fp32"):
+            if name == args.workload:
+                continue
+            extra[name] = time_workload(name, min(args.steps, 20), max(3, min(args.warmup, 5)),
+                                        dev, cpu_seconds=min(args.cpu_seconds, 4.0),
+                                        graph=name == "c2_decode")
+        line["workloads"] = extra
     return line
 
 
@@ -769,7 +961,7 @@ def run_reference(args):
         "config": {"workload": args.workload, "tokens_per_step": n, "hidden": H, "inter": I,
                    "experts": E, "top_k": K},
         "cpu_baseline": {"value": round(value, 2), "unit": "tokens/s", "cores": os.cpu_count(),
-                         "kind": "port",
+                         "kind": "port", "cpu_model": cpu_model(),
                          "sample": f"{n} tokens per step of the {T}-token workload, numpy fp32 "
                                    "oracle (CPU restatement of python/vesper/model.py:317-385)"},
         "e2e": {"value": round(value, 2), "unit": "tokens/s", "h2d_bytes_per_step": 0,
