@@ -135,7 +135,7 @@ VMOE_API int vmoe_forward_no_alloc(vmoe_handle* h, const void* x, int64_t tokens
 /* Where vmoe_forward keeps its intermediates inside the workspace (byte offsets), so a
  * caller can inspect the dispatch: for token t and slot k, slot_of[t*K + k] is the row of
  * the expert-major permuted buffer that holds x[t] (-1 when capacity dropped it); expert
- * e owns rows [expert_offsets[e], expert_offsets[e+1]) (padded to 128-row tiles), filled
+ * e owns rows [expert_offsets[e], expert_offsets[e+1]) (padded to vmoe_segment_align rows), filled
  * in ascending token order like the reference's nonzero() (python/vesper/model.py:347). */
 typedef struct vmoe_ws_layout {
   size_t slot_of;        /* int32 [T*K]                                  */
@@ -346,6 +346,12 @@ VMOE_API int vmoe_last_launch_count(const vmoe_handle* h);
  * expert segments are padded to this, and vmoe_ep_experts' tile_expert has one entry per
  * tile of this many rows.  Not part of the reference. */
 VMOE_API int vmoe_gemm_tile_rows(const vmoe_handle* h);
+
+/* Rows each expert segment of the permuted buffer is padded to in a vmoe_forward of
+ * `tokens` tokens: vmoe_gemm_tile_rows, or 16 for decode-sized bf16 batches (at most 256
+ * tokens), whose GEMMs take the weights as the MMA's M operand and each expert's rows as
+ * its N operand.  0 for a null handle or negative tokens.  Not part of the reference. */
+VMOE_API int vmoe_segment_align(const vmoe_handle* h, int64_t tokens);
 
 /* Last error message of this handle ("" if none), and a static text per code. */
 VMOE_API const char* vmoe_last_error(const vmoe_handle* h);

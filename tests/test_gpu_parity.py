@@ -41,12 +41,15 @@ def permutation_from_slots(layer, T, res):
 
 
 def check_dispatch(layer, T, res, oracle_idx):
-    """Slots are expert-major, padded to 128 rows, token-ascending within each expert."""
+    """Slots are expert-major, padded to the forward's segment alignment (whole GEMM tiles,
+    or 16 rows for a decode-sized bf16 batch), token-ascending within each expert."""
     slot, offs = permutation_from_slots(layer, T, res)
     E = layer.case.experts
     counts, perm_tok, _ = O.dispatch(oracle_idx, E)
     assert np.array_equal(res["counts"], counts)
-    assert (offs[1:] - offs[:-1] >= 0).all() and (offs % 128 == 0).all()
+    align = layer.handle.lib.vmoe_segment_align(layer.handle.ptr, T)
+    assert align in (16, 128, 256)
+    assert (offs[1:] - offs[:-1] >= 0).all() and (offs % align == 0).all()
     got = []
     for e in range(E):
         rows = []

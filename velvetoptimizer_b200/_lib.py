@@ -35,7 +35,8 @@ EXPORTED = (
     "vmoe_last_launch_count", "vmoe_last_error", "vmoe_status_string", "vmoe_abi_version",
     "vmoe_create_ep", "vmoe_ep_workspace_size", "vmoe_ep_route", "vmoe_ep_experts",
     "vmoe_ep_combine", "vmoe_ep_p2p_setup", "vmoe_ep_p2p_connect", "vmoe_ep_p2p_workspace_size",
-    "vmoe_ep_p2p_forward", "vmoe_gemm_tile_rows", "vmoe_ffn_create", "vmoe_ffn_workspace_size",
+    "vmoe_ep_p2p_forward", "vmoe_gemm_tile_rows", "vmoe_segment_align", "vmoe_ffn_create",
+    "vmoe_ffn_workspace_size",
     "vmoe_ffn_forward", "vmoe_forward_host_workspace_size", "vmoe_forward_host",
     "vmoe_set_norm", "vmoe_forward_residual", "vmoe_set_training", "vmoe_train_workspace_size",
     "vmoe_forward_train", "vmoe_backward", "vmoe_backward_stage_times",
@@ -177,6 +178,8 @@ def load() -> ctypes.CDLL:
     lib.vmoe_ffn_forward.restype = c_int
     lib.vmoe_gemm_tile_rows.argtypes = [H]
     lib.vmoe_gemm_tile_rows.restype = c_int
+    lib.vmoe_segment_align.argtypes = [H, c_int64]
+    lib.vmoe_segment_align.restype = c_int
     lib.vmoe_last_error.argtypes = [H]
     lib.vmoe_last_error.restype = c_char_p
     lib.vmoe_status_string.argtypes = [c_int]

@@ -1,0 +1,343 @@
+// Decode-sized grouped expert GEMMs on the 5th-generation tensor cores, operands swapped.
+//
+// Reference math (python/vesper/model.py:295-298, per expert e over its n_e routed rows):
+//   gated: h = ERA(x_e Wg_e^T + bg_e) * (x_e Wu_e^T + bu_e)     (ERA :69-76)
+//   plain: y = h_e Wd_e^T + bd_e
+// In a decode batch an expert receives a handful of rows (64 tokens, top-2 over 8 experts:
+// 16 rows each) while its weights are tens of megabytes, so the layer is bound by reading
+// every active expert's weights once from HBM.  The row-tiled GEMMs would pad each expert's
+// rows to a 256-row MMA tile.  Here the weights are the MMA's M operand (128 output features
+// per tile, K-major exactly as packed) and the expert's rows are the N operand, N = its
+// segment length (a multiple of 16, at most 256) written into the instruction descriptor
+// per work item at run time:
+//   D^T [128 features x N rows] = W_block [128 x K] . X_e^T
+// so the tensor cores do only the useful products and the weight stream sets the pace.
+//
+// Work items are (active expert, 128-row weight block), spread over a persistent grid.  For
+// the gated GEMM a block is 64 gate rows plus the 64 up rows of the same features (two
+// 64-row TMA boxes into one 128-row stage), so TMEM lanes 0..63 hold gate and 64..127 up
+// for the same features; the up warps hand their values to the gate warps through shared
+// memory.  Experts that received no rows are skipped: their weights are never read.
+//
+// Roles (192 threads, one CTA per SM):
+//   warp 0      TMA producer: per k-block one 16 KB weight tile and N/16 row tiles of the
+//               expert's activations (16-row boxes) into a ring of 128B-swizzled stages;
+//   warp 1      TMEM allocator (two accumulators of 256 columns) and MMA issuer
+//               (tcgen05.mma M = 128, N = rows, K = 16, four per k-block);
+//   warps 2..5  epilogue: tcgen05.ld of 16 columns (rows) at a time, bias, ERA * up (gated)
+//               and bf16 stores into the row-major output; the accumulator is released as
+//               soon as it has been read, so the next item's main loop overlaps.
+// Every wait is bounded (kWaitLimitNs) and reports a status code; after an abort the kernel
+// drains its own copies and MMAs (bounded) and frees TMEM.  No TMA multicast is used.
+#include <stdio.h>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace vmoe {
+namespace {
+
+constexpr int BK = 64;
+constexpr uint32_t A_BYTES = 128 * BK * 2;     // 16 KB: 128 weight rows x 64 K
+constexpr uint32_t B_ROW_BYTES = BK * 2;       // 128 B: one activation row x 64 K
+constexpr uint32_t B_BOX_ROWS = 16;            // rows per activation TMA box
+constexpr int kMaxStages = 12;
+constexpr uint32_t kAccCols = 256;             // one accumulator: up to 256 rows (N)
+constexpr uint32_t kTmemCols = 2 * kAccCols;
+constexpr size_t kSmemBudget = 220 * 1024;
+
+struct DecShared {
+  uint64_t full[kMaxStages];
+  uint64_t empty[kMaxStages];
+  uint64_t tfull[2];
+  uint64_t tempty[2];
+  uint64_t done;
+  uint32_t tmem_base;
+  int abort;
+  int issued;
+  int consumed;
+  int n_act;
+  int ep_ok[2][4];                 // gated epilogue: each warp's wait result, per item parity
+  int act_e[kDecodeMaxExperts];    // experts with rows, ascending id
+  int act_seg[kDecodeMaxExperts];  // first row of the expert's segment
+  int act_n[kDecodeMaxExperts];    // its rows, a multiple of 16 in [16, 256]
+  float xch[2][64][17];            // up values handed to the gate warps (17: no bank conflicts)
+};
+
+__device__ __forceinline__ bool aborted(const DecShared* sh) {
+  return *reinterpret_cast<const volatile int*>(&sh->abort) != 0;
+}
+__device__ __forceinline__ void set_abort(DecShared* sh, int* status, int code) {
+  *reinterpret_cast<volatile int*>(&sh->abort) = 1;
+  report(status, code);
+}
+
+__device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+
+__device__ __forceinline__ void store_bf16(__nv_bfloat16* p, float v) { *p = __float2bfloat16_rn(v); }
+
+template <bool GATED>
+__global__ void __launch_bounds__(192, 1)
+decode_gemm_kernel(const __grid_constant__ CUtensorMap a_map,
+                   const __grid_constant__ CUtensorMap b_map, const DecodeGemmArgs args) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  const uint32_t base = (raw + 1023u) & ~1023u;
+  uint8_t* gbase = smem_raw + (base - raw);
+  const int stages = args.stages;
+  const uint32_t b_slot = args.b_slot_bytes;
+  const uint32_t a_s = base;
+  const uint32_t b_s = base + static_cast<uint32_t>(stages) * A_BYTES;
+  DecShared* sh = reinterpret_cast<DecShared*>(gbase + static_cast<size_t>(stages) * (A_BYTES + b_slot));
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < stages; ++s) {
+      mbar_init(smem_u32(&sh->full[s]), 1);
+      mbar_init(smem_u32(&sh->empty[s]), 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(smem_u32(&sh->tfull[a]), 1);
+      mbar_init(smem_u32(&sh->tempty[a]), 4);
+    }
+    mbar_init(smem_u32(&sh->done), 1);
+    sh->abort = 0;
+    sh->issued = 0;
+    sh->consumed = 0;
+    // the experts that received rows, in ascending id, with their segments
+    int n = 0;
+    const int E = args.num_experts < kDecodeMaxExperts ? args.num_experts : kDecodeMaxExperts;
+    for (int e = 0; e < E; ++e) {
+      const int seg = args.offs[e], len = args.offs[e + 1] - seg;
+      if (len <= 0) continue;
+      int rows = len;
+      if (rows > args.n_max || (rows & 15) || seg < 0 ||
+          static_cast<int64_t>(seg) + rows > args.max_rows) {
+        report(args.status, kStatusBadTileCount);  // never read or write past the buffers
+        continue;
+      }
+      sh->act_e[n] = e;
+      sh->act_seg[n] = seg;
+      sh->act_n[n] = rows;
+      ++n;
+    }
+    sh->n_act = n;
+    fence_mbar_init();
+    prefetch_tmap(&a_map);
+    prefetch_tmap(&b_map);
+  }
+  if (warp == 1) tmem_alloc(smem_u32(&sh->tmem_base), kTmemCols);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = sh->tmem_base;
+  const int bpe = args.blocks_per_expert, k_blocks = args.k_blocks;
+  const int total = sh->n_act * bpe;
+
+  if (warp == 0) {
+    // ---------------- TMA producer ----------------
+    if (lane == 0) {
+      int it = 0;
+      bool ok = true;
+      for (int item = blockIdx.x; item < total && ok; item += gridDim.x) {
+        const int a = item / bpe, blk = item - a * bpe;
+        const int e = sh->act_e[a], seg = sh->act_seg[a], rows = sh->act_n[a];
+        // gated: gate rows [256 j + 64 hh, +64) and the up rows 128 further of block blk
+        const int a_row = GATED ? e * args.a_rows_per_expert + 256 * (blk >> 1) + 64 * (blk & 1)
+                                : e * args.a_rows_per_expert + 128 * blk;
+        const uint32_t tx = A_BYTES + static_cast<uint32_t>(rows) * B_ROW_BYTES;
+        for (int kb = 0; kb < k_blocks; ++kb, ++it) {
+          const int s = it % stages;
+          const uint32_t ph = (it / stages) & 1;
+          if (!mbar_wait(smem_u32(&sh->empty[s]), ph ^ 1)) {
+            set_abort(sh, args.status, kStatusTimeoutProducer);
+            ok = false;
+            break;
+          }
+          if (aborted(sh)) { ok = false; break; }
+          const uint32_t fb = smem_u32(&sh->full[s]);
+          mbar_arrive_expect_tx(fb, tx);
+          const uint32_t a_dst = a_s + s * A_BYTES;
+          if constexpr (GATED) {
+            tma_load_2d(a_dst, &a_map, fb, kb * BK, a_row);
+            tma_load_2d(a_dst + A_BYTES / 2, &a_map, fb, kb * BK, a_row + 128);
+          } else {
+            tma_load_2d(a_dst, &a_map, fb, kb * BK, a_row);
+          }
+          const uint32_t b_dst = b_s + s * b_slot;
+          for (int r = 0; r < rows; r += B_BOX_ROWS)
+            tma_load_2d(b_dst + r * B_ROW_BYTES, &b_map, fb, kb * BK, seg + r);
+          *reinterpret_cast<volatile int*>(&sh->issued) = it + 1;
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      int it = 0, local = 0;
+      for (int item = blockIdx.x; item < total; item += gridDim.x, ++local) {
+        const int a = item / bpe;
+        const uint32_t idesc = umma_idesc_bf16(128, sh->act_n[a]);
+        const int acc = local & 1;
+        const uint32_t aph = (local >> 1) & 1;
+        if (!mbar_wait(smem_u32(&sh->tempty[acc]), aph ^ 1)) {
+          set_abort(sh, args.status, kStatusTimeoutMma);
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem + acc * kAccCols;
+        bool ok = true;
+        for (int kb = 0; kb < k_blocks; ++kb, ++it) {
+          const int s = it % stages;
+          const uint32_t ph = (it / stages) & 1;
+          if (!mbar_wait(smem_u32(&sh->full[s]), ph)) {
+            set_abort(sh, args.status, kStatusTimeoutMma);
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = a_s + s * A_BYTES, b_addr = b_s + s * b_slot;
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k)
+            umma_bf16(d_tmem, umma_desc_sw128(a_addr + k * 32), umma_desc_sw128(b_addr + k * 32),
+                      idesc, (kb | k) != 0 ? 1u : 0u);
+          umma_commit(smem_u32(&sh->empty[s]));
+          *reinterpret_cast<volatile int*>(&sh->consumed) = it + 1;
+        }
+        if (!ok) break;
+        umma_commit(smem_u32(&sh->tfull[acc]));
+        if (aborted(sh)) break;
+      }
+      umma_commit(smem_u32(&sh->done));
+      if (!mbar_wait(smem_u32(&sh->done), 0)) report(args.status, kStatusTimeoutDrain);
+    }
+  } else {
+    // ---------------- epilogue (warps 2..5) ----------------
+    const int q = warp & 3;  // TMEM lane quarter: rows (features) 32q .. 32q + 31
+    __nv_bfloat16* out = static_cast<__nv_bfloat16*>(args.out);
+    int chunk = 0;           // 16-row chunks handed over so far (alternates the xch buffers)
+    int local = 0;
+    for (int item = blockIdx.x; item < total; item += gridDim.x, ++local) {
+      const int acc = local & 1;
+      const uint32_t aph = (local >> 1) & 1;
+      const bool got = mbar_wait(smem_u32(&sh->tfull[acc]), aph);
+      __syncwarp();
+      const bool warp_ok = __all_sync(0xffffffffu, got);
+      if constexpr (GATED) {
+        // the four warps hand values to each other through named barriers, so they must
+        // agree on going on: each publishes its own (bounded) wait's result and all read
+        // the four after the barrier (the flags of item i + 1 are written only after every
+        // warp passed item i's first hand-over barrier, so a double buffer suffices)
+        if (lane == 0) sh->ep_ok[local & 1][q] = warp_ok ? 1 : 0;
+        epi_bar();
+        const int* okf = sh->ep_ok[local & 1];
+        if (!(okf[0] && okf[1] && okf[2] && okf[3])) {
+          if (lane == 0 && !warp_ok) set_abort(sh, args.status, kStatusTimeoutEpilogue);
+          break;
+        }
+      } else if (!warp_ok) {
+        if (lane == 0) set_abort(sh, args.status, kStatusTimeoutEpilogue);
+        break;
+      }
+      tc_fence_after();
+      const int a = item / bpe, blk = item - a * bpe;
+      const int e = sh->act_e[a], seg = sh->act_seg[a], rows = sh->act_n[a];
+      const uint32_t t_row = tmem + (static_cast<uint32_t>(q * 32) << 16) + acc * kAccCols;
+      const bool limit = args.row_limit > 0;
+      if constexpr (GATED) {
+        // feature f of this lane (gate warps q = 0, 1; the up warps q = 2, 3 hold the same
+        // features' up values); packed bias: gate at 256 j + c, up at 256 j + 128 + c
+        const int fl = 32 * (q & 1) + lane;                  // 0..63 within the block
+        const int f = 64 * blk + fl;                         // feature (column of h)
+        const int64_t bcol = static_cast<int64_t>(e) * args.bias_ld + 256 * (blk >> 1) +
+                             64 * (blk & 1) + fl;
+        const float bg = args.bias[bcol], bu = args.bias[bcol + 128];
+        for (int c = 0; c < rows; c += 16, ++chunk) {
+          float (*x)[17] = sh->xch[chunk & 1];
+          float v[16];
+          tmem_ld16(t_row + c, v);
+          if (q >= 2) {
+#pragma unroll
+            for (int j = 0; j < 16; ++j) x[fl][j] = v[j] + bu;
+          }
+          epi_bar();
+          if (q < 2) {
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              const int64_t r = static_cast<int64_t>(seg) + c + j;
+              if (!limit || r < args.row_limit)
+                store_bf16(out + r * args.ldo + f, era_fast(v[j] + bg, args.gamma) * x[fl][j]);
+            }
+          }
+        }
+      } else {
+        const int f = 128 * blk + 32 * q + lane;  // output feature (column of y)
+        const float bias = args.bias ? args.bias[static_cast<int64_t>(e) * args.bias_ld + f] : 0.f;
+        for (int c = 0; c < rows; c += 16) {
+          float v[16];
+          tmem_ld16(t_row + c, v);
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            const int64_t r = static_cast<int64_t>(seg) + c + j;
+            if (!limit || r < args.row_limit) store_bf16(out + r * args.ldo + f, v[j] + bias);
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(&sh->tempty[acc]));
+    }
+  }
+
+  __syncthreads();
+  // after an abort: wait (bounded) for TMA loads that were issued but never consumed
+  if (threadIdx.x == 0 && aborted(sh)) {
+    const int issued = *reinterpret_cast<volatile int*>(&sh->issued);
+    const int consumed = *reinterpret_cast<volatile int*>(&sh->consumed);
+    for (int i = consumed; i < issued; ++i) {
+      if (!mbar_wait(smem_u32(&sh->full[i % stages]), (i / stages) & 1)) {
+        report(args.status, kStatusTimeoutDrain);
+        break;
+      }
+    }
+  }
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+}  // namespace
+
+int decode_gemm_stages(int n_max) {
+  const size_t stage = A_BYTES + static_cast<size_t>(n_max) * B_ROW_BYTES;
+  const size_t fixed = 1024 + sizeof(DecShared) + 64;
+  const int s = static_cast<int>((kSmemBudget - fixed) / stage);
+  return s > kMaxStages ? kMaxStages : s;
+}
+
+cudaError_t launch_decode_gemm(bool gated, const CUtensorMap& a_map, const CUtensorMap& b_map,
+                               DecodeGemmArgs args, int64_t max_items, int num_sms,
+                               cudaStream_t s) {
+  if (args.n_max < 16 || args.n_max > static_cast<int>(kAccCols) || (args.n_max & 15) ||
+      args.num_experts < 1 || args.num_experts > kDecodeMaxExperts || args.blocks_per_expert < 1 ||
+      args.k_blocks < 1 || !args.offs || !args.out || (gated && !args.bias))
+    return cudaErrorInvalidValue;
+  args.stages = decode_gemm_stages(args.n_max);
+  if (args.stages < 2) return cudaErrorInvalidValue;
+  args.b_slot_bytes = static_cast<uint32_t>(args.n_max) * B_ROW_BYTES;
+  const size_t smem = 1024 + static_cast<size_t>(args.stages) * (A_BYTES + args.b_slot_bytes) +
+                      sizeof(DecShared) + 64;
+  auto kern = gated ? decode_gemm_kernel<true> : decode_gemm_kernel<false>;
+  cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(smem));
+  if (err != cudaSuccess) return err;
+  int64_t grid = max_items < num_sms ? max_items : num_sms;
+  if (grid < 1) grid = 1;
+  kern<<<static_cast<unsigned>(grid), 192, smem, s>>>(a_map, b_map, args);
+  return cudaGetLastError();
+}
+
+}  // namespace vmoe

@@ -188,6 +188,40 @@ int tc_router_width(int E);
 cudaError_t launch_tc_router(const CUtensorMap& x_map, const CUtensorMap& w_map,
                              const TcGemmArgs& args, int num_sms, cudaStream_t s, bool ln);
 
+// ---- decode-sized expert GEMMs (operands swapped: weights are M, the rows are N) --------
+// Used when a forward has at most kDecodeMaxTokens tokens: every expert then receives at
+// most that many rows, its segment is padded to kDecodeRowAlign rows and becomes the MMA's
+// N (16..256); the weights are the M operand, 128 rows per work item.
+constexpr int kDecodeMaxTokens = 256;
+constexpr int kDecodeRowAlign = 16;
+constexpr int kDecodeMaxExperts = 256;
+struct DecodeGemmArgs {
+  const int* offs;          // [E+1] segment starts (rows), multiples of kDecodeRowAlign
+  int num_experts;          // E (<= kDecodeMaxExperts)
+  int64_t max_rows;         // rows the activation and output buffers hold
+  int k_blocks;             // ceil(K / 64)
+  int blocks_per_expert;    // work items per expert: 128-row weight blocks
+  int a_rows_per_expert;    // rows of the packed weight view per expert (2*Ipad or Hpad)
+  int n_max;                // largest segment (rows) any expert can have, multiple of 16
+  void* out;                // bf16 [max_rows, ldo]
+  int64_t ldo;
+  const float* bias;        // gated: interleaved gate|up [E, bias_ld]; plain: [E, bias_ld]
+  int64_t bias_ld;
+  float gamma;              // ERA gamma (gated)
+  int64_t row_limit;        // rows >= row_limit are not stored (0 = no limit)
+  int* status;
+  int stages;               // set by the launcher
+  uint32_t b_slot_bytes;    // set by the launcher
+};
+// gated = true : a_map = packed gate|up weights with 64-row boxes, b_map = x_perm (16-row
+//                boxes); out = h [rows, Ipad] = ERA(gate + bg) * (up + bu)
+// gated = false: a_map = packed down weights with 128-row boxes, b_map = h (16-row boxes);
+//                out = y [rows, Hpad] = down + bd
+cudaError_t launch_decode_gemm(bool gated, const CUtensorMap& a_map, const CUtensorMap& b_map,
+                               DecodeGemmArgs args, int64_t max_items, int num_sms,
+                               cudaStream_t s);
+int decode_gemm_stages(int n_max);
+
 // ---- backward --------------------------------------------------------------------------
 // Grouped weight gradient: for e < num_experts, dW_e = A_e^T B_e over the rows of e's
 // segment [seg_offs[e], seg_offs[e+1]) (multiples of 64; seg_offs null: one segment of

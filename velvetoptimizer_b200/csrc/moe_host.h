@@ -113,6 +113,10 @@ struct vmoe_handle {
   float* b_d = nullptr; // [E, Hpad]
   int* status = nullptr;
   CUtensorMap map_wgu{}, map_wd{};
+  // decode-sized forwards (at most decode_max_tokens tokens, bf16): the swapped-operand
+  // GEMMs read the packed weights through these maps (64-row gate|up boxes, 128-row down)
+  CUtensorMap map_wgu_dec{}, map_wd_dec{};
+  int decode_max_tokens = 0;  // 0: never
   int tile_rows = kTileM;  // GEMM M tile: 256 with CTA-pair GEMMs (bf16), else 128
   bool dense = false;      // a dense FeedForward handle (one expert, no router)
   CUtensorMap map_wr{};   // router weights for the tensor-core router (bf16, E <= 64)
@@ -253,6 +257,65 @@ int run_expert_gemms(vmoe_handle* h, void* xp, int64_t max_rows, const int* tile
   return check(pair ? launch_tc_gemm_pair(false, map_h, h->map_wd, a2, max_tiles, sms, s)
                     : launch_tc_gemm(false, map_h, h->map_wd, a2, max_tiles, sms, s),
                "gemm2");
+}
+
+// Whether a single-GPU forward of T tokens runs the decode-sized (swapped-operand) GEMMs.
+inline bool use_decode_gemms(const vmoe_handle* h, int64_t T) {
+  return h->dtype == kBF16 && !h->dense && h->ep_size == 1 && T > 0 &&
+         T <= h->decode_max_tokens && h->E_local <= kDecodeMaxExperts;
+}
+
+// Row alignment of the expert segments in a forward of T tokens.
+inline int segment_align(const vmoe_handle* h, int64_t T) {
+  return use_decode_gemms(h, T) ? kDecodeRowAlign : h->tile_rows;
+}
+
+// gate|up GEMM (+ ERA * up) then down GEMM over the expert-major buffer of a decode-sized
+// forward: segments padded to kDecodeRowAlign rows at offs[E+1], no tile map.
+template <typename Mark, typename Check>
+int run_decode_gemms(vmoe_handle* h, void* xp, int64_t max_rows, const int* offs, void* hb,
+                     void* yb, int64_t T, cudaStream_t s, Mark&& mark, Check&& check) {
+  const int64_t H = h->H, El = h->E_local;
+  char why[256];
+  CUtensorMap map_x, map_h;
+  if (!make_tmap_bf16(&map_x, xp, max_rows, H, H, kDecodeRowAlign, why, sizeof(why)))
+    return fail(h, VMOE_ERR_CUDA, "x_perm tensor map: %s", why);
+  if (!make_tmap_bf16(&map_h, hb, max_rows, h->Ipad, h->Ipad, kDecodeRowAlign, why, sizeof(why)))
+    return fail(h, VMOE_ERR_CUDA, "h tensor map: %s", why);
+  int64_t n_max = round_up(T, kDecodeRowAlign);
+  if (h->cfg.capacity > 0 && round_up(h->cfg.capacity, kDecodeRowAlign) < n_max)
+    n_max = round_up(h->cfg.capacity, kDecodeRowAlign);
+  DecodeGemmArgs a{};
+  a.offs = offs;
+  a.num_experts = static_cast<int>(El);
+  a.max_rows = max_rows;
+  a.k_blocks = static_cast<int>((H + 63) / 64);
+  a.blocks_per_expert = static_cast<int>(h->Ipad / 64);
+  a.a_rows_per_expert = static_cast<int>(2 * h->Ipad);
+  a.n_max = static_cast<int>(n_max);
+  a.out = hb;
+  a.ldo = h->Ipad;
+  a.bias = h->b_g;
+  a.bias_ld = 2 * h->Ipad;
+  a.gamma = h->cfg.era_gamma;
+  a.status = h->status;
+  int rc;
+  if ((rc = check(launch_decode_gemm(true, h->map_wgu_dec, map_x, a, El * a.blocks_per_expert,
+                                     h->num_sms, s),
+                  "gemm1 (decode)")) != VMOE_OK)
+    return rc;
+  mark();
+  a.k_blocks = static_cast<int>(h->Ipad / 64);
+  a.blocks_per_expert = static_cast<int>(h->Hpad / 128);
+  a.a_rows_per_expert = static_cast<int>(h->Hpad);
+  a.out = yb;
+  a.ldo = h->Hpad;
+  a.bias = h->b_d;
+  a.bias_ld = h->Hpad;
+  a.gamma = 0.f;
+  return check(launch_decode_gemm(false, h->map_wd_dec, map_h, a, El * a.blocks_per_expert,
+                                  h->num_sms, s),
+               "gemm2 (decode)");
 }
 
 int run_router(vmoe_handle* h, const void* x, int64_t T, float* logits, int32_t* idx, float* tw,

@@ -165,9 +165,13 @@ int forward_batch(vmoe_handle* h, const void* x, int64_t T, void* out, float* ro
                   "scan")) != VMOE_OK)
     return rc;
   mark();
+  // decode-sized batches: segments padded to 16 rows for the swapped-operand GEMMs, which
+  // need no tile map
+  const bool decode = use_decode_gemms(h, T);
   if ((rc = check(launch_plan(counts, psum_tot, T, static_cast<int>(E), static_cast<int>(K),
-                              h->cfg.capacity, static_cast<int>(h->tile_rows), offs, tiles,
-                              ntiles, aux, expert_counts, s),
+                              h->cfg.capacity, segment_align(h, T), offs,
+                              decode ? nullptr : tiles, decode ? nullptr : ntiles, aux,
+                              expert_counts, s),
                   "plan")) != VMOE_OK)
     return rc;
   mark();
@@ -177,8 +181,9 @@ int forward_batch(vmoe_handle* h, const void* x, int64_t T, void* out, float* ro
                   "dispatch")) != VMOE_OK)
     return rc;
   mark();
-  if ((rc = run_expert_gemms(h, xp, p.max_rows, tiles, ntiles, hb, yb, h->Hpad, s, mark,
-                             check)) != VMOE_OK)
+  if ((rc = decode ? run_decode_gemms(h, xp, p.max_rows, offs, hb, yb, T, s, mark, check)
+                   : run_expert_gemms(h, xp, p.max_rows, tiles, ntiles, hb, yb, h->Hpad, s, mark,
+                                      check)) != VMOE_OK)
     return rc;
   mark();
   if ((rc = check(launch_combine(h->dtype, yb, h->Hpad, idx, tw, slot, T, static_cast<int>(H),
@@ -358,6 +363,13 @@ int vmoe_create(const vmoe_config* cfg, int device, vmoe_handle** out) {
     h->Hpad = round_up(h->H, kDownTileN);
     const char* pair = getenv("VMOE_PAIR_GEMM");  // "0" selects the single-CTA GEMMs
     h->tile_rows = (pair && pair[0] == '0') ? kTileM : 2 * kTileM;
+    // forwards of at most this many tokens run the swapped-operand (decode) GEMMs;
+    // VMOE_DECODE_MAX_TOKENS lowers it (0: never)
+    h->decode_max_tokens = kDecodeMaxTokens;
+    if (const char* d = getenv("VMOE_DECODE_MAX_TOKENS")) {
+      const long v = strtol(d, nullptr, 10);
+      h->decode_max_tokens = v < 0 ? 0 : (v > kDecodeMaxTokens ? kDecodeMaxTokens : static_cast<int>(v));
+    }
   } else {
     h->Ipad = h->I;
     h->Hpad = h->H;
@@ -546,6 +558,9 @@ int vmoe_set_weights(vmoe_handle* h, const vmoe_weights* w, void* stream) {
       return fail(h, VMOE_ERR_CUDA, "gate/up tensor map: %s", why);
     if (!make_tmap_bf16(&h->map_wd, h->w_d, El * Hpad, Ipad, Ipad, b_box, why, sizeof(why)))
       return fail(h, VMOE_ERR_CUDA, "down tensor map: %s", why);
+    if (!make_tmap_bf16(&h->map_wgu_dec, h->w_g, El * 2 * Ipad, H, H, 64, why, sizeof(why)) ||
+        !make_tmap_bf16(&h->map_wd_dec, h->w_d, El * Hpad, Ipad, Ipad, 128, why, sizeof(why)))
+      return fail(h, VMOE_ERR_CUDA, "decode weight tensor maps: %s", why);
   }
   h->ready = true;
   if (h->ln_w && (rc = refold_norm(h, s)) != VMOE_OK) return rc;
@@ -883,5 +898,9 @@ int vmoe_stage_times(vmoe_handle* h, float* ms, int n, int* n_out, int* forwards
 int vmoe_last_launch_count(const vmoe_handle* h) { return h ? h->last_launches : 0; }
 
 int vmoe_gemm_tile_rows(const vmoe_handle* h) { return h ? h->tile_rows : 0; }
+
+int vmoe_segment_align(const vmoe_handle* h, int64_t tokens) {
+  return h && tokens >= 0 ? segment_align(h, tokens) : 0;
+}
 
 }  // extern "C"
