@@ -146,7 +146,10 @@ plan_carry_kernel(const int* __restrict__ counts, const int* __restrict__ carry_
 }
 
 // ---- 3. slot assignment + gather -----------------------------------------------------
-// grid = nblk, block = 128 (one thread per token of the routing block).  With a carry
+// grid = (nblk, S), block = 128 (one thread per token of the routing block).  The S blocks
+// of one routing block all derive its slots (cheap) and each copies every S-th group of
+// four tokens' rows, so that a small batch's rows are copied by many SMs; only the first
+// writes slot_of and the carry lists.  With a carry
 // (DispatchCarry::computed set) the token chunk's new rows follow the carried-in rows of
 // each segment, rows past the computed part go to the carry-out list instead of the buffer,
 // and slots are numbered from slot_base (the buffer's first row in a ring of buffers).
@@ -165,15 +168,15 @@ dispatch_kernel(const T* __restrict__ x, const int32_t* __restrict__ topk_idx,
                 int E, int K, int64_t capacity, int* __restrict__ slot_of, T* __restrict__ x_perm,
                 int64_t xp_ld, int* status, const float2* __restrict__ ln_stats,
                 const float* __restrict__ ln_w, const float* __restrict__ ln_b,
-                const DispatchCarry carry) {
+                const DispatchCarry carry, int rb) {
   extern __shared__ uint32_t dsm[];
   uint32_t* masks = dsm;                            // [4 warps][E] token bitmasks
   int* wbase = reinterpret_cast<int*>(dsm + 4 * E);  // [4][E]
   int* slots = wbase + 4 * E;                        // [128][K]
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int64_t blk = blockIdx.x;
-  const int64_t t = blk * kTileM + tid;
-  const bool valid = t < T_tok;
+  const int64_t t = blk * rb + tid;  // rb tokens per routing block (<= 128 threads)
+  const bool valid = tid < rb && t < T_tok;
 
   for (int i = tid; i < 4 * E; i += 128) masks[i] = 0u;
   __syncthreads();
@@ -201,7 +204,8 @@ dispatch_kernel(const T* __restrict__ x, const int32_t* __restrict__ topk_idx,
         if (over < 0) {
           slot = offs[e] + pos;
         } else if (over < kCarryCap) {
-          carry.list_out[e * kCarryCap + over] = static_cast<int>((carry.t0 + t) * K + k);
+          if (blockIdx.y == 0)
+            carry.list_out[e * kCarryCap + over] = static_cast<int>((carry.t0 + t) * K + k);
         } else {
           report(status, kStatusBadSlot);
         }
@@ -210,7 +214,8 @@ dispatch_kernel(const T* __restrict__ x, const int32_t* __restrict__ topk_idx,
       }
       if (slot >= offs[e + 1]) { report(status, kStatusBadSlot); slot = -1; }
       // a carried-out row gets its slot from the next chunk (carry_rows_kernel)
-      slot_of[t * K + k] = slot >= 0 ? static_cast<int>(carry.slot_base + slot) : -1;
+      if (blockIdx.y == 0)
+        slot_of[t * K + k] = slot >= 0 ? static_cast<int>(carry.slot_base + slot) : -1;
     }
     slots[tid * K + k] = slot;
   }
@@ -218,11 +223,11 @@ dispatch_kernel(const T* __restrict__ x, const int32_t* __restrict__ topk_idx,
   // gather: each warp copies whole rows with 16-byte vectors, reading x[t] once
   constexpr int V = Vec16<T>::N;
   const int nvec = H / V;
-  const int ntok = static_cast<int>(T_tok - blk * kTileM < kTileM ? T_tok - blk * kTileM : kTileM);
-  for (int i = warp; i < ntok; i += 4) {
-    const T* src = x + (blk * kTileM + i) * static_cast<int64_t>(H);
+  const int ntok = static_cast<int>(T_tok - blk * rb < rb ? T_tok - blk * rb : rb);
+  for (int i = warp + 4 * static_cast<int>(blockIdx.y); i < ntok; i += 4 * static_cast<int>(gridDim.y)) {
+    const T* src = x + (blk * rb + i) * static_cast<int64_t>(H);
     float2 st = make_float2(0.f, 0.f);
-    if constexpr (LN) st = ln_stats[blk * kTileM + i];
+    if constexpr (LN) st = ln_stats[blk * rb + i];
     for (int v0 = 0; v0 < nvec; v0 += 32 * 4) {
       uint4 buf[4];
 #pragma unroll
@@ -291,16 +296,19 @@ carry_rows_kernel(const T* __restrict__ x, int H, int K, const int* __restrict__
 }
 
 // ---- 4. combine --------------------------------------------------------------------
-// one warp per token; fp32 accumulation in ascending expert order (model.py:339-357).  KMAX
+// fp32 accumulation in ascending expert order (model.py:339-357).  `wpt` warps (1, 2, 4 or
+// 8) share one token's row, each taking every wpt-th 32-vector column group, so a small
+// batch still spreads over the SMs; the per-element sum is the same for any wpt.  KMAX
 // bounds top_k at compile time: the K rows of each 16-byte column chunk are loaded before
 // any is summed, so their loads are in flight together.
 template <typename T, int KMAX>
 __global__ void __launch_bounds__(256)
 combine_kernel(const T* __restrict__ y, int64_t y_ld, const int32_t* __restrict__ topk_idx,
                const float* __restrict__ topk_w, const int* __restrict__ slot_of, int64_t T_tok,
-               int H, int K, T* out, const T* resid) {
-  const int lane = threadIdx.x & 31;
-  const int64_t t = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
+               int H, int K, T* out, const T* resid, int wpt) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int64_t t = static_cast<int64_t>(blockIdx.x) * (8 / wpt) + warp / wpt;
+  const int part = warp % wpt;
   if (t >= T_tok) return;
   // the token's K (expert, slot, weight) triples sorted by expert id
   int ord_e[KMAX], ord_s[KMAX];
@@ -320,7 +328,7 @@ combine_kernel(const T* __restrict__ y, int64_t y_ld, const int32_t* __restrict_
   constexpr int V = Vec16<T>::N;
   const int nvec = H / V;
   T* orow = out + t * static_cast<int64_t>(H);
-  for (int v = lane; v < nvec; v += 32) {
+  for (int v = part * 32 + lane; v < nvec; v += 32 * wpt) {
     uint4 raw[KMAX];
 #pragma unroll
     for (int j = 0; j < KMAX; ++j)
@@ -421,29 +429,38 @@ template <typename T, bool LN>
 void dispatch_as(const void* x, const int32_t* topk_idx, const int* excl, const int* offs,
                  int64_t T_tok, int H, int E, int K, int64_t capacity, int* slot_of, void* x_perm,
                  int64_t xp_ld, int* status, const LnArgs* ln, cudaStream_t s,
-                 const DispatchCarry& carry) {
-  const unsigned nblk = static_cast<unsigned>((T_tok + kTileM - 1) / kTileM);
+                 const DispatchCarry& carry, int rb) {
+  const unsigned nblk = static_cast<unsigned>((T_tok + rb - 1) / rb);
+  if (nblk == 0) return;  // no tokens: nothing to place
   const size_t smem = (8 * static_cast<size_t>(E) + static_cast<size_t>(kTileM) * K) * 4;
   auto kern = dispatch_kernel<T, LN>;
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
-  kern<<<nblk, 128, smem, s>>>(static_cast<const T*>(x), topk_idx, excl, offs, T_tok, H, E, K,
+  // copy slices per routing block: about two blocks per SM in all, one slice per four
+  // tokens at most (S = 1 from about 4,700 tokens up)
+  unsigned slices = 2u * 148u / (nblk > 0 ? nblk : 1u);
+  const unsigned groups = static_cast<unsigned>((T_tok < rb ? T_tok : rb) + 3) / 4;
+  if (slices > groups) slices = groups;
+  if (slices > 32) slices = 32;
+  if (slices < 1) slices = 1;
+  kern<<<dim3(nblk, slices), 128, smem, s>>>(static_cast<const T*>(x), topk_idx, excl, offs, T_tok, H, E, K,
                                capacity, slot_of, static_cast<T*>(x_perm), xp_ld, status,
                                LN ? ln->stats : nullptr, LN ? ln->weight : nullptr,
-                               LN ? ln->bias : nullptr, carry);
+                               LN ? ln->bias : nullptr, carry, rb);
 }
 }  // namespace
 
 cudaError_t launch_dispatch(int dtype, const void* x, const int32_t* topk_idx, const int* excl,
                             const int* offs, int64_t T, int H, int E, int K, int64_t capacity,
                             int* slot_of, void* x_perm, int64_t xp_ld, int* status,
-                            const LnArgs* ln, cudaStream_t s) {
+                            const LnArgs* ln, cudaStream_t s, int rb) {
+  if (rb < 1 || rb > kTileM) return cudaErrorInvalidValue;
   const DispatchCarry none{nullptr, nullptr, nullptr, 0, 0};
   if (dtype == kF32) {
-    if (ln) dispatch_as<float, true>(x, topk_idx, excl, offs, T, H, E, K, capacity, slot_of, x_perm, xp_ld, status, ln, s, none);
-    else dispatch_as<float, false>(x, topk_idx, excl, offs, T, H, E, K, capacity, slot_of, x_perm, xp_ld, status, ln, s, none);
+    if (ln) dispatch_as<float, true>(x, topk_idx, excl, offs, T, H, E, K, capacity, slot_of, x_perm, xp_ld, status, ln, s, none, rb);
+    else dispatch_as<float, false>(x, topk_idx, excl, offs, T, H, E, K, capacity, slot_of, x_perm, xp_ld, status, ln, s, none, rb);
   } else {
-    if (ln) dispatch_as<__nv_bfloat16, true>(x, topk_idx, excl, offs, T, H, E, K, capacity, slot_of, x_perm, xp_ld, status, ln, s, none);
-    else dispatch_as<__nv_bfloat16, false>(x, topk_idx, excl, offs, T, H, E, K, capacity, slot_of, x_perm, xp_ld, status, ln, s, none);
+    if (ln) dispatch_as<__nv_bfloat16, true>(x, topk_idx, excl, offs, T, H, E, K, capacity, slot_of, x_perm, xp_ld, status, ln, s, none, rb);
+    else dispatch_as<__nv_bfloat16, false>(x, topk_idx, excl, offs, T, H, E, K, capacity, slot_of, x_perm, xp_ld, status, ln, s, none, rb);
   }
   return cudaGetLastError();
 }
@@ -455,9 +472,9 @@ cudaError_t launch_dispatch_carry(int dtype, const void* x, const int32_t* topk_
                                   int64_t t0, int64_t slot_base, int* status, cudaStream_t s) {
   const DispatchCarry carry{carry_in, computed, list_out, t0, slot_base};
   if (dtype == kF32)
-    dispatch_as<float, false>(x, topk_idx, excl, offs, T, H, E, K, 0, slot_of, x_perm, xp_ld, status, nullptr, s, carry);
+    dispatch_as<float, false>(x, topk_idx, excl, offs, T, H, E, K, 0, slot_of, x_perm, xp_ld, status, nullptr, s, carry, kTileM);
   else
-    dispatch_as<__nv_bfloat16, false>(x, topk_idx, excl, offs, T, H, E, K, 0, slot_of, x_perm, xp_ld, status, nullptr, s, carry);
+    dispatch_as<__nv_bfloat16, false>(x, topk_idx, excl, offs, T, H, E, K, 0, slot_of, x_perm, xp_ld, status, nullptr, s, carry, kTileM);
   return cudaGetLastError();
 }
 
@@ -479,9 +496,14 @@ cudaError_t launch_combine(int dtype, const void* y, int64_t y_ld, const int32_t
                            const float* topk_w, const int* slot_of, int64_t T, int H, int K,
                            void* out, const void* resid, cudaStream_t s) {
   if (K > 32) return cudaErrorInvalidValue;
-  const unsigned grid = static_cast<unsigned>((T + 7) / 8);
+  if (T <= 0) return cudaSuccess;
+  // warps per token: enough blocks for about two per SM (8 for a decode batch, 1 from
+  // about 2,400 tokens up)
+  int wpt = 1;
+  while (wpt < 8 && T * wpt < 2 * 148 * 8) wpt *= 2;
+  const unsigned grid = static_cast<unsigned>((T * wpt + 7) / 8);
   auto go = [&](auto kern, auto* yy, auto* o, auto* r) {
-    kern<<<grid, 256, 0, s>>>(yy, y_ld, topk_idx, topk_w, slot_of, T, H, K, o, r);
+    kern<<<grid, 256, 0, s>>>(yy, y_ld, topk_idx, topk_w, slot_of, T, H, K, o, r, wpt);
   };
   if (dtype == kF32) {
     const float* yy = static_cast<const float*>(y);

@@ -44,7 +44,7 @@ constexpr uint32_t B_BOX_ROWS = 16;            // rows per activation TMA box
 constexpr int kMaxStages = 12;
 constexpr uint32_t kAccCols = 256;             // one accumulator: up to 256 rows (N)
 constexpr uint32_t kTmemCols = 2 * kAccCols;
-constexpr size_t kSmemBudget = 220 * 1024;
+constexpr size_t kSmemDyn = 232448;            // the whole opt-in shared memory of a CTA
 
 struct DecShared {
   uint64_t full[kMaxStages];
@@ -57,12 +57,18 @@ struct DecShared {
   int issued;
   int consumed;
   int n_act;
+  int stages;                      // ring depth for the largest segment of this forward
+  uint32_t b_slot;                 // bytes of one stage's row tile (largest segment x 128)
   int ep_ok[2][4];                 // gated epilogue: each warp's wait result, per item parity
   int act_e[kDecodeMaxExperts];    // experts with rows, ascending id
   int act_seg[kDecodeMaxExperts];  // first row of the expert's segment
   int act_n[kDecodeMaxExperts];    // its rows, a multiple of 16 in [16, 256]
   float xch[2][64][17];            // up values handed to the gate warps (17: no bank conflicts)
 };
+
+// shared state first (fixed place), then the ring of stages, 1024-byte aligned
+constexpr uint32_t kSharedBytes = (sizeof(DecShared) + 1023) & ~1023u;
+constexpr uint32_t kRingBytes = static_cast<uint32_t>(kSmemDyn) - 1024 - kSharedBytes;
 
 __device__ __forceinline__ bool aborted(const DecShared* sh) {
   return *reinterpret_cast<const volatile int*>(&sh->abort) != 0;
@@ -83,29 +89,16 @@ decode_gemm_kernel(const __grid_constant__ CUtensorMap a_map,
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
-  uint8_t* gbase = smem_raw + (base - raw);
-  const int stages = args.stages;
-  const uint32_t b_slot = args.b_slot_bytes;
-  const uint32_t a_s = base;
-  const uint32_t b_s = base + static_cast<uint32_t>(stages) * A_BYTES;
-  DecShared* sh = reinterpret_cast<DecShared*>(gbase + static_cast<size_t>(stages) * (A_BYTES + b_slot));
+  DecShared* sh = reinterpret_cast<DecShared*>(smem_raw + (base - raw));
+  const uint32_t ring = base + kSharedBytes;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
-    for (int s = 0; s < stages; ++s) {
-      mbar_init(smem_u32(&sh->full[s]), 1);
-      mbar_init(smem_u32(&sh->empty[s]), 1);
-    }
-    for (int a = 0; a < 2; ++a) {
-      mbar_init(smem_u32(&sh->tfull[a]), 1);
-      mbar_init(smem_u32(&sh->tempty[a]), 4);
-    }
-    mbar_init(smem_u32(&sh->done), 1);
     sh->abort = 0;
     sh->issued = 0;
     sh->consumed = 0;
     // the experts that received rows, in ascending id, with their segments
-    int n = 0;
+    int n = 0, widest = kDecodeRowAlign;
     const int E = args.num_experts < kDecodeMaxExperts ? args.num_experts : kDecodeMaxExperts;
     for (int e = 0; e < E; ++e) {
       const int seg = args.offs[e], len = args.offs[e + 1] - seg;
@@ -119,9 +112,24 @@ decode_gemm_kernel(const __grid_constant__ CUtensorMap a_map,
       sh->act_e[n] = e;
       sh->act_seg[n] = seg;
       sh->act_n[n] = rows;
+      widest = rows > widest ? rows : widest;
       ++n;
     }
     sh->n_act = n;
+    // as many stages as the ring holds for this forward's widest segment (not the widest
+    // possible one): more weight tiles in flight per SM
+    sh->b_slot = static_cast<uint32_t>(widest) * B_ROW_BYTES;
+    int st = static_cast<int>(kRingBytes / (A_BYTES + sh->b_slot));
+    sh->stages = st > kMaxStages ? kMaxStages : st;
+    for (int s = 0; s < sh->stages; ++s) {
+      mbar_init(smem_u32(&sh->full[s]), 1);
+      mbar_init(smem_u32(&sh->empty[s]), 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(smem_u32(&sh->tfull[a]), 1);
+      mbar_init(smem_u32(&sh->tempty[a]), 4);
+    }
+    mbar_init(smem_u32(&sh->done), 1);
     fence_mbar_init();
     prefetch_tmap(&a_map);
     prefetch_tmap(&b_map);
@@ -133,6 +141,10 @@ decode_gemm_kernel(const __grid_constant__ CUtensorMap a_map,
   const uint32_t tmem = sh->tmem_base;
   const int bpe = args.blocks_per_expert, k_blocks = args.k_blocks;
   const int total = sh->n_act * bpe;
+  const int stages = sh->stages;
+  const uint32_t b_slot = sh->b_slot;
+  const uint32_t a_s = ring;
+  const uint32_t b_s = ring + static_cast<uint32_t>(stages) * A_BYTES;
 
   if (warp == 0) {
     // ---------------- TMA producer ----------------
@@ -312,9 +324,7 @@ decode_gemm_kernel(const __grid_constant__ CUtensorMap a_map,
 }  // namespace
 
 int decode_gemm_stages(int n_max) {
-  const size_t stage = A_BYTES + static_cast<size_t>(n_max) * B_ROW_BYTES;
-  const size_t fixed = 1024 + sizeof(DecShared) + 64;
-  const int s = static_cast<int>((kSmemBudget - fixed) / stage);
+  const int s = static_cast<int>(kRingBytes / (A_BYTES + static_cast<uint32_t>(n_max) * B_ROW_BYTES));
   return s > kMaxStages ? kMaxStages : s;
 }
 
@@ -325,11 +335,9 @@ cudaError_t launch_decode_gemm(bool gated, const CUtensorMap& a_map, const CUten
       args.num_experts < 1 || args.num_experts > kDecodeMaxExperts || args.blocks_per_expert < 1 ||
       args.k_blocks < 1 || !args.offs || !args.out || (gated && !args.bias))
     return cudaErrorInvalidValue;
-  args.stages = decode_gemm_stages(args.n_max);
-  if (args.stages < 2) return cudaErrorInvalidValue;
-  args.b_slot_bytes = static_cast<uint32_t>(args.n_max) * B_ROW_BYTES;
-  const size_t smem = 1024 + static_cast<size_t>(args.stages) * (A_BYTES + args.b_slot_bytes) +
-                      sizeof(DecShared) + 64;
+  if (decode_gemm_stages(args.n_max) < 2) return cudaErrorInvalidValue;
+  static_assert(kRingBytes / (A_BYTES + kAccCols * B_ROW_BYTES) >= 2, "two stages of the widest");
+  constexpr size_t smem = kSmemDyn;
   auto kern = gated ? decode_gemm_kernel<true> : decode_gemm_kernel<false>;
   cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(smem));

@@ -156,8 +156,11 @@ __device__ __forceinline__ void router_epilogue(const TcGemmArgs& args, TcShared
   __syncwarp();
   if (lane == 0) mbar_arrive(tempty_bar);
   const int E = args.num_experts, K = args.top_k;
-  const int64_t t = static_cast<int64_t>(m) * kTileM + q * 32 + lane;
-  const bool valid = t < args.tokens;
+  // routing block m holds tokens [m * rr, (m + 1) * rr); rows of the tile past rr hold
+  // stale shared memory (their accumulator rows are never used)
+  const int rr = args.route_rows > 0 ? args.route_rows : kTileM;
+  const int64_t t = static_cast<int64_t>(m) * rr + q * 32 + lane;
+  const bool valid = q * 32 + lane < rr && t < args.tokens;
   if constexpr (LN) {
     const float inv_h = 1.0f / static_cast<float>(args.ln_h);
     const float mean = sum_x * inv_h;
@@ -325,6 +328,10 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_constant_
   }
   const int total = num_m * n_tiles;
 
+  // the router's tiles may hold fewer than 128 tokens (a decode batch routed in small
+  // blocks over more SMs): the x box then has route_rows rows
+  const int a_rows = ROUTER && args.route_rows > 0 ? args.route_rows : kTileM;
+  const uint32_t stage_tx = static_cast<uint32_t>(a_rows) * BK * 2 + Cfg::B_BYTES;
   if (warp == 0) {
     // ---------------- TMA producer ----------------
     if (lane == 0) {
@@ -332,7 +339,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_constant_
       for (int tile = blockIdx.x; tile < total; tile += gridDim.x) {
         const int m = tile / n_tiles, n = tile - m * n_tiles;
         const int e = expert_of(args, m);
-        const int a_row = m * kTileM;
+        const int a_row = m * a_rows;
         const int b_row = e * args.b_rows_per_expert + n * BN;
         bool ok = true;
         for (int kb = 0; kb < k_blocks; ++kb, ++it) {
@@ -345,7 +352,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_constant_
           }
           if (aborted(sh)) { ok = false; break; }
           const uint32_t fb = smem_u32(&sh->full[s]);
-          mbar_arrive_expect_tx(fb, Cfg::STAGE_BYTES);
+          mbar_arrive_expect_tx(fb, stage_tx);
           tma_load_2d(a_s + s * A_BYTES, &a_map, fb, kb * BK, a_row);
           tma_load_2d(b_s + s * Cfg::B_BYTES, &b_map, fb, kb * BK, b_row);
           *reinterpret_cast<volatile int*>(&sh->issued) = it + 1;
@@ -584,6 +591,8 @@ int tc_router_width(int E) {
 
 cudaError_t launch_tc_router(const CUtensorMap& x_map, const CUtensorMap& w_map,
                              const TcGemmArgs& args, int num_sms, cudaStream_t s, bool ln) {
+  if (args.route_rows < 0 || args.route_rows > kTileM || args.route_rows % 16)
+    return cudaErrorInvalidValue;
   const int64_t work = args.m_tiles_host;
   if (ln) {
     if (!args.ln_stats || !args.ln_c || args.ln_h <= 0) return cudaErrorInvalidValue;

@@ -78,11 +78,12 @@ cudaError_t launch_aux_merge_ws(const void* ws, size_t stride, size_t counts_off
 cudaError_t launch_fill_tiles(int* tile_expert, int n, int* num_tiles, cudaStream_t s);
 
 // Stable expert-major slots for every (token, k) and the row gather x -> x_perm (with
-// `ln`: LayerNorm(x) rows, normalised on the way, rounded to the dtype).
+// `ln`: LayerNorm(x) rows, normalised on the way, rounded to the dtype).  `block_tokens`
+// (<= 128) is the routing block the router's histograms and the scan's prefixes use.
 cudaError_t launch_dispatch(int dtype, const void* x, const int32_t* topk_idx, const int* excl,
                             const int* offs, int64_t T, int H, int E, int K, int64_t capacity,
                             int* slot_of, void* x_perm, int64_t xp_ld, int* status,
-                            const LnArgs* ln, cudaStream_t s);
+                            const LnArgs* ln, cudaStream_t s, int block_tokens = kTileM);
 
 // out[t] = sum over the token's experts in ascending id of w * y[slot]  (fp32 sum); with
 // `resid`, out[t] = resid[t] + that sum rounded to the dtype (the residual add of the
@@ -112,6 +113,7 @@ struct TcGemmArgs {
   int num_experts;          // experts the weights hold (bounds tile_expert); router: E
   // router epilogue
   int64_t tokens;           // valid rows of A
+  int route_rows;           // router: tokens per routing block (M tile), <= 128; 0 = 128
   int top_k;
   float* logits;            // [T, E] or null
   int32_t* topk_idx;        // [T, K]
@@ -203,6 +205,7 @@ struct DecodeGemmArgs {
   int blocks_per_expert;    // work items per expert: 128-row weight blocks
   int a_rows_per_expert;    // rows of the packed weight view per expert (2*Ipad or Hpad)
   int n_max;                // largest segment (rows) any expert can have, multiple of 16
+                            // (the kernel sizes its ring for the widest one present)
   void* out;                // bf16 [max_rows, ldo]
   int64_t ldo;
   const float* bias;        // gated: interleaved gate|up [E, bias_ld]; plain: [E, bias_ld]
@@ -210,8 +213,6 @@ struct DecodeGemmArgs {
   float gamma;              // ERA gamma (gated)
   int64_t row_limit;        // rows >= row_limit are not stored (0 = no limit)
   int* status;
-  int stages;               // set by the launcher
-  uint32_t b_slot_bytes;    // set by the launcher
 };
 // gated = true : a_map = packed gate|up weights with 64-row boxes, b_map = x_perm (16-row
 //                boxes); out = h [rows, Ipad] = ERA(gate + bg) * (up + bu)

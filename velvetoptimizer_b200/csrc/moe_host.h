@@ -60,6 +60,7 @@ struct P2PChannel {
 };
 
 struct Plan {
+  int rb = kTileM;  // tokens per routing block (the router's histograms, the scan, dispatch)
   int nblk = 0;
   int64_t max_tiles = 0, max_rows = 0;
   size_t idx = 0, w = 0, hist = 0, psum = 0, excl = 0, counts = 0, psum_tot = 0, offs = 0,
@@ -270,6 +271,14 @@ inline int segment_align(const vmoe_handle* h, int64_t T) {
   return use_decode_gemms(h, T) ? kDecodeRowAlign : h->tile_rows;
 }
 
+// Tokens per routing block of a single-GPU forward of T tokens: a decode batch on the
+// tensor-core router is routed in blocks of 16 or 32 tokens so that several SMs share its
+// x stream (a token's logits are the same in any block); 128 otherwise.
+inline int routing_block(const vmoe_handle* h, int64_t T) {
+  if (!use_decode_gemms(h, T) || h->router_bn == 0) return kTileM;
+  return T <= 128 ? 16 : 32;
+}
+
 // gate|up GEMM (+ ERA * up) then down GEMM over the expert-major buffer of a decode-sized
 // forward: segments padded to kDecodeRowAlign rows at offs[E+1], no tile map.
 template <typename Mark, typename Check>
@@ -318,8 +327,9 @@ int run_decode_gemms(vmoe_handle* h, void* xp, int64_t max_rows, const int* offs
                "gemm2 (decode)");
 }
 
+// `rb` tokens per routing block (hist / psum rows); below 128 only on the tensor-core router
 int run_router(vmoe_handle* h, const void* x, int64_t T, float* logits, int32_t* idx, float* tw,
-               int* hist, float* psum, const LnArgs* ln, cudaStream_t s);
+               int* hist, float* psum, const LnArgs* ln, cudaStream_t s, int rb = kTileM);
 int forward_batch(vmoe_handle* h, const void* x, int64_t T, void* out, float* router_logits,
                   int32_t* topk_idx, float* topk_w, int32_t* expert_counts, float* aux_loss,
                   char* ws, const Plan& p, cudaStream_t s, bool prof, float* psum_tot_out,

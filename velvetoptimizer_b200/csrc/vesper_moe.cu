@@ -38,7 +38,8 @@ Plan make_plan(const vmoe_handle* h, int64_t T) {
   };
   const int64_t E = h->E, K = h->K;
   const size_t elt = dtype_bytes(h->dtype);
-  p.nblk = static_cast<int>((T + kTileM - 1) / kTileM);
+  p.rb = routing_block(h, T);
+  p.nblk = static_cast<int>((T + p.rb - 1) / p.rb);
   const int64_t tr = h->tile_rows;
   int64_t rows_bound = T * K + E * (tr - 1);
   if (h->cfg.capacity > 0) {
@@ -74,17 +75,18 @@ Plan make_plan(const vmoe_handle* h, int64_t T) {
 // through the folded weights (and its own row statistics), the CUDA-core router through a
 // statistics pass and normalisation on load.
 int run_router(vmoe_handle* h, const void* x, int64_t T, float* logits, int32_t* idx, float* tw,
-               int* hist, float* psum, const LnArgs* ln, cudaStream_t s) {
+               int* hist, float* psum, const LnArgs* ln, cudaStream_t s, int rb) {
   const int64_t H = h->H;
   cudaError_t e;
   if (h->dtype == kBF16 && h->router_bn > 0) {
     char why[256];
     CUtensorMap map_x;
-    if (!make_tmap_bf16(&map_x, x, T, H, H, kTileM, why, sizeof(why)))
+    if (!make_tmap_bf16(&map_x, x, T, H, H, static_cast<uint32_t>(rb), why, sizeof(why)))
       return fail(h, VMOE_ERR_CUDA, "x tensor map: %s", why);
     TcGemmArgs a{};
     a.num_m_tiles = nullptr;
-    a.m_tiles_host = static_cast<int>((T + kTileM - 1) / kTileM);
+    a.route_rows = rb;
+    a.m_tiles_host = static_cast<int>((T + rb - 1) / rb);
     a.tile_expert = nullptr;
     a.max_m_tiles = a.m_tiles_host;
     a.num_experts = static_cast<int>(h->E);
@@ -109,6 +111,8 @@ int run_router(vmoe_handle* h, const void* x, int64_t T, float* logits, int32_t*
     }
     e = launch_tc_router(map_x, ln ? h->map_wr_ln : h->map_wr, a, h->num_sms, s, ln != nullptr);
   } else {
+    if (rb != kTileM)
+      return fail(h, VMOE_ERR_INVALID_ARG, "the CUDA-core router routes 128-token blocks");
     e = launch_router(h->dtype, x, h->w_r, h->b_r, T, static_cast<int>(H), static_cast<int>(h->E),
                       static_cast<int>(h->K), logits, idx, tw, hist, psum, ln, s);
   }
@@ -158,7 +162,8 @@ int forward_batch(vmoe_handle* h, const void* x, int64_t T, void* out, float* ro
   };
   int rc;
   mark();
-  if ((rc = run_router(h, x, T, router_logits, idx, tw, hist, psum, ln, s)) != VMOE_OK) return rc;
+  if ((rc = run_router(h, x, T, router_logits, idx, tw, hist, psum, ln, s, p.rb)) != VMOE_OK)
+    return rc;
   mark();
   if ((rc = check(launch_scan_blocks(hist, psum, p.nblk, static_cast<int>(E), excl, counts,
                                      psum_tot, s),
@@ -177,7 +182,7 @@ int forward_batch(vmoe_handle* h, const void* x, int64_t T, void* out, float* ro
   mark();
   if ((rc = check(launch_dispatch(h->dtype, x, idx, excl, offs, T, static_cast<int>(H),
                                   static_cast<int>(E), static_cast<int>(K), h->cfg.capacity, slot,
-                                  xp, H, h->status, ln, s),
+                                  xp, H, h->status, ln, s, p.rb),
                   "dispatch")) != VMOE_OK)
     return rc;
   mark();
