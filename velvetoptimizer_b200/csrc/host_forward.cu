@@ -48,7 +48,7 @@ HostPlan make_host_plan(const vmoe_handle* h, int64_t T, int chunks) {
   hp.small = take(hp.small_stride * hp.chunks);
   hp.aux = take(4);
   if (hp.chunks == 1) {
-    hp.fwd = take(make_plan(h, T < ct ? T : ct).total);
+    hp.fwd = take(make_plan(h, T).total);  // the whole batch in one forward_batch
   } else {
     const int64_t E = h->E, K = h->K, tr = h->tile_rows;
     hp.nblk = static_cast<int>(ct / kTileM);

@@ -160,7 +160,10 @@ namespace vmoe_host {
 int fail(vmoe_handle* h, int code, const char* fmt, ...);
 int cuda_fail(vmoe_handle* h, cudaError_t e, const char* what);
 
-Plan make_plan(const vmoe_handle* h, int64_t T);
+// Workspace plan of a single-GPU forward of T tokens routed in blocks of `rb` tokens
+// (0: routing_block(h, T), the inference forward's choice; the training forward routes in
+// 128-token blocks).  The forward must route and dispatch with the plan's rb.
+Plan make_plan(const vmoe_handle* h, int64_t T, int rb = 0);
 
 template <typename T>
 int alloc(vmoe_handle* h, T** p, size_t bytes, const char* what) {
@@ -275,7 +278,9 @@ inline int segment_align(const vmoe_handle* h, int64_t T) {
 // tensor-core router is routed in blocks of 16 or 32 tokens so that several SMs share its
 // x stream (a token's logits are the same in any block); 128 otherwise.
 inline int routing_block(const vmoe_handle* h, int64_t T) {
-  if (!use_decode_gemms(h, T) || h->router_bn == 0) return kTileM;
+  // from the config alone (tc_router_width, as vmoe_set_weights picks the router), so a
+  // workspace sized before the weights are set stays valid
+  if (!use_decode_gemms(h, T) || tc_router_width(static_cast<int>(h->E)) == 0) return kTileM;
   return T <= 128 ? 16 : 32;
 }
 

@@ -16,7 +16,7 @@ struct TrainPlan {
 
 TrainPlan make_train_plan(const vmoe_handle* h, int64_t T) {
   TrainPlan tp;
-  tp.p = make_plan(h, T);
+  tp.p = make_plan(h, T, kTileM);  // routed in 128-token blocks
   size_t off = tp.p.total;
   auto take = [&](size_t bytes) {
     const size_t o = off;
@@ -132,7 +132,8 @@ int vmoe_forward_train(vmoe_handle* h, const void* x, int64_t tokens, void* out,
   float* aux = aux_loss ? aux_loss : reinterpret_cast<float*>(ws + p.aux);
   int* slot = reinterpret_cast<int*>(ws + p.slot);
   float* logits = reinterpret_cast<float*>(ws + tp.logits);
-  if ((rc = run_router(h, x, T, logits, idx, tw, hist, psum, nullptr, s)) != VMOE_OK) return rc;
+  if ((rc = run_router(h, x, T, logits, idx, tw, hist, psum, nullptr, s, p.rb)) != VMOE_OK)
+    return rc;
   if ((rc = check(launch_scan_blocks(hist, psum, p.nblk, static_cast<int>(E), excl, counts,
                                      psum_tot, s), "scan")) != VMOE_OK)
     return rc;
@@ -142,7 +143,7 @@ int vmoe_forward_train(vmoe_handle* h, const void* x, int64_t tokens, void* out,
     return rc;
   if ((rc = check(launch_dispatch(h->dtype, x, idx, excl, offs, T, static_cast<int>(H),
                                   static_cast<int>(E), static_cast<int>(K), h->cfg.capacity, slot,
-                                  ws + p.xp, H, h->status, nullptr, s), "dispatch")) != VMOE_OK)
+                                  ws + p.xp, H, h->status, nullptr, s, p.rb), "dispatch")) != VMOE_OK)
     return rc;
   // zero the padding rows of every segment: the weight gradients reduce over whole segments
   if ((rc = check(launch_zero_pad_rows(ws + p.xp, H * 2, H * 2, offs, counts, static_cast<int>(E),

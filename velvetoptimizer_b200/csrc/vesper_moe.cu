@@ -28,7 +28,7 @@ int cuda_fail(vmoe_handle* h, cudaError_t e, const char* what) {
   return fail(h, VMOE_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
 }
 
-Plan make_plan(const vmoe_handle* h, int64_t T) {
+Plan make_plan(const vmoe_handle* h, int64_t T, int rb) {
   Plan p;
   size_t off = 0;
   auto take = [&](size_t bytes) {
@@ -38,7 +38,7 @@ Plan make_plan(const vmoe_handle* h, int64_t T) {
   };
   const int64_t E = h->E, K = h->K;
   const size_t elt = dtype_bytes(h->dtype);
-  p.rb = routing_block(h, T);
+  p.rb = rb > 0 ? rb : routing_block(h, T);
   p.nblk = static_cast<int>((T + p.rb - 1) / p.rb);
   const int64_t tr = h->tile_rows;
   int64_t rows_bound = T * K + E * (tr - 1);
