@@ -47,16 +47,25 @@ constexpr int kSumCol = 64, kSqCol = 128, kLnAccCols = 256;
 constexpr uint32_t kOnesBytes = 16 * 128;  // 16-row K-major ones tile (row 0 = 1, rest 0)
 
 constexpr int BK = 64;
-constexpr uint32_t A_BYTES = kTileM * BK * 2;  // 16 KB
 
-template <int BN>
+// AR = rows of A a stage holds: 128 (a full M tile), or 32 for the router of a decode batch
+// routed in blocks of at most 32 tokens.  Such a stage is 4 KB of A, so the ring is deep
+// enough (32 stages) to have every k-block of a token block in flight at once; the MMA is
+// still M = 128 and reads past the slot into other stages' shared memory for rows 32..127,
+// whose accumulator rows the epilogue never uses.
+template <int BN, int AR = 128>
 struct TcCfg {
+  static constexpr uint32_t A_BYTES = AR * BK * 2;
   static constexpr uint32_t B_BYTES = BN * BK * 2;
   static constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int STAGES_FIT = static_cast<int>((200u * 1024u) / STAGE_BYTES);
-  static constexpr int STAGES = STAGES_FIT > 8 ? 8 : STAGES_FIT;
+  static constexpr int STAGES_MAX = AR == 128 ? 8 : 32;
+  static constexpr int STAGES = STAGES_FIT > STAGES_MAX ? STAGES_MAX : STAGES_FIT;
   static constexpr uint32_t TMEM_COLS = 2 * BN < 32 ? 32 : 2 * BN;  // power of two for BN in {16..256}
   static constexpr uint32_t IDESC = umma_idesc_bf16(kTileM, BN);
+  // an M = 128 MMA on the last stage's A slot reads 16 KB from its start
+  static_assert(AR == 128 || (STAGES - 1) * A_BYTES + 16384 <= STAGES * STAGE_BYTES,
+                "the MMA's reads past a short A slot stay inside the ring");
 };
 
 template <int STAGES>
@@ -78,10 +87,10 @@ struct TcShared {
   float ln_c[64];  // once per CTA so that the epilogue makes no global loads
 };
 
-template <int BN, int EPI = kPlain>
+template <int BN, int EPI = kPlain, int AR = 128>
 constexpr size_t tc_smem_bytes() {
-  return 1024 + TcCfg<BN>::STAGES * TcCfg<BN>::STAGE_BYTES + (EPI == kRouterLN ? kOnesBytes : 0) +
-         sizeof(TcShared<TcCfg<BN>::STAGES>) + 64;
+  return 1024 + TcCfg<BN, AR>::STAGES * TcCfg<BN, AR>::STAGE_BYTES +
+         (EPI == kRouterLN ? kOnesBytes : 0) + sizeof(TcShared<TcCfg<BN, AR>::STAGES>) + 64;
 }
 
 template <int STAGES>
@@ -260,11 +269,12 @@ __device__ __forceinline__ void router_epilogue(const TcGemmArgs& args, TcShared
   }
 }
 
-template <int EPI, int BN>
+template <int EPI, int BN, int AR = 128>
 __global__ void __launch_bounds__(tc_threads<EPI>(), 1)
 tc_gemm_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_constant__ CUtensorMap b_map,
                const TcGemmArgs args) {
-  using Cfg = TcCfg<BN>;
+  using Cfg = TcCfg<BN, AR>;
+  constexpr uint32_t A_BYTES = Cfg::A_BYTES;
   constexpr int STAGES = Cfg::STAGES;
   constexpr bool LN = EPI == kRouterLN;
   constexpr bool ROUTER = EPI == kRouter || EPI == kRouterLN;
@@ -330,6 +340,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_constant_
 
   // the router's tiles may hold fewer than 128 tokens (a decode batch routed in small
   // blocks over more SMs): the x box then has route_rows rows
+  // (launch_tc_router picks AR = 32 only for route_rows <= 32: a_rows never exceeds AR)
   const int a_rows = ROUTER && args.route_rows > 0 ? args.route_rows : kTileM;
   const uint32_t stage_tx = static_cast<uint32_t>(a_rows) * BK * 2 + Cfg::B_BYTES;
   if (warp == 0) {
@@ -518,13 +529,13 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_constant_
   }
 }
 
-template <int EPI, int BN>
+template <int EPI, int BN, int AR = 128>
 cudaError_t launch_cfg(const CUtensorMap& a_map, const CUtensorMap& b_map, const TcGemmArgs& args,
                        int64_t work, int num_sms, cudaStream_t s) {
-  constexpr size_t smem = tc_smem_bytes<BN, EPI>();
+  constexpr size_t smem = tc_smem_bytes<BN, EPI, AR>();
   static_assert(smem <= 232448, "shared memory budget");
   const int grid = static_cast<int>(work < num_sms ? (work > 0 ? work : 1) : num_sms);
-  auto kern = tc_gemm_kernel<EPI, BN>;
+  auto kern = tc_gemm_kernel<EPI, BN, AR>;
   cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(smem));
   if (err != cudaSuccess) return err;
@@ -594,12 +605,29 @@ cudaError_t launch_tc_router(const CUtensorMap& x_map, const CUtensorMap& w_map,
   if (args.route_rows < 0 || args.route_rows > kTileM || args.route_rows % 16)
     return cudaErrorInvalidValue;
   const int64_t work = args.m_tiles_host;
+  const bool short_blocks = args.route_rows > 0 && args.route_rows <= 32;
   if (ln) {
     if (!args.ln_stats || !args.ln_c || args.ln_h <= 0) return cudaErrorInvalidValue;
+    if (short_blocks) {
+      switch (tc_router_width(args.num_experts)) {
+        case 16: return launch_cfg<kRouterLN, 16, 32>(x_map, w_map, args, work, num_sms, s);
+        case 32: return launch_cfg<kRouterLN, 32, 32>(x_map, w_map, args, work, num_sms, s);
+        case 64: return launch_cfg<kRouterLN, 64, 32>(x_map, w_map, args, work, num_sms, s);
+        default: return cudaErrorInvalidValue;
+      }
+    }
     switch (tc_router_width(args.num_experts)) {
       case 16: return launch_cfg<kRouterLN, 16>(x_map, w_map, args, work, num_sms, s);
       case 32: return launch_cfg<kRouterLN, 32>(x_map, w_map, args, work, num_sms, s);
       case 64: return launch_cfg<kRouterLN, 64>(x_map, w_map, args, work, num_sms, s);
+      default: return cudaErrorInvalidValue;
+    }
+  }
+  if (short_blocks) {
+    switch (tc_router_width(args.num_experts)) {
+      case 16: return launch_cfg<kRouter, 16, 32>(x_map, w_map, args, work, num_sms, s);
+      case 32: return launch_cfg<kRouter, 32, 32>(x_map, w_map, args, work, num_sms, s);
+      case 64: return launch_cfg<kRouter, 64, 32>(x_map, w_map, args, work, num_sms, s);
       default: return cudaErrorInvalidValue;
     }
   }
