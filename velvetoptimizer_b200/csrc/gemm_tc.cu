@@ -207,8 +207,12 @@ __device__ __forceinline__ void router_epilogue(const TcGemmArgs& args, TcShared
     lg[e] = p;
     s += p;
   }
+  // one division, then products: BN correctly rounded divisions cost microseconds of this
+  // latency-bound epilogue (one warp per SM sub-partition); the probabilities differ from
+  // the quotients by at most a rounding of the reciprocal
+  const float inv_s = 1.0f / s;
 #pragma unroll
-  for (int e = 0; e < BN; ++e) lg[e] = lg[e] / s;
+  for (int e = 0; e < BN; ++e) lg[e] = lg[e] * inv_s;
   // top-K by (p desc, index asc) (model.py:326): strict '>' keeps the lowest index.  The
   // selection runs twice (the first pass sums the selected probabilities, the second writes
   // them renormalised and counts them) instead of keeping the chosen indices in a

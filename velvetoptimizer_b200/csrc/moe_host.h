@@ -263,6 +263,13 @@ int run_expert_gemms(vmoe_handle* h, void* xp, int64_t max_rows, const int* tile
                "gemm2");
 }
 
+// Rows of the packed router weights: E, padded with zero rows to the tensor-core router's
+// N tile (bf16, E <= 64) so that its weight boxes stay inside the tensor.
+inline int64_t router_rows(const vmoe_handle* h) {
+  const int64_t bn = h->dtype == kBF16 ? tc_router_width(static_cast<int>(h->E)) : 0;
+  return bn > h->E ? bn : h->E;
+}
+
 // Whether a single-GPU forward of T tokens runs the decode-sized (swapped-operand) GEMMs.
 inline bool use_decode_gemms(const vmoe_handle* h, int64_t T) {
   return h->dtype == kBF16 && !h->dense && h->ep_size == 1 && T > 0 &&

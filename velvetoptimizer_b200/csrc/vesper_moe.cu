@@ -230,17 +230,20 @@ int make_training_copies(vmoe_handle* h, cudaStream_t s) {
 int refold_norm(vmoe_handle* h, cudaStream_t s) {
   h->ln_ready = false;
   if (h->dtype == kBF16 && h->router_bn > 0) {
-    const int64_t E = h->E, H = h->H;
+    const int64_t E = h->E, H = h->H, Er = router_rows(h);
     int rc;
-    if (!h->w_r_ln && (rc = alloc(h, &h->w_r_ln, E * H * 2, "folded router weight")) != VMOE_OK)
-      return rc;
+    if (!h->w_r_ln) {  // zero rows past E (see router_rows); the fold writes rows < E
+      if ((rc = alloc(h, &h->w_r_ln, Er * H * 2, "folded router weight")) != VMOE_OK) return rc;
+      const cudaError_t z = cudaMemsetAsync(h->w_r_ln, 0, Er * H * 2, s);
+      if (z != cudaSuccess) return cuda_fail(h, z, "folded router weight");
+    }
     if (!h->b_r_ln && (rc = alloc(h, &h->b_r_ln, E * 4, "folded router bias")) != VMOE_OK) return rc;
     if (!h->c_ln && (rc = alloc(h, &h->c_ln, E * 4, "folded router sums")) != VMOE_OK) return rc;
     cudaError_t e = launch_fold_router_ln(h->w_r, h->b_r, h->ln_w, h->ln_b, static_cast<int>(E),
                                           static_cast<int>(H), h->w_r_ln, h->b_r_ln, h->c_ln, s);
     if (e != cudaSuccess) return cuda_fail(h, e, "router LayerNorm fold");
     char why[256];
-    if (!make_tmap_bf16(&h->map_wr_ln, h->w_r_ln, E, H, H, static_cast<uint32_t>(h->router_bn),
+    if (!make_tmap_bf16(&h->map_wr_ln, h->w_r_ln, Er, H, H, static_cast<uint32_t>(h->router_bn),
                         why, sizeof(why)))
       return fail(h, VMOE_ERR_CUDA, "folded router tensor map: %s", why);
   }
@@ -461,7 +464,10 @@ int vmoe_set_weights(vmoe_handle* h, const vmoe_weights* w, void* stream) {
   const bool bf16 = h->dtype == kBF16;
   const int R = h->cfg.lora_rank;
   int rc;
-  if ((rc = alloc_once(h, &h->w_r, E * H * elt, "router weight")) != VMOE_OK) return rc;
+  // the tensor-core router reads W_r in boxes of its N tile (16/32/64 rows): rows past E
+  // are zero, so no box reaches outside the tensor
+  const int64_t Er = router_rows(h);
+  if ((rc = alloc_once(h, &h->w_r, Er * H * elt, "router weight")) != VMOE_OK) return rc;
   if ((rc = alloc_once(h, &h->b_r, E * 4, "router bias")) != VMOE_OK) return rc;
   const int64_t gu_rows = bf16 ? 2 * Ipad : I;
   if ((rc = alloc_once(h, &h->w_g, El * gu_rows * H * elt, "gate weight")) != VMOE_OK) return rc;
@@ -479,6 +485,8 @@ int vmoe_set_weights(vmoe_handle* h, const vmoe_weights* w, void* stream) {
     e = cudaMemcpyAsync(h->w_r, w->router_w, E * H * elt, cudaMemcpyDeviceToDevice, s);
   else
     e = cudaMemsetAsync(h->w_r, 0, E * H * elt, s);
+  if (e == cudaSuccess && Er > E)
+    e = cudaMemsetAsync(static_cast<char*>(h->w_r) + E * H * elt, 0, (Er - E) * H * elt, s);
   if (e != cudaSuccess) return cuda_fail(h, e, "router weight copy");
   {
     PackBiasArgs b{h->dtype, w->router_b, nullptr, nullptr, nullptr, 0, 0.f,
@@ -554,7 +562,7 @@ int vmoe_set_weights(vmoe_handle* h, const vmoe_weights* w, void* stream) {
     char why[256];
     h->router_bn = tc_router_width(static_cast<int>(E));
     if (h->router_bn &&
-        !make_tmap_bf16(&h->map_wr, h->w_r, E, H, H, static_cast<uint32_t>(h->router_bn), why,
+        !make_tmap_bf16(&h->map_wr, h->w_r, Er, H, H, static_cast<uint32_t>(h->router_bn), why,
                         sizeof(why)))
       return fail(h, VMOE_ERR_CUDA, "router tensor map: %s", why);
     // B tiles: 256 rows per CTA, or 128 per CTA of a pair
