@@ -16,7 +16,13 @@ zero biases, FlyLoRA off.
 * ``e2e``    the same metric through the public API with x in pinned host memory and the
   output copied back to pinned host memory inside the timed region: on one GPU
   ``MoELayer.forward_host`` (token chunks whose copies overlap the layer), on N GPUs
-  ``ExpertParallelMoE.forward`` after a host->device copy.
+  ``ExpertParallelMoE.forward_host`` (each rank's token chunks copied in and out while the
+  other chunks exchange rows and run their GEMMs).
+* ``workloads`` (one GPU) the other configurations -- decode, prefill, skewed with
+  FlyLoRA, fp32 -- each timed after the headline region with its stage table, roofline and
+  the CPU restatement beside it.
+* ``ep_parity`` (N GPUs) every rank's output against a single-GPU forward of its tokens
+  with all experts, after the timed regions.
 * ``roofline`` the dominant kernel (the gate/up grouped GEMM) from CUDA events recorded
   around every launch of the timed region; algorithmic FLOPs = 4 * T * K * H * I.
 * ``cpu_baseline`` the CPU restatement of the reference algorithm (the oracle, numpy fp32)
@@ -598,10 +604,27 @@ def run_ours(args, rank, world, local_rank):
     x_host.copy_(x)
     out_host = torch.empty(x.shape, dtype=x.dtype, pin_memory=True)
     aux_host = torch.empty((), dtype=torch.float32, pin_memory=True)
+    e2e_layer = None
     if world == 1 and not args.prenorm:
         # the layer's host-buffer forward: token chunks whose copies overlap the layer
         def e2e_step():
             _, a = layer.forward_host(x_host, device=dev, chunks=args.host_chunks, out=out_host)
+            aux_host.copy_(a)
+    elif world > 1:
+        # the expert-parallel host-buffer forward: each token chunk's copies overlap the other
+        # chunks' exchange and GEMMs, so it needs 2+ chunks; with a 1-chunk device layer it
+        # gets its own 4-chunk layer
+        e2e_layer = layer
+        if layer.chunks < 2:
+            gw = global_weights(w, dev, seed=0)
+            e2e_layer = ExpertParallelMoE(cfg, gw, dev, torch.bfloat16, transport="p2p",
+                                          max_tokens=T, chunks=4)
+            del gw
+            torch.cuda.empty_cache()
+        x_host2d, out_host2d = x_host.reshape(-1, H), out_host.reshape(-1, H)
+
+        def e2e_step():
+            _, a = e2e_layer.forward_host(x_host2d, out=out_host2d)
             aux_host.copy_(a)
     else:
         def e2e_step():
@@ -626,6 +649,9 @@ def run_ours(args, rank, world, local_rank):
         dist.all_reduce(e2e_ms, op=dist.ReduceOp.MAX)
     e2e_value = world * T / (float(e2e_ms.item()) * 1e-3)
 
+    e2e_chunks = e2e_layer.chunks if e2e_layer is not None else None
+    if e2e_layer is not None and e2e_layer is not layer:
+        e2e_layer.close()
     ep_parity = None
     if world > 1 and not args.no_ep_parity:
         ep_parity = check_ep_parity(layer, x.reshape(-1, H), w, dev, world)
@@ -681,7 +707,9 @@ def run_ours(args, rank, world, local_rank):
                        if world == 1 and not args.prenorm else
                        "velvetoptimizer_b200.MoELayer.forward_residual after a host copy"
                        if world == 1 else
-                       "velvetoptimizer_b200.ep.ExpertParallelMoE.forward"},
+                       "velvetoptimizer_b200.ep.ExpertParallelMoE.forward_host "
+                       f"(vmoe_ep_p2p_forward_host: pinned host x/out, {e2e_chunks} token chunks "
+                       "whose copies overlap the other chunks' exchange and GEMMs)"},
         "roofline": {"kernel": roof_kernel,
                      "bound": "tensor", "achieved": round(achieved, 1),
                      "peak": pk["bf16_tflops"], "peak_source": pk["source"] + " bf16 burst",

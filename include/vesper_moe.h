@@ -309,6 +309,21 @@ VMOE_API int vmoe_ep_p2p_forward(vmoe_handle* h, const void* x, int64_t tokens, 
                                  float* router_logits, float* aux_loss, void* workspace,
                                  size_t workspace_bytes, void* stream);
 
+/* vmoe_ep_p2p_forward with x and out in HOST memory (the reference's CPU-tensor call of
+ * MoELayer.forward, python/vesper/model.py:317-364, served by this rank's GPU): each token
+ * chunk's rows are copied in on an internal copy stream before the chunk starts and copied
+ * out as soon as it ends, so the copies overlap the other chunks' exchange and GEMMs (give
+ * the handle 2 or more chunks at setup for any overlap).  Outputs are bit-identical to
+ * vmoe_ep_p2p_forward; aux_loss_host (optional) is a host fp32 scalar.  x_host / out_host
+ * [tokens, H] should be pinned.  Every rank calls it the same number of times, as
+ * vmoe_ep_p2p_forward.  Workspace (device, 256-byte aligned):
+ * vmoe_ep_p2p_host_workspace_size bytes (routing state plus device staging of max_tokens
+ * rows in and out).  Enqueued on `stream`, which ends after the last copy-out. */
+VMOE_API int vmoe_ep_p2p_host_workspace_size(const vmoe_handle* h, size_t* bytes);
+VMOE_API int vmoe_ep_p2p_forward_host(vmoe_handle* h, const void* x_host, int64_t tokens,
+                                      void* out_host, float* aux_loss_host, void* workspace,
+                                      size_t workspace_bytes, void* stream);
+
 /* ---- Dense FFN -----------------------------------------------------------------------
  * The non-MoE layers' FeedForward (python/vesper/model.py:249-270):
  *   out = down(ERA(gate(x)) * up(x)),  gate/up FlyLoRA linears folded as for the experts,

@@ -5,7 +5,8 @@
 Every rank builds the same global weights, routes its own tokens through the
 expert-parallel layer (experts sharded over the ranks, NCCL exchange) and through the
 single-GPU forward with all experts, and requires the outputs to be bit-identical (the same
-kernels compute each row and the combine order is fixed).  Exit code 0 on success.
+kernels compute each row and the combine order is fixed); the fused transport's host-buffer
+forward must reproduce its device forward bit for bit.  Exit code 0 on success.
 """
 import os
 import sys
@@ -96,6 +97,8 @@ def main():
                     x = torch.randn(T, cfg.hidden_size, generator=g, device=dev).to(dtype)
                     out, aux = layer(x)
                     out2, aux2 = layer(x)
+                    if transport != "nccl":  # the host-buffer forward (every rank calls it)
+                        out_h, aux_h = layer.forward_host(x.cpu().pin_memory())
                     torch.cuda.synchronize()
                     status = layer.device_status()
                     if status:
@@ -106,6 +109,12 @@ def main():
                         failures.append(f"{tag} it{it}: EP output differs from single GPU (max abs {d:.3e})")
                     if not torch.equal(out, out2):
                         failures.append(f"{tag} it{it}: EP output not deterministic")
+                    if transport != "nccl":
+                        if not torch.equal(out_h, out.cpu()):
+                            failures.append(f"{tag} it{it}: host-buffer EP output differs")
+                        if abs(aux_h.item() - aux.item()) > 1e-6 * abs(aux.item()):
+                            failures.append(f"{tag} it{it}: host-buffer aux {aux_h.item()} vs "
+                                            f"{aux.item()}")
                     if (abs(aux.item() - ref_aux.item()) > 1e-6 * abs(ref_aux.item())
                             or aux.item() != aux2.item()):
                         failures.append(f"{tag} it{it}: aux {aux.item()} vs {ref_aux.item()}")

@@ -35,7 +35,8 @@ EXPORTED = (
     "vmoe_last_launch_count", "vmoe_last_error", "vmoe_status_string", "vmoe_abi_version",
     "vmoe_create_ep", "vmoe_ep_workspace_size", "vmoe_ep_route", "vmoe_ep_experts",
     "vmoe_ep_combine", "vmoe_ep_p2p_setup", "vmoe_ep_p2p_connect", "vmoe_ep_p2p_workspace_size",
-    "vmoe_ep_p2p_forward", "vmoe_gemm_tile_rows", "vmoe_segment_align", "vmoe_ffn_create",
+    "vmoe_ep_p2p_forward", "vmoe_ep_p2p_host_workspace_size", "vmoe_ep_p2p_forward_host",
+    "vmoe_gemm_tile_rows", "vmoe_segment_align", "vmoe_ffn_create",
     "vmoe_ffn_workspace_size",
     "vmoe_ffn_forward", "vmoe_forward_host_workspace_size", "vmoe_forward_host",
     "vmoe_set_norm", "vmoe_forward_residual", "vmoe_set_training", "vmoe_train_workspace_size",
@@ -160,6 +161,11 @@ def load() -> ctypes.CDLL:
     lib.vmoe_ep_p2p_forward.argtypes = [H, c_void_p, c_int64, c_void_p, c_void_p, c_void_p,
                                         c_void_p, c_size_t, c_void_p]
     lib.vmoe_ep_p2p_forward.restype = c_int
+    lib.vmoe_ep_p2p_host_workspace_size.argtypes = [H, POINTER(c_size_t)]
+    lib.vmoe_ep_p2p_host_workspace_size.restype = c_int
+    lib.vmoe_ep_p2p_forward_host.argtypes = [H, c_void_p, c_int64, c_void_p, c_void_p, c_void_p,
+                                             c_size_t, c_void_p]
+    lib.vmoe_ep_p2p_forward_host.restype = c_int
     lib.vmoe_device_status.argtypes = [H, POINTER(c_int32), c_void_p]
     lib.vmoe_device_status.restype = c_int
     lib.vmoe_set_profiling.argtypes = [H, c_int]

@@ -462,53 +462,69 @@ int p2p_chunk(vmoe_handle* h, int c, const void* x, int64_t T, void* out, float*
 }
 }  // namespace
 
-int vmoe_ep_p2p_forward(vmoe_handle* h, const void* x, int64_t tokens, void* out,
-                        float* router_logits, float* aux_loss, void* workspace,
-                        size_t workspace_bytes, void* stream) {
-  if (!h) return VMOE_ERR_INVALID_ARG;
-  h->last_launches = 0;
-  if (!h->ready) return fail(h, VMOE_ERR_NOT_READY, "vmoe_set_weights has not been called");
-  if (!h->p2p_connected) return fail(h, VMOE_ERR_NOT_READY, "vmoe_ep_p2p_connect has not been called");
-  const int64_t E = h->E, K = h->K, H = h->H, T = tokens;
-  if (T < 0 || T > h->p2p_max_tokens)
-    return fail(h, VMOE_ERR_INVALID_ARG, "tokens must be in [0, %lld] (got %lld)",
-                static_cast<long long>(h->p2p_max_tokens), static_cast<long long>(T));
-  if (T > 0 && (!x || !out)) return fail(h, VMOE_ERR_INVALID_ARG, "x and out are required");
-  if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(out)) & 15u)
-    return fail(h, VMOE_ERR_INVALID_ARG, "x and out must be 16-byte aligned");
+namespace {
+// Host buffers of vmoe_ep_p2p_forward_host: each chunk's rows are copied in on h->host_in
+// before the chunk starts and copied out on h->host_out after it ends.
+struct HostIO {
+  const char* x_host;
+  char* out_host;
+  char* x_dev;    // staging, >= tokens rows
+  char* out_dev;  // staging, >= tokens rows
+};
+
+// One fused expert-parallel forward (every rank calls it): on `s` with one chunk and no host
+// buffers, else chunk c on internal stream c (its NVLink exchange overlapping the other
+// chunks' GEMMs, and with host buffers its copies overlapping the other chunks too).
+int ep_p2p_run(vmoe_handle* h, const void* x, int64_t T, void* out, float* router_logits,
+               float* aux_loss, char* ws, cudaStream_t s, const HostIO* io) {
+  const int64_t E = h->E, K = h->K, H = h->H;
   const int C = static_cast<int>(h->p2p.size());
   const size_t stride = p2p_chunk_stride(h);
-  if (!workspace || workspace_bytes < stride * C)
-    return fail(h, VMOE_ERR_WORKSPACE, "workspace needs %zu bytes (got %zu)", stride * C,
-                workspace ? workspace_bytes : static_cast<size_t>(0));
-  if (reinterpret_cast<uintptr_t>(workspace) & 255u)
-    return fail(h, VMOE_ERR_WORKSPACE, "workspace must be 256-byte aligned");
-  DeviceGuard g(h->device);
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  char* ws = static_cast<char*>(workspace);
   const P2PPlan p = make_p2p_plan(h, h->p2p_chunk_tokens);
-  const size_t elt = dtype_bytes(h->dtype);
+  const size_t row = static_cast<size_t>(H) * dtype_bytes(h->dtype);
   const bool prof = h->prof_count < h->prof_slots;
   cudaError_t e;
   int rc;
-  if (C == 1) {
+  if (C == 1 && !io) {
     if ((rc = p2p_chunk(h, 0, x, T, out, router_logits, ws, p, s, prof)) != VMOE_OK) return rc;
   } else {
-    // chunk c on its own stream: its dispatch and combine overlap the other chunks' GEMMs
     if ((e = cudaEventRecord(h->p2p_start, s)) != cudaSuccess) return cuda_fail(h, e, "event");
+    if (io) {  // the copy-in may overwrite the staging rows only after earlier work on s
+      if ((e = cudaStreamWaitEvent(h->host_in, h->p2p_start, 0)) != cudaSuccess)
+        return cuda_fail(h, e, "wait");
+      if ((e = cudaStreamWaitEvent(h->host_out, h->p2p_start, 0)) != cudaSuccess)
+        return cuda_fail(h, e, "wait");
+    }
     for (int c = 0; c < C; ++c) {
       cudaStream_t sc = h->p2p_streams[c];
       if ((e = cudaStreamWaitEvent(sc, h->p2p_start, 0)) != cudaSuccess) return cuda_fail(h, e, "wait");
       const int64_t t0 = c * h->p2p_chunk_tokens;
       int64_t tc = T - t0;
       tc = tc < 0 ? 0 : (tc > h->p2p_chunk_tokens ? h->p2p_chunk_tokens : tc);
-      const char* xc = static_cast<const char*>(x) + (tc > 0 ? t0 * H * elt : 0);
-      char* oc = static_cast<char*>(out) + (tc > 0 ? t0 * H * elt : 0);
+      const char* xbase = io ? io->x_dev : static_cast<const char*>(x);
+      char* obase = io ? io->out_dev : static_cast<char*>(out);
+      if (io) {
+        if (tc > 0 && (e = cudaMemcpyAsync(io->x_dev + t0 * row, io->x_host + t0 * row, tc * row,
+                                           cudaMemcpyHostToDevice, h->host_in)) != cudaSuccess)
+          return cuda_fail(h, e, "copy in");
+        if ((e = cudaEventRecord(h->host_in_ev[c], h->host_in)) != cudaSuccess ||
+            (e = cudaStreamWaitEvent(sc, h->host_in_ev[c], 0)) != cudaSuccess)
+          return cuda_fail(h, e, "copy-in order");
+      }
+      const char* xc = tc > 0 ? xbase + t0 * row : nullptr;
+      char* oc = tc > 0 ? obase + t0 * row : nullptr;
       float* lc = router_logits && tc > 0 ? router_logits + t0 * E : nullptr;
-      if ((rc = p2p_chunk(h, c, tc > 0 ? xc : nullptr, tc, tc > 0 ? oc : nullptr, lc,
-                          ws + c * stride, p, sc, prof && c == 0)) != VMOE_OK)
+      if ((rc = p2p_chunk(h, c, xc, tc, oc, lc, ws + c * stride, p, sc, prof && c == 0)) != VMOE_OK)
         return rc;
       if ((e = cudaEventRecord(h->p2p_done[c], sc)) != cudaSuccess) return cuda_fail(h, e, "event");
+      if (io) {
+        if ((e = cudaStreamWaitEvent(h->host_out, h->p2p_done[c], 0)) != cudaSuccess)
+          return cuda_fail(h, e, "copy-out order");
+        if (tc > 0 && (e = cudaMemcpyAsync(io->out_host + t0 * row, io->out_dev + t0 * row,
+                                           tc * row, cudaMemcpyDeviceToHost, h->host_out)) !=
+                          cudaSuccess)
+          return cuda_fail(h, e, "copy out");
+      }
     }
     for (int c = 0; c < C; ++c)
       if ((e = cudaStreamWaitEvent(s, h->p2p_done[c], 0)) != cudaSuccess) return cuda_fail(h, e, "wait");
@@ -519,7 +535,91 @@ int vmoe_ep_p2p_forward(vmoe_handle* h, const void* x, int64_t tokens, void* out
       return cuda_fail(h, e, "aux merge");
     ++h->last_launches;
   }
+  if (io) {  // s ends after the last copy-out
+    if ((e = cudaEventRecord(h->host_out_done, h->host_out)) != cudaSuccess ||
+        (e = cudaStreamWaitEvent(s, h->host_out_done, 0)) != cudaSuccess)
+      return cuda_fail(h, e, "copy-out join");
+  }
   if (prof) ++h->prof_count;
+  return VMOE_OK;
+}
+
+int check_p2p_call(vmoe_handle* h, int64_t T) {
+  h->last_launches = 0;
+  if (!h->ready) return fail(h, VMOE_ERR_NOT_READY, "vmoe_set_weights has not been called");
+  if (!h->p2p_connected) return fail(h, VMOE_ERR_NOT_READY, "vmoe_ep_p2p_connect has not been called");
+  if (T < 0 || T > h->p2p_max_tokens)
+    return fail(h, VMOE_ERR_INVALID_ARG, "tokens must be in [0, %lld] (got %lld)",
+                static_cast<long long>(h->p2p_max_tokens), static_cast<long long>(T));
+  return VMOE_OK;
+}
+
+void CUDART_CB write_nan_host(void* p) { *static_cast<float*>(p) = __builtin_nanf(""); }
+}  // namespace
+
+int vmoe_ep_p2p_forward(vmoe_handle* h, const void* x, int64_t tokens, void* out,
+                        float* router_logits, float* aux_loss, void* workspace,
+                        size_t workspace_bytes, void* stream) {
+  if (!h) return VMOE_ERR_INVALID_ARG;
+  const int64_t T = tokens;
+  int rc = check_p2p_call(h, T);
+  if (rc != VMOE_OK) return rc;
+  if (T > 0 && (!x || !out)) return fail(h, VMOE_ERR_INVALID_ARG, "x and out are required");
+  if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(out)) & 15u)
+    return fail(h, VMOE_ERR_INVALID_ARG, "x and out must be 16-byte aligned");
+  const size_t need = p2p_chunk_stride(h) * h->p2p.size();
+  if (!workspace || workspace_bytes < need)
+    return fail(h, VMOE_ERR_WORKSPACE, "workspace needs %zu bytes (got %zu)", need,
+                workspace ? workspace_bytes : static_cast<size_t>(0));
+  if (reinterpret_cast<uintptr_t>(workspace) & 255u)
+    return fail(h, VMOE_ERR_WORKSPACE, "workspace must be 256-byte aligned");
+  DeviceGuard g(h->device);
+  return ep_p2p_run(h, x, T, out, router_logits, aux_loss, static_cast<char*>(workspace),
+                    static_cast<cudaStream_t>(stream), nullptr);
+}
+
+int vmoe_ep_p2p_host_workspace_size(const vmoe_handle* h, size_t* bytes) {
+  if (!h || !bytes) return VMOE_ERR_INVALID_ARG;
+  if (h->p2p.empty()) return VMOE_ERR_NOT_READY;
+  const size_t rows = round_up(h->p2p_max_tokens > 0 ? h->p2p_max_tokens : 1, 16) *
+                      static_cast<size_t>(h->H) * dtype_bytes(h->dtype);
+  *bytes = p2p_chunk_stride(h) * h->p2p.size() + 2 * round_up(rows, 256) + 256;
+  return VMOE_OK;
+}
+
+int vmoe_ep_p2p_forward_host(vmoe_handle* h, const void* x_host, int64_t tokens, void* out_host,
+                             float* aux_loss_host, void* workspace, size_t workspace_bytes,
+                             void* stream) {
+  if (!h) return VMOE_ERR_INVALID_ARG;
+  const int64_t T = tokens;
+  int rc = check_p2p_call(h, T);
+  if (rc != VMOE_OK) return rc;
+  if (T > 0 && (!x_host || !out_host)) return fail(h, VMOE_ERR_INVALID_ARG, "x and out are required");
+  size_t need = 0;
+  vmoe_ep_p2p_host_workspace_size(h, &need);
+  if (!workspace || workspace_bytes < need)
+    return fail(h, VMOE_ERR_WORKSPACE, "workspace needs %zu bytes (got %zu)", need,
+                workspace ? workspace_bytes : static_cast<size_t>(0));
+  if (reinterpret_cast<uintptr_t>(workspace) & 255u)
+    return fail(h, VMOE_ERR_WORKSPACE, "workspace must be 256-byte aligned");
+  DeviceGuard g(h->device);
+  if ((rc = ensure_host_streams(h)) != VMOE_OK) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  char* ws = static_cast<char*>(workspace);
+  const size_t rows = round_up(h->p2p_max_tokens > 0 ? h->p2p_max_tokens : 1, 16) *
+                      static_cast<size_t>(h->H) * dtype_bytes(h->dtype);
+  const size_t x_off = p2p_chunk_stride(h) * h->p2p.size();
+  const size_t out_off = x_off + round_up(rows, 256), aux_off = out_off + round_up(rows, 256);
+  HostIO io{static_cast<const char*>(x_host), static_cast<char*>(out_host), ws + x_off,
+            ws + out_off};
+  float* aux_dev = reinterpret_cast<float*>(ws + aux_off);
+  rc = ep_p2p_run(h, nullptr, T, nullptr, nullptr, aux_loss_host ? aux_dev : nullptr, ws, s, &io);
+  if (rc != VMOE_OK) return rc;
+  if (aux_loss_host) {
+    cudaError_t e = T > 0 ? cudaMemcpyAsync(aux_loss_host, aux_dev, 4, cudaMemcpyDeviceToHost, s)
+                          : cudaLaunchHostFunc(s, write_nan_host, aux_loss_host);
+    if (e != cudaSuccess) return cuda_fail(h, e, "aux copy");
+  }
   return VMOE_OK;
 }
 

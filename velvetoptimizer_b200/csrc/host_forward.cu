@@ -184,7 +184,9 @@ int host_chunks_with_carry(vmoe_handle* h, int64_t T, const HostPlan& hp, char* 
 
 void CUDART_CB write_nan(void* p) { *static_cast<float*>(p) = __builtin_nanf(""); }
 
-int ensure_host_streams(vmoe_handle* h) {
+}  // namespace
+
+int vmoe_host::ensure_host_streams(vmoe_handle* h) {
   if (h->host_in) return VMOE_OK;
   cudaError_t e = cudaStreamCreateWithFlags(&h->host_in, cudaStreamNonBlocking);
   if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&h->host_out, cudaStreamNonBlocking);
@@ -203,8 +205,6 @@ int ensure_host_streams(vmoe_handle* h) {
   }
   return VMOE_OK;
 }
-
-}  // namespace
 
 extern "C" {
 

@@ -346,6 +346,8 @@ int forward_batch(vmoe_handle* h, const void* x, int64_t T, void* out, float* ro
                   int32_t* topk_idx, float* topk_w, int32_t* expert_counts, float* aux_loss,
                   char* ws, const Plan& p, cudaStream_t s, bool prof, float* psum_tot_out,
                   bool prenorm = false);
+// The host-buffer forwards' copy streams and per-chunk events, made on first use.
+int ensure_host_streams(vmoe_handle* h);
 // Transposed copies of the packed weights for the backward GEMMs (training handles).
 int make_training_copies(vmoe_handle* h, cudaStream_t s);
 // Fold the LayerNorm into the router weights (vmoe_set_norm).

@@ -160,6 +160,7 @@ class ExpertParallelMoE:
         self.transport = transport
         self.max_tokens = max_tokens
         self._p2p_ws = None
+        self._host_ws = None
         if transport == "p2p":
             if max_tokens is None:
                 raise ValueError("transport='p2p' needs max_tokens (tokens per rank per forward)")
@@ -213,6 +214,41 @@ class ExpertParallelMoE:
                                            ctypes.c_void_p(self._p2p_ws.data_ptr()),
                                            self._p2p_ws.numel(), stream), h, "vmoe_ep_p2p_forward")
         self.launches = lib.vmoe_last_launch_count(h)
+        return out, aux
+
+    def forward_host(self, x: torch.Tensor, out: torch.Tensor | None = None):
+        """``forward`` for x [T, H] in host memory (fused NVLink transport): each token
+        chunk's rows are copied to this rank's GPU, run and copied back with the copies
+        overlapping the other chunks (``vmoe_ep_p2p_forward_host``).  x and ``out`` should
+        be pinned.  Returns (out [T, H], aux_loss) as host tensors, ready on return; out is
+        bit-identical to ``forward`` of the same tokens."""
+        if self.transport != "p2p":
+            raise ValueError("forward_host runs on the fused NVLink transport ('p2p')")
+        if x.device.type != "cpu":
+            raise ValueError("forward_host takes a host tensor; use forward for CUDA tensors")
+        lib, h, dev = self.lib, self.h, self.device
+        T, H = x.shape
+        x = x.contiguous()
+        if out is None:
+            out = torch.empty(x.shape, dtype=x.dtype, pin_memory=x.is_pinned())
+        elif out.shape != x.shape or out.dtype != x.dtype or out.device.type != "cpu" \
+                or not out.is_contiguous():
+            raise ValueError("out must be a contiguous host tensor shaped and typed like x")
+        n = ctypes.c_size_t()
+        _lib.check(lib.vmoe_ep_p2p_host_workspace_size(h, ctypes.byref(n)), h)
+        if self._host_ws is None or self._host_ws.numel() < n.value:
+            self._host_ws = torch.empty(max(n.value, 256), dtype=torch.uint8, device=dev)
+        aux = torch.empty((), dtype=torch.float32, pin_memory=True)
+        stream = torch.cuda.current_stream(dev)
+        _lib.check(lib.vmoe_ep_p2p_forward_host(h, ctypes.c_void_p(x.data_ptr()), T,
+                                                ctypes.c_void_p(out.data_ptr()),
+                                                ctypes.c_void_p(aux.data_ptr()),
+                                                ctypes.c_void_p(self._host_ws.data_ptr()),
+                                                self._host_ws.numel(),
+                                                ctypes.c_void_p(stream.cuda_stream)),
+                   h, "vmoe_ep_p2p_forward_host")
+        self.launches = lib.vmoe_last_launch_count(h)
+        stream.synchronize()
         return out, aux
 
     def set_profiling(self, forwards: int) -> None:
