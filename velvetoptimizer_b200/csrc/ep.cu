@@ -400,8 +400,10 @@ int p2p_chunk(vmoe_handle* h, int c, const void* x, int64_t T, void* out, float*
 
   cudaEvent_t* ev = prof ? &h->prof_ev[static_cast<size_t>(h->prof_count) * (kStages + 1)] : nullptr;
   int stage = 0;
+  NvtxStages nvtx(kNvtxStageNames, kStages);
   auto mark = [&]() {
     if (prof) cudaEventRecord(ev[stage], s);
+    nvtx.next(stage);
     ++stage;
   };
   auto check = [&](cudaError_t err, const char* what) -> int {

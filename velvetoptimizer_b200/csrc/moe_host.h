@@ -17,6 +17,8 @@
 #include <string>
 #include <vector>
 
+#include <nvtx3/nvToolsExt.h>
+
 #include "../../include/vesper_moe.h"
 #include "kernels.h"
 
@@ -30,6 +32,29 @@ constexpr int kBwdStages = 9;
 const char* const kBwdStageNames[kBwdStages] = {
     "combine_bwd", "router_bwd", "dh_glu_bwd_gemm", "dx_gemm", "router_dx_gemm", "dx_gather",
     "wgrad_down", "wgrad_gate_up", "wgrad_router"};
+// NVTX range names of the stages (host timeline of Nsight Systems; no cost without a tool)
+const char* const kNvtxStageNames[kStages] = {
+    "vmoe.router", "vmoe.scan", "vmoe.plan", "vmoe.dispatch", "vmoe.gemm1_gate_up_era",
+    "vmoe.gemm2_down", "vmoe.combine"};
+const char* const kNvtxBwdStageNames[kBwdStages] = {
+    "vmoe.bwd.combine", "vmoe.bwd.router", "vmoe.bwd.dh_glu", "vmoe.bwd.dx_gemm",
+    "vmoe.bwd.router_dx", "vmoe.bwd.dx_gather", "vmoe.bwd.wgrad_down",
+    "vmoe.bwd.wgrad_gate_up", "vmoe.bwd.wgrad_router"};
+
+// One NVTX range per stage: next(i) closes stage i-1's range and opens stage i's (i <
+// count); the destructor closes whatever is still open (an error return mid-forward).
+struct NvtxStages {
+  const char* const* names;
+  int count;
+  int open = 0;
+  NvtxStages(const char* const* n, int c) : names(n), count(c) {}
+  void next(int i) {
+    if (open) { nvtxRangePop(); open = 0; }
+    if (i < count) { nvtxRangePushA(names[i]); open = 1; }
+  }
+  ~NvtxStages() { if (open) nvtxRangePop(); }
+};
+
 constexpr int kGateUpInterleave = 128;  // rows of gate (then up) per 256-row B tile
 constexpr int kDownTileN = 256;         // N tile of the down projection
 

@@ -209,8 +209,10 @@ int vmoe_backward(vmoe_handle* h, const void* x, const void* dout, int64_t token
   cudaEvent_t* pev =
       prof ? &h->bprof_ev[static_cast<size_t>(h->bprof_count) * (kBwdStages + 1)] : nullptr;
   int stage = 0;
+  NvtxStages nvtx(kNvtxBwdStageNames, kBwdStages);
   auto mark = [&]() {
     if (prof) cudaEventRecord(pev[stage], s);
+    nvtx.next(stage);
     ++stage;
   };
 
