@@ -302,6 +302,8 @@ def stage_table(stages, alg, pk, scale=1.0, weight_bound=False, fp32=False, ep=F
     profiled stages processed (the first token chunk of an expert-parallel forward)."""
     total = max(sum(stages.values()), 1e-9)
     rep = {}
+    # a decode batch runs both expert GEMMs in one launch: its "gemm1" stage holds both
+    merged = weight_bound and stages.get("gemm2_down", 0.0) < 0.01 * stages.get("gemm1_gate_up_era", 1.0)
     for name, t_ms in stages.items():
         rec = {"ms": round(t_ms, 4), "share": round(t_ms / total, 4)}
         sec = max(t_ms, 1e-9) * 1e-3
@@ -312,7 +314,16 @@ def stage_table(stages, alg, pk, scale=1.0, weight_bound=False, fp32=False, ep=F
                 rec.update(achieved=round(tf, 2), unit="TFLOP/s", frac=None,
                            bound="fp32 CUDA cores (no measured peak)")
             elif weight_bound:
-                gbs = alg[f"{key}_weight_bytes"] / sec / 1e9
+                if merged and key == "gemm2":
+                    rec["note"] = "runs inside the gemm1 stage's launch"
+                    rep[name] = rec
+                    continue
+                wbytes = alg[f"{key}_weight_bytes"]
+                if merged:
+                    wbytes += alg["gemm2_weight_bytes"]
+                    tf = (alg["gemm1_flop"] + alg["gemm2_flop"]) * scale / sec / 1e12
+                    rec["note"] = "gate|up and down GEMMs in one launch"
+                gbs = wbytes / sec / 1e9
                 rec.update(achieved=round(gbs, 1), unit="GB/s", frac=round(gbs / pk["hbm_gbs"], 4),
                            bound="hbm (expert weights read once)", tflops=round(tf, 2))
             else:

@@ -120,3 +120,22 @@ def test_decode_threshold_selects_the_path(monkeypatch):
     f32 = AbiLayer(case, make_inputs(case), "f32")
     assert f32.handle.lib.vmoe_segment_align(f32.handle.ptr, 64) == 128
     f32.close()
+
+
+@pytest.mark.parametrize("name", ["t64_e8k2_bias", "t64_e64k8_lora_zipf", "t17_odd_dims"])
+def test_decode_one_launch_equals_two(name, monkeypatch):
+    """Both decode GEMMs in one launch (the down GEMM's work items wait on per-expert counts
+    of stored gate|up blocks) give the same bits as the two GEMMs launched one after the
+    other (VMOE_DECODE_FUSED=0)."""
+    case = DECODE_CASES[name]
+    inp = bf16_inputs(make_inputs(case))
+    fused = AbiLayer(case, inp, "bf16")
+    monkeypatch.setenv("VMOE_DECODE_FUSED", "0")
+    split = AbiLayer(case, inp, "bf16")
+    monkeypatch.delenv("VMOE_DECODE_FUSED")
+    for _ in range(2):  # the counters start from zero every forward
+        a, b = fused.run(inp["x"]), split.run(inp["x"])
+        assert np.array_equal(a["out"], b["out"])
+        assert a["aux"] == b["aux"]
+    fused.close()
+    split.close()

@@ -72,7 +72,7 @@ __global__ void __launch_bounds__(1024)
 plan_kernel(const int* __restrict__ counts, const float* __restrict__ psum_tot, int64_t T, int E,
             int K, int64_t capacity, int row_align, int* __restrict__ offs,
             int* __restrict__ tile_expert, int* __restrict__ num_tiles, float* __restrict__ aux,
-            int32_t* __restrict__ counts_out) {
+            int32_t* __restrict__ counts_out, int* __restrict__ zero_e) {
   __shared__ int pad_s[1024];
   __shared__ int off_s[1025];
   const int tid = threadIdx.x;
@@ -101,6 +101,8 @@ plan_kernel(const int* __restrict__ counts, const float* __restrict__ psum_tot, 
   }
   __syncthreads();
   for (int e = tid; e <= E; e += blockDim.x) offs[e] = off_s[e];
+  if (zero_e)
+    for (int e = tid; e < E; e += blockDim.x) zero_e[e] = 0;
   if (tile_expert && tid < E) {  // one entry per row_align-row GEMM tile
     const int t0 = off_s[tid] / row_align, nt = pad_s[tid] / row_align;
     for (int j = 0; j < nt; ++j) tile_expert[t0 + j] = tid;
@@ -410,9 +412,10 @@ cudaError_t launch_scan_blocks(const int* hist, const float* psum, int nblk, int
 
 cudaError_t launch_plan(const int* counts, const float* psum_tot, int64_t T, int E, int K,
                         int64_t capacity, int row_align, int* offs, int* tile_expert,
-                        int* num_tiles, float* aux, int32_t* counts_out, cudaStream_t s) {
+                        int* num_tiles, float* aux, int32_t* counts_out, cudaStream_t s,
+                        int* zero_e) {
   plan_kernel<<<1, 1024, 0, s>>>(counts, psum_tot, T, E, K, capacity, row_align, offs,
-                                 tile_expert, num_tiles, aux, counts_out);
+                                 tile_expert, num_tiles, aux, counts_out, zero_e);
   return cudaGetLastError();
 }
 

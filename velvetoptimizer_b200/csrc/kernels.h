@@ -43,7 +43,8 @@ cudaError_t launch_scan_blocks(const int* hist, const float* psum, int nblk, int
 // count, aux loss, caller counts.
 cudaError_t launch_plan(const int* counts, const float* psum_tot, int64_t T, int E, int K,
                         int64_t capacity, int row_align, int* offs, int* tile_expert,
-                        int* num_tiles, float* aux, int32_t* counts_out, cudaStream_t s);
+                        int* num_tiles, float* aux, int32_t* counts_out, cudaStream_t s,
+                        int* zero_e = nullptr);  // [E] ints set to 0 (nullable)
 
 // Token chunks with carried rows (the host-buffer forward): expert e's segment holds the
 // carry_in[e] rows carried in from the previous chunk, then this chunk's counts[e] new rows;
@@ -201,25 +202,37 @@ struct DecodeGemmArgs {
   const int* offs;          // [E+1] segment starts (rows), multiples of kDecodeRowAlign
   int num_experts;          // E (<= kDecodeMaxExperts)
   int64_t max_rows;         // rows the activation and output buffers hold
-  int k_blocks;             // ceil(K / 64)
-  int blocks_per_expert;    // work items per expert: 128-row weight blocks
-  int a_rows_per_expert;    // rows of the packed weight view per expert (2*Ipad or Hpad)
   int n_max;                // largest segment (rows) any expert can have, multiple of 16
                             // (the kernel sizes its ring for the widest one present)
-  void* out;                // bf16 [max_rows, ldo]
-  int64_t ldo;
-  const float* bias;        // gated: interleaved gate|up [E, bias_ld]; plain: [E, bias_ld]
-  int64_t bias_ld;
-  float gamma;              // ERA gamma (gated)
-  int64_t row_limit;        // rows >= row_limit are not stored (0 = no limit)
   int* status;
+  int64_t row_limit;        // rows >= row_limit are not stored (0 = no limit)
+  // phase 1, gate|up (bpe1 = 0: none): h = ERA(gate + bg) * (up + bu)
+  int bpe1;                 // work items per expert: 64-feature blocks (Ipad / 64)
+  int k_blocks1;            // ceil(H / 64)
+  int a_rows1;              // rows of the packed gate|up view per expert (2 * Ipad)
+  void* h;                  // bf16 [max_rows, ldh]
+  int64_t ldh;
+  const float* bias1;       // interleaved gate|up bias [E, bias1_ld]
+  int64_t bias1_ld;
+  float gamma;              // ERA gamma
+  // phase 2, down (bpe2 = 0: none): y = h Wd^T + bd
+  int bpe2;                 // work items per expert: 128-feature blocks (Hpad / 128)
+  int k_blocks2;            // Ipad / 64
+  int a_rows2;              // rows of the packed down view per expert (Hpad)
+  void* y;                  // bf16 [max_rows, ldy]
+  int64_t ldy;
+  const float* bias2;       // [E, bias2_ld], or null
+  int64_t bias2_ld;
+  // both phases in one launch: [E] counts of each expert's stored gate|up blocks, zero
+  // before the launch
+  int* ready;
 };
-// gated = true : a_map = packed gate|up weights with 64-row boxes, b_map = x_perm (16-row
-//                boxes); out = h [rows, Ipad] = ERA(gate + bg) * (up + bu)
-// gated = false: a_map = packed down weights with 128-row boxes, b_map = h (16-row boxes);
-//                out = y [rows, Hpad] = down + bd
-cudaError_t launch_decode_gemm(bool gated, const CUtensorMap& a_map, const CUtensorMap& b_map,
-                               DecodeGemmArgs args, int64_t max_items, int num_sms,
+// a1_map: packed gate|up weights, 64-row boxes; b1_map: x_perm, 16-row boxes;
+// a2_map: packed down weights, 128-row boxes;   b2_map: h, 16-row boxes.
+// With bpe1 > 0 and bpe2 > 0 both phases run in one cooperative launch.
+cudaError_t launch_decode_gemm(const CUtensorMap& a1_map, const CUtensorMap& b1_map,
+                               const CUtensorMap& a2_map, const CUtensorMap& b2_map,
+                               const DecodeGemmArgs& args, int64_t max_items, int num_sms,
                                cudaStream_t s);
 int decode_gemm_stages(int n_max);
 

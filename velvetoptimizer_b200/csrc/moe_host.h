@@ -89,7 +89,8 @@ struct Plan {
   int nblk = 0;
   int64_t max_tiles = 0, max_rows = 0;
   size_t idx = 0, w = 0, hist = 0, psum = 0, excl = 0, counts = 0, psum_tot = 0, offs = 0,
-         tiles = 0, ntiles = 0, aux = 0, slot = 0, stats = 0, xp = 0, h = 0, y = 0, total = 0;
+         tiles = 0, ntiles = 0, aux = 0, slot = 0, stats = 0, xp = 0, h = 0, y = 0, ready = 0,
+         total = 0;
 };
 
 }  // namespace vmoe_host
@@ -143,6 +144,7 @@ struct vmoe_handle {
   // GEMMs read the packed weights through these maps (64-row gate|up boxes, 128-row down)
   CUtensorMap map_wgu_dec{}, map_wd_dec{};
   int decode_max_tokens = 0;  // 0: never
+  bool decode_fused = true;   // both decode GEMMs in one launch
   int tile_rows = kTileM;  // GEMM M tile: 256 with CTA-pair GEMMs (bf16), else 128
   bool dense = false;      // a dense FeedForward handle (one expert, no router)
   CUtensorMap map_wr{};   // router weights for the tensor-core router (bf16, E <= 64)
@@ -317,10 +319,12 @@ inline int routing_block(const vmoe_handle* h, int64_t T) {
 }
 
 // gate|up GEMM (+ ERA * up) then down GEMM over the expert-major buffer of a decode-sized
-// forward: segments padded to kDecodeRowAlign rows at offs[E+1], no tile map.
+// forward: segments padded to kDecodeRowAlign rows at offs[E+1], no tile map.  One
+// cooperative launch runs both (`ready`: the per-expert counters the plan kernel zeroed);
+// VMOE_DECODE_FUSED=0 at handle creation runs them as two launches instead.
 template <typename Mark, typename Check>
 int run_decode_gemms(vmoe_handle* h, void* xp, int64_t max_rows, const int* offs, void* hb,
-                     void* yb, int64_t T, cudaStream_t s, Mark&& mark, Check&& check) {
+                     void* yb, int64_t T, int* ready, cudaStream_t s, Mark&& mark, Check&& check) {
   const int64_t H = h->H, El = h->E_local;
   char why[256];
   CUtensorMap map_x, map_h;
@@ -335,31 +339,41 @@ int run_decode_gemms(vmoe_handle* h, void* xp, int64_t max_rows, const int* offs
   a.offs = offs;
   a.num_experts = static_cast<int>(El);
   a.max_rows = max_rows;
-  a.k_blocks = static_cast<int>((H + 63) / 64);
-  a.blocks_per_expert = static_cast<int>(h->Ipad / 64);
-  a.a_rows_per_expert = static_cast<int>(2 * h->Ipad);
   a.n_max = static_cast<int>(n_max);
-  a.out = hb;
-  a.ldo = h->Ipad;
-  a.bias = h->b_g;
-  a.bias_ld = 2 * h->Ipad;
-  a.gamma = h->cfg.era_gamma;
   a.status = h->status;
+  a.bpe1 = static_cast<int>(h->Ipad / 64);
+  a.k_blocks1 = static_cast<int>((H + 63) / 64);
+  a.a_rows1 = static_cast<int>(2 * h->Ipad);
+  a.h = hb;
+  a.ldh = h->Ipad;
+  a.bias1 = h->b_g;
+  a.bias1_ld = 2 * h->Ipad;
+  a.gamma = h->cfg.era_gamma;
+  a.bpe2 = static_cast<int>(h->Hpad / 128);
+  a.k_blocks2 = static_cast<int>(h->Ipad / 64);
+  a.a_rows2 = static_cast<int>(h->Hpad);
+  a.y = yb;
+  a.ldy = h->Hpad;
+  a.bias2 = h->b_d;
+  a.bias2_ld = h->Hpad;
+  if (h->decode_fused) {
+    a.ready = ready;
+    const int rc = check(launch_decode_gemm(h->map_wgu_dec, map_x, h->map_wd_dec, map_h, a,
+                                            El * (a.bpe1 + a.bpe2), h->num_sms, s),
+                         "gemm1 + gemm2 (decode)");
+    mark();  // one launch: the gemm2 stage is empty
+    return rc;
+  }
+  DecodeGemmArgs a1 = a, a2 = a;
+  a1.bpe2 = 0;
+  a2.bpe1 = 0;
   int rc;
-  if ((rc = check(launch_decode_gemm(true, h->map_wgu_dec, map_x, a, El * a.blocks_per_expert,
-                                     h->num_sms, s),
+  if ((rc = check(launch_decode_gemm(h->map_wgu_dec, map_x, h->map_wd_dec, map_h, a1,
+                                     El * a1.bpe1, h->num_sms, s),
                   "gemm1 (decode)")) != VMOE_OK)
     return rc;
   mark();
-  a.k_blocks = static_cast<int>(h->Ipad / 64);
-  a.blocks_per_expert = static_cast<int>(h->Hpad / 128);
-  a.a_rows_per_expert = static_cast<int>(h->Hpad);
-  a.out = yb;
-  a.ldo = h->Hpad;
-  a.bias = h->b_d;
-  a.bias_ld = h->Hpad;
-  a.gamma = 0.f;
-  return check(launch_decode_gemm(false, h->map_wd_dec, map_h, a, El * a.blocks_per_expert,
+  return check(launch_decode_gemm(h->map_wgu_dec, map_x, h->map_wd_dec, map_h, a2, El * a2.bpe2,
                                   h->num_sms, s),
                "gemm2 (decode)");
 }

@@ -65,6 +65,7 @@ Plan make_plan(const vmoe_handle* h, int64_t T, int rb) {
   p.xp = take(static_cast<size_t>(p.max_rows) * h->H * elt);
   p.h = take(static_cast<size_t>(p.max_rows) * h->Ipad * elt);
   p.y = take(static_cast<size_t>(p.max_rows) * h->Hpad * elt);
+  p.ready = take(E * 4);
   p.total = off;
   return p;
 }
@@ -145,6 +146,7 @@ int forward_batch(vmoe_handle* h, const void* x, int64_t T, void* out, float* ro
   int* ntiles = reinterpret_cast<int*>(ws + p.ntiles);
   float* aux = aux_loss ? aux_loss : reinterpret_cast<float*>(ws + p.aux);
   int* slot = reinterpret_cast<int*>(ws + p.slot);
+  int* ready = reinterpret_cast<int*>(ws + p.ready);
   void* xp = ws + p.xp;
   void* hb = ws + p.h;
   void* yb = ws + p.y;
@@ -178,7 +180,7 @@ int forward_batch(vmoe_handle* h, const void* x, int64_t T, void* out, float* ro
   if ((rc = check(launch_plan(counts, psum_tot, T, static_cast<int>(E), static_cast<int>(K),
                               h->cfg.capacity, segment_align(h, T), offs,
                               decode ? nullptr : tiles, decode ? nullptr : ntiles, aux,
-                              expert_counts, s),
+                              expert_counts, s, decode ? ready : nullptr),
                   "plan")) != VMOE_OK)
     return rc;
   mark();
@@ -188,7 +190,7 @@ int forward_batch(vmoe_handle* h, const void* x, int64_t T, void* out, float* ro
                   "dispatch")) != VMOE_OK)
     return rc;
   mark();
-  if ((rc = decode ? run_decode_gemms(h, xp, p.max_rows, offs, hb, yb, T, s, mark, check)
+  if ((rc = decode ? run_decode_gemms(h, xp, p.max_rows, offs, hb, yb, T, ready, s, mark, check)
                    : run_expert_gemms(h, xp, p.max_rows, tiles, ntiles, hb, yb, h->Hpad, s, mark,
                                       check)) != VMOE_OK)
     return rc;
@@ -376,6 +378,7 @@ int vmoe_create(const vmoe_config* cfg, int device, vmoe_handle** out) {
     // forwards of at most this many tokens run the swapped-operand (decode) GEMMs;
     // VMOE_DECODE_MAX_TOKENS lowers it (0: never)
     h->decode_max_tokens = kDecodeMaxTokens;
+    if (const char* f = getenv("VMOE_DECODE_FUSED")) h->decode_fused = f[0] != '0';
     if (const char* d = getenv("VMOE_DECODE_MAX_TOKENS")) {
       const long v = strtol(d, nullptr, 10);
       h->decode_max_tokens = v < 0 ? 0 : (v > kDecodeMaxTokens ? kDecodeMaxTokens : static_cast<int>(v));
