@@ -133,9 +133,13 @@ def test_decode_one_launch_equals_two(name, monkeypatch):
     monkeypatch.setenv("VMOE_DECODE_FUSED", "0")
     split = AbiLayer(case, inp, "bf16")
     monkeypatch.delenv("VMOE_DECODE_FUSED")
+    ipad = -(-case.inter // 128) * 128
+    one_launch = ipad // 64 <= -(-case.hidden // 64)  # down items no larger than gate|up ones
     for _ in range(2):  # the counters start from zero every forward
         a, b = fused.run(inp["x"]), split.run(inp["x"])
         assert np.array_equal(a["out"], b["out"])
         assert a["aux"] == b["aux"]
+        n_fused, n_split = fused.handle.last_launch_count(), split.handle.last_launch_count()
+        assert n_fused == n_split - (1 if one_launch else 0), (n_fused, n_split)
     fused.close()
     split.close()

@@ -188,8 +188,7 @@ int fail(vmoe_handle* h, int code, const char* fmt, ...);
 int cuda_fail(vmoe_handle* h, cudaError_t e, const char* what);
 
 // Workspace plan of a single-GPU forward of T tokens routed in blocks of `rb` tokens
-// (0: routing_block(h, T), the inference forward's choice; the training forward routes in
-// 128-token blocks).  The forward must route and dispatch with the plan's rb.
+// (0: routing_block(h, T)).  The forward must route and dispatch with the plan's rb.
 Plan make_plan(const vmoe_handle* h, int64_t T, int rb = 0);
 
 template <typename T>
@@ -356,7 +355,11 @@ int run_decode_gemms(vmoe_handle* h, void* xp, int64_t max_rows, const int* offs
   a.ldy = h->Hpad;
   a.bias2 = h->b_d;
   a.bias2_ld = h->Hpad;
-  if (h->decode_fused) {
+  // one launch when a down-GEMM work item (128 rows x Ipad) is no larger than a gate|up one
+  // (128 rows x H): larger ones, started only once their expert's gate|up blocks are all
+  // stored, would end the launch on a few SMs (measured: 166 us in one launch against
+  // 153 us in two for 64 tokens at H 2048, I 8192, E 8; 91 against 109 us at I 1024, E 64)
+  if (h->decode_fused && a.k_blocks2 <= a.k_blocks1) {
     a.ready = ready;
     const int rc = check(launch_decode_gemm(h->map_wgu_dec, map_x, h->map_wd_dec, map_h, a,
                                             El * (a.bpe1 + a.bpe2), h->num_sms, s),

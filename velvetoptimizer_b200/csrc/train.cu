@@ -16,7 +16,9 @@ struct TrainPlan {
 
 TrainPlan make_train_plan(const vmoe_handle* h, int64_t T) {
   TrainPlan tp;
-  tp.p = make_plan(h, T, kTileM);  // routed in 128-token blocks
+  // the inference forward's routing blocks (only the forward's scan reads their histograms),
+  // so that routing, aux and outputs are bit-identical to vmoe_forward's
+  tp.p = make_plan(h, T);
   size_t off = tp.p.total;
   auto take = [&](size_t bytes) {
     const size_t o = off;
