@@ -28,6 +28,14 @@ enum DeviceStatus : int {
 // Upper bound on any single spin-wait inside a kernel (ns of %globaltimer).
 constexpr uint64_t kWaitLimitNs = 2000000000ull;
 
+// Programmatic dependent launch: wait until the kernel before this one on the stream has
+// completed and its memory is visible, then let the kernel after this one launch.  Both are
+// no-ops for a kernel launched without the attribute (see launch_kernel).
+__device__ __forceinline__ void pdl_wait_and_trigger() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 __device__ __forceinline__ void report(int* status, int code) {
   if (status) atomicCAS(status, 0, code);
 }

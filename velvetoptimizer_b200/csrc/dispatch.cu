@@ -25,6 +25,7 @@ namespace {
 __global__ void __launch_bounds__(256)
 scan_blocks_kernel(const int* __restrict__ hist, const float* __restrict__ psum, int nblk, int E,
                    int* __restrict__ excl, int* __restrict__ counts, float* __restrict__ psum_tot) {
+  pdl_wait_and_trigger();
   const int e = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int per = (nblk + 255) / 256;
   const int b0 = min(nblk, tid * per), b1 = min(nblk, b0 + per);
@@ -73,6 +74,7 @@ plan_kernel(const int* __restrict__ counts, const float* __restrict__ psum_tot, 
             int K, int64_t capacity, int row_align, int* __restrict__ offs,
             int* __restrict__ tile_expert, int* __restrict__ num_tiles, float* __restrict__ aux,
             int32_t* __restrict__ counts_out, int* __restrict__ zero_e) {
+  pdl_wait_and_trigger();
   __shared__ int pad_s[1024];
   __shared__ int off_s[1025];
   const int tid = threadIdx.x;
@@ -171,6 +173,7 @@ dispatch_kernel(const T* __restrict__ x, const int32_t* __restrict__ topk_idx,
                 int64_t xp_ld, int* status, const float2* __restrict__ ln_stats,
                 const float* __restrict__ ln_w, const float* __restrict__ ln_b,
                 const DispatchCarry carry, int rb) {
+  pdl_wait_and_trigger();
   extern __shared__ uint32_t dsm[];
   uint32_t* masks = dsm;                            // [4 warps][E] token bitmasks
   int* wbase = reinterpret_cast<int*>(dsm + 4 * E);  // [4][E]
@@ -308,6 +311,7 @@ __global__ void __launch_bounds__(256)
 combine_kernel(const T* __restrict__ y, int64_t y_ld, const int32_t* __restrict__ topk_idx,
                const float* __restrict__ topk_w, const int* __restrict__ slot_of, int64_t T_tok,
                int H, int K, T* out, const T* resid, int wpt) {
+  pdl_wait_and_trigger();
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int64_t t = static_cast<int64_t>(blockIdx.x) * (8 / wpt) + warp / wpt;
   const int part = warp % wpt;
@@ -406,17 +410,16 @@ cudaError_t launch_aux_merge_ws(const void* ws, size_t stride, size_t counts_off
 
 cudaError_t launch_scan_blocks(const int* hist, const float* psum, int nblk, int E, int* excl,
                                int* counts, float* psum_tot, cudaStream_t s) {
-  scan_blocks_kernel<<<E, 256, 0, s>>>(hist, psum, nblk, E, excl, counts, psum_tot);
-  return cudaGetLastError();
+  return launch_kernel(scan_blocks_kernel, dim3(E), dim3(256), 0, s, hist, psum, nblk, E, excl,
+                       counts, psum_tot);
 }
 
 cudaError_t launch_plan(const int* counts, const float* psum_tot, int64_t T, int E, int K,
                         int64_t capacity, int row_align, int* offs, int* tile_expert,
                         int* num_tiles, float* aux, int32_t* counts_out, cudaStream_t s,
                         int* zero_e) {
-  plan_kernel<<<1, 1024, 0, s>>>(counts, psum_tot, T, E, K, capacity, row_align, offs,
-                                 tile_expert, num_tiles, aux, counts_out, zero_e);
-  return cudaGetLastError();
+  return launch_kernel(plan_kernel, dim3(1), dim3(1024), 0, s, counts, psum_tot, T, E, K,
+                       capacity, row_align, offs, tile_expert, num_tiles, aux, counts_out, zero_e);
 }
 
 cudaError_t launch_plan_carry(const int* counts, const int* carry_in, int E, bool last,
@@ -429,15 +432,17 @@ cudaError_t launch_plan_carry(const int* counts, const int* carry_in, int E, boo
 
 namespace {
 template <typename T, bool LN>
-void dispatch_as(const void* x, const int32_t* topk_idx, const int* excl, const int* offs,
+cudaError_t dispatch_as(const void* x, const int32_t* topk_idx, const int* excl, const int* offs,
                  int64_t T_tok, int H, int E, int K, int64_t capacity, int* slot_of, void* x_perm,
                  int64_t xp_ld, int* status, const LnArgs* ln, cudaStream_t s,
                  const DispatchCarry& carry, int rb) {
   const unsigned nblk = static_cast<unsigned>((T_tok + rb - 1) / rb);
-  if (nblk == 0) return;  // no tokens: nothing to place
+  if (nblk == 0) return cudaSuccess;  // no tokens: nothing to place
   const size_t smem = (8 * static_cast<size_t>(E) + static_cast<size_t>(kTileM) * K) * 4;
   auto kern = dispatch_kernel<T, LN>;
-  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       static_cast<int>(smem));
+  if (e != cudaSuccess) return e;
   // copy slices per routing block: about two blocks per SM in all, one slice per four
   // tokens at most (S = 1 from about 4,700 tokens up)
   unsigned slices = 2u * 148u / (nblk > 0 ? nblk : 1u);
@@ -445,10 +450,10 @@ void dispatch_as(const void* x, const int32_t* topk_idx, const int* excl, const 
   if (slices > groups) slices = groups;
   if (slices > 32) slices = 32;
   if (slices < 1) slices = 1;
-  kern<<<dim3(nblk, slices), 128, smem, s>>>(static_cast<const T*>(x), topk_idx, excl, offs, T_tok, H, E, K,
-                               capacity, slot_of, static_cast<T*>(x_perm), xp_ld, status,
-                               LN ? ln->stats : nullptr, LN ? ln->weight : nullptr,
-                               LN ? ln->bias : nullptr, carry, rb);
+  return launch_kernel(kern, dim3(nblk, slices), dim3(128), smem, s, static_cast<const T*>(x),
+                       topk_idx, excl, offs, T_tok, H, E, K, capacity, slot_of,
+                       static_cast<T*>(x_perm), xp_ld, status, LN ? ln->stats : nullptr,
+                       LN ? ln->weight : nullptr, LN ? ln->bias : nullptr, carry, rb);
 }
 }  // namespace
 
@@ -459,13 +464,11 @@ cudaError_t launch_dispatch(int dtype, const void* x, const int32_t* topk_idx, c
   if (rb < 1 || rb > kTileM) return cudaErrorInvalidValue;
   const DispatchCarry none{nullptr, nullptr, nullptr, 0, 0};
   if (dtype == kF32) {
-    if (ln) dispatch_as<float, true>(x, topk_idx, excl, offs, T, H, E, K, capacity, slot_of, x_perm, xp_ld, status, ln, s, none, rb);
-    else dispatch_as<float, false>(x, topk_idx, excl, offs, T, H, E, K, capacity, slot_of, x_perm, xp_ld, status, ln, s, none, rb);
-  } else {
-    if (ln) dispatch_as<__nv_bfloat16, true>(x, topk_idx, excl, offs, T, H, E, K, capacity, slot_of, x_perm, xp_ld, status, ln, s, none, rb);
-    else dispatch_as<__nv_bfloat16, false>(x, topk_idx, excl, offs, T, H, E, K, capacity, slot_of, x_perm, xp_ld, status, ln, s, none, rb);
+    if (ln) return dispatch_as<float, true>(x, topk_idx, excl, offs, T, H, E, K, capacity, slot_of, x_perm, xp_ld, status, ln, s, none, rb);
+    return dispatch_as<float, false>(x, topk_idx, excl, offs, T, H, E, K, capacity, slot_of, x_perm, xp_ld, status, ln, s, none, rb);
   }
-  return cudaGetLastError();
+  if (ln) return dispatch_as<__nv_bfloat16, true>(x, topk_idx, excl, offs, T, H, E, K, capacity, slot_of, x_perm, xp_ld, status, ln, s, none, rb);
+  return dispatch_as<__nv_bfloat16, false>(x, topk_idx, excl, offs, T, H, E, K, capacity, slot_of, x_perm, xp_ld, status, ln, s, none, rb);
 }
 
 cudaError_t launch_dispatch_carry(int dtype, const void* x, const int32_t* topk_idx,
@@ -475,10 +478,8 @@ cudaError_t launch_dispatch_carry(int dtype, const void* x, const int32_t* topk_
                                   int64_t t0, int64_t slot_base, int* status, cudaStream_t s) {
   const DispatchCarry carry{carry_in, computed, list_out, t0, slot_base};
   if (dtype == kF32)
-    dispatch_as<float, false>(x, topk_idx, excl, offs, T, H, E, K, 0, slot_of, x_perm, xp_ld, status, nullptr, s, carry, kTileM);
-  else
-    dispatch_as<__nv_bfloat16, false>(x, topk_idx, excl, offs, T, H, E, K, 0, slot_of, x_perm, xp_ld, status, nullptr, s, carry, kTileM);
-  return cudaGetLastError();
+    return dispatch_as<float, false>(x, topk_idx, excl, offs, T, H, E, K, 0, slot_of, x_perm, xp_ld, status, nullptr, s, carry, kTileM);
+  return dispatch_as<__nv_bfloat16, false>(x, topk_idx, excl, offs, T, H, E, K, 0, slot_of, x_perm, xp_ld, status, nullptr, s, carry, kTileM);
 }
 
 cudaError_t launch_carry_rows(int dtype, const void* x, int H, int E, int K, const int* list_in,
@@ -506,26 +507,25 @@ cudaError_t launch_combine(int dtype, const void* y, int64_t y_ld, const int32_t
   while (wpt < 8 && T * wpt < 2 * 148 * 8) wpt *= 2;
   const unsigned grid = static_cast<unsigned>((T * wpt + 7) / 8);
   auto go = [&](auto kern, auto* yy, auto* o, auto* r) {
-    kern<<<grid, 256, 0, s>>>(yy, y_ld, topk_idx, topk_w, slot_of, T, H, K, o, r, wpt);
+    return launch_kernel(kern, dim3(grid), dim3(256), 0, s, yy, y_ld, topk_idx, topk_w, slot_of,
+                         T, H, K, o, r, wpt);
   };
   if (dtype == kF32) {
     const float* yy = static_cast<const float*>(y);
     float* o = static_cast<float*>(out);
     const float* r = static_cast<const float*>(resid);
-    if (K <= 2) go(combine_kernel<float, 2>, yy, o, r);
-    else if (K <= 4) go(combine_kernel<float, 4>, yy, o, r);
-    else if (K <= 8) go(combine_kernel<float, 8>, yy, o, r);
-    else go(combine_kernel<float, 32>, yy, o, r);
-  } else {
-    const __nv_bfloat16* yy = static_cast<const __nv_bfloat16*>(y);
-    __nv_bfloat16* o = static_cast<__nv_bfloat16*>(out);
-    const __nv_bfloat16* r = static_cast<const __nv_bfloat16*>(resid);
-    if (K <= 2) go(combine_kernel<__nv_bfloat16, 2>, yy, o, r);
-    else if (K <= 4) go(combine_kernel<__nv_bfloat16, 4>, yy, o, r);
-    else if (K <= 8) go(combine_kernel<__nv_bfloat16, 8>, yy, o, r);
-    else go(combine_kernel<__nv_bfloat16, 32>, yy, o, r);
+    if (K <= 2) return go(combine_kernel<float, 2>, yy, o, r);
+    if (K <= 4) return go(combine_kernel<float, 4>, yy, o, r);
+    if (K <= 8) return go(combine_kernel<float, 8>, yy, o, r);
+    return go(combine_kernel<float, 32>, yy, o, r);
   }
-  return cudaGetLastError();
+  const __nv_bfloat16* yy = static_cast<const __nv_bfloat16*>(y);
+  __nv_bfloat16* o = static_cast<__nv_bfloat16*>(out);
+  const __nv_bfloat16* r = static_cast<const __nv_bfloat16*>(resid);
+  if (K <= 2) return go(combine_kernel<__nv_bfloat16, 2>, yy, o, r);
+  if (K <= 4) return go(combine_kernel<__nv_bfloat16, 4>, yy, o, r);
+  if (K <= 8) return go(combine_kernel<__nv_bfloat16, 8>, yy, o, r);
+  return go(combine_kernel<__nv_bfloat16, 32>, yy, o, r);
 }
 
 }  // namespace vmoe

@@ -126,6 +126,7 @@ decode_gemm_kernel(const __grid_constant__ CUtensorMap a1_map,
                    const __grid_constant__ CUtensorMap b1_map,
                    const __grid_constant__ CUtensorMap a2_map,
                    const __grid_constant__ CUtensorMap b2_map, const DecodeGemmArgs args) {
+  pdl_wait_and_trigger();
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
@@ -418,6 +419,9 @@ cudaError_t launch_decode_gemm(const CUtensorMap& a1_map, const CUtensorMap& b1_
   if (err != cudaSuccess) return err;
   int64_t grid = max_items < num_sms ? max_items : num_sms;
   if (grid < 1) grid = 1;
+  if (!fused)  // programmatic dependent launch when the caller's scope asks for it
+    return launch_kernel(decode_gemm_kernel, dim3(static_cast<unsigned>(grid)), dim3(192), smem,
+                         s, a1_map, b1_map, a2_map, b2_map, args);
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeCooperative;  // a phase-2 item waits for other CTAs' work
@@ -427,10 +431,8 @@ cudaError_t launch_decode_gemm(const CUtensorMap& a1_map, const CUtensorMap& b1_
   cfg.dynamicSmemBytes = smem;
   cfg.stream = s;
   cfg.attrs = attr;
-  cfg.numAttrs = fused ? 1 : 0;
-  err = cudaLaunchKernelEx(&cfg, decode_gemm_kernel, a1_map, b1_map, a2_map, b2_map, args);
-  if (err != cudaSuccess) return err;
-  return cudaGetLastError();
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, decode_gemm_kernel, a1_map, b1_map, a2_map, b2_map, args);
 }
 
 }  // namespace vmoe

@@ -285,6 +285,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_constant_
   constexpr uint32_t TCOLS = LN ? 2 * kLnAccCols : Cfg::TMEM_COLS;
   constexpr uint32_t ACC_COLS = LN ? kLnAccCols : BN;
   static_assert(!LN || BN <= kSumCol, "the LayerNorm router keeps E <= 64 logit columns");
+  pdl_wait_and_trigger();
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
@@ -543,8 +544,7 @@ cudaError_t launch_cfg(const CUtensorMap& a_map, const CUtensorMap& b_map, const
   cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(smem));
   if (err != cudaSuccess) return err;
-  kern<<<grid, tc_threads<EPI>(), smem, s>>>(a_map, b_map, args);
-  return cudaGetLastError();
+  return launch_kernel(kern, dim3(grid), dim3(tc_threads<EPI>()), smem, s, a_map, b_map, args);
 }
 
 PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {

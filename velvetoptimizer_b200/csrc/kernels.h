@@ -10,6 +10,37 @@ namespace vmoe {
 
 enum Dtype { kF32 = 0, kBF16 = 1 };
 
+// ---- programmatic dependent launch ------------------------------------------------------
+// While a PdlScope(true) is alive on the launching thread (a decode-sized forward, whose
+// kernels each fit in one wave), launches through launch_kernel carry
+// cudaLaunchAttributeProgrammaticStreamSerialization: a kernel's launch and the start of its
+// CTAs overlap the end of the kernel before it on the stream.  Every kernel launched so waits
+// for its predecessor (griddepcontrol.wait) before it touches global memory.
+inline thread_local bool g_launch_pdl = false;
+struct PdlScope {
+  bool prev;
+  explicit PdlScope(bool on) : prev(g_launch_pdl) { g_launch_pdl = on; }
+  ~PdlScope() { g_launch_pdl = prev; }
+};
+
+template <typename... KArgs, typename... Args>
+cudaError_t launch_kernel(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                          cudaStream_t s, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  if (g_launch_pdl) {
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+  }
+  return cudaLaunchKernelEx(&cfg, kern, args...);
+}
+
 // Rows per routing block and per grouped-GEMM M tile: every expert segment of the
 // permuted buffer is padded to a multiple of this, so each M tile has one expert.
 constexpr int kTileM = 128;

@@ -144,7 +144,8 @@ struct vmoe_handle {
   // GEMMs read the packed weights through these maps (64-row gate|up boxes, 128-row down)
   CUtensorMap map_wgu_dec{}, map_wd_dec{};
   int decode_max_tokens = 0;  // 0: never
-  bool decode_fused = true;   // both decode GEMMs in one launch
+  bool decode_fused = true;   // both decode GEMMs in one launch (where it pays)
+  bool decode_pdl = true;     // decode forwards' kernels with programmatic dependent launch
   int tile_rows = kTileM;  // GEMM M tile: 256 with CTA-pair GEMMs (bf16), else 128
   bool dense = false;      // a dense FeedForward handle (one expert, no router)
   CUtensorMap map_wr{};   // router weights for the tensor-core router (bf16, E <= 64)

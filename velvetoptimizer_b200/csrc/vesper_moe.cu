@@ -154,6 +154,9 @@ int forward_batch(vmoe_handle* h, const void* x, int64_t T, void* out, float* ro
   cudaEvent_t* ev = prof ? &h->prof_ev[static_cast<size_t>(h->prof_count) * (kStages + 1)] : nullptr;
   int stage = 0;
   NvtxStages nvtx(kNvtxStageNames, kStages);
+  // a decode batch's kernels each fit in one wave: launch them with programmatic dependent
+  // launch, each overlapping the end of the one before (VMOE_PDL=0 at handle creation: off)
+  PdlScope pdl(use_decode_gemms(h, T) && h->decode_pdl);
   auto mark = [&]() {
     if (prof) cudaEventRecord(ev[stage], s);
     nvtx.next(stage);
@@ -379,6 +382,7 @@ int vmoe_create(const vmoe_config* cfg, int device, vmoe_handle** out) {
     // VMOE_DECODE_MAX_TOKENS lowers it (0: never)
     h->decode_max_tokens = kDecodeMaxTokens;
     if (const char* f = getenv("VMOE_DECODE_FUSED")) h->decode_fused = f[0] != '0';
+    if (const char* f = getenv("VMOE_PDL")) h->decode_pdl = f[0] != '0';
     if (const char* d = getenv("VMOE_DECODE_MAX_TOKENS")) {
       const long v = strtol(d, nullptr, 10);
       h->decode_max_tokens = v < 0 ? 0 : (v > kDecodeMaxTokens ? kDecodeMaxTokens : static_cast<int>(v));
