@@ -143,3 +143,25 @@ def test_decode_one_launch_equals_two(name, monkeypatch):
         assert n_fused == n_split - (1 if one_launch else 0), (n_fused, n_split)
     fused.close()
     split.close()
+
+
+@pytest.mark.parametrize("name", ["t64_e8k2_bias", "t64_e64k8_lora_zipf", "t256_all_rows"])
+def test_decode_folded_plan_equals_plan_kernels(name, monkeypatch):
+    """The decode forward derives the expert offsets, counts and aux loss inside its
+    dispatch from the router's histograms; with the scan and plan kernels instead
+    (VMOE_FOLD_PLAN=0) every output is the same to the bit and two more kernels launch."""
+    case = DECODE_CASES[name]
+    inp = bf16_inputs(make_inputs(case))
+    folded = AbiLayer(case, inp, "bf16")
+    monkeypatch.setenv("VMOE_FOLD_PLAN", "0")
+    kernels = AbiLayer(case, inp, "bf16")
+    monkeypatch.delenv("VMOE_FOLD_PLAN")
+    for _ in range(2):
+        a, b = folded.run(inp["x"]), kernels.run(inp["x"])
+        for key in ("out", "logits", "topk_idx", "topk_w", "counts", "aux"):
+            assert np.array_equal(a[key], b[key]), key
+        check_dispatch(folded, case.tokens, a, a["topk_idx"])
+        n_a, n_b = folded.handle.last_launch_count(), kernels.handle.last_launch_count()
+        assert n_a == n_b - 2, (n_a, n_b)
+    folded.close()
+    kernels.close()

@@ -435,3 +435,30 @@ def test_ffn_bf16_writes_only_its_rows():
     got = out[:T].float().cpu().numpy()
     assert O.norm_rel_err(got, O.ffn_forward(inp, case)) < BF16_TOL
     h.close()
+
+
+def test_banded_tile_order_is_bit_identical(monkeypatch):
+    """The pair GEMMs may take each expert's output tiles in bands of n tiles (every m tile
+    of the expert per band) instead of row-major; each tile is computed the same way in
+    either order, so the outputs are the same to the bit.  Bands of 3 of the gate|up GEMM's
+    8 n tiles leave a narrower last band; Zipf routing gives the experts runs of different
+    lengths."""
+    case = MoECase(tokens=2048, hidden=512, inter=1024, experts=4, top_k=2, zipf_alpha=1.2,
+                   seed=61)
+    inp = bf16_inputs(make_inputs(case))
+    monkeypatch.setenv("VMOE_GEMM1_BAND", "0")
+    monkeypatch.setenv("VMOE_GEMM2_BAND", "0")
+    rowmajor = AbiLayer(case, inp, "bf16")
+    monkeypatch.setenv("VMOE_GEMM1_BAND", "3")
+    monkeypatch.setenv("VMOE_GEMM2_BAND", "1")
+    banded = AbiLayer(case, inp, "bf16")
+    monkeypatch.delenv("VMOE_GEMM1_BAND")
+    monkeypatch.delenv("VMOE_GEMM2_BAND")
+    assert rowmajor.handle.lib.vmoe_segment_align(rowmajor.handle.ptr, case.tokens) == 256
+    a, b = rowmajor.run(inp["x"]), banded.run(inp["x"])
+    assert np.array_equal(a["out"], b["out"])
+    assert a["aux"] == b["aux"]
+    forced = O.moe_forward(inp, case, force_idx=a["topk_idx"])
+    assert O.norm_rel_err(b["out"], forced["out"]) < 2e-2
+    rowmajor.close()
+    banded.close()

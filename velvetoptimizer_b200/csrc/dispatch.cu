@@ -19,6 +19,28 @@
 namespace vmoe {
 namespace {
 
+// Fixed-shape warp sum (xor butterfly): the scan's per-warp partial probability sums.
+__device__ __forceinline__ float warp_sum_fixed(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// Switch load-balancing loss (model.py:366-385) from the per-expert counts and probability
+// sums, summed in ascending expert order.
+__device__ __forceinline__ float aux_loss_of(const int* counts, const float* psum_tot, int64_t T,
+                                             int E, int K) {
+  const float inv_tk = 1.0f / static_cast<float>(T * K);
+  const float inv_t = 1.0f / static_cast<float>(T);
+  float s = 0.f;
+  for (int e = 0; e < E; ++e) {
+    const float f = static_cast<float>(counts[e]) * inv_tk;
+    const float p = psum_tot[e] * inv_t;
+    s += f * p;
+  }
+  return static_cast<float>(E) * s;
+}
+
 // ---- 1. per-expert exclusive scan over routing blocks --------------------------------
 // grid = E, block = 256: column e of hist[nblk][E] -> excl[nblk][E], counts[e]; column
 // sums of psum in a fixed order.
@@ -45,9 +67,7 @@ scan_blocks_kernel(const int* __restrict__ hist, const float* __restrict__ psum,
     if (lane >= o) inc += n;
   }
   // fixed-shape tree for the float sum
-  float fs = ps;
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) fs += __shfl_xor_sync(0xffffffffu, fs, o);
+  const float fs = warp_sum_fixed(ps);
   if (lane == 31) wsum[warp] = inc;
   if (lane == 0) wps[warp] = fs;
   __syncthreads();
@@ -90,16 +110,7 @@ plan_kernel(const int* __restrict__ counts, const float* __restrict__ psum_tot, 
     for (int e = 0; e < E; ++e) { off_s[e] = run; run += pad_s[e]; }
     off_s[E] = run;
     if (num_tiles) *num_tiles = run / row_align;
-    // Switch load-balancing loss (model.py:366-385), fixed summation order
-    const float inv_tk = 1.0f / static_cast<float>(T * K);
-    const float inv_t = 1.0f / static_cast<float>(T);
-    float s = 0.f;
-    for (int e = 0; e < E; ++e) {
-      const float f = static_cast<float>(counts[e]) * inv_tk;
-      const float p = psum_tot[e] * inv_t;
-      s += f * p;
-    }
-    if (aux) *aux = static_cast<float>(E) * s;
+    if (aux) *aux = aux_loss_of(counts, psum_tot, T, E, K);
   }
   __syncthreads();
   for (int e = tid; e <= E; e += blockDim.x) offs[e] = off_s[e];
@@ -172,7 +183,7 @@ dispatch_kernel(const T* __restrict__ x, const int32_t* __restrict__ topk_idx,
                 int E, int K, int64_t capacity, int* __restrict__ slot_of, T* __restrict__ x_perm,
                 int64_t xp_ld, int* status, const float2* __restrict__ ln_stats,
                 const float* __restrict__ ln_w, const float* __restrict__ ln_b,
-                const DispatchCarry carry, int rb) {
+                const DispatchCarry carry, int rb, const DispatchPlan plan) {
   pdl_wait_and_trigger();
   extern __shared__ uint32_t dsm[];
   uint32_t* masks = dsm;                            // [4 warps][E] token bitmasks
@@ -184,6 +195,54 @@ dispatch_kernel(const T* __restrict__ x, const int32_t* __restrict__ topk_idx,
   const bool valid = tid < rb && t < T_tok;
 
   for (int i = tid; i < 4 * E; i += 128) masks[i] = 0u;
+  const int* excl_row = plan.hist ? nullptr : excl + blk * E;  // this block's prefixes [E]
+  if (plan.hist) {
+    // the scan and the plan of a decode-sized batch, in every CTA: this routing block's
+    // prefixes and the expert offsets from the router's histograms (the same sums as the
+    // scan and plan kernels); the first CTA also writes the plan's outputs
+    int* excl_s = slots + kTileM * K;  // [E]
+    int* offs_s = excl_s + E;          // [E + 1]
+    int* cnt_s = offs_s + E + 1;       // [E]
+    int* pad_s = cnt_s + E;            // [E]
+    float* ptot_s = reinterpret_cast<float*>(pad_s + E);  // [E]
+    const int nblk = static_cast<int>(gridDim.x);
+    const bool first = blockIdx.x == 0 && blockIdx.y == 0;
+    for (int e = tid; e < E; e += 128) {
+      int run = 0, mine = 0;
+      for (int b = 0; b < nblk; ++b) {
+        if (b == blk) mine = run;
+        run += plan.hist[static_cast<int64_t>(b) * E + e];
+      }
+      excl_s[e] = mine;
+      cnt_s[e] = run;
+      const int kept = capacity > 0 && run > capacity ? static_cast<int>(capacity) : run;
+      pad_s[e] = (kept + plan.row_align - 1) / plan.row_align * plan.row_align;
+    }
+    if (first) {  // probability sums: lane b holds block b's (nblk <= 32), fixed tree
+      for (int e = warp; e < E; e += 4) {
+        const float v = lane < nblk ? plan.psum[static_cast<int64_t>(lane) * E + e] : 0.f;
+        const float tot = warp_sum_fixed(v);
+        if (lane == 0) ptot_s[e] = tot;
+      }
+    }
+    __syncthreads();
+    if (tid == 0) {
+      int run = 0;
+      for (int e = 0; e < E; ++e) { offs_s[e] = run; run += pad_s[e]; }
+      offs_s[E] = run;
+      if (first && plan.aux) *plan.aux = aux_loss_of(cnt_s, ptot_s, T_tok, E, K);
+    }
+    __syncthreads();
+    if (first) {
+      for (int e = tid; e <= E; e += 128) plan.offs_out[e] = offs_s[e];
+      if (plan.counts_out)
+        for (int e = tid; e < E; e += 128) plan.counts_out[e] = cnt_s[e];
+      if (plan.zero)
+        for (int i = tid; i < plan.zero_n; i += 128) plan.zero[i] = 0;
+    }
+    excl_row = excl_s;
+    offs = offs_s;
+  }
   __syncthreads();
   if (valid) {
     for (int k = 0; k < K; ++k) {
@@ -202,7 +261,7 @@ dispatch_kernel(const T* __restrict__ x, const int32_t* __restrict__ topk_idx,
     int slot = -1;  // row of x_perm (relative to x_perm)
     if (valid) {
       const int e = topk_idx[t * K + k];
-      const int rank = excl[blk * E + e] + wbase[warp * E + e] + __popc(masks[warp * E + e] & lt);
+      const int rank = excl_row[e] + wbase[warp * E + e] + __popc(masks[warp * E + e] & lt);
       if (carry.computed) {
         const int pos = carry.carry_in[e] + rank;  // position in the segment
         const int over = pos - carry.computed[e];
@@ -435,10 +494,14 @@ template <typename T, bool LN>
 cudaError_t dispatch_as(const void* x, const int32_t* topk_idx, const int* excl, const int* offs,
                  int64_t T_tok, int H, int E, int K, int64_t capacity, int* slot_of, void* x_perm,
                  int64_t xp_ld, int* status, const LnArgs* ln, cudaStream_t s,
-                 const DispatchCarry& carry, int rb) {
+                 const DispatchCarry& carry, int rb, const DispatchPlan& plan) {
   const unsigned nblk = static_cast<unsigned>((T_tok + rb - 1) / rb);
   if (nblk == 0) return cudaSuccess;  // no tokens: nothing to place
-  const size_t smem = (8 * static_cast<size_t>(E) + static_cast<size_t>(kTileM) * K) * 4;
+  if (plan.hist && (nblk > 32 || E > 1024 || carry.computed || !plan.psum || !plan.offs_out ||
+                    plan.row_align < 1))
+    return cudaErrorInvalidValue;
+  const size_t smem = (8 * static_cast<size_t>(E) + static_cast<size_t>(kTileM) * K +
+                       (plan.hist ? 5 * static_cast<size_t>(E) + 1 : 0)) * 4;
   auto kern = dispatch_kernel<T, LN>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        static_cast<int>(smem));
@@ -453,22 +516,23 @@ cudaError_t dispatch_as(const void* x, const int32_t* topk_idx, const int* excl,
   return launch_kernel(kern, dim3(nblk, slices), dim3(128), smem, s, static_cast<const T*>(x),
                        topk_idx, excl, offs, T_tok, H, E, K, capacity, slot_of,
                        static_cast<T*>(x_perm), xp_ld, status, LN ? ln->stats : nullptr,
-                       LN ? ln->weight : nullptr, LN ? ln->bias : nullptr, carry, rb);
+                       LN ? ln->weight : nullptr, LN ? ln->bias : nullptr, carry, rb, plan);
 }
 }  // namespace
 
 cudaError_t launch_dispatch(int dtype, const void* x, const int32_t* topk_idx, const int* excl,
                             const int* offs, int64_t T, int H, int E, int K, int64_t capacity,
                             int* slot_of, void* x_perm, int64_t xp_ld, int* status,
-                            const LnArgs* ln, cudaStream_t s, int rb) {
+                            const LnArgs* ln, cudaStream_t s, int rb, const DispatchPlan* plan) {
   if (rb < 1 || rb > kTileM) return cudaErrorInvalidValue;
   const DispatchCarry none{nullptr, nullptr, nullptr, 0, 0};
+  const DispatchPlan p = plan ? *plan : DispatchPlan{};
   if (dtype == kF32) {
-    if (ln) return dispatch_as<float, true>(x, topk_idx, excl, offs, T, H, E, K, capacity, slot_of, x_perm, xp_ld, status, ln, s, none, rb);
-    return dispatch_as<float, false>(x, topk_idx, excl, offs, T, H, E, K, capacity, slot_of, x_perm, xp_ld, status, ln, s, none, rb);
+    if (ln) return dispatch_as<float, true>(x, topk_idx, excl, offs, T, H, E, K, capacity, slot_of, x_perm, xp_ld, status, ln, s, none, rb, p);
+    return dispatch_as<float, false>(x, topk_idx, excl, offs, T, H, E, K, capacity, slot_of, x_perm, xp_ld, status, ln, s, none, rb, p);
   }
-  if (ln) return dispatch_as<__nv_bfloat16, true>(x, topk_idx, excl, offs, T, H, E, K, capacity, slot_of, x_perm, xp_ld, status, ln, s, none, rb);
-  return dispatch_as<__nv_bfloat16, false>(x, topk_idx, excl, offs, T, H, E, K, capacity, slot_of, x_perm, xp_ld, status, ln, s, none, rb);
+  if (ln) return dispatch_as<__nv_bfloat16, true>(x, topk_idx, excl, offs, T, H, E, K, capacity, slot_of, x_perm, xp_ld, status, ln, s, none, rb, p);
+  return dispatch_as<__nv_bfloat16, false>(x, topk_idx, excl, offs, T, H, E, K, capacity, slot_of, x_perm, xp_ld, status, ln, s, none, rb, p);
 }
 
 cudaError_t launch_dispatch_carry(int dtype, const void* x, const int32_t* topk_idx,
@@ -477,9 +541,10 @@ cudaError_t launch_dispatch_carry(int dtype, const void* x, const int32_t* topk_
                                   const int* carry_in, const int* computed, int* list_out,
                                   int64_t t0, int64_t slot_base, int* status, cudaStream_t s) {
   const DispatchCarry carry{carry_in, computed, list_out, t0, slot_base};
+  const DispatchPlan none{};
   if (dtype == kF32)
-    return dispatch_as<float, false>(x, topk_idx, excl, offs, T, H, E, K, 0, slot_of, x_perm, xp_ld, status, nullptr, s, carry, kTileM);
-  return dispatch_as<__nv_bfloat16, false>(x, topk_idx, excl, offs, T, H, E, K, 0, slot_of, x_perm, xp_ld, status, nullptr, s, carry, kTileM);
+    return dispatch_as<float, false>(x, topk_idx, excl, offs, T, H, E, K, 0, slot_of, x_perm, xp_ld, status, nullptr, s, carry, kTileM, none);
+  return dispatch_as<__nv_bfloat16, false>(x, topk_idx, excl, offs, T, H, E, K, 0, slot_of, x_perm, xp_ld, status, nullptr, s, carry, kTileM, none);
 }
 
 cudaError_t launch_carry_rows(int dtype, const void* x, int H, int E, int K, const int* list_in,

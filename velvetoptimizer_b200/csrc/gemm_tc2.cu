@@ -66,6 +66,48 @@ __device__ __forceinline__ int pair_expert_of(const TcGemmArgs& args, int m) {
 
 enum PairEpi { kPairPlain = 0, kPairGated = 1, kPairGluBwd = 2, kPairPush = 3 };
 
+// Tile index -> (m tile, n tile).  Row-major over (m, n) unless args.band_n = b > 0: then
+// each expert's tiles (its m tiles form one run of tile_expert, written contiguously by the
+// plan) are taken in bands of b n tiles, every m tile of the expert for band 0, then band 1,
+// ...: a wave of consecutive tiles shares a few A tiles and b B tiles, and the expert's A and
+// the band's B stay in L2 while the band lasts.  Either order is a permutation of the same
+// tiles inside each expert's range of tile indices.  A CTA's tiles ascend, so the run bounds
+// are found by a short scan only when the CTA moves to another expert's run.
+struct TileOrder {
+  int m0 = 0, m1 = 0;  // the current expert run [m0, m1) of m tiles
+  __device__ __forceinline__ void coords(const TcGemmArgs& args, int num_m, int n_tiles,
+                                         int tile, int& m, int& n) {
+    const int mt = tile / n_tiles;
+    const int nb = args.band_n;
+    if (nb <= 0 || nb >= n_tiles || !args.tile_expert) {
+      m = mt;
+      n = tile - mt * n_tiles;
+      return;
+    }
+    if (mt < m0 || mt >= m1) {
+      const int e = args.tile_expert[mt];
+      m0 = mt;
+      while (m0 > 0 && args.tile_expert[m0 - 1] == e) --m0;
+      m1 = mt + 1;
+      while (m1 < num_m && args.tile_expert[m1] == e) ++m1;
+    }
+    const int cnt = m1 - m0;
+    const int l = tile - m0 * n_tiles;  // 0 .. cnt * n_tiles - 1
+    const int full = n_tiles / nb;      // whole bands; then one band of the rest
+    const int band = l / (cnt * nb);
+    if (band < full) {
+      const int r = l - band * cnt * nb;
+      m = m0 + r / nb;
+      n = band * nb + r % nb;
+    } else {
+      const int w = n_tiles - full * nb;
+      const int r = l - full * cnt * nb;
+      m = m0 + r / w;
+      n = full * nb + r % w;
+    }
+  }
+};
+
 // push epilogue staging: per epilogue warp 32 rows x 64 bf16 columns, 144-byte row pitch
 constexpr int PUSH_PITCH = 72;  // elements
 constexpr uint32_t PUSH_STG_BYTES = 4 * 32 * PUSH_PITCH * 2;
@@ -136,8 +178,10 @@ tc_gemm_pair_kernel(const __grid_constant__ CUtensorMap a_map,
     // ---------------- TMA producer (both CTAs) ----------------
     if (lane == 0) {
       int it = 0;
+      TileOrder order;
       for (int tile = pair; tile < total; tile += num_pairs) {
-        const int m = tile / n_tiles, n = tile - m * n_tiles;
+        int m, n;
+        order.coords(args, num_m, n_tiles, tile, m, n);
         const int e = pair_expert_of(args, m);
         const int a_row = m * PAIR_M + static_cast<int>(rank) * kTileM;
         const int b_row = e * args.b_rows_per_expert + n * BN + static_cast<int>(rank) * (BN / 2);
@@ -203,6 +247,7 @@ tc_gemm_pair_kernel(const __grid_constant__ CUtensorMap a_map,
     const int q = warp & 3;                     // TMEM lane quarter this warp may access
     const int part = (warp - 2) >> 2;           // which share of the columns (GLU backward)
     int local = 0;
+    TileOrder order;
     for (int tile = pair; tile < total; tile += num_pairs, ++local) {
       const int acc = local & 1;
       const uint32_t aph = (local >> 1) & 1;
@@ -213,7 +258,8 @@ tc_gemm_pair_kernel(const __grid_constant__ CUtensorMap a_map,
         break;
       }
       tc_fence_after();
-      const int m = tile / n_tiles, n = tile - m * n_tiles;
+      int m, n;
+      order.coords(args, num_m, n_tiles, tile, m, n);
       const int e = pair_expert_of(args, m);
       const int64_t row = static_cast<int64_t>(m) * PAIR_M + rank * kTileM + q * 32 + lane;
       const uint32_t t_row = tmem + (static_cast<uint32_t>(q * 32) << 16) + acc * BN;

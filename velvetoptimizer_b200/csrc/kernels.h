@@ -109,13 +109,30 @@ cudaError_t launch_aux_merge_ws(const void* ws, size_t stride, size_t counts_off
 // Tile map of a dense layer: n tiles, all expert 0.
 cudaError_t launch_fill_tiles(int* tile_expert, int n, int* num_tiles, cudaStream_t s);
 
+// The scan and plan of a batch of at most 32 routing blocks, folded into its dispatch:
+// every dispatch CTA derives its block's prefixes and the expert offsets (segments padded to
+// row_align rows) from the router's histograms, with the same sums as launch_scan_blocks and
+// launch_plan; the first CTA writes offs_out [E + 1], the caller's counts, the aux loss and
+// zero_n zeros at `zero`.  No tile map is written.
+struct DispatchPlan {
+  const int* hist;      // [nblk][E]; null: excl and offs come from the scan and plan kernels
+  const float* psum;    // [nblk][E]
+  int row_align;
+  int* offs_out;
+  int32_t* counts_out;  // nullable
+  float* aux;           // nullable
+  int* zero;            // nullable
+  int zero_n;
+};
+
 // Stable expert-major slots for every (token, k) and the row gather x -> x_perm (with
 // `ln`: LayerNorm(x) rows, normalised on the way, rounded to the dtype).  `block_tokens`
 // (<= 128) is the routing block the router's histograms and the scan's prefixes use.
 cudaError_t launch_dispatch(int dtype, const void* x, const int32_t* topk_idx, const int* excl,
                             const int* offs, int64_t T, int H, int E, int K, int64_t capacity,
                             int* slot_of, void* x_perm, int64_t xp_ld, int* status,
-                            const LnArgs* ln, cudaStream_t s, int block_tokens = kTileM);
+                            const LnArgs* ln, cudaStream_t s, int block_tokens = kTileM,
+                            const DispatchPlan* plan = nullptr);
 
 // out[t] = sum over the token's experts in ascending id of w * y[slot]  (fp32 sum); with
 // `resid`, out[t] = resid[t] + that sum rounded to the dtype (the residual add of the
@@ -153,6 +170,9 @@ struct TcGemmArgs {
   int* hist;                // [ceil(T/128), E]
   float* psum;              // [ceil(T/128), E]
   int n_tiles;              // output tiles per expert along N
+  // pair GEMM tile order: 0 = row-major over (m, n); b > 0 = each expert's n tiles in bands
+  // of b, every m tile of the expert per band (its band of B stays in L2 across the band)
+  int band_n;
   int k_blocks;             // ceil(K / 64)
   int b_rows_per_expert;    // rows of the 2-D weight view per expert
   void* out;                // bf16 output

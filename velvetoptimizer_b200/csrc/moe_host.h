@@ -146,6 +146,10 @@ struct vmoe_handle {
   int decode_max_tokens = 0;  // 0: never
   bool decode_fused = true;   // both decode GEMMs in one launch (where it pays)
   bool decode_pdl = true;     // decode forwards' kernels with programmatic dependent launch
+  bool decode_fold_plan = true;  // decode forwards: scan and plan inside the dispatch
+  int l2_bytes = 0;           // the device's L2 size
+  // pair GEMM tile order (TcGemmArgs::band_n): -1 = chosen from the weight sizes
+  int gemm1_band = -1, gemm2_band = -1;
   int tile_rows = kTileM;  // GEMM M tile: 256 with CTA-pair GEMMs (bf16), else 128
   bool dense = false;      // a dense FeedForward handle (one expert, no router)
   CUtensorMap map_wr{};   // router weights for the tensor-core router (bf16, E <= 64)
@@ -206,6 +210,16 @@ int alloc_once(vmoe_handle* h, T** p, size_t bytes, const char* what) {
 }
 
 
+// Pair GEMM tile order for expert weights (B) of b_bytes per expert: bands of 8 n tiles
+// once an expert's B is too large to stay in L2 beside the A tiles and outputs streaming
+// through it, row-major otherwise (measured on the gate|up GEMM: 3.55 -> 3.32 ms with 64 MB
+// of B per expert, 6.62 -> 7.61 ms with 32 MB, so the switch sits between the two);
+// forced >= 0 (VMOE_GEMM1_BAND / VMOE_GEMM2_BAND at handle creation) overrides.
+inline int gemm_band(const vmoe_handle* h, int forced, int64_t b_bytes) {
+  if (forced >= 0) return forced;
+  return b_bytes > static_cast<int64_t>(h->l2_bytes) * 2 / 5 ? 8 : 0;
+}
+
 // gate|up GEMM (+ ERA * up) then down GEMM over an expert-major buffer of `max_rows`
 // rows (a multiple of 128) whose M tiles map to experts through tiles / ntiles.
 template <typename Mark, typename Check>
@@ -255,6 +269,7 @@ int run_expert_gemms(vmoe_handle* h, void* xp, int64_t max_rows, const int* tile
   a1.gu_out = gu_out;  // training: keep the pre-activations for the backward
   a1.gu_ld = 2 * h->Ipad;
   const bool pair = h->tile_rows != kTileM;
+  a1.band_n = pair ? gemm_band(h, h->gemm1_band, 2 * h->Ipad * H * 2) : 0;
   if ((rc = check(pair ? launch_tc_gemm_pair(true, map_x, h->map_wgu, a1, max_tiles, sms, s)
                        : launch_tc_gemm(true, map_x, h->map_wgu, a1, max_tiles, sms, s),
                   "gemm1")) != VMOE_OK)
@@ -275,6 +290,7 @@ int run_expert_gemms(vmoe_handle* h, void* xp, int64_t max_rows, const int* tile
   a2.gamma = 0.f;
   a2.status = h->status;
   a2.row_limit = out_rows;  // rows past the caller's output are computed but not stored
+  a2.band_n = pair ? gemm_band(h, h->gemm2_band, h->Hpad * h->Ipad * 2) : 0;
   if (push) {  // outputs straight into the source ranks' return buffers over NVLink
     a2.push_ret = reinterpret_cast<const int64_t*>(push->peer_base_local + push->ret_off);
     a2.push_peers = push->peer_base;

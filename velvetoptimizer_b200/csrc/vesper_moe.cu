@@ -168,28 +168,33 @@ int forward_batch(vmoe_handle* h, const void* x, int64_t T, void* out, float* ro
     return VMOE_OK;
   };
   int rc;
+  // decode-sized batches: segments padded to 16 rows for the swapped-operand GEMMs, which
+  // need no tile map, and the scan and plan run inside the dispatch (two launches fewer)
+  const bool decode = use_decode_gemms(h, T);
+  const bool fold_plan = decode && h->decode_fold_plan && p.nblk <= 32 && !psum_tot_out;
   mark();
   if ((rc = run_router(h, x, T, router_logits, idx, tw, hist, psum, ln, s, p.rb)) != VMOE_OK)
     return rc;
   mark();
-  if ((rc = check(launch_scan_blocks(hist, psum, p.nblk, static_cast<int>(E), excl, counts,
+  if (!fold_plan &&
+      (rc = check(launch_scan_blocks(hist, psum, p.nblk, static_cast<int>(E), excl, counts,
                                      psum_tot, s),
                   "scan")) != VMOE_OK)
     return rc;
   mark();
-  // decode-sized batches: segments padded to 16 rows for the swapped-operand GEMMs, which
-  // need no tile map
-  const bool decode = use_decode_gemms(h, T);
-  if ((rc = check(launch_plan(counts, psum_tot, T, static_cast<int>(E), static_cast<int>(K),
+  if (!fold_plan &&
+      (rc = check(launch_plan(counts, psum_tot, T, static_cast<int>(E), static_cast<int>(K),
                               h->cfg.capacity, segment_align(h, T), offs,
                               decode ? nullptr : tiles, decode ? nullptr : ntiles, aux,
                               expert_counts, s, decode ? ready : nullptr),
                   "plan")) != VMOE_OK)
     return rc;
   mark();
+  const DispatchPlan folded{hist, psum, segment_align(h, T), offs, expert_counts, aux, ready,
+                            static_cast<int>(E)};
   if ((rc = check(launch_dispatch(h->dtype, x, idx, excl, offs, T, static_cast<int>(H),
                                   static_cast<int>(E), static_cast<int>(K), h->cfg.capacity, slot,
-                                  xp, H, h->status, ln, s, p.rb),
+                                  xp, H, h->status, ln, s, p.rb, fold_plan ? &folded : nullptr),
                   "dispatch")) != VMOE_OK)
     return rc;
   mark();
@@ -383,6 +388,9 @@ int vmoe_create(const vmoe_config* cfg, int device, vmoe_handle** out) {
     h->decode_max_tokens = kDecodeMaxTokens;
     if (const char* f = getenv("VMOE_DECODE_FUSED")) h->decode_fused = f[0] != '0';
     if (const char* f = getenv("VMOE_PDL")) h->decode_pdl = f[0] != '0';
+    if (const char* f = getenv("VMOE_FOLD_PLAN")) h->decode_fold_plan = f[0] != '0';
+    if (const char* f = getenv("VMOE_GEMM1_BAND")) h->gemm1_band = static_cast<int>(strtol(f, nullptr, 10));
+    if (const char* f = getenv("VMOE_GEMM2_BAND")) h->gemm2_band = static_cast<int>(strtol(f, nullptr, 10));
     if (const char* d = getenv("VMOE_DECODE_MAX_TOKENS")) {
       const long v = strtol(d, nullptr, 10);
       h->decode_max_tokens = v < 0 ? 0 : (v > kDecodeMaxTokens ? kDecodeMaxTokens : static_cast<int>(v));
@@ -393,6 +401,7 @@ int vmoe_create(const vmoe_config* cfg, int device, vmoe_handle** out) {
   }
   DeviceGuard g(device);
   cudaDeviceGetAttribute(&h->num_sms, cudaDevAttrMultiProcessorCount, device);
+  cudaDeviceGetAttribute(&h->l2_bytes, cudaDevAttrL2CacheSize, device);
   if (h->dtype == kBF16) {
     int major = 0, minor = 0;
     cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, device);
