@@ -83,6 +83,10 @@ BF16_CASES = {
     "tc_e64k2_lora": MoECase(tokens=700, hidden=512, inter=256, experts=64, top_k=2,
                              lora_on=True, seed=42),
     "tc_e8k2_h1024": MoECase(tokens=300, hidden=1024, inter=512, experts=8, top_k=2, seed=43),
+    # decode-sized batches: routing blocks of 16 / 32 tokens copied by all the router's threads
+    "tc_e8k2_decode48": MoECase(tokens=48, hidden=512, inter=256, experts=8, top_k=2, seed=45),
+    "tc_e16k4_decode200": MoECase(tokens=200, hidden=256, inter=384, experts=16, top_k=4,
+                                  seed=46),
     # CUDA-core router (E > 64) on bf16 inputs
     "simt_e80k2": MoECase(tokens=333, hidden=256, inter=256, experts=80, top_k=2, seed=44),
 }
