@@ -275,6 +275,24 @@ def test_module_fp32_matches_reference_c1():
 
 
 @torch.no_grad()
+def test_module_eager_call_equals_registered_op():
+    """In eager mode the module runs the custom op's body directly; calling the registered op
+    (the path a tracer takes) gives the same bits."""
+    case = BF16_CASES["lora_zipf_e32k8"]
+    inp = make_inputs(case)
+    m = _load_module(case, inp, torch.bfloat16)
+    x = torch.from_numpy(inp["x"]).reshape(1, case.tokens, case.hidden).cuda().to(torch.bfloat16)
+    out, aux, logits = m(x, return_router_logits=True)
+    packed = m.packed_for(x.device, x.dtype)
+    out2, logits2, aux2 = torch.ops.vesper_moe.forward(x.reshape(case.tokens, case.hidden),
+                                                        packed.id, True)
+    assert torch.equal(out.reshape(case.tokens, case.hidden), out2)
+    assert torch.equal(logits.reshape(case.tokens, case.experts), logits2)
+    assert torch.equal(aux, aux2)
+    m.close()
+
+
+@torch.no_grad()
 def test_module_bf16_lora_matches_oracle():
     case = BF16_CASES["lora_zipf_e32k8"]
     inp = make_inputs(case)

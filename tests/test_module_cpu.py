@@ -4,6 +4,7 @@ Every forward compares a key of (data pointer, version) per parameter with the k
 packed weights were built from.  The parameter list behind the key is cached; these tests
 pin that every way of changing a weight still changes the key.
 """
+import pytest
 import torch
 import torch.nn as nn
 
@@ -157,3 +158,24 @@ def test_hooks_installed_by_the_first_layer_not_at_import():
     repo = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
     r = subprocess.run([sys.executable, "-c", code], cwd=repo, capture_output=True, text=True)
     assert r.returncode == 0, r.stderr
+
+
+def test_native_pairs_match_the_parameters():
+    """The native helper returns every parameter's (data pointer, version), 16 bytes each,
+    and the key moves with an in-place write."""
+    import struct
+
+    from velvetoptimizer_b200 import moe
+    if moe._native_pairs is None:
+        pytest.skip("the host helper is not built")
+    layer = small_layer()
+    plist = layer._param_list()
+    raw = moe._native_pairs(plist)
+    vals = struct.unpack(f"{2 * len(plist)}Q", raw)
+    assert all(vals[2 * i] == p.data_ptr() and vals[2 * i + 1] == p._version
+               for i, p in enumerate(plist))
+    with torch.no_grad():
+        plist[-1].add_(1.0)
+    assert moe._native_pairs(plist) != raw
+    with pytest.raises(TypeError):
+        moe._native_pairs([1, 2])

@@ -65,8 +65,42 @@ def _compile(src: str, verbose: bool, extra: list[str]) -> str:
     return obj
 
 
+PARAM_KEY_SRC = os.path.join(PKG, "csrc_py", "param_key.cpp")
+PARAM_KEY_LIB = os.path.join(LIB_DIR, "_param_key.so")
+
+
+def build_param_key(force: bool = False, verbose: bool = False) -> str:
+    """The modules' host helper (csrc_py/param_key.cpp, a CPython extension against torch's
+    headers): g++ only, no GPU code.  Skips work when up to date."""
+    if (not force and os.path.exists(PARAM_KEY_LIB)
+            and os.path.getmtime(PARAM_KEY_SRC) <= os.path.getmtime(PARAM_KEY_LIB)):
+        return PARAM_KEY_LIB
+    import sysconfig
+
+    import torch
+    tdir = os.path.dirname(torch.__file__)
+    abi = int(getattr(torch._C, "_GLIBCXX_USE_CXX11_ABI", True))
+    cmd = [os.environ.get("CXX", "g++"), "-O2", "-std=c++17", "-fPIC", "-shared",
+           f"-D_GLIBCXX_USE_CXX11_ABI={abi}", "-I", sysconfig.get_paths()["include"],
+           "-I", os.path.join(tdir, "include"),
+           "-I", os.path.join(tdir, "include", "torch", "csrc", "api", "include"),
+           PARAM_KEY_SRC, "-o", PARAM_KEY_LIB + ".tmp", "-L", os.path.join(tdir, "lib"),
+           "-lc10", "-ltorch", "-ltorch_cpu", "-ltorch_python",
+           f"-Wl,-rpath,{os.path.join(tdir, 'lib')}"]
+    os.makedirs(LIB_DIR, exist_ok=True)
+    if verbose:
+        print(" ".join(cmd), flush=True)
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    if r.returncode != 0:
+        raise RuntimeError(f"param_key build failed:\n{r.stdout}\n{r.stderr}")
+    os.replace(PARAM_KEY_LIB + ".tmp", PARAM_KEY_LIB)
+    return PARAM_KEY_LIB
+
+
 def build(force: bool = False, verbose: bool = False, extra: list[str] | None = None) -> str:
-    """Compile and link the library; returns its path.  Skips work when up to date."""
+    """Compile and link the library (and the modules' host helper); returns the library's
+    path.  Skips work when up to date."""
+    build_param_key(force=force, verbose=verbose)
     if not force and not extra and up_to_date():
         return LIB
     os.makedirs(BUILD, exist_ok=True)
