@@ -83,7 +83,10 @@ __global__ void p2p_signal_kernel(P2PArgs a, int which) {
   if (threadIdx.x < a.G) st_release_sys(sig_ptr(a, threadIdx.x, which, a.me), a.epoch);
 }
 
-// grid = max(1, nblk) blocks of 128 threads (one thread per token of a 128-token block)
+// grid = (max(1, nblk), S) blocks of 128 threads (one thread per token of a 128-token
+// block): the S blocks of a routing block all derive its rows (cheap) and each copies every
+// S-th group of four tokens, so that many CTAs keep row stores in flight over NVLink; only
+// the first writes the block's row map and return addresses
 template <typename T>
 __global__ void __launch_bounds__(128)
 p2p_dispatch_kernel(P2PArgs a, const T* __restrict__ x, const int32_t* __restrict__ topk_idx,
@@ -107,7 +110,8 @@ p2p_dispatch_kernel(P2PArgs a, const T* __restrict__ x, const int32_t* __restric
   for (int i = tid; i < 4 * E; i += 128) masks[i] = 0u;
   __syncthreads();
   const bool ok = ok_s != 0;
-  if (!ok && blk == 0 && tid == 0) *a.num_tiles = 0;  // no GEMM work after a failed wait
+  const bool first = blockIdx.y == 0;
+  if (!ok && blk == 0 && first && tid == 0) *a.num_tiles = 0;  // no GEMM work after a failed wait
   if (ok) {
     const int* all_counts = reinterpret_cast<const int*>(a.peer_base[a.me] + a.counts_off);
     for (int i = tid; i < G * E; i += 128) cnt[i] = all_counts[i];
@@ -133,7 +137,7 @@ p2p_dispatch_kernel(P2PArgs a, const T* __restrict__ x, const int32_t* __restric
       }
     }
     // block 0 writes this rank's tile map (segments of its local experts)
-    if (blk == 0 && tid == 0) {
+    if (blk == 0 && first && tid == 0) {
       *a.num_tiles = 0;
       int64_t t0 = 0;
       for (int el = 0; el < El; ++el) {
@@ -168,7 +172,7 @@ p2p_dispatch_kernel(P2PArgs a, const T* __restrict__ x, const int32_t* __restric
         row = base_s[e] + excl[blk * E + e] + wbase[warp * E + e] + __popc(masks[warp * E + e] & lt);
       }
     }
-    if (t < T_tok) {  // -1 also when the wait gave up: the combine then skips the row
+    if (t < T_tok && first) {  // -1 also when the wait gave up: the combine then skips the row
       a.dest_rank[t * K + k] = d;
       a.dest_row[t * K + k] = row;
       if (a.push && d >= 0) {
@@ -187,7 +191,8 @@ p2p_dispatch_kernel(P2PArgs a, const T* __restrict__ x, const int32_t* __restric
   const int nvec = static_cast<int>(a.H / V);
   const int64_t left = T_tok - blk * kTileM;
   const int ntok = ok ? static_cast<int>(left < kTileM ? (left > 0 ? left : 0) : kTileM) : 0;
-  for (int i = warp; i < ntok; i += 4) {
+  for (int i = warp + 4 * static_cast<int>(blockIdx.y); i < ntok;
+       i += 4 * static_cast<int>(gridDim.y)) {
     const T* src = x + (blk * kTileM + i) * a.H;
     for (int v0 = 0; v0 < nvec; v0 += 32 * 4) {
       uint4 buf[4];
@@ -214,7 +219,7 @@ p2p_dispatch_kernel(P2PArgs a, const T* __restrict__ x, const int32_t* __restric
   __syncthreads();
   if (tid == 0) {
     const int done = atomicAdd(a.block_counter, 1);
-    if (done == static_cast<int>(gridDim.x) - 1) {
+    if (done == static_cast<int>(gridDim.x * gridDim.y) - 1) {
       __threadfence_system();
       *a.block_counter = 0;
       for (int d = 0; d < G; ++d) st_release_sys(sig_ptr(a, d, 1, a.me), a.epoch);
@@ -364,7 +369,10 @@ cudaError_t launch_p2p_dispatch(int dtype, const P2PArgs& a, const void* x,
                                 const int32_t* topk_idx, const int* excl, int64_t T,
                                 size_t min_smem, cudaStream_t s) {
   const unsigned nblk = static_cast<unsigned>((T + kTileM - 1) / kTileM);
-  const unsigned grid = nblk > 0 ? nblk : 1;
+  // copy slices per routing block: about 2048 CTAs in all, at most 32 (one per four tokens)
+  unsigned slices = (2048u + (nblk > 0 ? nblk : 1u) - 1) / (nblk > 0 ? nblk : 1u);
+  if (slices > 32) slices = 32;
+  const dim3 grid(nblk > 0 ? nblk : 1, slices);
   size_t smem = p2p_dispatch_smem(a.E, a.K, a.G);
   if (smem < min_smem) smem = min_smem;  // see launch_p2p_combine
   if (dtype == kF32) {
