@@ -32,6 +32,8 @@
 // every dispatch).  Every spin is bounded by kWaitLimitNs and reports a status code.
 // No TMA or any bulk copy touches peer memory: peers are read and written with plain
 // vector loads and stores only.
+#include <stdlib.h>
+
 #include "common.cuh"
 #include "kernels.h"
 
@@ -372,6 +374,8 @@ cudaError_t launch_p2p_dispatch(int dtype, const P2PArgs& a, const void* x,
   // copy slices per routing block: about 2048 CTAs in all, at most 32 (one per four tokens)
   unsigned slices = (2048u + (nblk > 0 ? nblk : 1u) - 1) / (nblk > 0 ? nblk : 1u);
   if (slices > 32) slices = 32;
+  const char* one_slice = getenv("VMOE_EP_DISPATCH_SLICES");
+  if (one_slice && one_slice[0] == '1') slices = 1;
   const dim3 grid(nblk > 0 ? nblk : 1, slices);
   size_t smem = p2p_dispatch_smem(a.E, a.K, a.G);
   if (smem < min_smem) smem = min_smem;  // see launch_p2p_combine
