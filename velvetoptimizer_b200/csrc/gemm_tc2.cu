@@ -116,11 +116,12 @@ __device__ __forceinline__ void st_peer_v4(char* p, uint4 v) {
   *reinterpret_cast<uint4*>(p) = v;
 }
 
-// Epilogue warps per CTA: four (one per TMEM lane quarter), eight for the GLU backward,
-// whose epilogue (ERA and its derivative, two loads and two stores per element) outlasts a
-// tile's main loop with four: two warps share each lane quarter, each taking half the columns.
+// Epilogue warps per CTA: four (one per TMEM lane quarter), eight for the gated gate|up
+// epilogue and the GLU backward, whose per-element work (ERA, or ERA and its derivative with
+// two loads and two stores) outlasts a short tile's main loop with four (32 k-blocks at
+// d_model 2048): two warps share each lane quarter, each taking half the columns.
 template <int EPI>
-constexpr int pair_epi_warps() { return EPI == kPairGluBwd ? 8 : 4; }
+constexpr int pair_epi_warps() { return EPI == kPairGluBwd || EPI == kPairGated ? 8 : 4; }
 template <int EPI>
 constexpr int pair_threads() { return 64 + 32 * pair_epi_warps<EPI>(); }
 
@@ -245,7 +246,7 @@ tc_gemm_pair_kernel(const __grid_constant__ CUtensorMap a_map,
   } else {
     // ---------------- epilogue (warps 2..5, both CTAs) ----------------
     const int q = warp & 3;                     // TMEM lane quarter this warp may access
-    const int part = (warp - 2) >> 2;           // which share of the columns (GLU backward)
+    const int part = (warp - 2) >> 2;  // which share of the columns (eight epilogue warps)
     int local = 0;
     TileOrder order;
     for (int tile = pair; tile < total; tile += num_pairs, ++local) {
@@ -271,8 +272,9 @@ tc_gemm_pair_kernel(const __grid_constant__ CUtensorMap a_map,
         __nv_bfloat16* gup = args.gu_out ? static_cast<__nv_bfloat16*>(args.gu_out) +
                                                row * args.gu_ld + n * BN
                                          : nullptr;
+        constexpr int kColsG = (BN / 2) / (pair_epi_warps<EPI>() / 4);  // gate columns per warp
 #pragma unroll 1
-        for (int c = 0; c < BN / 2; c += 32) {
+        for (int c = part * kColsG; c < (part + 1) * kColsG; c += 32) {
           float g[32], u[32];
           tmem_ld32(t_row + c, g);
           tmem_ld32(t_row + BN / 2 + c, u);
