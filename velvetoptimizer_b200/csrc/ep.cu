@@ -249,15 +249,7 @@ int vmoe_ep_p2p_setup(vmoe_handle* h, int64_t max_tokens, int chunks, void* ipc_
     return fail(h, VMOE_ERR_UNSUPPORTED_SHAPE, "bf16 expert parallelism needs hidden %% %d == 0",
                 kDownTileN);
   const int64_t G = h->ep_size, E = h->E, K = h->K, El = h->E_local, H = h->H;
-  // uneven chunks (VMOE_EP_UNEVEN=1, three chunks or more): the first chunk's dispatch and
-  // the last one's combine overlap no other chunk's GEMMs, so those two chunks are half the
-  // size of the others; a chunk then holds at most max_tokens / (chunks - 1) tokens plus one
-  // 128-token block of rounding
-  const char* ue = getenv("VMOE_EP_UNEVEN");
-  const bool uneven = chunks >= 3 && ue && ue[0] == '1';
-  const int64_t chunk_tokens =
-      uneven ? round_up((max_tokens + chunks - 2) / (chunks - 1) + kTileM, kTileM)
-             : round_up((max_tokens + chunks - 1) / chunks, kTileM);
+  const int64_t chunk_tokens = round_up((max_tokens + chunks - 1) / chunks, kTileM);
   const int64_t cap = round_up(G * chunk_tokens * K + El * (h->tile_rows - 1), h->tile_rows);
   if (cap >= (static_cast<int64_t>(1) << 31))
     return fail(h, VMOE_ERR_UNSUPPORTED_SHAPE, "receive capacity of %lld rows is too large",
@@ -311,10 +303,10 @@ int vmoe_ep_p2p_setup(vmoe_handle* h, int64_t max_tokens, int chunks, void* ipc_
   h->p2p_cap_rows = cap;
   h->p2p_max_tokens = max_tokens;
   h->p2p_chunk_tokens = chunk_tokens;
-  h->p2p_uneven = uneven;
-  // VMOE_EP_RESERVE_SMS=n keeps n SMs out of the chunked GEMM grid for the NVLink transfer
-  // kernels (off by default: on 2 GPUs it measured slower)
-  h->p2p_reserve_sms = 0;
+  // with token chunks, 16 SMs stay out of the chunked GEMM grid for the NVLink transfer
+  // kernels of the other chunks (measured on 4 GPUs, 4 chunks: 14.7 ms per step with none
+  // reserved, 13.8 with 8, 13.5 with 16); VMOE_EP_RESERVE_SMS=n overrides
+  h->p2p_reserve_sms = chunks > 1 ? 16 : 0;
   if (const char* r = getenv("VMOE_EP_RESERVE_SMS")) h->p2p_reserve_sms = chunks > 1 ? atoi(r) : 0;
   if (h->p2p_reserve_sms < 0 || h->p2p_reserve_sms > h->num_sms / 2) h->p2p_reserve_sms = 0;
   return VMOE_OK;
@@ -445,8 +437,8 @@ int p2p_chunk(vmoe_handle* h, int c, const void* x, int64_t T, void* out, float*
   // than a GEMM CTA leaves free, so they only run on the reserved SMs
   const size_t xfer_smem = h->p2p_reserve_sms > 0 ? 48 * 1024 : 0;
   const int gemm_sms = h->num_sms - h->p2p_reserve_sms;
-  if ((rc = check(launch_p2p_dispatch(h->dtype, a, x, idx, excl, T, xfer_smem, s), "dispatch")) !=
-      VMOE_OK)
+  if ((rc = check(launch_p2p_dispatch(h->dtype, a, x, idx, excl, T, xfer_smem, !chained, s),
+                  "dispatch")) != VMOE_OK)
     return rc;
   if (chained && (e = cudaEventRecord(h->p2p_sent[c], s)) != cudaSuccess)
     return cuda_fail(h, e, "dispatch order");
@@ -483,29 +475,6 @@ struct HostIO {
   char* out_dev;  // staging, >= tokens rows
 };
 
-// Tokens [t0, t0 + tc) of chunk c of a T-token forward (T <= p2p_max_tokens).  Equal chunks
-// are p2p_chunk_tokens long from the start (later ones empty when T is small); uneven ones
-// split T with weights 1/2, 1, ..., 1, 1/2 at 128-token boundaries.  Either way every chunk
-// holds at most p2p_chunk_tokens tokens.
-void p2p_chunk_range(const vmoe_handle* h, int64_t T, int c, int64_t& t0, int64_t& tc) {
-  const int C = static_cast<int>(h->p2p.size());
-  if (!h->p2p_uneven) {
-    t0 = c * h->p2p_chunk_tokens;
-    tc = T - t0;
-    tc = tc < 0 ? 0 : (tc > h->p2p_chunk_tokens ? h->p2p_chunk_tokens : tc);
-    return;
-  }
-  // boundary i (0 < i < C) at T * (i - 1/2) / (C - 1), rounded up to 128 tokens
-  auto bound = [&](int i) -> int64_t {
-    if (i <= 0) return 0;
-    if (i >= C) return T;
-    const int64_t b = round_up((T * (2 * i - 1) + 2 * (C - 1) - 1) / (2 * (C - 1)), kTileM);
-    return b < T ? b : T;
-  };
-  t0 = bound(c);
-  tc = bound(c + 1) - t0;
-}
-
 // One fused expert-parallel forward (every rank calls it): on `s` with one chunk and no host
 // buffers, else chunk c on internal stream c (its NVLink exchange overlapping the other
 // chunks' GEMMs, and with host buffers its copies overlapping the other chunks too).
@@ -532,8 +501,9 @@ int ep_p2p_run(vmoe_handle* h, const void* x, int64_t T, void* out, float* route
     for (int c = 0; c < C; ++c) {
       cudaStream_t sc = h->p2p_streams[c];
       if ((e = cudaStreamWaitEvent(sc, h->p2p_start, 0)) != cudaSuccess) return cuda_fail(h, e, "wait");
-      int64_t t0, tc;
-      p2p_chunk_range(h, T, c, t0, tc);
+      const int64_t t0 = c * h->p2p_chunk_tokens;
+      int64_t tc = T - t0;
+      tc = tc < 0 ? 0 : (tc > h->p2p_chunk_tokens ? h->p2p_chunk_tokens : tc);
       const char* xbase = io ? io->x_dev : static_cast<const char*>(x);
       char* obase = io ? io->out_dev : static_cast<char*>(out);
       if (io) {

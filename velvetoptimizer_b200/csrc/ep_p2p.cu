@@ -32,8 +32,6 @@
 // every dispatch).  Every spin is bounded by kWaitLimitNs and reports a status code.
 // No TMA or any bulk copy touches peer memory: peers are read and written with plain
 // vector loads and stores only.
-#include <stdlib.h>
-
 #include "common.cuh"
 #include "kernels.h"
 
@@ -369,13 +367,13 @@ size_t p2p_dispatch_smem(int E, int K, int G) {
 
 cudaError_t launch_p2p_dispatch(int dtype, const P2PArgs& a, const void* x,
                                 const int32_t* topk_idx, const int* excl, int64_t T,
-                                size_t min_smem, cudaStream_t s) {
+                                size_t min_smem, bool spread, cudaStream_t s) {
   const unsigned nblk = static_cast<unsigned>((T + kTileM - 1) / kTileM);
-  // copy slices per routing block: about 2048 CTAs in all, at most 32 (one per four tokens)
+  // copy slices per routing block with `spread`: about 2048 CTAs in all, at most 32 (one per
+  // four tokens); else one CTA per routing block
   unsigned slices = (2048u + (nblk > 0 ? nblk : 1u) - 1) / (nblk > 0 ? nblk : 1u);
   if (slices > 32) slices = 32;
-  const char* one_slice = getenv("VMOE_EP_DISPATCH_SLICES");
-  if (one_slice && one_slice[0] == '1') slices = 1;
+  if (!spread) slices = 1;
   const dim3 grid(nblk > 0 ? nblk : 1, slices);
   size_t smem = p2p_dispatch_smem(a.E, a.K, a.G);
   if (smem < min_smem) smem = min_smem;  // see launch_p2p_combine

@@ -391,9 +391,12 @@ struct P2PArgs {
 cudaError_t launch_p2p_publish(const P2PArgs& a, const int* counts, cudaStream_t s);
 cudaError_t launch_p2p_wait(const P2PArgs& a, int which, cudaStream_t s);
 cudaError_t launch_p2p_signal(const P2PArgs& a, int which, cudaStream_t s);
+// spread: the copies of every routing block split over several CTAs (about 2048 in all) --
+// for a forward in one token chunk, whose dispatch runs alone; token chunks dispatch while
+// other chunks' GEMMs run, and there one CTA per routing block leaves the GEMMs their SMs
 cudaError_t launch_p2p_dispatch(int dtype, const P2PArgs& a, const void* x,
                                 const int32_t* topk_idx, const int* excl, int64_t T,
-                                size_t min_smem, cudaStream_t s);
+                                size_t min_smem, bool spread, cudaStream_t s);
 // Push mode: the combine reads every token's K rows from this rank's own return buffer.
 cudaError_t launch_p2p_combine_local(int dtype, const P2PArgs& a, const int32_t* topk_idx,
                                      const float* topk_w, int64_t T, void* out, size_t min_smem,

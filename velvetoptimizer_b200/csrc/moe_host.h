@@ -117,9 +117,6 @@ struct vmoe_handle {
   size_t p2p_ret_off = 0, p2p_back_off = 0;
   int64_t p2p_back_rows = 0;
   int64_t p2p_cap_rows = 0, p2p_max_tokens = 0, p2p_chunk_tokens = 0;
-  // token chunks of a forward: equal (c * p2p_chunk_tokens on), or uneven: the first and
-  // the last half the size of the others (p2p_chunk_range)
-  bool p2p_uneven = false;
   cudaStream_t p2p_streams[kMaxChunks] = {};
   cudaEvent_t p2p_start = nullptr;
   cudaEvent_t p2p_done[kMaxChunks] = {};
