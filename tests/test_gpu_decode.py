@@ -165,3 +165,21 @@ def test_decode_folded_plan_equals_plan_kernels(name, monkeypatch):
         assert n_a == n_b - 2, (n_a, n_b)
     folded.close()
     kernels.close()
+
+
+def test_decode_without_programmatic_dependent_launch(monkeypatch):
+    """A decode forward launches its kernels with programmatic dependent launch (each waits
+    for its predecessor before touching memory); without it (VMOE_PDL=0) the outputs are the
+    same to the bit."""
+    case = DECODE_CASES["t64_e8k2_bias"]
+    inp = bf16_inputs(make_inputs(case))
+    pdl = AbiLayer(case, inp, "bf16")
+    monkeypatch.setenv("VMOE_PDL", "0")
+    plain = AbiLayer(case, inp, "bf16")
+    monkeypatch.delenv("VMOE_PDL")
+    for _ in range(2):
+        a, b = pdl.run(inp["x"]), plain.run(inp["x"])
+        for key in ("out", "logits", "topk_idx", "topk_w", "counts", "aux"):
+            assert np.array_equal(a[key], b[key]), key
+    pdl.close()
+    plain.close()
